@@ -1,0 +1,341 @@
+"""Benchmark of the sparse-DiT refinement torso on B200 (BASELINE configs[1] by default).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload stack|attention]
+
+One step = one forward of the 24-block stack (C=1024, 16 heads x 64, GELU MLP 4x,
+1370 condition tokens) over T=32,768 voxel tokens of one object in fp16, inputs
+resident in HBM.  ``value`` is block tokens/s = blocks * T / step time (whole job,
+max over ranks).  With N>1 GPUs (torchrun) the T tokens are split into N query
+slices and every block all-gathers K/V over NCCL (strong scaling).
+
+Rank 0 prints one JSON line.  ``--impl reference`` times the CPU path instead: the
+oracle port of the reference block (the reference itself is Python that cannot travel
+to the GPU box), on the host's cores, on a row-sampled bounded sample of the same
+workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO / "hi3dv1.0-mlx_b200"))
+
+T_TOKENS = 32768
+CHANNELS = 1024
+HEADS = 16
+COND = 1370
+BLOCKS = 24
+GRID, RADIUS, THICK = 64, 24.0, 3.0
+
+
+def _peaks() -> dict:
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained", d["bf16_tflops"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+def _profile_traffic(name: str) -> float | None:
+    """DRAM bytes per launch recorded from an ncu capture in profiles/<name>.md (or None)."""
+    p = REPO / "profiles" / f"{name}.md"
+    if not p.exists():
+        return None
+    m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", p.read_text())
+    return float(m.group(1)) if m else None
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.file = None
+
+    def __enter__(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.file,
+                                         stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        if self.proc is None or self.file is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = [r.split(",") for r in Path(self.file.name).read_text().splitlines() if r.strip()]
+        os.unlink(self.file.name)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            r = [c.strip() for c in r]
+            if len(r) < 9:
+                continue
+            try:
+                sm.append(float(r[1]))
+                mx = float(r[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, r[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- inputs
+
+
+def make_inputs(seed: int = 0):
+    from hi3d_b200 import synthetic, transformer
+
+    coords = synthetic.shell_coords(T_TOKENS, GRID, RADIUS, THICK, seed=seed)
+    cos, sin = transformer.rope_tables(coords, CHANNELS // HEADS)
+    x = synthetic.features(T_TOKENS, CHANNELS, seed=seed + 1)
+    mod = synthetic.modulation(CHANNELS, 0.5, seed=seed + 2).astype(np.float16)
+    cond = synthetic.features(COND, CHANNELS, seed=seed + 3)
+    return coords, cos, sin, x, mod, cond
+
+
+def device_weights(device, seed: int = 100) -> list[dict]:
+    """24 blocks of N(0, 0.02) fp16 weights generated on the device (seeded)."""
+    import torch
+
+    from hi3d_b200.synthetic import BLOCK_LINEARS
+
+    g = torch.Generator(device=device).manual_seed(seed)
+    c, d = CHANNELS, CHANNELS // HEADS
+    blocks = []
+    for _ in range(BLOCKS):
+        w = {}
+        for name, i_mult, o_mult in BLOCK_LINEARS:
+            w[f"{name}.weight"] = (torch.randn((o_mult * c, i_mult * c), generator=g, device=device) * 0.02).half()
+            w[f"{name}.bias"] = (torch.randn(o_mult * c, generator=g, device=device) * 0.02).half()
+        w["cross_attn.to_kv.weight"] = (torch.randn((2 * c, c), generator=g, device=device) * 0.02).half()
+        w["cross_attn.to_kv.bias"] = (torch.randn(2 * c, generator=g, device=device) * 0.02).half()
+        w["modulation"] = torch.randn((1, 6 * c), generator=g, device=device) / c ** 0.5
+        w["norm2.weight"] = torch.ones(c, device=device)
+        w["norm2.bias"] = torch.zeros(c, device=device)
+        w["self_attn.q_rms_norm.gamma"] = torch.ones((HEADS, d), device=device)
+        w["self_attn.k_rms_norm.gamma"] = torch.ones((HEADS, d), device=device)
+        blocks.append(w)
+    return blocks
+
+
+# ----------------------------------------------------------------------------- CPU baseline
+
+
+def cpu_block_seconds(sample: int, seed: int = 0) -> tuple[float, dict]:
+    """One fp32 CPU block at the full workload size, estimated from a row sample (oracle port)."""
+    from hi3d_b200 import synthetic
+    from oracle import ops
+
+    coords, cos, sin, x, mod, cond = make_inputs(seed)
+    w = synthetic.block_weights(CHANNELS, CHANNELS, HEADS, seed=seed + 5)
+    return ops.block_seconds_sampled(w, x, mod, cos, sin, cond, HEADS, sample=sample, seed=seed)
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    sample = 1024
+    secs = []
+    for i in range(args.warmup + args.steps):
+        s, phases = cpu_block_seconds(sample, seed=0)
+        if i >= args.warmup:
+            secs.append(s)
+    per_block = statistics.median(secs)
+    value = T_TOKENS / per_block
+    cores = os.cpu_count()
+    line = {
+        "impl": "reference", "metric": "block_tokens_per_s", "value": value, "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_block * BLOCKS * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"cfg1 block on CPU: T={T_TOKENS}, C={CHANNELS}, H={HEADS}x64, L={COND}",
+                   "blocks": BLOCKS},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": f"one fp32 block at T={T_TOKENS}: K/V side on all rows, {sample} sampled query "
+                                   f"rows for the rest, scaled by T/{sample}; numpy oracle port of the reference"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- GPU arm
+
+
+def run_ours(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    from hi3d_b200 import _lib, attention, dist as hdist, transformer
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    _lib.load()
+
+    coords, cos, sin, x, mod, cond = make_inputs(0)
+    if T_TOKENS % world:
+        raise ValueError("T must divide by the number of GPUs")
+    tl = T_TOKENS // world
+    rows = slice(rank * tl, (rank + 1) * tl)
+    weights = device_weights(dev)
+    x_host = torch.from_numpy(x[rows]).pin_memory()
+    x_dev = x_host.to(dev)
+    cos_d, sin_d = torch.from_numpy(cos[rows]).to(dev), torch.from_numpy(sin[rows]).to(dev)
+    mod_d = torch.from_numpy(mod).to(dev)
+    cond_d = torch.from_numpy(cond).to(dev)
+    if world == 1:
+        stack = transformer.BlockStack(weights, HEADS)
+        run = lambda xin: stack(xin[None], mod_d, cos_d, sin_d, kvs)[0]
+    else:
+        stack = hdist.ShardedBlockStack(weights, HEADS)
+        run = lambda xin: stack(xin, mod_d, cos_d, sin_d, kvs)
+    kvs = [transformer.context_kv(w, cond_d, HEADS) for w in weights]
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        run(x_dev)
+    torch.cuda.synchronize()
+    barrier()
+
+    # ---- device-resident timed region (attention launches timed live with events)
+    stream = torch.cuda.current_stream()
+    attention.TIMER.start()
+    _lib.LAUNCHES[0] = 0
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        torch.cuda.synchronize()
+        barrier()
+        start.record(stream)
+        for _ in range(args.steps):
+            run(x_dev)
+        end.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+    launches = _lib.LAUNCHES[0]
+    attn = attention.TIMER.stop()
+    ms = start.elapsed_time(end)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_per_step = ms / args.steps
+    value = BLOCKS * T_TOKENS / (ms_per_step / 1e3)
+
+    # ---- end to end through the public API: pinned host input -> stack -> host output
+    out_host = torch.empty_like(x_host).pin_memory()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    barrier()
+    e0.record(stream)
+    for _ in range(args.steps):
+        xin = x_host.to(dev, non_blocking=True)
+        out_host.copy_(run(xin), non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_value = BLOCKS * T_TOKENS / (e2e_ms / args.steps / 1e3)
+
+    # ---- roofline of the dominant kernel (self-attention)
+    peaks = _peaks()
+    self_launches = [r for r in attn if r["kind"] == "self"]
+    avg_s = sum(r["ms"] for r in self_launches) / max(1, len(self_launches)) / 1e3
+    flops = self_launches[0]["flops"] if self_launches else 0.0
+    achieved = flops / avg_s / 1e12 if avg_s > 0 else 0.0
+    peak = peaks["bf16_tflops_sustained"]
+    attn_share = sum(r["ms"] for r in attn) / ms if ms > 0 else None
+    roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                "traffic": _profile_traffic("flash_attn_fwd_cfg1"), "kernel": "hi3d::attn::flash_fwd_kernel<half,64>",
+                "peak_source": f"{peaks['source']} bf16_tflops_sustained (burst {peaks['bf16_tflops']})",
+                "flops_per_launch": flops, "avg_launch_ms": avg_s * 1e3, "attention_time_share": attn_share}
+
+    line = {
+        "metric": "block_tokens_per_s", "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": {"workload": f"cfg1: {BLOCKS}-block sparse-DiT stack fwd, T={T_TOKENS} shell tokens in {GRID}^3, "
+                               f"C={CHANNELS}, {HEADS}x{CHANNELS // HEADS} heads, {COND} cond tokens, fp16",
+                   "blocks": BLOCKS, "tokens": T_TOKENS, "parallelism": f"query-sharded x{world}" if world > 1 else "none",
+                   "l2": "inputs larger than L2 (705 MB of weights + activations per step)"},
+        "roofline": roofline,
+        "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": x_host.numel() * 2,
+                "d2h_bytes_per_step": out_host.numel() * 2},
+        "gpu_launches": launches,
+        "clocks": clocks.summary(),
+        "attention_tflops": achieved,
+    }
+    if rank == 0 and world == 1:
+        secs, phases = cpu_block_seconds(1024, seed=0)
+        cpu_value = T_TOKENS / secs
+        line["cpu_baseline"] = {"value": cpu_value, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+                                "sample": f"one fp32 block at T={T_TOKENS} (numpy oracle port): K/V side on all "
+                                          f"rows, 1024 sampled query rows for the rest, scaled by T/1024"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

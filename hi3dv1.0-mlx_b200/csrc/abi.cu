@@ -1,0 +1,87 @@
+// Library-level parts of the C ABI: status strings, the device status word,
+// and the driver entry point used to encode TMA tensor maps.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "abi.h"
+#include "common.cuh"
+
+namespace hi3d {
+
+__device__ DeviceStatus g_status;
+
+static thread_local char t_last_error[512] = "";
+
+int set_error(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(t_last_error, sizeof(t_last_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(HI3D_ERR_CUDA, "%s: launch failed: %s", what, cudaGetErrorString(e));
+  return HI3D_OK;
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+int encode_tmap(CUtensorMap* map, CUtensorMapDataType type, int rank, const void* base, const uint64_t* dims,
+                const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swizzle) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return set_error(HI3D_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  cuuint32_t elem_strides[5] = {1, 1, 1, 1, 1};
+  CUresult r = fn(map, type, (cuuint32_t)rank, const_cast<void*>(base), (const cuuint64_t*)dims,
+                  (const cuuint64_t*)strides_bytes, (const cuuint32_t*)box, elem_strides,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(HI3D_ERR_INVALID_ARGUMENT, "cuTensorMapEncodeTiled failed (%d): rank %d dims %llu,%llu", (int)r,
+                     rank, (unsigned long long)dims[0], (unsigned long long)(rank > 1 ? dims[1] : 0));
+  return HI3D_OK;
+}
+
+}  // namespace hi3d
+
+using namespace hi3d;
+
+extern "C" int hi3d_version(void) { return 100; }
+
+extern "C" const char* hi3d_last_error_string(void) { return t_last_error; }
+
+extern "C" int hi3d_device_status(int* code, int* where, int* block, int* detail, int reset) {
+  DeviceStatus s;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return set_error(HI3D_ERR_CUDA, "cudaDeviceSynchronize: %s", cudaGetErrorString(e));
+  e = cudaMemcpyFromSymbol(&s, g_status, sizeof(s));
+  if (e != cudaSuccess) return set_error(HI3D_ERR_CUDA, "reading device status: %s", cudaGetErrorString(e));
+  if (code) *code = s.code;
+  if (where) *where = s.where;
+  if (block) *block = s.block;
+  if (detail) *detail = s.detail;
+  if (reset) {
+    DeviceStatus z = {0, 0, 0, 0};
+    e = cudaMemcpyToSymbol(g_status, &z, sizeof(z));
+    if (e != cudaSuccess) return set_error(HI3D_ERR_CUDA, "clearing device status: %s", cudaGetErrorString(e));
+  }
+  return HI3D_OK;
+}

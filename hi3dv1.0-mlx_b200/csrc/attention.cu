@@ -1,0 +1,401 @@
+// Flash attention forward for sm_100a: tcgen05 MMAs with TMEM accumulators,
+// TMA-fed K/V ring, two 128-row query tiles per CTA so the tensor core works
+// on one tile while the softmax warps process the other.
+//
+// Numerics (attention.py:84-233 of the reference): S = Q K^T in fp32; online
+// softmax in the exp2 domain (scale * log2 e folded into one multiplier);
+// P = exp2(s - m) summed unrounded into l, rounded to the I/O type for the
+// P V product, which accumulates in fp32; output O / l rounded once.
+//
+// CTA layout (384 threads):
+//   warp 0      TMA producer (one lane): Q tiles once, then K/V blocks into
+//               an NST-stage ring
+//   warp 1      MMA issuer (one lane); also owns the TMEM allocation
+//   warps 4-7   softmax + O correction + epilogue of query tile 0
+//   warps 8-11  the same for query tile 1
+// TMEM (512 columns): tile i at column 256*i holds S [BK cols, fp32],
+// P [BK/2 cols, packed 16-bit pairs] and O [D cols, fp32].
+#include <type_traits>
+
+#include "abi.h"
+#include "common.cuh"
+
+namespace hi3d {
+namespace attn {
+
+constexpr int kThreads = 384;
+constexpr int kRowsPerTile = 128;
+
+template <int D>
+struct Cfg {
+  static constexpr int NCH = (D + 63) / 64;           // 64-element (128-byte) chunks per row
+  static constexpr int BK = D <= 64 ? 128 : 64;       // keys per block
+  static constexpr int NST = D <= 64 ? 4 : 4;         // K/V ring stages
+  static constexpr int Q_CHUNK = kRowsPerTile * 128;  // bytes of one Q chunk
+  static constexpr int KV_CHUNK = BK * 128;           // bytes of one K or V chunk
+  static constexpr int Q_BYTES = 2 * NCH * Q_CHUNK;
+  static constexpr int KV_STAGE = NCH * KV_CHUNK;
+  static constexpr int S_COL = 0;
+  static constexpr int P_COL = BK;
+  static constexpr int O_COL = BK + BK / 2;
+  static constexpr int SMEM = Q_BYTES + 2 * NST * KV_STAGE + 1024 /*align*/ + 256 /*barriers*/;
+  static_assert(O_COL + D <= 256, "TMEM budget per tile");
+};
+
+struct Params {
+  void* out;
+  int64_t o_row, o_head, o_batch;
+  const int32_t* cu_q;
+  const int32_t* cu_k;
+  int64_t nq, nk;
+  int num_seqs, heads, tiles_per_seq;
+  int kv_batched;  // 0: one K/V set shared by all sequences
+  float scale2;  // softmax scale * log2(e)
+};
+
+struct Barriers {
+  uint64_t q_full;
+  uint64_t k_full[4];
+  uint64_t v_full[4];
+  uint64_t kv_empty[4];
+  uint64_t s_full[2];
+  uint64_t p_full[2];
+  uint64_t o_done[2];
+  uint32_t tmem_base;
+  int abort;
+};
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kThreads, 1)
+    flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                     const __grid_constant__ CUtensorMap tmV, const Params p) {
+  using C = Cfg<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;                         // [2][NCH][128 rows][128 B]
+  uint8_t* sK = smem + C::Q_BYTES;            // [NST][NCH][BK][128 B]
+  uint8_t* sV = sK + C::NST * C::KV_STAGE;    // [NST][NCH][BK][128 B]
+  Barriers* bar = reinterpret_cast<Barriers*>(sV + C::NST * C::KV_STAGE);
+
+  // ---- work decode: (head, sequence, 256-row query block) ----
+  const int bid = blockIdx.x;
+  const int t = bid % p.tiles_per_seq;
+  const int rest = bid / p.tiles_per_seq;
+  const int b = rest % p.num_seqs;
+  const int h = rest / p.num_seqs;
+  int64_t q_start = 0, q_len = p.nq, k_start = 0, k_len = p.nk;
+  int bq = b, bk = p.kv_batched ? b : 0;
+  if (p.cu_q) {
+    q_start = p.cu_q[b];
+    q_len = p.cu_q[b + 1] - q_start;
+    bq = 0;
+  }
+  if (p.cu_k) {
+    k_start = p.cu_k[b];
+    k_len = p.cu_k[b + 1] - k_start;
+    bk = 0;
+  }
+  const int64_t q_row0 = (int64_t)t * 2 * kRowsPerTile;
+  if (q_row0 >= q_len || k_len <= 0) return;  // uniform across the CTA
+  const int nblk = (int)((k_len + C::BK - 1) / C::BK);
+
+  const int warp = warp_id(), lane = lane_id();
+  if (threadIdx.x == 0) {
+    mbar_init(&bar->q_full, 1);
+    for (int s = 0; s < C::NST; ++s) {
+      mbar_init(&bar->k_full[s], 1);
+      mbar_init(&bar->v_full[s], 1);
+      mbar_init(&bar->kv_empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bar->s_full[i], 1);
+      mbar_init(&bar->p_full[i], kRowsPerTile);
+      mbar_init(&bar->o_done[i], 1);
+    }
+    bar->abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&bar->tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bar->tmem_base;
+  volatile int* abort = &bar->abort;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      mbar_arrive_expect_tx(&bar->q_full, C::Q_BYTES);
+      for (int i = 0; i < 2; ++i)
+        for (int c = 0; c < C::NCH; ++c)
+          tma_load_4d(sQ + (i * C::NCH + c) * C::Q_CHUNK, &tmQ, &bar->q_full, c * 64,
+                      (int)(q_start + q_row0 + i * kRowsPerTile), h, bq);
+      int issued = 0;
+      for (int j = 0; j < nblk; ++j) {
+        const int s = j % C::NST, n = j / C::NST;
+        if (!mbar_wait(&bar->kv_empty[s], (n & 1) ^ 1, abort, 1)) break;
+        const int krow = (int)(k_start + (int64_t)j * C::BK);
+        mbar_arrive_expect_tx(&bar->k_full[s], C::KV_STAGE);
+        for (int c = 0; c < C::NCH; ++c)
+          tma_load_4d(sK + s * C::KV_STAGE + c * C::KV_CHUNK, &tmK, &bar->k_full[s], c * 64, krow, h, bk);
+        mbar_arrive_expect_tx(&bar->v_full[s], C::KV_STAGE);
+        for (int c = 0; c < C::NCH; ++c)
+          tma_load_4d(sV + s * C::KV_STAGE + c * C::KV_CHUNK, &tmV, &bar->v_full[s], c * 64, krow, h, bk);
+        issued = j + 1;
+      }
+      if (*abort) {
+        // Drain: let every copy already issued land before the CTA exits.
+        mbar_wait(&bar->q_full, 0, abort, 2);
+        for (int j = (issued > C::NST ? issued - C::NST : 0); j < issued; ++j) {
+          const int s = j % C::NST, n = j / C::NST;
+          volatile int no_abort = 0;
+          mbar_wait(&bar->k_full[s], n & 1, &no_abort, 3);
+          mbar_wait(&bar->v_full[s], n & 1, &no_abort, 3);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    // Order per block j: PV_0(j), S_0(j+1), PV_1(j), S_1(j+1).  S_i(j+1) is
+    // issued as soon as softmax i has published P_i(j) (it has read S_i(j) by
+    // then), so one tile's softmax overlaps the other tile's MMAs.
+    if (lane == 0) {
+      constexpr uint32_t fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
+      constexpr uint32_t idesc_s = make_idesc(1, fmt, 0, 0, kRowsPerTile, C::BK);
+      constexpr uint32_t idesc_pv = make_idesc(1, fmt, 0, 1, kRowsPerTile, D);
+      const uint32_t sQa = smem_u32(sQ), sKa = smem_u32(sK), sVa = smem_u32(sV);
+      auto issue_s = [&](int i, int s) {
+#pragma unroll
+        for (int ks = 0; ks < D / 16; ++ks) {
+          const uint32_t off = (uint32_t)(ks & 3) * 32;
+          const uint64_t da = smem_desc(sQa + (i * C::NCH + (ks >> 2)) * C::Q_CHUNK + off, 16, 1024, kLayoutSW128);
+          const uint64_t db = smem_desc(sKa + s * C::KV_STAGE + (ks >> 2) * C::KV_CHUNK + off, 16, 1024, kLayoutSW128);
+          mma_f16_ss(tmem + 256 * i + C::S_COL, da, db, idesc_s, ks > 0 ? 1u : 0u);
+        }
+        tc_commit(&bar->s_full[i]);
+      };
+      bool ok = mbar_wait(&bar->q_full, 0, abort, 10) && mbar_wait(&bar->k_full[0], 0, abort, 11);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0, 0);
+        issue_s(1, 0);
+      }
+      for (int j = 0; ok && j < nblk; ++j) {
+        const int s = j % C::NST, n = j / C::NST;
+        const int s1 = (j + 1) % C::NST, n1 = (j + 1) / C::NST;
+        if (!(ok = mbar_wait(&bar->v_full[s], n & 1, abort, 13))) break;
+        if (j + 1 < nblk && !(ok = mbar_wait(&bar->k_full[s1], n1 & 1, abort, 11))) break;
+        for (int i = 0; i < 2; ++i) {
+          if (!(ok = mbar_wait(&bar->p_full[i], j & 1, abort, 14))) break;
+          tc_fence_after();
+#pragma unroll
+          for (int ks = 0; ks < C::BK / 16; ++ks) {
+            const uint64_t db = smem_desc(sVa + s * C::KV_STAGE + ks * 2048, C::KV_CHUNK, 1024, kLayoutSW128);
+            mma_f16_ts(tmem + 256 * i + C::O_COL, tmem + 256 * i + C::P_COL + ks * 8, db, idesc_pv,
+                       (j > 0 || ks > 0) ? 1u : 0u);
+          }
+          tc_commit(&bar->o_done[i]);
+          if (j + 1 < nblk) issue_s(i, s1);
+        }
+        if (!ok) break;
+        // Release the stage only when a later block will be loaded into it, so
+        // that every commit has a waiter before the CTA exits.
+        if (j + C::NST < nblk) tc_commit(&bar->kv_empty[s]);
+      }
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------ softmax
+    const int i = (warp - 4) >> 2;   // query tile
+    const int sub = warp & 3;        // TMEM lane quarter
+    const int row = sub * 32 + lane; // row within the tile
+    const uint32_t lane_addr = (uint32_t)(sub * 32) << 16;
+    const uint32_t tS = tmem + lane_addr + 256 * i + C::S_COL;
+    const uint32_t tP = tmem + lane_addr + 256 * i + C::P_COL;
+    const uint32_t tO = tmem + lane_addr + 256 * i + C::O_COL;
+    const float scale2 = p.scale2;
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nblk; ++j) {
+      if (!(ok = mbar_wait(&bar->s_full[i], j & 1, abort, 20))) break;
+      tc_fence_after();
+      uint32_t sv[C::BK];
+#pragma unroll
+      for (int c = 0; c < C::BK / 32; ++c) tmem_ld32(tS + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[c * 32]));
+      tmem_wait_ld();
+
+      const int klim = (int)(k_len - (int64_t)j * C::BK);  // valid keys in this block
+      if (klim < C::BK) {
+#pragma unroll
+        for (int e = 0; e < C::BK; ++e)
+          if (e >= klim) sv[e] = __float_as_uint(-INFINITY);
+      }
+      float mx = __uint_as_float(sv[0]);
+#pragma unroll
+      for (int e = 1; e < C::BK; ++e) mx = fmaxf(mx, __uint_as_float(sv[e]));
+      const float m_new = fmaxf(m_run, mx * scale2);
+      const float alpha = ex2_approx(m_run - m_new);
+      const float neg_m = -m_new;
+      float rsum = 0.f;
+#pragma unroll
+      for (int c = 0; c < C::BK / 32; ++c) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const float p0 = ex2_approx(fmaf(__uint_as_float(sv[c * 32 + 2 * e]), scale2, neg_m));
+          const float p1 = ex2_approx(fmaf(__uint_as_float(sv[c * 32 + 2 * e + 1]), scale2, neg_m));
+          rsum += p0 + p1;
+          pk[e] = Cvt<T>::pack2(p0, p1);
+        }
+        // P of block j overwrites P of block j-1: wait until P V of block
+        // j-1 has completed (which also makes O final for the correction).
+        if (c == 0 && j > 0) {
+          if (!(ok = mbar_wait(&bar->o_done[i], (j - 1) & 1, abort, 21))) break;
+          tc_fence_after();
+        }
+        tmem_st16(tP + c * 16, pk);
+      }
+      if (!ok) break;
+      // O *= alpha (skipped when no row of this warp changed its maximum)
+      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
+#pragma unroll
+        for (int oc = 0; oc < (D + 31) / 32; ++oc) {
+          uint32_t r[32];
+          tmem_ld32(tO + oc * 32, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
+          tmem_st32(tO + oc * 32, r);
+        }
+      }
+      l_run = l_run * alpha + rsum;
+      m_run = m_new;
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&bar->p_full[i]);
+    }
+    // ---- epilogue: O / l -> out[row, h*D + d]
+    if (ok && mbar_wait(&bar->o_done[i], (nblk - 1) & 1, abort, 22)) {
+      tc_fence_after();
+      const int64_t qrow = q_row0 + i * kRowsPerTile + row;
+      const float inv = 1.0f / l_run;
+      T* dst = reinterpret_cast<T*>(p.out) + (int64_t)(p.cu_q ? 0 : b) * p.o_batch + (q_start + qrow) * p.o_row +
+               (int64_t)h * p.o_head;
+#pragma unroll
+      for (int oc = 0; oc < (D + 31) / 32; ++oc) {
+        uint32_t r[32];
+        tmem_ld32(tO + oc * 32, r);
+        tmem_wait_ld();
+        if (qrow < q_len) {
+#pragma unroll
+          for (int e = 0; e < 32 && oc * 32 + e < D; e += 8) {
+            uint4 w;
+            w.x = Cvt<T>::pack2(__uint_as_float(r[e]) * inv, __uint_as_float(r[e + 1]) * inv);
+            w.y = Cvt<T>::pack2(__uint_as_float(r[e + 2]) * inv, __uint_as_float(r[e + 3]) * inv);
+            w.z = Cvt<T>::pack2(__uint_as_float(r[e + 4]) * inv, __uint_as_float(r[e + 5]) * inv);
+            w.w = Cvt<T>::pack2(__uint_as_float(r[e + 6]) * inv, __uint_as_float(r[e + 7]) * inv);
+            *reinterpret_cast<uint4*>(dst + oc * 32 + e) = w;
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace attn
+
+static int make_attn_map(CUtensorMap* map, const void* base, int dtype, int D, int64_t rows, int heads,
+                         int64_t batch, int64_t row_stride, int64_t head_stride, int64_t batch_stride, int box_rows) {
+  const uint64_t esz = 2;
+  uint64_t dims[4] = {(uint64_t)D, (uint64_t)rows, (uint64_t)heads, (uint64_t)batch};
+  uint64_t strides[3] = {(uint64_t)row_stride * esz, (uint64_t)head_stride * esz,
+                         (uint64_t)(batch_stride ? batch_stride : rows * row_stride) * esz};
+  uint32_t box[4] = {64, (uint32_t)box_rows, 1, 1};
+  CUtensorMapDataType t = dtype == HI3D_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  return encode_tmap(map, t, 4, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+template <typename T, int D>
+static int launch_attn(const hi3d_attn_args* a, cudaStream_t st) {
+  using C = attn::Cfg<D>;
+  const bool varlen_q = a->cu_seqlens_q != nullptr, varlen_k = a->cu_seqlens_k != nullptr;
+  const int64_t qb = varlen_q ? 1 : a->num_seqs;
+  const int64_t kb = varlen_k ? 1 : (a->k_batch == 0 ? 1 : a->num_seqs);
+  CUtensorMap mq, mk, mv;
+  int rc;
+  if ((rc = make_attn_map(&mq, a->q, a->dtype, D, a->nq, a->heads, qb, a->q_row, a->q_head, a->q_batch,
+                          attn::kRowsPerTile)))
+    return rc;
+  if ((rc = make_attn_map(&mk, a->k, a->dtype, D, a->nk, a->heads, kb, a->k_row, a->k_head, a->k_batch, C::BK)))
+    return rc;
+  if ((rc = make_attn_map(&mv, a->v, a->dtype, D, a->nk, a->heads, kb, a->v_row, a->v_head, a->v_batch, C::BK)))
+    return rc;
+  attn::Params p;
+  p.out = a->out;
+  p.o_row = a->o_row;
+  p.o_head = a->o_head;
+  p.o_batch = a->o_batch;
+  p.cu_q = a->cu_seqlens_q;
+  p.cu_k = a->cu_seqlens_k;
+  p.nq = a->nq;
+  p.nk = a->nk;
+  p.num_seqs = a->num_seqs;
+  p.heads = a->heads;
+  p.kv_batched = (!varlen_k && a->k_batch != 0) ? 1 : 0;
+  const int64_t qlen_max = varlen_q ? a->max_seqlen_q : a->nq;
+  p.tiles_per_seq = (int)((qlen_max + 2 * attn::kRowsPerTile - 1) / (2 * attn::kRowsPerTile));
+  p.scale2 = a->scale * 1.4426950408889634f;
+  const int64_t grid = (int64_t)p.tiles_per_seq * a->num_seqs * a->heads;
+  if (grid == 0) return HI3D_OK;
+  if (grid > 0x7fffffff) return set_error(HI3D_ERR_INVALID_ARGUMENT, "flash_attn: too many tiles");
+  auto kern = attn::flash_fwd_kernel<T, D>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+  if (e != cudaSuccess) return set_error(HI3D_ERR_CUDA, "flash_attn: smem attribute: %s", cudaGetErrorString(e));
+  kern<<<(unsigned)grid, attn::kThreads, C::SMEM, st>>>(mq, mk, mv, p);
+  return check_launch("flash_attn_fwd");
+}
+
+}  // namespace hi3d
+
+using namespace hi3d;
+
+extern "C" int hi3d_flash_attn_fwd(const hi3d_attn_args* a, void* stream) {
+  if (!a || !a->q || !a->k || !a->v || !a->out)
+    return set_error(HI3D_ERR_INVALID_ARGUMENT, "flash_attn: null pointer");
+  if (a->dtype != HI3D_F16 && a->dtype != HI3D_BF16)
+    return set_error(HI3D_ERR_INVALID_ARGUMENT, "flash_attn: dtype must be f16 or bf16");
+  if (a->head_dim != 64 && a->head_dim != 96 && a->head_dim != 128)
+    return set_error(HI3D_ERR_UNSUPPORTED, "flash_attn: head_dim %d not supported (64, 96, 128)", a->head_dim);
+  if (a->num_seqs < 0 || a->heads <= 0 || a->nq < 0 || a->nk < 0)
+    return set_error(HI3D_ERR_INVALID_ARGUMENT, "flash_attn: negative sizes");
+  if (!aligned16(a->q) || !aligned16(a->k) || !aligned16(a->v) || !aligned16(a->out))
+    return set_error(HI3D_ERR_INVALID_ARGUMENT, "flash_attn: pointers must be 16-byte aligned");
+  const int64_t strides[] = {a->q_row, a->q_head, a->q_batch, a->k_row, a->k_head, a->k_batch,
+                             a->v_row, a->v_head, a->v_batch, a->o_row, a->o_head, a->o_batch};
+  for (int64_t s : strides)
+    if (s < 0 || s % 8) return set_error(HI3D_ERR_INVALID_ARGUMENT, "flash_attn: strides must be multiples of 8");
+  if (a->cu_seqlens_q && a->max_seqlen_q <= 0 && a->nq > 0)
+    return set_error(HI3D_ERR_INVALID_ARGUMENT, "flash_attn: varlen needs max_seqlen_q");
+  if (a->nq == 0 || a->num_seqs == 0) return HI3D_OK;
+  if (a->nq > 0x7fffffff || a->nk > 0x7fffffff)
+    return set_error(HI3D_ERR_INVALID_ARGUMENT, "flash_attn: more than 2^31 rows");
+  cudaStream_t st = as_stream(stream);
+  const bool bf = a->dtype == HI3D_BF16;
+  switch (a->head_dim) {
+    case 64: return bf ? launch_attn<__nv_bfloat16, 64>(a, st) : launch_attn<__half, 64>(a, st);
+    case 96: return bf ? launch_attn<__nv_bfloat16, 96>(a, st) : launch_attn<__half, 96>(a, st);
+    default: return bf ? launch_attn<__nv_bfloat16, 128>(a, st) : launch_attn<__half, 128>(a, st);
+  }
+}

@@ -1,0 +1,392 @@
+// HBM-bound row kernels of the block: LayerNorm + adaLN modulation,
+// RoPE + per-head QK RMS norm + head split, gate/residual and GELU epilogues.
+//
+// All of them move 16 bytes per lane per access and reduce with warp
+// shuffles; none touches shared memory.  Rounding follows the reference
+// operators exactly where it is specified (see each kernel).
+#include "abi.h"
+#include "common.cuh"
+
+namespace hi3d {
+
+// 16-byte vector of 8 I/O elements.
+struct alignas(16) Vec8 {
+  uint32_t w[4];
+};
+
+template <typename T>
+__device__ __forceinline__ void unpack8(const Vec8& v, float (&f)[8]) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const T* h = reinterpret_cast<const T*>(&v.w[i]);
+    f[2 * i] = Cvt<T>::to_f(h[0]);
+    f[2 * i + 1] = Cvt<T>::to_f(h[1]);
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ T round_t(float v) {
+  return Cvt<T>::from_f(v);
+}
+
+// ---------------------------------------------------------------------------
+// LayerNorm32 (+ affine) (+ modulation), one warp per row.
+//
+// Semantics of kernels.py:162-201: fp32 sum -> mean = sum / C; fp32 sum of
+// squared deviations; inv = 1 / sqrt(sumsq / C + eps) (IEEE sqrt and divide);
+// y = (x - mean) * inv; affine y = y * w + b without contraction; h = T(y);
+// modulation h = T(float(h) * float(scale)); h = T(float(h) + float(shift)).
+// NCH = ceil(channels / 256) chunks of 8 elements per lane held in registers
+// (channels % 8 == 0, <= 4096).
+// ---------------------------------------------------------------------------
+template <typename T, int NCH, bool AFFINE, bool MODULATE>
+__global__ void __launch_bounds__(256) ln_mod_kernel(const T* __restrict__ x, T* __restrict__ out, int64_t rows,
+                                                     int C, float eps, const float* __restrict__ weight,
+                                                     const float* __restrict__ bias, const T* __restrict__ scale,
+                                                     const T* __restrict__ shift, int64_t rows_per_batch,
+                                                     int64_t mod_stride) {
+  const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int lane = threadIdx.x & 31;
+  const T* xr = x + row * C;
+  T* yr = out + row * C;
+
+  // chunk c covers channels [c*256, c*256+256); only the last chunk can be partial
+  float v[NCH][8];
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    Vec8 raw = {};
+    if (c * 256 + lane * 8 < C) raw = *reinterpret_cast<const Vec8*>(xr + c * 256 + lane * 8);
+    unpack8<T>(raw, v[c]);
+  }
+  float sum = 0.f;
+#pragma unroll
+  for (int c = 0; c < NCH; ++c)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) sum += v[c][i];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  const float mean = __fdiv_rn(sum, (float)C);
+  float sq = 0.f;
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    if (c * 256 + lane * 8 < C) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float d = __fsub_rn(v[c][i], mean);
+        sq = __fmaf_rn(d, d, sq);
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sq, (float)C), eps)));
+
+  const int64_t mb = MODULATE ? (row / rows_per_batch) * mod_stride : 0;
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    const int base = c * 256 + lane * 8;
+    if (base >= C) continue;
+    Vec8 o;
+    Vec8 sc, sh;
+    if (MODULATE) {
+      sc = *reinterpret_cast<const Vec8*>(scale + mb + base);
+      sh = *reinterpret_cast<const Vec8*>(shift + mb + base);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; i += 2) {
+      float y0 = __fmul_rn(__fsub_rn(v[c][i], mean), inv);
+      float y1 = __fmul_rn(__fsub_rn(v[c][i + 1], mean), inv);
+      if (AFFINE) {
+        y0 = __fadd_rn(__fmul_rn(y0, weight[base + i]), bias[base + i]);
+        y1 = __fadd_rn(__fmul_rn(y1, weight[base + i + 1]), bias[base + i + 1]);
+      }
+      T h0 = round_t<T>(y0), h1 = round_t<T>(y1);
+      if (MODULATE) {
+        const T* s2 = reinterpret_cast<const T*>(&sc.w[i / 2]);
+        const T* t2 = reinterpret_cast<const T*>(&sh.w[i / 2]);
+        h0 = round_t<T>(__fmul_rn(Cvt<T>::to_f(h0), Cvt<T>::to_f(s2[0])));
+        h1 = round_t<T>(__fmul_rn(Cvt<T>::to_f(h1), Cvt<T>::to_f(s2[1])));
+        h0 = round_t<T>(__fadd_rn(Cvt<T>::to_f(h0), Cvt<T>::to_f(t2[0])));
+        h1 = round_t<T>(__fadd_rn(Cvt<T>::to_f(h1), Cvt<T>::to_f(t2[1])));
+      }
+      T pair[2] = {h0, h1};
+      o.w[i / 2] = *reinterpret_cast<uint32_t*>(pair);
+    }
+    *reinterpret_cast<Vec8*>(yr + base) = o;
+  }
+}
+
+template <typename T, int NCH>
+static void launch_ln(const void* x, void* out, int64_t rows, int C, float eps, const float* w, const float* b,
+                      const void* sc, const void* sh, int64_t rpb, int64_t ms, cudaStream_t st) {
+  dim3 grid((unsigned)((rows + 7) / 8)), block(256);
+  const T* xt = (const T*)x;
+  T* ot = (T*)out;
+  const T* s = (const T*)sc;
+  const T* t = (const T*)sh;
+  if (w && sc)
+    ln_mod_kernel<T, NCH, true, true><<<grid, block, 0, st>>>(xt, ot, rows, C, eps, w, b, s, t, rpb, ms);
+  else if (w)
+    ln_mod_kernel<T, NCH, true, false><<<grid, block, 0, st>>>(xt, ot, rows, C, eps, w, b, s, t, rpb, ms);
+  else if (sc)
+    ln_mod_kernel<T, NCH, false, true><<<grid, block, 0, st>>>(xt, ot, rows, C, eps, w, b, s, t, rpb, ms);
+  else
+    ln_mod_kernel<T, NCH, false, false><<<grid, block, 0, st>>>(xt, ot, rows, C, eps, w, b, s, t, rpb, ms);
+}
+
+template <typename T>
+static int dispatch_ln(const void* x, void* out, int64_t rows, int C, float eps, const float* w, const float* b,
+                       const void* sc, const void* sh, int64_t rpb, int64_t ms, cudaStream_t st) {
+  switch ((C + 255) / 256) {
+#define HI3D_LN_CASE(n) \
+  case n:               \
+    launch_ln<T, n>(x, out, rows, C, eps, w, b, sc, sh, rpb, ms, st); break;
+    HI3D_LN_CASE(1)
+    HI3D_LN_CASE(2)
+    HI3D_LN_CASE(3)
+    HI3D_LN_CASE(4)
+    HI3D_LN_CASE(5)
+    HI3D_LN_CASE(6)
+    HI3D_LN_CASE(7)
+    HI3D_LN_CASE(8)
+    HI3D_LN_CASE(9)
+    HI3D_LN_CASE(10)
+    HI3D_LN_CASE(11)
+    HI3D_LN_CASE(12)
+    HI3D_LN_CASE(13)
+    HI3D_LN_CASE(14)
+    HI3D_LN_CASE(15)
+    HI3D_LN_CASE(16)
+#undef HI3D_LN_CASE
+    default:
+      return set_error(HI3D_ERR_UNSUPPORTED, "layer_norm_modulate: channels %d not supported (multiple of 8, <= 4096)",
+                       C);
+  }
+  return check_launch("layer_norm_modulate");
+}
+
+// ---------------------------------------------------------------------------
+// RoPE + QK RMS norm + split.  A group of G = D/8 lanes (rounded up to a power
+// of two) handles one (row, part, head); each active lane owns 8 consecutive
+// channels = 4 rotation pairs.  Norm reduction by xor-shuffles in the group.
+// kernels.py:22-57 semantics: re = x0 c - x1 s, im = x0 s + x1 c (fp32);
+// nrm = max(sqrt(sum re^2 + im^2), 1e-12); y = re / nrm * g * sqrt(D).
+// ---------------------------------------------------------------------------
+template <typename T, int D>
+__global__ void __launch_bounds__(256) qkv_rope_rms_kernel(const T* __restrict__ qkv, const float* __restrict__ cosv,
+                                                           const float* __restrict__ sinv,
+                                                           const float* __restrict__ gq,
+                                                           const float* __restrict__ gk, T* __restrict__ q,
+                                                           T* __restrict__ k, T* __restrict__ v, int64_t M,
+                                                           int64_t N, int H, int token_major) {
+  constexpr int ACTIVE = D / 8;
+  constexpr int G = ACTIVE <= 8 ? 8 : (ACTIVE <= 16 ? 16 : 32);
+  constexpr int GROUPS_PER_WARP = 32 / G;
+  const int lane = threadIdx.x & 31;
+  const int sub = lane % G;
+  const int64_t unit = ((int64_t)blockIdx.x * 8 + (threadIdx.x >> 5)) * GROUPS_PER_WARP + lane / G;
+  const int64_t total = M * 3 * H;
+  const bool valid = unit < total && sub < ACTIVE;
+  if (unit >= total) return;
+  const int64_t m = unit / (3 * H);
+  const int ph = (int)(unit % (3 * H));
+  const int part = ph / H, h = ph % H;
+  const int64_t b = m / N, n = m % N;
+  const T* src = qkv + (m * 3 + part) * (int64_t)H * D;
+  const int64_t dst_off = token_major ? ((b * N + n) * H + h) * D : ((b * H + h) * N + n) * D;
+  const int c0 = sub * 8;
+  Vec8 raw = {};
+  if (valid) raw = *reinterpret_cast<const Vec8*>(src + c0);
+  if (part == 2) {
+    if (valid) *reinterpret_cast<Vec8*>(v + dst_off + c0) = raw;
+    return;
+  }
+  float x[8];
+  unpack8<T>(raw, x);
+  float r[8];
+  float ss = 0.f;
+  if (valid) {
+    const float* cs = cosv + n * (D / 2) + c0 / 2;
+    const float* sn = sinv + n * (D / 2) + c0 / 2;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float c = cs[i], s = sn[i];
+      r[2 * i] = x[2 * i] * c - x[2 * i + 1] * s;
+      r[2 * i + 1] = x[2 * i] * s + x[2 * i + 1] * c;
+      ss += r[2 * i] * r[2 * i] + r[2 * i + 1] * r[2 * i + 1];
+    }
+  }
+#pragma unroll
+  for (int o = G / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if (!valid) return;
+  const float nrm = fmaxf(sqrtf(ss), 1e-12f);
+  const float scale = sqrtf((float)D);
+  const float* g = (part == 0 ? gq : gk) + h * D + c0;
+  Vec8 o;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) o.w[i] = Cvt<T>::pack2(r[2 * i] / nrm * g[2 * i] * scale, r[2 * i + 1] / nrm * g[2 * i + 1] * scale);
+  *reinterpret_cast<Vec8*>((part == 0 ? q : k) + dst_off + c0) = o;
+}
+
+template <typename T>
+static int dispatch_rope(const void* qkv, const float* c, const float* s, const float* gq, const float* gk, void* q,
+                         void* k, void* v, int64_t M, int64_t N, int H, int D, int tm, cudaStream_t st) {
+  const int64_t units = M * 3 * H;
+  auto grid_for = [&](int G) { return (unsigned)(((units + (32 / G) - 1) / (32 / G) + 7) / 8); };
+#define HI3D_ROPE(DD, GG)                                                                                            \
+  qkv_rope_rms_kernel<T, DD><<<grid_for(GG), 256, 0, st>>>((const T*)qkv, c, s, gq, gk, (T*)q, (T*)k, (T*)v, M, N, \
+                                                           H, tm)
+  switch (D) {
+    case 32: HI3D_ROPE(32, 8); break;
+    case 64: HI3D_ROPE(64, 8); break;
+    case 96: HI3D_ROPE(96, 16); break;
+    case 128: HI3D_ROPE(128, 16); break;
+    default:
+      return set_error(HI3D_ERR_UNSUPPORTED, "qkv_rope_rms: head_dim %d not supported (32, 64, 96, 128)", D);
+  }
+#undef HI3D_ROPE
+  return check_launch("qkv_rope_rms");
+}
+
+// ---------------------------------------------------------------------------
+// x <- T(x + T(y * gate)), 8 elements per thread.
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void gate_residual_kernel(T* __restrict__ x, const T* __restrict__ y, const T* __restrict__ gate,
+                                     int64_t rows, int C, int64_t rows_per_batch, int64_t gate_stride) {
+  const int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  if (i >= rows * C) return;
+  const int64_t row = i / C;
+  const int c = (int)(i % C);
+  Vec8 xv = *reinterpret_cast<const Vec8*>(x + i);
+  Vec8 yv = *reinterpret_cast<const Vec8*>(y + i);
+  Vec8 gv;
+  if (gate) gv = *reinterpret_cast<const Vec8*>(gate + (row / rows_per_batch) * gate_stride + c);
+  Vec8 o;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const T* xa = reinterpret_cast<const T*>(&xv.w[j]);
+    const T* ya = reinterpret_cast<const T*>(&yv.w[j]);
+    T res[2];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      float yy = Cvt<T>::to_f(ya[e]);
+      if (gate) yy = Cvt<T>::to_f(round_t<T>(__fmul_rn(yy, Cvt<T>::to_f(reinterpret_cast<const T*>(&gv.w[j])[e]))));
+      res[e] = round_t<T>(__fadd_rn(Cvt<T>::to_f(xa[e]), yy));
+    }
+    o.w[j] = *reinterpret_cast<uint32_t*>(res);
+  }
+  *reinterpret_cast<Vec8*>(x + i) = o;
+}
+
+// gelu_tanh in fp32: 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))), rounded once.
+template <typename T>
+__global__ void gelu_kernel(const T* __restrict__ x, T* __restrict__ out, int64_t count) {
+  const int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  if (i >= count) return;
+  Vec8 xv = *reinterpret_cast<const Vec8*>(x + i);
+  float f[8];
+  unpack8<T>(xv, f);
+  Vec8 o;
+  const float k0 = 0.7978845608028654f;  // sqrt(2 / pi)
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    float a = f[2 * j], b = f[2 * j + 1];
+    float ga = 0.5f * a * (1.0f + tanhf(k0 * (a + 0.044715f * a * a * a)));
+    float gb = 0.5f * b * (1.0f + tanhf(k0 * (b + 0.044715f * b * b * b)));
+    o.w[j] = Cvt<T>::pack2(ga, gb);
+  }
+  *reinterpret_cast<Vec8*>(out + i) = o;
+}
+
+}  // namespace hi3d
+
+using namespace hi3d;
+
+extern "C" int hi3d_layer_norm_modulate(const void* x, void* out, int64_t rows, int64_t channels, float eps,
+                                        const float* weight, const float* bias, const void* scale,
+                                        const void* shift, int64_t rows_per_batch, int64_t mod_stride, int dtype,
+                                        void* stream) {
+  if (!x || !out || rows < 0 || channels <= 0)
+    return set_error(HI3D_ERR_INVALID_ARGUMENT, "layer_norm_modulate: bad pointers or sizes");
+  if (channels % 8 || channels > 4096)
+    return set_error(HI3D_ERR_UNSUPPORTED, "layer_norm_modulate: channels must be a multiple of 8 and <= 4096");
+  if ((weight == nullptr) != (bias == nullptr) || (scale == nullptr) != (shift == nullptr))
+    return set_error(HI3D_ERR_INVALID_ARGUMENT, "layer_norm_modulate: weight/bias and scale/shift come in pairs");
+  if (!aligned16(x) || !aligned16(out) || (scale && (!aligned16(scale) || !aligned16(shift))))
+    return set_error(HI3D_ERR_INVALID_ARGUMENT, "layer_norm_modulate: pointers must be 16-byte aligned");
+  if (scale && (rows_per_batch <= 0 || mod_stride % 8))
+    return set_error(HI3D_ERR_INVALID_ARGUMENT, "layer_norm_modulate: bad rows_per_batch / mod_stride");
+  if (rows == 0) return HI3D_OK;
+  if (rows_per_batch <= 0) rows_per_batch = rows;
+  cudaStream_t st = as_stream(stream);
+  if (dtype == HI3D_F16)
+    return dispatch_ln<__half>(x, out, rows, (int)channels, eps, weight, bias, scale, shift, rows_per_batch,
+                               mod_stride, st);
+  if (dtype == HI3D_BF16)
+    return dispatch_ln<__nv_bfloat16>(x, out, rows, (int)channels, eps, weight, bias, scale, shift, rows_per_batch,
+                                      mod_stride, st);
+  return set_error(HI3D_ERR_INVALID_ARGUMENT, "layer_norm_modulate: dtype must be f16 or bf16");
+}
+
+extern "C" int hi3d_qkv_rope_rms(const void* qkv, const float* cos, const float* sin, const float* gamma_q,
+                                 const float* gamma_k, void* q, void* k, void* v, int64_t batch, int64_t n, int heads,
+                                 int head_dim, int out_layout, int dtype, void* stream) {
+  if (!qkv || !cos || !sin || !gamma_q || !gamma_k || !q || !k || !v || batch < 0 || n < 0 || heads <= 0)
+    return set_error(HI3D_ERR_INVALID_ARGUMENT, "qkv_rope_rms: bad pointers or sizes");
+  if (head_dim % 2) return set_error(HI3D_ERR_INVALID_ARGUMENT, "qkv_rope_rms: head_dim must be even");
+  if (out_layout != 0 && out_layout != 1)
+    return set_error(HI3D_ERR_INVALID_ARGUMENT, "qkv_rope_rms: out_layout must be 0 ([B,H,N,D]) or 1 ([B,N,H,D])");
+  if (!aligned16(qkv) || !aligned16(q) || !aligned16(k) || !aligned16(v))
+    return set_error(HI3D_ERR_INVALID_ARGUMENT, "qkv_rope_rms: pointers must be 16-byte aligned");
+  const int64_t M = batch * n;
+  if (M == 0) return HI3D_OK;
+  cudaStream_t st = as_stream(stream);
+  if (dtype == HI3D_F16)
+    return dispatch_rope<__half>(qkv, cos, sin, gamma_q, gamma_k, q, k, v, M, n, heads, head_dim, out_layout, st);
+  if (dtype == HI3D_BF16)
+    return dispatch_rope<__nv_bfloat16>(qkv, cos, sin, gamma_q, gamma_k, q, k, v, M, n, heads, head_dim, out_layout,
+                                        st);
+  return set_error(HI3D_ERR_INVALID_ARGUMENT, "qkv_rope_rms: dtype must be f16 or bf16");
+}
+
+extern "C" int hi3d_gate_residual(void* x, const void* y, const void* gate, int64_t rows, int64_t channels,
+                                  int64_t rows_per_batch, int64_t gate_stride, int dtype, void* stream) {
+  if (!x || !y || rows < 0 || channels <= 0 || channels % 8)
+    return set_error(HI3D_ERR_INVALID_ARGUMENT, "gate_residual: bad pointers or sizes (channels % 8 == 0)");
+  if (!aligned16(x) || !aligned16(y) || (gate && !aligned16(gate)) || gate_stride % 8)
+    return set_error(HI3D_ERR_INVALID_ARGUMENT, "gate_residual: pointers must be 16-byte aligned");
+  if (rows == 0) return HI3D_OK;
+  if (rows_per_batch <= 0) rows_per_batch = rows;
+  const int64_t threads = rows * channels / 8;
+  dim3 grid((unsigned)((threads + 255) / 256));
+  cudaStream_t st = as_stream(stream);
+  if (dtype == HI3D_F16)
+    gate_residual_kernel<__half><<<grid, 256, 0, st>>>((__half*)x, (const __half*)y, (const __half*)gate, rows,
+                                                       (int)channels, rows_per_batch, gate_stride);
+  else if (dtype == HI3D_BF16)
+    gate_residual_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>((__nv_bfloat16*)x, (const __nv_bfloat16*)y,
+                                                              (const __nv_bfloat16*)gate, rows, (int)channels,
+                                                              rows_per_batch, gate_stride);
+  else
+    return set_error(HI3D_ERR_INVALID_ARGUMENT, "gate_residual: dtype must be f16 or bf16");
+  return check_launch("gate_residual");
+}
+
+extern "C" int hi3d_gelu_tanh(const void* x, void* out, int64_t count, int dtype, void* stream) {
+  if (!x || !out || count < 0 || count % 8)
+    return set_error(HI3D_ERR_INVALID_ARGUMENT, "gelu_tanh: bad pointers or count (multiple of 8)");
+  if (!aligned16(x) || !aligned16(out))
+    return set_error(HI3D_ERR_INVALID_ARGUMENT, "gelu_tanh: pointers must be 16-byte aligned");
+  if (count == 0) return HI3D_OK;
+  dim3 grid((unsigned)((count / 8 + 255) / 256));
+  cudaStream_t st = as_stream(stream);
+  if (dtype == HI3D_F16)
+    gelu_kernel<__half><<<grid, 256, 0, st>>>((const __half*)x, (__half*)out, count);
+  else if (dtype == HI3D_BF16)
+    gelu_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>((const __nv_bfloat16*)x, (__nv_bfloat16*)out, count);
+  else
+    return set_error(HI3D_ERR_INVALID_ARGUMENT, "gelu_tanh: dtype must be f16 or bf16");
+  return check_launch("gelu_tanh");
+}

@@ -1,0 +1,151 @@
+"""Flash attention on the B200 tensor cores (tcgen05 + TMEM, TMA-fed).
+
+:func:`flash_attention` keeps the signature and output layout of
+``hi3d_mac.mlx_backend.attention.flash_attention`` (src/hi3d_mac/mlx_backend/attention.py:238-277);
+:func:`flash_attn_varlen` is the packed variable-length form the upstream
+``flash_attn`` API needs (src/sparc3d/nn/sparse/attention/full_attn.py:56-76).
+
+Arithmetic (as the reference kernel, attention.py:19-22): ``S = Q K^T`` in fp32,
+online softmax in fp32 in the exp2 domain, ``P`` rounded to the input dtype for
+``P V`` which accumulates in fp32, output ``O / l`` rounded once.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+
+SUPPORTED_HEAD_DIMS = (64, 96, 128)
+
+
+def _strides3(t: torch.Tensor, layout: str) -> tuple[int, int, int]:
+    """(row, head, batch) element strides of a 4-D tensor in ``bhnd`` / ``bnhd`` layout."""
+    s = t.stride()
+    if layout == "bhnd":
+        return s[2], s[1], s[0]
+    return s[1], s[2], s[0]
+
+
+def _check_inner(t: torch.Tensor, name: str) -> None:
+    if t.stride(-1) != 1:
+        raise ValueError(f"{name} must have a contiguous head dimension")
+
+
+class KernelTimer:
+    """Optional CUDA-event timing of every attention launch on the launching stream.
+
+    ``start()`` arms it, ``stop()`` synchronises and returns one record per launch
+    (``kind``: "self" when queries and keys are the same sequence length, else "cross";
+    ``flops`` = 4 * Nq * Nk * H * D for dense launches, None for varlen ones).
+    """
+
+    def __init__(self):
+        self.records = None
+
+    def start(self) -> None:
+        self.records = []
+
+    def stop(self) -> list[dict]:
+        recs, self.records = self.records or [], None
+        torch.cuda.synchronize()
+        return [dict(r, ms=r.pop("e0").elapsed_time(r.pop("e1"))) for r in recs]
+
+
+TIMER = KernelTimer()
+
+
+def _launch(args: _lib.AttnArgs, dev_tensor: torch.Tensor) -> None:
+    stream = _lib.stream(dev_tensor)
+    rec = TIMER.records is not None
+    if rec:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+    rc = _lib.load().hi3d_flash_attn_fwd(ctypes.byref(args), stream)
+    _lib.check(rc, "flash_attention")
+    if rec:
+        e1.record()
+        dense = not args.cu_seqlens_q
+        flops = 4.0 * args.nq * args.nk * args.heads * args.head_dim * args.num_seqs if dense else None
+        TIMER.records.append({"kind": "self" if args.nq == args.nk else "cross", "flops": flops, "e0": e0, "e1": e1})
+
+
+def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float,
+                    q_layout: str = "bhnd") -> torch.Tensor:
+    """``softmax(q k^T * scale) v`` for fp16/bf16 inputs, returned as ``[B, Nq, H * D]``.
+
+    Args:
+        q: ``[B, H, Nq, D]`` (``q_layout="bhnd"``) or ``[B, Nq, H, D]`` (``"bnhd"``).
+        k, v: ``[B, H, Nk, D]``, or ``[1, H, Nk, D]`` shared by every batch element.
+        scale: softmax scale applied to ``q k^T``.
+    """
+    _lib.require_cuda(q, k, v)
+    if q_layout == "bhnd":
+        batch, heads, nq, dim = q.shape
+    elif q_layout == "bnhd":
+        batch, nq, heads, dim = q.shape
+    else:
+        raise ValueError(f"unknown q layout {q_layout!r}")
+    nk = k.shape[2]
+    if (dim not in SUPPORTED_HEAD_DIMS or k.shape[1] != heads or k.shape[3] != dim or k.shape[0] not in (1, batch)
+            or v.shape != k.shape):
+        raise ValueError(f"unsupported shapes q {tuple(q.shape)} k {tuple(k.shape)}")
+    if q.dtype not in (torch.float16, torch.bfloat16) or k.dtype != q.dtype or v.dtype != q.dtype:
+        raise ValueError("flash_attention takes float16 (or bfloat16) inputs of one dtype")
+    for t, n in ((q, "q"), (k, "k"), (v, "v")):
+        _check_inner(t, n)
+    out = torch.empty((batch, nq, heads * dim), dtype=q.dtype, device=q.device)
+    if nq == 0 or batch == 0:
+        return out
+    qr, qh, qb = _strides3(q, q_layout)
+    kr, kh, kb = _strides3(k, "bhnd")
+    vr, vh, vb = _strides3(v, "bhnd")
+    if k.shape[0] == 1:
+        kb = vb = 0
+    args = _lib.AttnArgs(
+        q=q.data_ptr(), k=k.data_ptr(), v=v.data_ptr(), out=out.data_ptr(),
+        q_row=qr, q_head=qh, q_batch=qb, k_row=kr, k_head=kh, k_batch=kb, v_row=vr, v_head=vh, v_batch=vb,
+        o_row=heads * dim, o_head=dim, o_batch=nq * heads * dim,
+        cu_seqlens_q=None, cu_seqlens_k=None, nq=nq, nk=nk, max_seqlen_q=nq,
+        num_seqs=batch, heads=heads, head_dim=dim, dtype=_lib.dtype_code(q), scale=float(scale))
+    _launch(args, q)
+    return out
+
+
+def flash_attn_varlen(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqlens_q: torch.Tensor,
+                      cu_seqlens_k: torch.Tensor | None, max_seqlen_q: int, scale: float,
+                      out: torch.Tensor | None = None) -> torch.Tensor:
+    """Packed variable-length attention: ``q [Tq, H, D]``, ``k, v [Tk, H, D]`` (any row
+    stride, contiguous head dim), ``cu_seqlens_*`` int32 ``[num_seqs + 1]`` on the device.
+    ``cu_seqlens_k=None`` shares all ``Tk`` keys with every sequence.  Returns ``[Tq, H, D]``.
+    """
+    _lib.require_cuda(q, k, v, cu_seqlens_q, cu_seqlens_k)
+    tq, heads, dim = q.shape
+    tk = k.shape[0]
+    if dim not in SUPPORTED_HEAD_DIMS or k.shape[1:] != (heads, dim) or v.shape[1:] != (heads, dim):
+        raise ValueError(f"unsupported shapes q {tuple(q.shape)} k {tuple(k.shape)} v {tuple(v.shape)}")
+    if q.dtype not in (torch.float16, torch.bfloat16) or k.dtype != q.dtype or v.dtype != q.dtype:
+        raise ValueError("flash attention takes float16 or bfloat16 inputs of one dtype")
+    for t, n in ((q, "q"), (k, "k"), (v, "v")):
+        _check_inner(t, n)
+    cu_q = cu_seqlens_q.to(torch.int32).contiguous()
+    cu_k = None if cu_seqlens_k is None else cu_seqlens_k.to(torch.int32).contiguous()
+    num_seqs = cu_q.numel() - 1
+    if cu_k is not None and cu_k.numel() != cu_q.numel():
+        raise ValueError("cu_seqlens_q and cu_seqlens_k must have the same length")
+    if out is None:
+        out = torch.empty((tq, heads, dim), dtype=q.dtype, device=q.device)
+    if tq == 0 or num_seqs <= 0:
+        return out
+    args = _lib.AttnArgs(
+        q=q.data_ptr(), k=k.data_ptr(), v=v.data_ptr(), out=out.data_ptr(),
+        q_row=q.stride(0), q_head=q.stride(1), q_batch=0, k_row=k.stride(0), k_head=k.stride(1), k_batch=0,
+        v_row=v.stride(0), v_head=v.stride(1), v_batch=0,
+        o_row=out.stride(0), o_head=out.stride(1), o_batch=0,
+        cu_seqlens_q=cu_q.data_ptr(), cu_seqlens_k=None if cu_k is None else cu_k.data_ptr(),
+        nq=tq, nk=tk, max_seqlen_q=int(max_seqlen_q), num_seqs=num_seqs, heads=heads, head_dim=dim,
+        dtype=_lib.dtype_code(q), scale=float(scale))
+    _launch(args, q)
+    return out

@@ -1,0 +1,77 @@
+"""Query-sharded execution of the block stack across the GPUs of one node.
+
+Rank ``r`` of ``P`` owns a contiguous slice of the object's tokens (query rows).
+Everything in the block is row-local except self-attention, which needs the
+keys/values of every token: each block all-gathers K and V (token-major
+``[T/P, H, D]`` shards -> ``[T, H, D]``) with NCCL over NVLink, then runs the
+local queries against all keys.  Cross-attention K/V (the condition) are
+replicated.  This is a plain context-parallel split; softmax rows never cross
+ranks, so the result equals the single-GPU block up to GEMM shape effects.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from . import attention, kernels
+from .transformer import _modulation, linear
+
+
+def block_forward_sharded(w: dict, x: torch.Tensor, mod: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+                          ck: torch.Tensor, cv: torch.Tensor, heads: int, group=None,
+                          kv_buffers: tuple[torch.Tensor, torch.Tensor] | None = None) -> torch.Tensor:
+    """One block on this rank's rows ``x [T/P, C]`` (updated in place) of a single object."""
+    t_local, c = x.shape
+    world = dist.get_world_size(group)
+    d = c // heads
+    scale = d ** -0.5
+    dt = x.dtype
+    shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp = _modulation(w, mod, c, dt)
+
+    h = kernels.layer_norm_modulate(x, 1e-6, scale=scale_msa, shift=shift_msa)
+    qkv = linear(h, w, "self_attn.to_qkv")
+    q, k, v = kernels.qkv_rope_rms(qkv, cos, sin, w["self_attn.q_rms_norm.gamma"],
+                                   w["self_attn.k_rms_norm.gamma"], 1, heads, d, token_major=True)
+    if kv_buffers is None:
+        kv_buffers = tuple(torch.empty((world * t_local, heads, d), dtype=dt, device=x.device) for _ in range(2))
+    k_all, v_all = kv_buffers
+    hk = dist.all_gather_into_tensor(k_all, k[0], group=group, async_op=True)
+    hv = dist.all_gather_into_tensor(v_all, v[0], group=group, async_op=True)
+    hk.wait()
+    hv.wait()
+    a = attention.flash_attention(q, k_all.permute(1, 0, 2)[None], v_all.permute(1, 0, 2)[None], scale,
+                                  q_layout="bnhd")
+    kernels.gate_residual(x, linear(a[0], w, "self_attn.to_out"), gate_msa)
+
+    h = kernels.layer_norm_modulate(x, 1e-6, weight=w["norm2.weight"], bias=w["norm2.bias"])
+    qc = linear(h, w, "cross_attn.to_q").view(1, t_local, heads, d)
+    o = attention.flash_attention(qc, ck, cv, scale, q_layout="bnhd")[0]
+    kernels.gate_residual(x, linear(o, w, "cross_attn.to_out"), None)
+
+    h = kernels.layer_norm_modulate(x, 1e-6, scale=scale_mlp, shift=shift_mlp)
+    h = kernels.gelu_tanh(linear(h, w, "mlp.mlp.0"))
+    kernels.gate_residual(x, linear(h, w, "mlp.mlp.2"), gate_mlp)
+    return x
+
+
+class ShardedBlockStack:
+    """The block stack over ``P`` ranks, token-sharded; weights replicated on every rank."""
+
+    def __init__(self, weights: list[dict], heads: int, group=None):
+        self.weights = weights
+        self.heads = heads
+        self.group = group
+        self._kv = None
+
+    def __call__(self, x_local: torch.Tensor, mod: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+                 kvs: list[tuple[torch.Tensor, torch.Tensor]]) -> torch.Tensor:
+        x = x_local.clone()
+        t_local, c = x.shape
+        world = dist.get_world_size(self.group)
+        shape = (world * t_local, self.heads, c // self.heads)
+        if self._kv is None or self._kv[0].shape != shape or self._kv[0].device != x.device:
+            self._kv = tuple(torch.empty(shape, dtype=x.dtype, device=x.device) for _ in range(2))
+        for i, w in enumerate(self.weights):
+            block_forward_sharded(w, x, mod, cos, sin, kvs[i][0], kvs[i][1], self.heads, self.group, self._kv)
+        return x

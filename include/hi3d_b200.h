@@ -1,0 +1,143 @@
+/*
+ * hi3d_b200 C ABI: the sparse-voxel refinement-transformer block of Hi3D v1.0
+ * (Sparc3D) on NVIDIA B200 (sm_100a).
+ *
+ * Every entry point takes raw device pointers, sizes and a CUDA stream
+ * (`void* stream`, a cudaStream_t; NULL = legacy default stream), enqueues its
+ * work asynchronously and returns an int status (HI3D_OK = 0).  No entry point
+ * synchronises the host or allocates device memory: the caller owns inputs,
+ * outputs and workspaces.  On failure `hi3d_last_error_string()` describes the
+ * problem (thread-local, valid until the next call on that thread).
+ *
+ * Kernels never trap.  Waits inside kernels are bounded; a wait that runs out
+ * (which only a library bug can cause) records HI3D_ERR_DEVICE_TIMEOUT in the
+ * library's device status word, read with hi3d_device_status().
+ *
+ * Each declaration cites the reference interface it replaces, as
+ * path:line inside the devin-lai/Hi3Dv1.0-mlx source tree.
+ */
+#ifndef HI3D_B200_H_
+#define HI3D_B200_H_
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define HI3D_API __attribute__((visibility("default")))
+#else
+#define HI3D_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define HI3D_OK 0
+#define HI3D_ERR_INVALID_ARGUMENT 1 /* shape/dtype/layout violation (Python: ValueError) */
+#define HI3D_ERR_UNSUPPORTED 2      /* valid but not implemented (Python: NotImplementedError) */
+#define HI3D_ERR_CUDA 3             /* a CUDA runtime/driver call failed */
+#define HI3D_ERR_DEVICE_TIMEOUT 4   /* a bounded device-side wait ran out */
+#define HI3D_ERR_CAPACITY 5         /* a caller-provided workspace is too small */
+
+/* ---- element types ----------------------------------------------------- */
+#define HI3D_F16 0
+#define HI3D_BF16 1
+#define HI3D_F32 2
+
+/* ---- library ----------------------------------------------------------- */
+HI3D_API int hi3d_version(void);
+HI3D_API const char* hi3d_last_error_string(void);
+
+/* Copies the device status word (first device-side error) to the host; with
+ * reset != 0 clears it afterwards.  Synchronises the current device. */
+HI3D_API int hi3d_device_status(int* code, int* where, int* block, int* detail, int reset);
+
+/* ---- LayerNorm32 + adaLN modulation ------------------------------------- */
+/* Replaces kernels.layer_norm_modulate (src/hi3d_mac/mlx_backend/kernels.py:206-237,
+ * kernel :162-201) and upstream LayerNorm32 (src/sparc3d/nn/norm.py:12-17).
+ * Per row of x [rows, channels]: fp32 mean, two-pass fp32 variance,
+ * inv = 1/sqrt(var + eps); y = (x - mean) * inv; optional fp32 affine
+ * (weight/bias, NULL to skip); round to the I/O type; optional modulation
+ * (scale/shift in the I/O type, both NULL to skip) with two roundings:
+ * h = round(h * scale); h = round(h + shift).  `mod_stride` is the element
+ * stride between the scale/shift vectors of consecutive batch elements
+ * (0 = one vector for all rows); `rows_per_batch` maps rows to batch elements. */
+HI3D_API int hi3d_layer_norm_modulate(const void* x, void* out, int64_t rows, int64_t channels, float eps,
+                             const float* weight, const float* bias, const void* scale, const void* shift,
+                             int64_t rows_per_batch, int64_t mod_stride, int dtype, void* stream);
+
+/* ---- RoPE + per-head QK RMS norm + head split --------------------------- */
+/* Replaces kernels.qkv_rope_rms / qkv_rope_rms_simd
+ * (src/hi3d_mac/mlx_backend/kernels.py:62-90, :137-157; kernels :22-57, :93-133) and the upstream
+ * pair RotaryPositionEmbedder + SparseMultiHeadRMSNorm (src/sparc3d/nn/rope.py:14-93,
+ * src/sparc3d/nn/sparse/attention/modules.py:17-32).
+ * qkv [batch*n, 3*heads*head_dim] (channel = part*H*D + h*D + d); cos/sin [n, head_dim/2] fp32;
+ * gamma_q/gamma_k [heads, head_dim] fp32.  Q and K: rotate adjacent pairs in fp32, then
+ * r / max(||r||_2, 1e-12) * gamma * sqrt(head_dim); V copied bit-exactly.
+ * Outputs q, k, v in the input type, [batch, heads, n, head_dim] (out_layout 0, the reference's
+ * layout) or token-major [batch, n, heads, head_dim] (out_layout 1, rows ready to be gathered
+ * across ranks). */
+HI3D_API int hi3d_qkv_rope_rms(const void* qkv, const float* cos, const float* sin, const float* gamma_q,
+                      const float* gamma_k, void* q, void* k, void* v, int64_t batch, int64_t n, int heads,
+                      int head_dim, int out_layout, int dtype, void* stream);
+
+/* ---- flash attention (tcgen05 / TMEM, TMA-fed) --------------------------- */
+/* Replaces attention.flash_attention (src/hi3d_mac/mlx_backend/attention.py:238-277,
+ * kernel :84-233) and the upstream flash_attn varlen API as called at
+ * src/sparc3d/nn/sparse/attention/full_attn.py:56-76 (shimmed at
+ * src/hi3d_mac/torch_backend/attention.py:77-109).
+ *
+ * out = softmax(scale * Q K^T) V per sequence, non-causal.  S and the online
+ * softmax in fp32 (exp2 domain), P rounded to the I/O type for P V, fp32 PV
+ * accumulation, output O / l rounded once.
+ *
+ * Sequence b reads query rows [q_start, q_start + q_len) of batch slice b:
+ *   cu_seqlens_q == NULL: q_start = 0, q_len = nq, batch offset b * q_batch_stride
+ *   cu_seqlens_q != NULL: q_start = cu_seqlens_q[b], q_len = cu_seqlens_q[b+1] - q_start,
+ *                         batch offset 0 (packed varlen).  Same for keys/values.
+ * Element (row r, head h, dim d) of tensor X is at X + b*X_batch + r*X_row + h*X_head + d
+ * (strides in elements; d is contiguous).  All pointers 16-byte aligned, all strides
+ * multiples of 8 elements.  head_dim in {64, 96, 128}; dtype F16 or BF16.
+ * cu_seqlens_* are device int32 arrays of num_seqs + 1 entries; max_seqlen_q bounds q_len.
+ * Keys/values may be shared by all sequences (k_batch_stride = 0, cu_seqlens_k = NULL). */
+typedef struct hi3d_attn_args {
+  const void* q;
+  const void* k;
+  const void* v;
+  void* out;
+  int64_t q_row, q_head, q_batch;
+  int64_t k_row, k_head, k_batch;
+  int64_t v_row, v_head, v_batch;
+  int64_t o_row, o_head, o_batch;
+  const int32_t* cu_seqlens_q;
+  const int32_t* cu_seqlens_k;
+  int64_t nq;           /* rows per sequence (dense) or total rows (varlen) */
+  int64_t nk;
+  int64_t max_seqlen_q; /* varlen: longest query sequence */
+  int32_t num_seqs;     /* batch (dense) or number of packed sequences (varlen) */
+  int32_t heads;
+  int32_t head_dim;
+  int32_t dtype;
+  float scale;
+} hi3d_attn_args;
+
+HI3D_API int hi3d_flash_attn_fwd(const hi3d_attn_args* args, void* stream);
+
+/* ---- elementwise epilogues of the block --------------------------------- */
+/* x <- x + y * gate (all in the I/O type, two roundings: round(y*gate), then round(x + .)).
+ * Replaces the residual/gate expressions at src/hi3d_mac/mlx_backend/transformer.py:570,588
+ * (upstream src/sparc3d/nn/sparse/transformer/modulated.py:59-65).
+ * x, y [rows, channels]; gate [channels] per batch element (gate_stride apart), NULL = 1.
+ * rows_per_batch maps rows to batch elements. */
+HI3D_API int hi3d_gate_residual(void* x, const void* y, const void* gate, int64_t rows, int64_t channels,
+                       int64_t rows_per_batch, int64_t gate_stride, int dtype, void* stream);
+
+/* out = gelu_tanh(x) computed in fp32 and rounded once.
+ * Replaces gelu_tanh, src/hi3d_mac/mlx_backend/transformer.py:176-179. */
+HI3D_API int hi3d_gelu_tanh(const void* x, void* out, int64_t count, int dtype, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HI3D_B200_H_ */

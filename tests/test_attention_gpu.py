@@ -1,0 +1,109 @@
+"""tcgen05 flash attention vs exact float64 attention (and the reference's shim outputs).
+
+The bound is the reference's (tests/test_mlx_kernels.py:163-179): relative RMS error < 3e-4
+for fp16 (output rounding alone is ~2e-4), and ``bnhd`` bit-identical to ``bhnd``.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+from conftest import GOLDEN, rel_rms
+
+from hi3d_b200 import attention
+from hi3d_b200.torch_backend import attention as shim
+from oracle import ops
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _t(a, dtype):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(DEV, dtype)
+
+
+SHAPES = [(2, 333, 333, False), (1, 77, 291, True), (2, 300, 129, True), (1, 5, 3, False), (2, 1000, 31, False),
+          (1, 256, 1370, True), (1, 129, 257, False)]
+
+
+@pytest.mark.parametrize("batch,nq,nk,shared", SHAPES)
+@pytest.mark.parametrize("h,d", [(22, 96), (16, 64), (4, 128)])
+def test_flash_attention_matches_float64(batch, nq, nk, shared, h, d):
+    rng = np.random.default_rng(0)
+    q = (rng.standard_normal((batch, h, nq, d)) * 2).astype(np.float16)
+    k = (rng.standard_normal((1 if shared else batch, h, nk, d)) * 2).astype(np.float16)
+    v = rng.standard_normal(k.shape).astype(np.float16)
+    exact = ops.attention_f64(q, k, v, d ** -0.5)
+    qt, kt, vt = _t(q, torch.float16), _t(k, torch.float16), _t(v, torch.float16)
+    out = attention.flash_attention(qt, kt, vt, d ** -0.5)
+    got = out.float().cpu().numpy()
+    err = rel_rms(got, exact)
+    assert err < 3e-4, err
+    bnhd = attention.flash_attention(qt.transpose(1, 2).contiguous(), kt, vt, d ** -0.5, q_layout="bnhd")
+    assert torch.equal(bnhd, out)
+
+
+@pytest.mark.parametrize("d", [64, 96])
+def test_flash_attention_bf16(d):
+    rng = np.random.default_rng(1)
+    q = rng.standard_normal((1, 8, 700, d)).astype(np.float32) * 2
+    k = rng.standard_normal((1, 8, 900, d)).astype(np.float32) * 2
+    v = rng.standard_normal((1, 8, 900, d)).astype(np.float32)
+    qt, kt, vt = (_t(a, torch.bfloat16) for a in (q, k, v))
+    exact = ops.attention_f64(*(t.float().cpu().numpy() for t in (qt, kt, vt)), d ** -0.5)
+    got = attention.flash_attention(qt, kt, vt, d ** -0.5).float().cpu().numpy()
+    assert rel_rms(got, exact) < 4e-3
+
+
+def test_varlen_packed_with_empty_and_ragged_sequences():
+    rng = np.random.default_rng(2)
+    h, d = 16, 64
+    cu = np.array([0, 100, 100, 357, 700, 701], np.int32)
+    qkv = (rng.standard_normal((701, 3, h, d)) * 2).astype(np.float16)
+    exact = ops.attention_varlen(qkv[:, 0], qkv[:, 1], qkv[:, 2], cu, cu, d ** -0.5)
+    t = _t(qkv, torch.float16)
+    got = shim.flash_attn_varlen_qkvpacked_func(t, _t(cu, torch.int32), 343).float().cpu().numpy()
+    assert rel_rms(got, exact) < 3e-4
+
+
+def test_cross_attention_shared_keys_varlen():
+    rng = np.random.default_rng(3)
+    h, d, L = 16, 64, 1370
+    cu = np.array([0, 500, 1200], np.int32)
+    q = (rng.standard_normal((1200, h, d)) * 2).astype(np.float16)
+    kv = (rng.standard_normal((L, 2, h, d)) * 2).astype(np.float16)
+    exact = ops.attention_varlen(q, kv[:, 0], kv[:, 1], cu, None, d ** -0.5)
+    kvt = _t(kv, torch.float16)
+    got = attention.flash_attn_varlen(_t(q, torch.float16), kvt[:, 0], kvt[:, 1], _t(cu, torch.int32), None, 700,
+                                      d ** -0.5).float().cpu().numpy()
+    assert rel_rms(got, exact) < 3e-4
+
+
+def test_shim_matches_reference_golden():
+    g = np.load(GOLDEN / "attention.npz")
+    qkv = _t(g["qkv"], torch.float16)
+    got = shim.flash_attn_varlen_qkvpacked_func(qkv, _t(g["cu"], torch.int32), 90).float().cpu().numpy()
+    assert rel_rms(got, g["self_out"]) < 2e-3  # fp16 input rounding vs the fp32 reference
+    got = shim.flash_attn_varlen_kvpacked_func(_t(g["q"], torch.float16), _t(g["kv"], torch.float16),
+                                               torch.tensor([0, 70]), torch.tensor([0, 30]), 70, 30)
+    assert rel_rms(got.float().cpu().numpy(), g["cross_out"]) < 2e-3
+    with pytest.raises(NotImplementedError):
+        shim.flash_attn_varlen_qkvpacked_func(qkv, _t(g["cu"], torch.int32), 90, causal=True)
+
+
+def test_long_sequence_sampled_rows_and_determinism():
+    """32k keys: check 192 sampled query rows against float64, and bit-identical reruns."""
+    rng = np.random.default_rng(4)
+    h, d, n = 2, 64, 32768
+    q = (rng.standard_normal((1, h, n, d)) * 2).astype(np.float16)
+    k = (rng.standard_normal((1, h, n, d)) * 2).astype(np.float16)
+    v = rng.standard_normal((1, h, n, d)).astype(np.float16)
+    qt, kt, vt = (_t(a, torch.float16) for a in (q, k, v))
+    out = attention.flash_attention(qt, kt, vt, d ** -0.5)
+    again = attention.flash_attention(qt, kt, vt, d ** -0.5)
+    assert torch.equal(out, again)
+    rows = np.sort(rng.choice(n, 192, replace=False))
+    exact = ops.attention_f64(q[:, :, rows], k, v, d ** -0.5)
+    got = out[:, rows].float().cpu().numpy()
+    assert rel_rms(got, exact) < 3e-4
