@@ -1,12 +1,18 @@
 """Benchmark of the sparse-DiT refinement torso on B200 (BASELINE configs[1] by default).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload stack|attention]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload stack|attention|attention262k]
 
 One step = one forward of the 24-block stack (C=1024, 16 heads x 64, GELU MLP 4x,
 1370 condition tokens) over T=32,768 voxel tokens of one object in fp16, inputs
 resident in HBM.  ``value`` is block tokens/s = blocks * T / step time (whole job,
 max over ranks).  With N>1 GPUs (torchrun) the T tokens are split into N query
 slices and every block all-gathers K/V over NCCL (strong scaling).
+
+``--workload attention`` times the self-attention kernel alone at the same size
+(T=32,768, 16x64 heads, fp16); ``--workload attention262k`` the high-resolution
+config (262,144 tokens packed as 4 objects of 65,536, bf16, varlen), query-sharded
+over the GPUs.  Both report attention TFLOP/s (4 * Nq * Nk * H * D per object).
 
 Rank 0 prints one JSON line.  ``--impl reference`` times the CPU path instead: the
 oracle port of the reference block (the reference itself is Python that cannot travel
@@ -153,39 +159,76 @@ def device_weights(device, seed: int = 100) -> list[dict]:
 # ----------------------------------------------------------------------------- CPU baseline
 
 
+_CPU_CACHE: dict = {}
+
+
 def cpu_block_seconds(sample: int, seed: int = 0) -> tuple[float, dict]:
     """One fp32 CPU block at the full workload size, estimated from a row sample (oracle port)."""
     from hi3d_b200 import synthetic
     from oracle import ops
 
-    coords, cos, sin, x, mod, cond = make_inputs(seed)
-    w = synthetic.block_weights(CHANNELS, CHANNELS, HEADS, seed=seed + 5)
+    if "block" not in _CPU_CACHE:
+        coords, cos, sin, x, mod, cond = make_inputs(seed)
+        w = synthetic.block_weights(CHANNELS, CHANNELS, HEADS, seed=seed + 5)
+        _CPU_CACHE["block"] = (w, x, mod, cos, sin, cond)
+    w, x, mod, cos, sin, cond = _CPU_CACHE["block"]
     return ops.block_seconds_sampled(w, x, mod, cos, sin, cond, HEADS, sample=sample, seed=seed)
+
+
+def cpu_attention_tflops(big: bool, sample: int = 256) -> tuple[float, str]:
+    """fp32 numpy attention of ``sample`` query rows against one whole object (all heads),
+    scaled to TFLOP/s with the same 4 * Nq * Nk * H * D count as the GPU arm."""
+    per = 65536 if big else T_TOKENS
+    d = CHANNELS // HEADS
+    if ("attn", big) not in _CPU_CACHE:
+        rng = np.random.default_rng(7)
+        _CPU_CACHE[("attn", big)] = tuple(rng.standard_normal((HEADS, n, d)).astype(np.float32)
+                                          for n in (sample, per, per))
+    q, k, v = _CPU_CACHE[("attn", big)]
+    t0 = time.perf_counter()
+    for h in range(HEADS):
+        s = q[h] @ k[h].T * np.float32(d ** -0.5)
+        p = np.exp(s - s.max(-1, keepdims=True))
+        _ = (p / p.sum(-1, keepdims=True)) @ v[h]
+    secs = time.perf_counter() - t0
+    return 4.0 * sample * per * HEADS * d / secs / 1e12, f"{sample} query rows x {per} keys x {HEADS} heads, fp32"
 
 
 def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    sample = 1024
-    secs = []
-    for i in range(args.warmup + args.steps):
-        s, phases = cpu_block_seconds(sample, seed=0)
-        if i >= args.warmup:
-            secs.append(s)
-    per_block = statistics.median(secs)
-    value = T_TOKENS / per_block
     cores = os.cpu_count()
+    if args.workload == "stack":
+        sample = 512
+        secs = []
+        for i in range(args.warmup + args.steps):
+            s, _ = cpu_block_seconds(sample, seed=0)
+            if i >= args.warmup:
+                secs.append(s)
+        per_block = statistics.median(secs)
+        value, unit, metric = T_TOKENS / per_block, "tokens/s", "block_tokens_per_s"
+        ms_step = per_block * BLOCKS * 1e3
+        desc = (f"one fp32 block at T={T_TOKENS} per step (numpy oracle port of the reference block): K/V side on "
+                f"all rows, {sample} sampled query rows for the rest, scaled by T/{sample}")
+        workload = f"cfg1 block on CPU: T={T_TOKENS}, C={CHANNELS}, H={HEADS}x64, L={COND}"
+    else:
+        big = args.workload == "attention262k"
+        vals = []
+        for i in range(args.warmup + args.steps):
+            v, desc = cpu_attention_tflops(big)
+            if i >= args.warmup:
+                vals.append(v)
+        value, unit, metric = statistics.median(vals), "TFLOP/s", "attention_tflops"
+        ms_step = None
+        workload = "cfg4 self-attention on CPU" if big else "cfg1 self-attention on CPU"
     line = {
-        "impl": "reference", "metric": "block_tokens_per_s", "value": value, "unit": "tokens/s",
-        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_block * BLOCKS * 1e3,
+        "impl": "reference", "metric": metric, "value": value, "unit": unit,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"cfg1 block on CPU: T={T_TOKENS}, C={CHANNELS}, H={HEADS}x64, L={COND}",
-                   "blocks": BLOCKS},
-        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
-                         "sample": f"one fp32 block at T={T_TOKENS}: K/V side on all rows, {sample} sampled query "
-                                   f"rows for the rest, scaled by T/{sample}; numpy oracle port of the reference"},
-        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "config": {"workload": workload, "blocks": BLOCKS},
+        "cpu_baseline": {"value": value, "unit": unit, "cores": cores, "kind": "port", "sample": desc},
+        "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
@@ -314,7 +357,118 @@ def run_ours(args) -> None:
         cpu_value = T_TOKENS / secs
         line["cpu_baseline"] = {"value": cpu_value, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
                                 "sample": f"one fp32 block at T={T_TOKENS} (numpy oracle port): K/V side on all "
-                                          f"rows, 1024 sampled query rows for the rest, scaled by T/1024"}
+                                          f"rows, 1024 sampled query rows for the rest, scaled by T/1024",
+                                "seconds_per_block": secs}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_attention(args, big: bool) -> None:
+    """Self-attention kernel alone: cfg1 (T=32768 fp16, one object) or cfg4 (4 x 65536 bf16 varlen)."""
+    import torch
+    import torch.distributed as dist
+
+    from hi3d_b200 import _lib, attention
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    _lib.load()
+    d = CHANNELS // HEADS
+    if big:
+        objects, per, dtype = 4, 65536, torch.bfloat16
+    else:
+        objects, per, dtype = 1, T_TOKENS, torch.float16
+    total = objects * per
+    g = torch.Generator(device=dev).manual_seed(7)
+    # RoPE'd, RMS-normalised queries/keys have per-head norm sqrt(D): unit-variance entries
+    k = torch.randn((total, HEADS, d), generator=g, device=dev).to(dtype)
+    v = torch.randn((total, HEADS, d), generator=g, device=dev).to(dtype)
+    # query rows of this rank: a contiguous slice of every object (keys stay per object)
+    if per % world:
+        raise ValueError("tokens per object must divide by the number of GPUs")
+    ql = per // world
+    q = torch.randn((objects * ql, HEADS, d), generator=g, device=dev).to(dtype)
+    cu_q = torch.arange(0, objects + 1, device=dev, dtype=torch.int32) * ql
+    cu_k = torch.arange(0, objects + 1, device=dev, dtype=torch.int32) * per
+    out = torch.empty_like(q)
+    flops = 4.0 * objects * ql * per * HEADS * d  # per rank per launch
+
+    def step():
+        attention.flash_attn_varlen(q, k, v, cu_q, cu_k, ql, d ** -0.5, out=out)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    _lib.LAUNCHES[0] = 0
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+    launches = _lib.LAUNCHES[0]
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_step = ms / args.steps
+    tflops = flops * world / (ms_step / 1e3) / 1e12
+    per_gpu = flops / (ms_step / 1e3) / 1e12
+    peaks = _peaks()
+    # end to end: q/k/v from pinned host memory, output back to the host
+    hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
+    hout = torch.empty_like(hq).pin_memory()
+    torch.cuda.synchronize()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for _ in range(args.steps):
+        dq, dk, dv = (t.to(dev, non_blocking=True) for t in (hq, hk, hv))
+        hout.copy_(attention.flash_attn_varlen(dq, dk, dv, cu_q, cu_k, ql, d ** -0.5), non_blocking=True)
+    f1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = f0.elapsed_time(f1) / args.steps
+    name = "flash_attn_fwd_cfg4" if big else "flash_attn_fwd_cfg1"
+    cpu = None
+    if rank == 0 and world == 1:
+        cv, cdesc = cpu_attention_tflops(big)
+        cpu = {"value": cv, "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": "port", "sample": cdesc}
+    line = {
+        "metric": "attention_tflops", "value": tflops, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16" if big else "f16", "data": "synthetic",
+        "config": {"workload": (f"cfg4: self-attention, {objects} objects x {per} tokens varlen, {HEADS}x{d} heads, bf16"
+                                if big else f"cfg1: self-attention, T={per}, {HEADS}x{d} heads, fp16"),
+                   "tokens": total, "parallelism": f"query-sharded x{world}" if world > 1 else "none",
+                   "l2": "inputs larger than L2" if total * HEADS * d * 2 * 3 > 126e6 else "inputs fit in L2"},
+        "roofline": {"bound": "tensor", "achieved": per_gpu, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": per_gpu / peaks["bf16_tflops"], "traffic": _profile_traffic(name),
+                     "peak_source": f"{peaks['source']} bf16_tflops (burst; kernel timed alone)"},
+        "e2e": {"value": flops * world / (e2e_ms / 1e3) / 1e12, "unit": "TFLOP/s",
+                "h2d_bytes_per_step": (q.numel() + k.numel() + v.numel()) * 2,
+                "d2h_bytes_per_step": out.numel() * 2},
+        "gpu_launches": launches,
+        "clocks": clocks.summary(),
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -328,13 +482,16 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["stack", "attention", "attention262k"], default="stack")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
-    else:
+    elif args.workload == "stack":
         run_ours(args)
+    else:
+        run_attention(args, big=args.workload == "attention262k")
 
 
 if __name__ == "__main__":

@@ -187,10 +187,12 @@ __global__ void __launch_bounds__(256) qkv_rope_rms_kernel(const T* __restrict__
   const int sub = lane % G;
   const int64_t unit = ((int64_t)blockIdx.x * 8 + (threadIdx.x >> 5)) * GROUPS_PER_WARP + lane / G;
   const int64_t total = M * 3 * H;
-  const bool valid = unit < total && sub < ACTIVE;
-  if (unit >= total) return;
-  const int64_t m = unit / (3 * H);
-  const int ph = (int)(unit % (3 * H));
+  // No early exit before the group reduction: every lane of the warp takes part
+  // in the full-mask shuffles, inactive lanes contribute zero.
+  const bool in_range = unit < total;
+  const bool valid = in_range && sub < ACTIVE;
+  const int64_t m = in_range ? unit / (3 * H) : 0;
+  const int ph = in_range ? (int)(unit % (3 * H)) : 0;
   const int part = ph / H, h = ph % H;
   const int64_t b = m / N, n = m % N;
   const T* src = qkv + (m * 3 + part) * (int64_t)H * D;
@@ -198,15 +200,11 @@ __global__ void __launch_bounds__(256) qkv_rope_rms_kernel(const T* __restrict__
   const int c0 = sub * 8;
   Vec8 raw = {};
   if (valid) raw = *reinterpret_cast<const Vec8*>(src + c0);
-  if (part == 2) {
-    if (valid) *reinterpret_cast<Vec8*>(v + dst_off + c0) = raw;
-    return;
-  }
   float x[8];
   unpack8<T>(raw, x);
-  float r[8];
+  float r[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
   float ss = 0.f;
-  if (valid) {
+  if (valid && part != 2) {
     const float* cs = cosv + n * (D / 2) + c0 / 2;
     const float* sn = sinv + n * (D / 2) + c0 / 2;
 #pragma unroll
@@ -220,12 +218,17 @@ __global__ void __launch_bounds__(256) qkv_rope_rms_kernel(const T* __restrict__
 #pragma unroll
   for (int o = G / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
   if (!valid) return;
+  if (part == 2) {
+    *reinterpret_cast<Vec8*>(v + dst_off + c0) = raw;
+    return;
+  }
   const float nrm = fmaxf(sqrtf(ss), 1e-12f);
   const float scale = sqrtf((float)D);
   const float* g = (part == 0 ? gq : gk) + h * D + c0;
   Vec8 o;
 #pragma unroll
-  for (int i = 0; i < 4; ++i) o.w[i] = Cvt<T>::pack2(r[2 * i] / nrm * g[2 * i] * scale, r[2 * i + 1] / nrm * g[2 * i + 1] * scale);
+  for (int i = 0; i < 4; ++i)
+    o.w[i] = Cvt<T>::pack2(r[2 * i] / nrm * g[2 * i] * scale, r[2 * i + 1] / nrm * g[2 * i + 1] * scale);
   *reinterpret_cast<Vec8*>((part == 0 ? q : k) + dst_off + c0) = o;
 }
 

@@ -227,6 +227,8 @@ def attention_varlen(q: np.ndarray, k: np.ndarray, v: np.ndarray, cu_q, cu_k, sc
     for i in range(len(cu_q) - 1):
         qs = slice(int(cu_q[i]), int(cu_q[i + 1]))
         ks = slice(0, k.shape[0]) if cu_k is None else slice(int(cu_k[i]), int(cu_k[i + 1]))
+        if qs.stop <= qs.start:
+            continue
         qq, kk, vv = (np.asarray(t[sl], dtype) for t, sl in ((q, qs), (k, ks), (v, ks)))
         for h in range(q.shape[1]):
             s = qq[:, h] @ kk[:, h].T * scale
