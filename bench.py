@@ -1,7 +1,7 @@
 """Benchmark of the sparse-DiT refinement torso on B200 (BASELINE configs[1] by default).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload stack|attention|attention262k]
+                    [--workload stack|stack_w8a8|attention|attention262k]
 
 One step = one forward of the 24-block stack (C=1024, 16 heads x 64, GELU MLP 4x,
 1370 condition tokens) over T=32,768 voxel tokens of one object in fp16, inputs
@@ -259,6 +259,8 @@ def run_ours(args) -> None:
     tl = T_TOKENS // world
     rows = slice(rank * tl, (rank + 1) * tl)
     weights = device_weights(dev)
+    if args.workload == "stack_w8a8":
+        weights = [transformer.to_w8a8(w) for w in weights]
     x_host = torch.from_numpy(x[rows]).pin_memory()
     x_dev = x_host.to(dev)
     cos_d, sin_d = torch.from_numpy(cos[rows]).to(dev), torch.from_numpy(sin[rows]).to(dev)
@@ -341,8 +343,12 @@ def run_ours(args) -> None:
         "metric": "block_tokens_per_s", "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-        "config": {"workload": f"cfg1: {BLOCKS}-block sparse-DiT stack fwd, T={T_TOKENS} shell tokens in {GRID}^3, "
-                               f"C={CHANNELS}, {HEADS}x{CHANNELS // HEADS} heads, {COND} cond tokens, fp16",
+        "config": {"workload": (f"cfg2: W8A8 {BLOCKS}-block stack fwd (int8 signed-H64 activations, int8 rotated "
+                                f"weights, int32 accumulate, fp16 dequant), T={T_TOKENS}, C={CHANNELS}, "
+                                f"{HEADS}x{CHANNELS // HEADS} heads, {COND} cond tokens"
+                                if args.workload == "stack_w8a8" else
+                                f"cfg1: {BLOCKS}-block sparse-DiT stack fwd, T={T_TOKENS} shell tokens in {GRID}^3, "
+                                f"C={CHANNELS}, {HEADS}x{CHANNELS // HEADS} heads, {COND} cond tokens, fp16"),
                    "blocks": BLOCKS, "tokens": T_TOKENS, "parallelism": f"query-sharded x{world}" if world > 1 else "none",
                    "l2": "inputs larger than L2 (705 MB of weights + activations per step)"},
         "roofline": roofline,
@@ -482,13 +488,13 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["stack", "attention", "attention262k"], default="stack")
+    ap.add_argument("--workload", choices=["stack", "stack_w8a8", "attention", "attention262k"], default="stack")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
-    elif args.workload == "stack":
+    elif args.workload in ("stack", "stack_w8a8"):
         run_ours(args)
     else:
         run_attention(args, big=args.workload == "attention262k")

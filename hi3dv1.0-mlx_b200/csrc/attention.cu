@@ -7,12 +7,14 @@
 // P = exp2(s - m) summed unrounded into l, rounded to the I/O type for the
 // P V product, which accumulates in fp32; output O / l rounded once.
 //
-// CTA layout (384 threads):
+// CTA layout (320 threads):
 //   warp 0      TMA producer (one lane): Q tiles once, then K/V blocks into
 //               an NST-stage ring
 //   warp 1      MMA issuer (one lane); also owns the TMEM allocation
-//   warps 4-7   softmax + O correction + epilogue of query tile 0
-//   warps 8-11  the same for query tile 1
+//   warps 2-5   softmax + O correction + epilogue of query tile 0
+//   warps 6-9   the same for query tile 1
+// A warp reaches TMEM lanes 32*(warp % 4) .. +31, so each group of four
+// consecutive warps covers the 128 rows of its tile.
 // TMEM (512 columns): tile i at column 256*i holds S [BK cols, fp32],
 // P [BK/2 cols, packed 16-bit pairs] and O [D cols, fp32].
 #include <type_traits>
@@ -23,8 +25,13 @@
 namespace hi3d {
 namespace attn {
 
-constexpr int kThreads = 384;
+constexpr int kThreads = 320;
 constexpr int kRowsPerTile = 128;
+// Exponentials per 16-pair chunk of a score row evaluated by the FMA-pipe
+// polynomial (the rest use the MUFU ex2 unit), balancing the two pipes.
+constexpr int kEmuPairs = 6;
+// Row maximum growth (log2 units) tolerated before O and l are rescaled.
+constexpr float kRescaleLog2 = 8.0f;
 
 template <int D>
 struct Cfg {
@@ -209,9 +216,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (j + C::NST < nblk) tc_commit(&bar->kv_empty[s]);
       }
     }
-  } else if (warp >= 4) {
+  } else {
     // ------------------------------------------------------------ softmax
-    const int i = (warp - 4) >> 2;   // query tile
+    const int i = (warp - 2) >> 2;   // query tile
     const int sub = warp & 3;        // TMEM lane quarter
     const int row = sub * 32 + lane; // row within the tile
     const uint32_t lane_addr = (uint32_t)(sub * 32) << 16;
@@ -219,6 +226,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tP = tmem + lane_addr + 256 * i + C::P_COL;
     const uint32_t tO = tmem + lane_addr + 256 * i + C::O_COL;
     const float scale2 = p.scale2;
+    const uint64_t scale2x2 = f2_pack(scale2, scale2);
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
     for (int j = 0; j < nblk; ++j) {
@@ -237,19 +245,36 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       float mx = __uint_as_float(sv[0]);
 #pragma unroll
-      for (int e = 1; e < C::BK; ++e) mx = fmaxf(mx, __uint_as_float(sv[e]));
-      const float m_new = fmaxf(m_run, mx * scale2);
-      const float alpha = ex2_approx(m_run - m_new);
-      const float neg_m = -m_new;
-      float rsum = 0.f;
+      for (int e = 1; e + 1 < C::BK; e += 2) mx = fmax3(mx, __uint_as_float(sv[e]), __uint_as_float(sv[e + 1]));
+      mx = fmaxf(mx, __uint_as_float(sv[C::BK - 1]));
+      // Running maximum in the scaled log2 domain.  The maximum used for the
+      // exponentials (m_run) only moves when a row's maximum grows by more than
+      // kRescaleLog2; until then P may reach 2^kRescaleLog2 (exact in the 16-bit
+      // P and in fp32 l), and O needs no correction.  O / l is unchanged.
+      const float m_blk = mx * scale2;
+      const bool grow = m_blk > m_run + kRescaleLog2;
+      const float m_new = grow ? m_blk : m_run;
+      const float alpha = grow ? ex2_approx(m_run - m_new) : 1.0f;
+      const uint64_t negm = f2_pack(-m_new, -m_new);
+      uint64_t acc = f2_pack(0.f, 0.f);
 #pragma unroll
       for (int c = 0; c < C::BK / 32; ++c) {
         uint32_t pk[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
-          const float p0 = ex2_approx(fmaf(__uint_as_float(sv[c * 32 + 2 * e]), scale2, neg_m));
-          const float p1 = ex2_approx(fmaf(__uint_as_float(sv[c * 32 + 2 * e + 1]), scale2, neg_m));
-          rsum += p0 + p1;
+          const uint64_t sx = f2_pack(__uint_as_float(sv[c * 32 + 2 * e]), __uint_as_float(sv[c * 32 + 2 * e + 1]));
+          const uint64_t xx = f2_fma(sx, scale2x2, negm);
+          uint64_t pp;
+          if (e < kEmuPairs) {
+            pp = f2_exp2_poly(xx);
+          } else {
+            float x0, x1;
+            f2_unpack(xx, x0, x1);
+            pp = f2_pack(ex2_approx(x0), ex2_approx(x1));
+          }
+          acc = f2_add(acc, pp);
+          float p0, p1;
+          f2_unpack(pp, p0, p1);
           pk[e] = Cvt<T>::pack2(p0, p1);
         }
         // P of block j overwrites P of block j-1: wait until P V of block
@@ -261,8 +286,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_st16(tP + c * 16, pk);
       }
       if (!ok) break;
-      // O *= alpha (skipped when no row of this warp changed its maximum)
-      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
+      // O *= alpha, only when a row of this warp moved its maximum
+      if (j > 0 && __any_sync(0xffffffffu, grow)) {
 #pragma unroll
         for (int oc = 0; oc < (D + 31) / 32; ++oc) {
           uint32_t r[32];
@@ -273,7 +298,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_st32(tO + oc * 32, r);
         }
       }
-      l_run = l_run * alpha + rsum;
+      float a0, a1;
+      f2_unpack(acc, a0, a1);
+      l_run = l_run * alpha + (a0 + a1);
       m_run = m_new;
       tmem_wait_st();
       tc_fence_before();
@@ -289,6 +316,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int oc = 0; oc < (D + 31) / 32; ++oc) {
         uint32_t r[32];
+        __syncwarp();
         tmem_ld32(tO + oc * 32, r);
         tmem_wait_ld();
         if (qrow < q_len) {

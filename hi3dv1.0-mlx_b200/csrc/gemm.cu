@@ -1,0 +1,383 @@
+// Persistent tcgen05 GEMM for the block's projections: C = A W^T with fused
+// epilogues.  One kernel template serves
+//   * the W8A8 path: int8 A [M,K] x int8 W [N,K] -> exact int32 accumulators in
+//     TMEM, dequantised in the epilogue as half(float(acc) * sa[m] * sw[n] + bias[n])
+//     (w8a8.py:61-80 of the reference, evaluated left to right without FMA);
+//   * the 16-bit path: f16/bf16 A x W -> fp32 accumulators, half(acc + bias[n])
+//     (mx.addmm, transformer.py:119).
+// Epilogue variants on the rounded 16-bit result y: store y; store gelu_tanh(y)
+// (GELU in fp32, transformer.py:176-179); or update a residual stream in place,
+// x = round(x + round(y * gate)) (transformer.py:570, :588).
+//
+// CTA (192 threads), one per SM, looping over 128 x 256 output tiles:
+//   warp 0     TMA producer: A [128 x 128 B] and W [256 x 128 B] per stage
+//   warp 1     MMA issuer (one lane), TMEM owner; two 256-column accumulators
+//              so the epilogue of one tile overlaps the MMAs of the next
+//   warps 2-5  epilogue, one output row per thread (TMEM lane = row)
+#include <type_traits>
+
+#include "abi.h"
+#include "common.cuh"
+
+namespace hi3d {
+namespace gemm {
+
+constexpr int kThreads = 192;
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BKB = 128;  // K bytes per stage (one 128-byte swizzle row)
+constexpr int NST = 4;
+constexpr int A_STAGE = BM * BKB;
+constexpr int B_STAGE = BN * BKB;
+constexpr int SMEM = NST * (A_STAGE + B_STAGE) + 1024 + 256;
+
+enum Kind { KIND_F16 = 0, KIND_BF16 = 1, KIND_I8 = 2 };
+enum Epi { EPI_STORE = 0, EPI_GELU = 1, EPI_RESIDUAL = 2 };
+
+struct Params {
+  void* out;          // [M, ldo] output (or the residual stream for EPI_RESIDUAL)
+  int64_t ldo;
+  const void* bias;   // [N] in the output type, or null
+  const float* sa;    // [M] per-row activation scales (int8 path)
+  const float* sw;    // [N] per-column weight scales (int8 path)
+  const void* gate;   // [N] per batch element (EPI_RESIDUAL), or null
+  int64_t rows_per_batch, gate_stride;
+  int M, N, K;        // K in elements
+  int tiles_m, tiles_n;
+};
+
+struct Barriers {
+  uint64_t full[NST];
+  uint64_t empty[NST];
+  uint64_t acc_full[2];
+  uint64_t acc_empty[2];
+  uint32_t tmem_base;
+  int abort;
+};
+
+template <typename OutT>
+__device__ __forceinline__ float gelu_tanh_f(float a) {
+  const float k0 = 0.7978845608028654f;  // sqrt(2 / pi)
+  return 0.5f * a * (1.0f + tanhf(k0 * (a + 0.044715f * a * a * a)));
+}
+
+template <int KIND, int EPI, typename OutT>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + NST * A_STAGE;
+  Barriers* bar = reinterpret_cast<Barriers*>(sB + NST * B_STAGE);
+  constexpr int ESZ = KIND == KIND_I8 ? 1 : 2;
+  constexpr int BKE = BKB / ESZ;  // K elements per stage
+
+  const int warp = warp_id(), lane = lane_id();
+  const int num_tiles = p.tiles_m * p.tiles_n;
+  const int kblocks = (p.K + BKE - 1) / BKE;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NST; ++s) {
+      mbar_init(&bar->full[s], 1);
+      mbar_init(&bar->empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&bar->acc_full[a], 1);
+      mbar_init(&bar->acc_empty[a], BM);
+    }
+    bar->abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&bar->tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bar->tmem_base;
+  volatile int* abort = &bar->abort;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmA);
+      tma_prefetch_desc(&tmB);
+      int it = 0;  // global k-block counter (ring position)
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+        const int m0 = (tile / p.tiles_n) * BM, n0 = (tile % p.tiles_n) * BN;
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const int s = it % NST, n = it / NST;
+          if (!(ok = mbar_wait(&bar->empty[s], (n & 1) ^ 1, abort, 101))) break;
+          mbar_arrive_expect_tx(&bar->full[s], A_STAGE + B_STAGE);
+          tma_load_2d(sA + s * A_STAGE, &tmA, &bar->full[s], kb * BKE, m0);
+          tma_load_2d(sB + s * B_STAGE, &tmB, &bar->full[s], kb * BKE, n0);
+        }
+      }
+      volatile int no_abort = 0;
+      if (!ok) {
+        // drain the copies already in flight before leaving
+        for (int j = (it > NST ? it - NST : 0); j < it; ++j) mbar_wait(&bar->full[j % NST], (j / NST) & 1, &no_abort, 102);
+      } else {
+        // producer tail: wait for the MMA warp's last releases of each stage, so
+        // no barrier arrive is still in flight when the CTA exits
+        for (int j = (it > NST ? it - NST : 0); j < it; ++j) mbar_wait(&bar->empty[j % NST], (j / NST) & 1, abort, 103);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = KIND == KIND_I8 ? make_idesc(2, 1, 0, 0, BM, BN)
+                                                 : make_idesc(1, KIND == KIND_BF16 ? 1 : 0, 0, 0, BM, BN);
+      const uint32_t sAa = smem_u32(sA), sBa = smem_u32(sB);
+      int it = 0, local = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x, ++local) {
+        const int acc = local & 1, use = local >> 1;
+        if (!(ok = mbar_wait(&bar->acc_empty[acc], (use & 1) ^ 1, abort, 110))) break;
+        tc_fence_after();
+        const uint32_t d = tmem + acc * BN;
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const int s = it % NST, n = it / NST;
+          if (!(ok = mbar_wait(&bar->full[s], n & 1, abort, 111))) break;
+          tc_fence_after();
+#pragma unroll
+          for (int k = 0; k < BKB / 32; ++k) {
+            const uint64_t da = smem_desc(sAa + s * A_STAGE + k * 32, 16, 1024, kLayoutSW128);
+            const uint64_t db = smem_desc(sBa + s * B_STAGE + k * 32, 16, 1024, kLayoutSW128);
+            if (KIND == KIND_I8)
+              mma_i8_ss(d, da, db, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+            else
+              mma_f16_ss(d, da, db, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          tc_commit(&bar->empty[s]);
+        }
+        if (!ok) break;
+        tc_commit(&bar->acc_full[acc]);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int sub = warp & 3;
+    const int r = sub * 32 + lane;
+    const uint32_t lane_addr = (uint32_t)(sub * 32) << 16;
+    int local = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+      const int acc = local & 1, use = local >> 1;
+      if (!mbar_wait(&bar->acc_full[acc], use & 1, abort, 120)) break;
+      tc_fence_after();
+      const int m = (tile / p.tiles_n) * BM + r;
+      const int n0 = (tile % p.tiles_n) * BN;
+      const bool row_ok = m < p.M;
+      float sa = 1.0f;
+      if (KIND == KIND_I8 && row_ok) sa = p.sa[m];
+      OutT* orow = reinterpret_cast<OutT*>(p.out) + (int64_t)m * p.ldo;
+      const OutT* grow = nullptr;
+      if (EPI == EPI_RESIDUAL && p.gate) grow = reinterpret_cast<const OutT*>(p.gate) + (m / p.rows_per_batch) * p.gate_stride;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t v[32];
+        __syncwarp();
+        tmem_ld32(tmem + lane_addr + acc * BN + c * 32, v);
+        tmem_wait_ld();
+        const int nb = n0 + c * 32;
+        if (!row_ok || nb >= p.N) continue;
+#pragma unroll
+        for (int e = 0; e < 32; e += 8) {
+          const int n = nb + e;
+          if (n >= p.N) break;
+          if constexpr (std::is_same<OutT, int32_t>::value) {
+            // raw exact int32 accumulators (verification / custom dequantisation)
+            if (n + 8 <= p.N) {
+              *reinterpret_cast<uint4*>(orow + n) = make_uint4(v[e], v[e + 1], v[e + 2], v[e + 3]);
+              *reinterpret_cast<uint4*>(orow + n + 4) = make_uint4(v[e + 4], v[e + 5], v[e + 6], v[e + 7]);
+            } else {
+              for (int q = 0; q < 8 && n + q < p.N; ++q) orow[n + q] = (int32_t)v[e + q];
+            }
+            continue;
+          } else {
+          float y[8];
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const int nn = min(n + q, p.N - 1);
+            float t;
+            if (KIND == KIND_I8) {
+              t = __fmul_rn(__fmul_rn(__int2float_rn((int)v[e + q]), sa), p.sw[nn]);
+            } else {
+              t = __uint_as_float(v[e + q]);
+            }
+            if (p.bias) t = __fadd_rn(t, Cvt<OutT>::to_f(reinterpret_cast<const OutT*>(p.bias)[nn]));
+            y[q] = Cvt<OutT>::to_f(Cvt<OutT>::from_f(t));  // round to the output type
+            if (EPI == EPI_GELU) y[q] = gelu_tanh_f<OutT>(y[q]);
+          }
+          if (EPI == EPI_RESIDUAL) {
+            if (n + 8 <= p.N) {
+              uint4 xv = *reinterpret_cast<const uint4*>(orow + n);
+              uint4 gv = grow ? *reinterpret_cast<const uint4*>(grow + n) : make_uint4(0, 0, 0, 0);
+              const OutT* xa = reinterpret_cast<const OutT*>(&xv);
+              const OutT* ga = reinterpret_cast<const OutT*>(&gv);
+#pragma unroll
+              for (int q = 0; q < 8; ++q) {
+                float g = y[q];
+                if (grow) g = Cvt<OutT>::to_f(Cvt<OutT>::from_f(__fmul_rn(g, Cvt<OutT>::to_f(ga[q]))));
+                y[q] = __fadd_rn(Cvt<OutT>::to_f(xa[q]), g);
+              }
+            } else {
+              for (int q = 0; q < 8 && n + q < p.N; ++q) {
+                float g = y[q];
+                if (grow) g = Cvt<OutT>::to_f(Cvt<OutT>::from_f(__fmul_rn(g, Cvt<OutT>::to_f(grow[n + q]))));
+                y[q] = __fadd_rn(Cvt<OutT>::to_f(orow[n + q]), g);
+              }
+            }
+          }
+          if (n + 8 <= p.N) {
+            uint4 w;
+            w.x = Cvt<OutT>::pack2(y[0], y[1]);
+            w.y = Cvt<OutT>::pack2(y[2], y[3]);
+            w.z = Cvt<OutT>::pack2(y[4], y[5]);
+            w.w = Cvt<OutT>::pack2(y[6], y[7]);
+            *reinterpret_cast<uint4*>(orow + n) = w;
+          } else {
+            for (int q = 0; q < 8 && n + q < p.N; ++q) orow[n + q] = Cvt<OutT>::from_f(y[q]);
+          }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&bar->acc_empty[acc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace gemm
+
+static int num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+template <int KIND, int EPI, typename OutT>
+static int launch_gemm(const void* a, const void* w, int M, int N, int K, const gemm::Params& prm, cudaStream_t st) {
+  using namespace gemm;
+  const int esz = KIND == KIND_I8 ? 1 : 2;
+  const CUtensorMapDataType t = KIND == KIND_I8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                : KIND == KIND_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                    : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUtensorMap ma, mb;
+  uint64_t da[2] = {(uint64_t)K, (uint64_t)M}, db[2] = {(uint64_t)K, (uint64_t)N};
+  uint64_t sa[1] = {(uint64_t)K * esz}, sb[1] = {(uint64_t)K * esz};
+  uint32_t ba[2] = {(uint32_t)(BKB / esz), BM}, bb[2] = {(uint32_t)(BKB / esz), BN};
+  int rc;
+  if ((rc = encode_tmap(&ma, t, 2, a, da, sa, ba, CU_TENSOR_MAP_SWIZZLE_128B))) return rc;
+  if ((rc = encode_tmap(&mb, t, 2, w, db, sb, bb, CU_TENSOR_MAP_SWIZZLE_128B))) return rc;
+  Params p = prm;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.tiles_m = (M + BM - 1) / BM;
+  p.tiles_n = (N + BN - 1) / BN;
+  const int tiles = p.tiles_m * p.tiles_n;
+  const int grid = tiles < num_sms() ? tiles : num_sms();
+  auto kern = gemm_kernel<KIND, EPI, OutT>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+  if (e != cudaSuccess) return set_error(HI3D_ERR_CUDA, "gemm: smem attribute: %s", cudaGetErrorString(e));
+  kern<<<grid, kThreads, SMEM, st>>>(ma, mb, p);
+  return check_launch("gemm");
+}
+
+template <int KIND, typename OutT>
+static int dispatch_epi(int epi, const void* a, const void* w, int M, int N, int K, const gemm::Params& p,
+                        cudaStream_t st) {
+  switch (epi) {
+    case gemm::EPI_STORE: return launch_gemm<KIND, gemm::EPI_STORE, OutT>(a, w, M, N, K, p, st);
+    case gemm::EPI_GELU: return launch_gemm<KIND, gemm::EPI_GELU, OutT>(a, w, M, N, K, p, st);
+    case gemm::EPI_RESIDUAL: return launch_gemm<KIND, gemm::EPI_RESIDUAL, OutT>(a, w, M, N, K, p, st);
+  }
+  return set_error(HI3D_ERR_INVALID_ARGUMENT, "gemm: unknown epilogue %d", epi);
+}
+
+static int check_common(const char* what, const void* a, const void* w, const void* out, int64_t m, int64_t n,
+                        int64_t k, int64_t ldo, int epi, const void* gate, int64_t rows_per_batch, int64_t gate_stride) {
+  if (!a || !w || !out) return set_error(HI3D_ERR_INVALID_ARGUMENT, "%s: null pointer", what);
+  if (m < 0 || n <= 0 || k <= 0 || m > 0x7fffffff || n > 0x7fffffff || k > 0x7fffffff)
+    return set_error(HI3D_ERR_INVALID_ARGUMENT, "%s: bad sizes m=%lld n=%lld k=%lld", what, (long long)m,
+                     (long long)n, (long long)k);
+  if (ldo < n || ldo % 4 || !aligned16(a) || !aligned16(w) || !aligned16(out))
+    return set_error(HI3D_ERR_INVALID_ARGUMENT, "%s: ldo must be >= n and 16-byte rows; pointers 16-byte aligned", what);
+  if (epi < 0 || epi > 2) return set_error(HI3D_ERR_INVALID_ARGUMENT, "%s: unknown epilogue %d", what, epi);
+  if (gate && (epi != gemm::EPI_RESIDUAL || rows_per_batch <= 0 || gate_stride % 8 || !aligned16(gate)))
+    return set_error(HI3D_ERR_INVALID_ARGUMENT, "%s: gate needs the residual epilogue, rows_per_batch > 0, aligned",
+                     what);
+  return HI3D_OK;
+}
+
+}  // namespace hi3d
+
+using namespace hi3d;
+
+extern "C" int hi3d_gemm_w8a8(const int8_t* a, const int8_t* w, const float* sa, const float* sw, const void* bias,
+                              void* out, int64_t m, int64_t n, int64_t k, int64_t ldo, int epilogue,
+                              const void* gate, int64_t rows_per_batch, int64_t gate_stride, int out_dtype,
+                              void* stream) {
+  int rc = check_common("gemm_w8a8", a, w, out, m, n, k, ldo, epilogue, gate, rows_per_batch, gate_stride);
+  if (rc) return rc;
+  if ((!sa || !sw) && out_dtype != HI3D_I32)
+    return set_error(HI3D_ERR_INVALID_ARGUMENT, "gemm_w8a8: activation and weight scales are required");
+  if (k % 16) return set_error(HI3D_ERR_INVALID_ARGUMENT, "gemm_w8a8: K must be a multiple of 16");
+  if (out_dtype != HI3D_I32 && ldo % 8)
+    return set_error(HI3D_ERR_INVALID_ARGUMENT, "gemm_w8a8: ldo must be a multiple of 8 for 16-bit outputs");
+  if (m == 0) return HI3D_OK;
+  gemm::Params p = {};
+  p.out = out;
+  p.ldo = ldo;
+  p.bias = bias;
+  p.sa = sa;
+  p.sw = sw;
+  p.gate = gate;
+  p.rows_per_batch = rows_per_batch > 0 ? rows_per_batch : m;
+  p.gate_stride = gate_stride;
+  cudaStream_t st = as_stream(stream);
+  if (out_dtype == HI3D_F16)
+    return dispatch_epi<gemm::KIND_I8, __half>(epilogue, a, w, (int)m, (int)n, (int)k, p, st);
+  if (out_dtype == HI3D_BF16)
+    return dispatch_epi<gemm::KIND_I8, __nv_bfloat16>(epilogue, a, w, (int)m, (int)n, (int)k, p, st);
+  if (out_dtype == HI3D_I32) {
+    if (epilogue != gemm::EPI_STORE)
+      return set_error(HI3D_ERR_INVALID_ARGUMENT, "gemm_w8a8: int32 output stores raw accumulators only");
+    return launch_gemm<gemm::KIND_I8, gemm::EPI_STORE, int32_t>(a, w, (int)m, (int)n, (int)k, p, st);
+  }
+  return set_error(HI3D_ERR_INVALID_ARGUMENT, "gemm_w8a8: out dtype must be f16, bf16 or i32");
+}
+
+extern "C" int hi3d_gemm(const void* a, const void* w, const void* bias, void* out, int64_t m, int64_t n, int64_t k,
+                         int64_t ldo, int epilogue, const void* gate, int64_t rows_per_batch, int64_t gate_stride,
+                         int dtype, void* stream) {
+  int rc = check_common("gemm", a, w, out, m, n, k, ldo, epilogue, gate, rows_per_batch, gate_stride);
+  if (rc) return rc;
+  if (k % 8) return set_error(HI3D_ERR_INVALID_ARGUMENT, "gemm: K must be a multiple of 8");
+  if (ldo % 8) return set_error(HI3D_ERR_INVALID_ARGUMENT, "gemm: ldo must be a multiple of 8");
+  if (m == 0) return HI3D_OK;
+  gemm::Params p = {};
+  p.out = out;
+  p.ldo = ldo;
+  p.bias = bias;
+  p.gate = gate;
+  p.rows_per_batch = rows_per_batch > 0 ? rows_per_batch : m;
+  p.gate_stride = gate_stride;
+  cudaStream_t st = as_stream(stream);
+  if (dtype == HI3D_F16) return dispatch_epi<gemm::KIND_F16, __half>(epilogue, a, w, (int)m, (int)n, (int)k, p, st);
+  if (dtype == HI3D_BF16)
+    return dispatch_epi<gemm::KIND_BF16, __nv_bfloat16>(epilogue, a, w, (int)m, (int)n, (int)k, p, st);
+  return set_error(HI3D_ERR_INVALID_ARGUMENT, "gemm: dtype must be f16 or bf16");
+}

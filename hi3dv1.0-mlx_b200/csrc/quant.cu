@@ -1,0 +1,151 @@
+// Dynamic per-row int8 quantisation of activations with the signed 64-point
+// Hadamard rotation of the reference W8A8 path (w8a8.py:25-58, :95-102).
+//
+// Per row and per 64-element block: y = H64(x * sign) / 8 with H64 the
+// natural-order (Sylvester) Walsh-Hadamard transform, evaluated as six
+// butterfly stages over the element index bits 0..5 in that order; stage b
+// maps (u at bit clear, v at bit set) to (u + v, u - v), and the last stage
+// also multiplies by 0.125.  This is the reference's operation order for every
+// element (its five xor-shuffle stages over lane bits 0-4, then the (c, c+32)
+// pair), so the fp32 values, and hence the int8 codes, are reproduced exactly.
+// Then s = max(max|y|, 1e-8) / 127 and q = clamp(rint(y / s), -127, 127)
+// (round half to even), all in IEEE fp32.
+//
+// Layout: one warp per row; each lane owns 8 consecutive elements (16-byte
+// loads), so bits 0-2 of the element index are in-register stages and bits
+// 3-5 are xor-shuffles across lanes 1, 2 and 4 apart.
+#include "abi.h"
+#include "common.cuh"
+
+namespace hi3d {
+
+template <typename T>
+__device__ __forceinline__ void load8(const T* p, float (&f)[8]) {
+  const uint4 raw = *reinterpret_cast<const uint4*>(p);
+  const T* h = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) f[i] = Cvt<T>::to_f(h[i]);
+}
+
+// (clear, set) -> (clear + set, clear - set) across lanes `dist` apart
+__device__ __forceinline__ float butterfly_lane(float v, int dist, bool set) {
+  const float other = __shfl_xor_sync(0xffffffffu, v, dist);
+  return set ? __fsub_rn(other, v) : __fadd_rn(v, other);
+}
+
+template <typename T, int ITERS, bool ROTATE>
+__global__ void __launch_bounds__(256) quant_h64_kernel(const T* __restrict__ x, const float* __restrict__ sign,
+                                                        int8_t* __restrict__ q, float* __restrict__ scale, int64_t rows,
+                                                        int K) {
+  const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (row >= rows) return;  // whole warp leaves together
+  const int lane = threadIdx.x & 31;
+  const T* xr = x + row * K;
+  float y[ITERS][8];
+  float amax = 0.f;
+#pragma unroll
+  for (int it = 0; it < ITERS; ++it) {
+    const int base = it * 256 + lane * 8;
+    const bool active = base < K;
+    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (active) {
+      load8<T>(xr + base, v);
+      if (ROTATE) {
+        const float4 s0 = *reinterpret_cast<const float4*>(sign + base);
+        const float4 s1 = *reinterpret_cast<const float4*>(sign + base + 4);
+        v[0] = __fmul_rn(v[0], s0.x); v[1] = __fmul_rn(v[1], s0.y);
+        v[2] = __fmul_rn(v[2], s0.z); v[3] = __fmul_rn(v[3], s0.w);
+        v[4] = __fmul_rn(v[4], s1.x); v[5] = __fmul_rn(v[5], s1.y);
+        v[6] = __fmul_rn(v[6], s1.z); v[7] = __fmul_rn(v[7], s1.w);
+      }
+    }
+    if (ROTATE) {
+      // element bits 0, 1, 2: in registers
+#pragma unroll
+      for (int d = 1; d < 8; d <<= 1) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          if (i & d) continue;
+          const float u = v[i], w = v[i | d];
+          v[i] = __fadd_rn(u, w);
+          v[i | d] = __fsub_rn(u, w);
+        }
+      }
+      // element bits 3, 4: lanes 1 and 2 apart; bit 5: lanes 4 apart, with the 1/8 scale
+      const int g = lane & 7;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = butterfly_lane(v[i], 1, g & 1);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = butterfly_lane(v[i], 2, g & 2);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(butterfly_lane(v[i], 4, g & 4), 0.125f);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      y[it][i] = v[i];
+      if (active) amax = fmaxf(amax, fabsf(v[i]));
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  const float s = __fdiv_rn(fmaxf(amax, 1e-8f), 127.0f);
+  if (lane == 0) scale[row] = s;
+  int8_t* qr = q + row * K;
+#pragma unroll
+  for (int it = 0; it < ITERS; ++it) {
+    const int base = it * 256 + lane * 8;
+    if (base >= K) continue;
+    uint32_t w[2] = {0u, 0u};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float r = rintf(__fdiv_rn(y[it][i], s));
+      r = fminf(fmaxf(r, -127.0f), 127.0f);
+      w[i >> 2] |= ((uint32_t)(uint8_t)(int8_t)(int)r) << (8 * (i & 3));
+    }
+    *reinterpret_cast<uint2*>(qr + base) = make_uint2(w[0], w[1]);
+  }
+}
+
+template <typename T, bool ROTATE>
+static int launch_quant(const void* x, const float* sign, int8_t* q, float* scale, int64_t rows, int K,
+                        cudaStream_t st) {
+  const dim3 grid((unsigned)((rows + 7) / 8)), block(256);
+  switch ((K + 255) / 256) {
+#define HI3D_Q(n) \
+  case n: quant_h64_kernel<T, n, ROTATE><<<grid, block, 0, st>>>((const T*)x, sign, q, scale, rows, K); break;
+    HI3D_Q(1) HI3D_Q(2) HI3D_Q(3) HI3D_Q(4) HI3D_Q(5) HI3D_Q(6) HI3D_Q(7) HI3D_Q(8)
+    HI3D_Q(9) HI3D_Q(10) HI3D_Q(11) HI3D_Q(12) HI3D_Q(13) HI3D_Q(14) HI3D_Q(15) HI3D_Q(16)
+    HI3D_Q(17) HI3D_Q(18) HI3D_Q(19) HI3D_Q(20) HI3D_Q(21) HI3D_Q(22) HI3D_Q(23) HI3D_Q(24)
+    HI3D_Q(25) HI3D_Q(26) HI3D_Q(27) HI3D_Q(28) HI3D_Q(29) HI3D_Q(30) HI3D_Q(31) HI3D_Q(32)
+    HI3D_Q(33) HI3D_Q(34)
+#undef HI3D_Q
+    default:
+      return set_error(HI3D_ERR_UNSUPPORTED, "quantize_act_i8: width %d above 8704 not supported", K);
+  }
+  return check_launch("quantize_act_i8");
+}
+
+}  // namespace hi3d
+
+using namespace hi3d;
+
+extern "C" int hi3d_quantize_act_i8(const void* x, const float* multiplier, int8_t* q, float* scale, int64_t rows,
+                                    int64_t k, int rotate, int dtype, void* stream) {
+  if (!x || !q || !scale || rows < 0 || k <= 0)
+    return set_error(HI3D_ERR_INVALID_ARGUMENT, "quantize_act_i8: bad pointers or sizes");
+  if (k % 64) return set_error(HI3D_ERR_INVALID_ARGUMENT, "signed H64 requires width divisible by 64");
+  if (rotate && !multiplier)
+    return set_error(HI3D_ERR_INVALID_ARGUMENT, "quantize_act_i8: the rotation needs the sign multiplier");
+  if (!aligned16(x) || !aligned16(q) || (multiplier && !aligned16(multiplier)))
+    return set_error(HI3D_ERR_INVALID_ARGUMENT, "quantize_act_i8: pointers must be 16-byte aligned");
+  if (rows == 0) return HI3D_OK;
+  cudaStream_t st = as_stream(stream);
+  const int K = (int)k;
+  if (dtype == HI3D_F16)
+    return rotate ? launch_quant<__half, true>(x, multiplier, q, scale, rows, K, st)
+                  : launch_quant<__half, false>(x, multiplier, q, scale, rows, K, st);
+  if (dtype == HI3D_BF16)
+    return rotate ? launch_quant<__nv_bfloat16, true>(x, multiplier, q, scale, rows, K, st)
+                  : launch_quant<__nv_bfloat16, false>(x, multiplier, q, scale, rows, K, st);
+  return set_error(HI3D_ERR_INVALID_ARGUMENT, "quantize_act_i8: dtype must be f16 or bf16");
+}

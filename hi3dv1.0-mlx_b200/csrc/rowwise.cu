@@ -195,7 +195,7 @@ __global__ void __launch_bounds__(256) qkv_rope_rms_kernel(const T* __restrict__
   const int ph = in_range ? (int)(unit % (3 * H)) : 0;
   const int part = ph / H, h = ph % H;
   const int64_t b = m / N, n = m % N;
-  const T* src = qkv + (m * 3 + part) * (int64_t)H * D;
+  const T* src = qkv + ((m * 3 + part) * (int64_t)H + h) * D;  // kernels.py:31
   const int64_t dst_off = token_major ? ((b * N + n) * H + h) * D : ((b * H + h) * N + n) * D;
   const int c0 = sub * 8;
   Vec8 raw = {};

@@ -22,7 +22,8 @@ ERR_CUDA = 3
 ERR_DEVICE_TIMEOUT = 4
 ERR_CAPACITY = 5
 
-F16, BF16, F32 = 0, 1, 2
+F16, BF16, F32, I32 = 0, 1, 2, 3
+EPI_STORE, EPI_GELU, EPI_RESIDUAL = 0, 1, 2
 
 _c_void_p = ctypes.c_void_p
 _i64 = ctypes.c_int64
@@ -57,6 +58,9 @@ SIGNATURES: dict[str, tuple] = {
     "hi3d_flash_attn_fwd": (_i32, [ctypes.POINTER(AttnArgs), _c_void_p]),
     "hi3d_gate_residual": (_i32, [_c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64, _i64, _i32, _c_void_p]),
     "hi3d_gelu_tanh": (_i32, [_c_void_p, _c_void_p, _i64, _i32, _c_void_p]),
+    "hi3d_gemm": (_i32, [_c_void_p] * 4 + [_i64] * 4 + [_i32, _c_void_p, _i64, _i64, _i32, _c_void_p]),
+    "hi3d_gemm_w8a8": (_i32, [_c_void_p] * 6 + [_i64] * 4 + [_i32, _c_void_p, _i64, _i64, _i32, _c_void_p]),
+    "hi3d_quantize_act_i8": (_i32, [_c_void_p] * 4 + [_i64, _i64, _i32, _i32, _c_void_p]),
 }
 
 _lib = None

@@ -42,16 +42,16 @@ def block_forward_sharded(w: dict, x: torch.Tensor, mod: torch.Tensor, cos: torc
     hv.wait()
     a = attention.flash_attention(q, k_all.permute(1, 0, 2)[None], v_all.permute(1, 0, 2)[None], scale,
                                   q_layout="bnhd")
-    kernels.gate_residual(x, linear(a[0], w, "self_attn.to_out"), gate_msa)
+    linear(a[0], w, "self_attn.to_out", epilogue="residual", residual=x, gate=gate_msa)
 
     h = kernels.layer_norm_modulate(x, 1e-6, weight=w["norm2.weight"], bias=w["norm2.bias"])
     qc = linear(h, w, "cross_attn.to_q").view(1, t_local, heads, d)
     o = attention.flash_attention(qc, ck, cv, scale, q_layout="bnhd")[0]
-    kernels.gate_residual(x, linear(o, w, "cross_attn.to_out"), None)
+    linear(o, w, "cross_attn.to_out", epilogue="residual", residual=x)
 
     h = kernels.layer_norm_modulate(x, 1e-6, scale=scale_mlp, shift=shift_mlp)
-    h = kernels.gelu_tanh(linear(h, w, "mlp.mlp.0"))
-    kernels.gate_residual(x, linear(h, w, "mlp.mlp.2"), gate_mlp)
+    h = linear(h, w, "mlp.mlp.0", epilogue="gelu")
+    linear(h, w, "mlp.mlp.2", epilogue="residual", residual=x, gate=gate_mlp)
     return x
 
 

@@ -27,6 +27,8 @@ import numpy as np
 import torch
 
 from . import attention, kernels
+from . import linear as _linear
+from . import w8a8 as _w8a8
 
 # fp16 GEMMs accumulate in fp32, as mx.addmm does (transformer.py:119).
 torch.backends.cuda.matmul.allow_fp16_reduced_precision_reduction = False
@@ -75,9 +77,32 @@ def to_device(w: dict, device, dtype: torch.dtype = torch.float16) -> dict:
     return out
 
 
-def linear(x: torch.Tensor, w: dict, name: str) -> torch.Tensor:
-    """``x @ W^T + b`` in the weight dtype with fp32 accumulation (transformer.py:111-119)."""
-    return torch.addmm(w[f"{name}.bias"], x, w[f"{name}.weight"].t())
+def linear(x: torch.Tensor, w: dict, name: str, epilogue: str = "store", residual: torch.Tensor | None = None,
+           gate: torch.Tensor | None = None) -> torch.Tensor:
+    """Projection ``name`` of a block: ``x @ W^T + b`` on the tcgen05 GEMM, in the weight dtype
+    with fp32 accumulation (transformer.py:111-119), or through int8 when the block holds W8A8
+    weights (``<name>.w8_scale`` present, the hook at transformer.py:504-507).  ``epilogue``
+    fuses GELU or the gated residual update into the GEMM."""
+    if f"{name}.w8_scale" in w:
+        return _w8a8.linear(x, w[f"{name}.weight"], w[f"{name}.w8_scale"], w[f"{name}.bias"], epilogue=epilogue,
+                            residual=residual, gate=gate)
+    return _linear.linear(x, w[f"{name}.weight"], w[f"{name}.bias"], epilogue=epilogue, residual=residual, gate=gate)
+
+
+BLOCK_PROJECTIONS = ("self_attn.to_qkv", "self_attn.to_out", "cross_attn.to_q", "cross_attn.to_out", "mlp.mlp.0",
+                     "mlp.mlp.2")
+
+
+def to_w8a8(w: dict, rotate: bool = True) -> dict:
+    """Block weights in the ``hi3d-w8a8-h64`` form: the six block projections as int8 rows in
+    the rotated domain plus ``<name>.w8_scale`` (models/w8a8/manifest.json:9-16); the condition
+    K/V projection, norms and modulation stay as they are."""
+    out = dict(w)
+    for name in BLOCK_PROJECTIONS:
+        q, s = _w8a8.quantize_weight(w[f"{name}.weight"], rotate=rotate)
+        out[f"{name}.weight"] = q
+        out[f"{name}.w8_scale"] = s
+    return out
 
 
 def context_kv(w: dict, cond: torch.Tensor, heads: int) -> tuple[torch.Tensor, torch.Tensor]:
@@ -128,22 +153,22 @@ def block_forward(w: dict, x: torch.Tensor, mod: torch.Tensor, cos: torch.Tensor
     q, k, v = kernels.qkv_rope_rms(qkv, cos, sin, w["self_attn.q_rms_norm.gamma"],
                                    w["self_attn.k_rms_norm.gamma"], batch, heads, d)
     a = attention.flash_attention(q, k, v, scale)
-    kernels.gate_residual(x, linear(a.view(-1, c), w, "self_attn.to_out").view(batch, n, c), gate_msa)
+    linear(a, w, "self_attn.to_out", epilogue="residual", residual=x, gate=gate_msa)
 
     # cross-attention (positive branches), constant for the zero-condition branch
     h = kernels.layer_norm_modulate(x, 1e-6, weight=w["norm2.weight"], bias=w["norm2.bias"])
     for b in range(n_pos):
         qc = linear(h[b], w, "cross_attn.to_q").view(1, n, heads, d)
         o = attention.flash_attention(qc, ck, cv, scale, q_layout="bnhd")[0]
-        kernels.gate_residual(x[b], linear(o, w, "cross_attn.to_out"), None)
+        linear(o, w, "cross_attn.to_out", epilogue="residual", residual=x[b])
     if negative is not None:
         for b in range(n_pos, batch):
             kernels.gate_residual(x[b], negative.to(dt).expand(n, c).contiguous(), None)
 
     # MLP
     h = kernels.layer_norm_modulate(x, 1e-6, scale=scale_mlp, shift=shift_mlp)
-    h = kernels.gelu_tanh(linear(h.view(-1, c), w, "mlp.mlp.0"))
-    kernels.gate_residual(x, linear(h, w, "mlp.mlp.2").view(batch, n, c), gate_mlp)
+    h = linear(h, w, "mlp.mlp.0", epilogue="gelu")
+    linear(h, w, "mlp.mlp.2", epilogue="residual", residual=x, gate=gate_mlp)
     return x
 
 
@@ -168,17 +193,17 @@ def block_forward_packed(w: dict, x: torch.Tensor, mod: torch.Tensor, cos: torch
                                    w["self_attn.k_rms_norm.gamma"], 1, heads, d)
     tr = lambda z: z[0].permute(1, 0, 2)  # [1, H, T, D] -> [T, H, D] view
     a = attention.flash_attn_varlen(tr(q), tr(k), tr(v), cu_seqlens, cu_seqlens, max_seqlen, scale)
-    kernels.gate_residual(x, linear(a.view(t, c), w, "self_attn.to_out"), gate_msa)
+    linear(a.view(t, c), w, "self_attn.to_out", epilogue="residual", residual=x, gate=gate_msa)
 
     h = kernels.layer_norm_modulate(x, 1e-6, weight=w["norm2.weight"], bias=w["norm2.bias"])
     qc = linear(h, w, "cross_attn.to_q").view(t, heads, d)
     o = attention.flash_attn_varlen(qc, ck[0].permute(1, 0, 2), cv[0].permute(1, 0, 2), cu_seqlens, None,
                                     max_seqlen, scale)
-    kernels.gate_residual(x, linear(o.view(t, c), w, "cross_attn.to_out"), None)
+    linear(o.view(t, c), w, "cross_attn.to_out", epilogue="residual", residual=x)
 
     h = kernels.layer_norm_modulate(x, 1e-6, scale=scale_mlp, shift=shift_mlp)
-    h = kernels.gelu_tanh(linear(h, w, "mlp.mlp.0"))
-    kernels.gate_residual(x, linear(h, w, "mlp.mlp.2"), gate_mlp)
+    h = linear(h, w, "mlp.mlp.0", epilogue="gelu")
+    linear(h, w, "mlp.mlp.2", epilogue="residual", residual=x, gate=gate_mlp)
     return x
 
 

@@ -43,6 +43,7 @@ extern "C" {
 #define HI3D_F16 0
 #define HI3D_BF16 1
 #define HI3D_F32 2
+#define HI3D_I32 3 /* raw int32 accumulators (hi3d_gemm_w8a8 output only) */
 
 /* ---- library ----------------------------------------------------------- */
 HI3D_API int hi3d_version(void);
@@ -122,6 +123,39 @@ typedef struct hi3d_attn_args {
 } hi3d_attn_args;
 
 HI3D_API int hi3d_flash_attn_fwd(const hi3d_attn_args* args, void* stream);
+
+/* ---- projections (tcgen05 GEMM with fused epilogues) --------------------- */
+/* out = epilogue(A W^T): A [m, k] and W [n, k] row-major (K-major, as nn.Linear weights),
+ * out [m, ldo] row-major.  Epilogues act on y = round(acc + bias) (bias [n] in the output
+ * type, may be NULL):
+ *   0  store y
+ *   1  store gelu_tanh(y) (GELU in fp32, rounded once; transformer.py:176-179)
+ *   2  residual update in place: out[m, n] = round(out[m, n] + round(y * gate[n])) with
+ *      gate [n] per batch element (gate_stride apart, rows_per_batch rows each), or
+ *      out += y when gate is NULL (transformer.py:570, :584, :588)
+ * hi3d_gemm replaces the fp16 projection mx.addmm (src/hi3d_mac/mlx_backend/transformer.py:111-119,
+ * 501-516): 16-bit A and W, fp32 accumulation.  k % 8 == 0. */
+HI3D_API int hi3d_gemm(const void* a, const void* w, const void* bias, void* out, int64_t m, int64_t n, int64_t k,
+                       int64_t ldo, int epilogue, const void* gate, int64_t rows_per_batch, int64_t gate_stride,
+                       int dtype, void* stream);
+
+/* Replaces w8a8.linear's GEMM (src/hi3d_mac/mlx_backend/w8a8.py:61-80, :105-119): int8 A [m, k]
+ * x int8 W [n, k] with exact int32 accumulation, dequantised as
+ * y = round(float(acc) * sa[m] * sw[n] + float(bias[n])) evaluated left to right without FMA,
+ * then the epilogue above.  out_dtype HI3D_I32 stores the raw accumulators (epilogue 0,
+ * scales and bias ignored).  k % 16 == 0. */
+HI3D_API int hi3d_gemm_w8a8(const int8_t* a, const int8_t* w, const float* sa, const float* sw, const void* bias,
+                            void* out, int64_t m, int64_t n, int64_t k, int64_t ldo, int epilogue,
+                            const void* gate, int64_t rows_per_batch, int64_t gate_stride, int out_dtype,
+                            void* stream);
+
+/* Replaces w8a8.quantize_activation (src/hi3d_mac/mlx_backend/w8a8.py:25-58, :95-102):
+ * per row of x [rows, k] (k % 64 == 0), y = H64(x * multiplier) / 8 per 64-block (signed
+ * natural-order Walsh-Hadamard, rotate != 0) or y = x (rotate == 0); s = max(max|y|, 1e-8) / 127;
+ * q = clamp(rint(y / s), -127, 127).  Writes q [rows, k] int8 and scale [rows] fp32.
+ * The fp32 butterfly follows the reference's operation order, so codes are reproducible. */
+HI3D_API int hi3d_quantize_act_i8(const void* x, const float* multiplier, int8_t* q, float* scale, int64_t rows,
+                                  int64_t k, int rotate, int dtype, void* stream);
 
 /* ---- elementwise epilogues of the block --------------------------------- */
 /* x <- x + y * gate (all in the I/O type, two roundings: round(y*gate), then round(x + .)).

@@ -57,6 +57,25 @@ def test_config0_block_matches_fp32_oracle():
     assert rel_l2(y[0].float().cpu().numpy(), ref) < TOL
 
 
+def test_block_with_strong_gates_and_update():
+    """O(1) adaLN gates so every branch moves the output; also bound the error of the
+    block's update (out - x) itself, which exposes any wrong branch."""
+    coords, w, x, mod, ctx, cos, sin = _config0(n=2048, c=1024, heads=16, L=300, seed=30)
+    rng = np.random.default_rng(31)
+    w["modulation"] = rng.standard_normal((1, 6 * 1024)).astype(np.float32) * 0.5
+    w["self_attn.q_rms_norm.gamma"] = rng.uniform(0.5, 1.5, (16, 64)).astype(np.float32)
+    w["self_attn.k_rms_norm.gamma"] = rng.uniform(0.5, 1.5, (16, 64)).astype(np.float32)
+    heads = 16
+    wd = transformer.to_device(w, DEV)
+    ck, cv = transformer.context_kv(wd, _t(ctx), heads)
+    y = transformer.block_forward(wd, _t(x)[None], _t(mod), _t(cos), _t(sin), ck, cv, None, heads)[0]
+    ref = ops.block_forward_f32(w, x.astype(np.float32), mod, cos, sin, ctx, heads)
+    got = y.float().cpu().numpy()
+    assert rel_l2(got, ref) < TOL
+    xf = x.astype(np.float32)
+    assert rel_l2(got - xf, ref - xf) < 5e-3
+
+
 def test_cfg_batch_with_zero_condition_branch():
     coords, w, x, mod, ctx, cos, sin = _config0(n=1000, c=256, heads=4, L=77, seed=10)
     heads = 4
@@ -82,3 +101,22 @@ def test_two_block_stack():
     ref = ops.block_forward_f32(w, x.astype(np.float32), mod, cos, sin, ctx, heads)
     ref = ops.block_forward_f32(w2, ref, mod, cos, sin, ctx, heads)
     assert rel_l2(y[0].float().cpu().numpy(), ref) < TOL
+
+
+def test_w8a8_block_close_to_fp32_oracle():
+    """cfg2 path: the six block projections through int8 (signed-H64 activations, rotated int8
+    weights, exact int32 accumulation).  Bounded by int8 quantisation error."""
+    coords, w, x, mod, ctx, cos, sin = _config0(n=2048, c=1024, heads=16, L=300, seed=40)
+    rng = np.random.default_rng(41)
+    w["modulation"] = rng.standard_normal((1, 6 * 1024)).astype(np.float32) * 0.5
+    heads = 16
+    wd = transformer.to_w8a8(transformer.to_device(w, DEV))
+    assert wd["self_attn.to_qkv.weight"].dtype == torch.int8
+    ck, cv = transformer.context_kv(wd, _t(ctx), heads)
+    y = transformer.block_forward(wd, _t(x)[None], _t(mod), _t(cos), _t(sin), ck, cv, None, heads)[0]
+    ref = ops.block_forward_f32(w, x.astype(np.float32), mod, cos, sin, ctx, heads)
+    got = y.float().cpu().numpy()
+    assert np.isfinite(got).all()
+    assert rel_l2(got, ref) < 1e-2
+    xf = x.astype(np.float32)
+    assert rel_l2(got - xf, ref - xf) < 5e-2

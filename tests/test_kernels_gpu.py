@@ -131,14 +131,15 @@ def test_gate_residual_bit_exact():
     assert np.array_equal(xt.cpu().numpy(), ops.gate_residual(x, y, None))
 
 
-def test_gelu_tanh_within_one_ulp():
-    """fp32 evaluation of the reference formula, rounded once: within one fp16 ulp of the
-    numpy evaluation everywhere.  (``1 + tanh(z)`` cancels for negative inputs, so
-    implementations that differ in the last fp32 bit of tanh flip a few percent of roundings.)"""
+def test_gelu_tanh_matches_float64():
+    """fp32 evaluation of the reference formula, rounded once.  ``1 + tanh(z)`` cancels for
+    negative inputs, so the fp32 formula (here and in the reference) carries an absolute error
+    of a few 1e-7 * |x| there; elsewhere the result is within one fp16 rounding of exact."""
     rng = np.random.default_rng(9)
     x = (rng.standard_normal((300, 4096)) * 3).astype(np.float16)
-    got = kernels.gelu_tanh(_t(x)).cpu().numpy()
+    got = kernels.gelu_tanh(_t(x)).cpu().numpy().astype(np.float64)
+    xd = x.astype(np.float64)
+    exact = 0.5 * xd * (1 + np.tanh(np.sqrt(2 / np.pi) * (xd + 0.044715 * xd ** 3)))
+    assert (np.abs(got - exact) <= 2.0 ** -11 * np.abs(exact) + 1e-6 * (1 + np.abs(xd))).all()
     ref = ops.gelu_tanh(x)
-    assert (got == ref).mean() > 0.95
-    diff = np.abs(got.view(np.int16).astype(np.int32) - ref.view(np.int16).astype(np.int32))
-    assert diff.max() <= 1
+    assert (got.astype(np.float16) == ref).mean() > 0.95
