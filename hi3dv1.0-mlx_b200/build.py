@@ -1,7 +1,6 @@
 """Build the sm_100a shared library ``hi3d_b200/_lib/libhi3d_b200.so`` in place.
 
-Compiles every ``csrc/*.cu`` with nvcc (relocatable device code, one object
-per file, in parallel) and links them into one shared library that exports
+Compiles every ``csrc/*.cu`` with nvcc (one object per file, in parallel) and links them into one shared library that exports
 the C ABI declared in ``include/hi3d_b200.h``.  Objects are rebuilt only
 when a source or header is newer than the object.
 
@@ -26,7 +25,7 @@ LIB = HERE / "hi3d_b200" / "_lib" / "libhi3d_b200.so"
 
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-FLAGS = ["-O3", "-std=c++17", "-rdc=true", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
+FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
          "--expt-relaxed-constexpr", f"-I{INCLUDE}", f"-I{CSRC}"]
 
 
@@ -56,7 +55,7 @@ def build(force: bool = False, jobs: int | None = None, verbose: bool = True) ->
         objs = list(pool.map(lambda s: _compile(s, force), sources))
     newest = max(o.stat().st_mtime for o in objs)
     if force or not LIB.exists() or LIB.stat().st_mtime < newest:
-        cmd = [NVCC, *ARCH, "-shared", "-rdc=true", *[str(o) for o in objs], "-o", str(LIB)]
+        cmd = [NVCC, *ARCH, "-shared", *[str(o) for o in objs], "-o", str(LIB)]
         proc = subprocess.run(cmd, capture_output=True, text=True)
         if proc.returncode != 0:
             raise RuntimeError(f"link failed:\n{proc.stderr}")

@@ -10,7 +10,12 @@
 
 namespace hi3d {
 
-__device__ DeviceStatus g_status;
+static StatusReader g_readers[16];
+static int g_num_readers = 0;
+
+void register_status_reader(StatusReader fn) {
+  if (g_num_readers < 16) g_readers[g_num_readers++] = fn;
+}
 
 static thread_local char t_last_error[512] = "";
 
@@ -69,19 +74,18 @@ extern "C" int hi3d_version(void) { return 100; }
 extern "C" const char* hi3d_last_error_string(void) { return t_last_error; }
 
 extern "C" int hi3d_device_status(int* code, int* where, int* block, int* detail, int reset) {
-  DeviceStatus s;
   cudaError_t e = cudaDeviceSynchronize();
   if (e != cudaSuccess) return set_error(HI3D_ERR_CUDA, "cudaDeviceSynchronize: %s", cudaGetErrorString(e));
-  e = cudaMemcpyFromSymbol(&s, g_status, sizeof(s));
-  if (e != cudaSuccess) return set_error(HI3D_ERR_CUDA, "reading device status: %s", cudaGetErrorString(e));
-  if (code) *code = s.code;
-  if (where) *where = s.where;
-  if (block) *block = s.block;
-  if (detail) *detail = s.detail;
-  if (reset) {
-    DeviceStatus z = {0, 0, 0, 0};
-    e = cudaMemcpyToSymbol(g_status, &z, sizeof(z));
-    if (e != cudaSuccess) return set_error(HI3D_ERR_CUDA, "clearing device status: %s", cudaGetErrorString(e));
+  DeviceStatus first = {0, 0, 0, 0};
+  for (int i = 0; i < g_num_readers; ++i) {
+    DeviceStatus s;
+    e = g_readers[i](&s, reset != 0);
+    if (e != cudaSuccess) return set_error(HI3D_ERR_CUDA, "reading device status: %s", cudaGetErrorString(e));
+    if (first.code == 0 && s.code != 0) first = s;
   }
+  if (code) *code = first.code;
+  if (where) *where = first.where;
+  if (block) *block = first.block;
+  if (detail) *detail = first.detail;
   return HI3D_OK;
 }

@@ -29,7 +29,10 @@ constexpr int kThreads = 320;
 constexpr int kRowsPerTile = 128;
 // Exponentials per 16-pair chunk of a score row evaluated by the FMA-pipe
 // polynomial (the rest use the MUFU ex2 unit), balancing the two pipes.
-constexpr int kEmuPairs = 6;
+#ifndef HI3D_ATTN_EMU_PAIRS
+#define HI3D_ATTN_EMU_PAIRS 4
+#endif
+constexpr int kEmuPairs = HI3D_ATTN_EMU_PAIRS;
 // Row maximum growth (log2 units) tolerated before O and l are rescaled.
 constexpr float kRescaleLog2 = 8.0f;
 
@@ -176,14 +179,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
       constexpr uint32_t idesc_s = make_idesc(1, fmt, 0, 0, kRowsPerTile, C::BK);
       constexpr uint32_t idesc_pv = make_idesc(1, fmt, 0, 1, kRowsPerTile, D);
-      const uint32_t sQa = smem_u32(sQ), sKa = smem_u32(sK), sVa = smem_u32(sV);
+      // Base descriptors, built once.  Moving a descriptor by `off` bytes adds
+      // off >> 4 to its start-address field (no carry: shared addresses < 2^18).
+      const uint64_t dQ = smem_desc(smem_u32(sQ), 16, 1024, kLayoutSW128);
+      const uint64_t dK = smem_desc(smem_u32(sK), 16, 1024, kLayoutSW128);
+      const uint64_t dV = smem_desc(smem_u32(sV), C::KV_CHUNK, 1024, kLayoutSW128);
       auto issue_s = [&](int i, int s) {
+        const uint64_t dKs = dK + (uint64_t)((s * C::KV_STAGE) >> 4);
+        const uint32_t d = tmem + 256 * i + C::S_COL;
 #pragma unroll
         for (int ks = 0; ks < D / 16; ++ks) {
-          const uint32_t off = (uint32_t)(ks & 3) * 32;
-          const uint64_t da = smem_desc(sQa + (i * C::NCH + (ks >> 2)) * C::Q_CHUNK + off, 16, 1024, kLayoutSW128);
-          const uint64_t db = smem_desc(sKa + s * C::KV_STAGE + (ks >> 2) * C::KV_CHUNK + off, 16, 1024, kLayoutSW128);
-          mma_f16_ss(tmem + 256 * i + C::S_COL, da, db, idesc_s, ks > 0 ? 1u : 0u);
+          const uint32_t off_q = ((i * C::NCH + (ks >> 2)) * C::Q_CHUNK + (ks & 3) * 32) >> 4;
+          const uint32_t off_k = ((ks >> 2) * C::KV_CHUNK + (ks & 3) * 32) >> 4;
+          mma_f16_ss(d, dQ + off_q, dKs + off_k, idesc_s, ks > 0 ? 1u : 0u);
         }
         tc_commit(&bar->s_full[i]);
       };
@@ -201,12 +209,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < 2; ++i) {
           if (!(ok = mbar_wait(&bar->p_full[i], j & 1, abort, 14))) break;
           tc_fence_after();
+          const uint64_t dVs = dV + (uint64_t)((s * C::KV_STAGE) >> 4);
+          const uint32_t dO = tmem + 256 * i + C::O_COL, aP = tmem + 256 * i + C::P_COL;
 #pragma unroll
-          for (int ks = 0; ks < C::BK / 16; ++ks) {
-            const uint64_t db = smem_desc(sVa + s * C::KV_STAGE + ks * 2048, C::KV_CHUNK, 1024, kLayoutSW128);
-            mma_f16_ts(tmem + 256 * i + C::O_COL, tmem + 256 * i + C::P_COL + ks * 8, db, idesc_pv,
-                       (j > 0 || ks > 0) ? 1u : 0u);
-          }
+          for (int ks = 0; ks < C::BK / 16; ++ks)
+            mma_f16_ts(dO, aP + ks * 8, dVs + (uint64_t)(ks * (2048 >> 4)), idesc_pv, (j > 0 || ks > 0) ? 1u : 0u);
           tc_commit(&bar->o_done[i]);
           if (j + 1 < nblk) issue_s(i, s1);
         }
@@ -243,10 +250,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int e = 0; e < C::BK; ++e)
           if (e >= klim) sv[e] = __float_as_uint(-INFINITY);
       }
-      float mx = __uint_as_float(sv[0]);
+      // Row maximum with four independent chains (a single chain of BK dependent
+      // max operations would leave the two softmax warps of each sub-partition
+      // waiting on latency).
+      float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-      for (int e = 1; e + 1 < C::BK; e += 2) mx = fmax3(mx, __uint_as_float(sv[e]), __uint_as_float(sv[e + 1]));
-      mx = fmaxf(mx, __uint_as_float(sv[C::BK - 1]));
+      for (int e = 0; e < C::BK; e += 8) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          mq[u] = fmax3(mq[u], __uint_as_float(sv[e + 2 * u]), __uint_as_float(sv[e + 2 * u + 1]));
+      }
+      const float mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
       // Running maximum in the scaled log2 domain.  The maximum used for the
       // exponentials (m_run) only moves when a row's maximum grows by more than
       // kRescaleLog2; until then P may reach 2^kRescaleLog2 (exact in the 16-bit
@@ -256,7 +270,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float m_new = grow ? m_blk : m_run;
       const float alpha = grow ? ex2_approx(m_run - m_new) : 1.0f;
       const uint64_t negm = f2_pack(-m_new, -m_new);
-      uint64_t acc = f2_pack(0.f, 0.f);
+      uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};  // four independent packed row-sum chains
 #pragma unroll
       for (int c = 0; c < C::BK / 32; ++c) {
         uint32_t pk[16];
@@ -272,7 +286,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             f2_unpack(xx, x0, x1);
             pp = f2_pack(ex2_approx(x0), ex2_approx(x1));
           }
-          acc = f2_add(acc, pp);
+          acc[e & 3] = f2_add(acc[e & 3], pp);
           float p0, p1;
           f2_unpack(pp, p0, p1);
           pk[e] = Cvt<T>::pack2(p0, p1);
@@ -298,9 +312,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_st32(tO + oc * 32, r);
         }
       }
-      float a0, a1;
-      f2_unpack(acc, a0, a1);
-      l_run = l_run * alpha + (a0 + a1);
+      float a0, a1, a2, a3;
+      f2_unpack(f2_add(acc[0], acc[1]), a0, a1);
+      f2_unpack(f2_add(acc[2], acc[3]), a2, a3);
+      l_run = l_run * alpha + ((a0 + a1) + (a2 + a3));
       m_run = m_new;
       tmem_wait_st();
       tc_fence_before();

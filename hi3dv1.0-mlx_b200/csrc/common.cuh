@@ -18,21 +18,16 @@
 #include <stdint.h>
 
 #include "hi3d_b200.h"
+#include "status.h"
 
 namespace hi3d {
 
 // ---------------------------------------------------------------------------
-// device error word (one per library instance, zeroed by the host)
+// device error word: one per translation unit (no relocatable device code is
+// needed); each unit registers a host reader with the library at load time and
+// hi3d_device_status() merges them.
 // ---------------------------------------------------------------------------
-struct DeviceStatus {
-  int code;      // first error code seen (HI3D_ERR_*), 0 if none
-  int where;     // kernel-specific site id
-  int block;     // blockIdx.x of the reporting CTA
-  int detail;    // extra info (phase, index)
-};
-
-// Defined in abi.cu; every kernel that can time out reports here.
-extern __device__ DeviceStatus g_status;
+static __device__ DeviceStatus g_status;
 
 __device__ __forceinline__ void report_error(int code, int where, int detail) {
   if (atomicCAS(&g_status.code, 0, code) == 0) {
@@ -41,6 +36,22 @@ __device__ __forceinline__ void report_error(int code, int where, int detail) {
     g_status.detail = detail;
   }
 }
+
+namespace {
+// Copies this unit's status word to `out` (and clears it when `reset`).
+cudaError_t read_unit_status(DeviceStatus* out, bool reset) {
+  cudaError_t e = cudaMemcpyFromSymbol(out, g_status, sizeof(DeviceStatus));
+  if (e == cudaSuccess && reset) {
+    const DeviceStatus zero = {0, 0, 0, 0};
+    e = cudaMemcpyToSymbol(g_status, &zero, sizeof(DeviceStatus));
+  }
+  return e;
+}
+struct UnitStatusRegistrar {
+  UnitStatusRegistrar() { register_status_reader(&read_unit_status); }
+};
+const UnitStatusRegistrar unit_status_registrar;
+}  // namespace
 
 // Every bounded wait gives up after kWaitNs of wall time (read from the
 // %globaltimer nanosecond clock), far above any legal wait in these kernels

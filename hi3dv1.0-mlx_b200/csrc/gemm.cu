@@ -44,6 +44,7 @@ struct Params {
   int64_t rows_per_batch, gate_stride;
   int M, N, K;        // K in elements
   int tiles_m, tiles_n;
+  int vec;            // 1 when output rows (and gate rows) allow 16-byte accesses
 };
 
 struct Barriers {
@@ -186,7 +187,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (n >= p.N) break;
           if constexpr (std::is_same<OutT, int32_t>::value) {
             // raw exact int32 accumulators (verification / custom dequantisation)
-            if (n + 8 <= p.N) {
+            if (p.vec && n + 8 <= p.N) {
               *reinterpret_cast<uint4*>(orow + n) = make_uint4(v[e], v[e + 1], v[e + 2], v[e + 3]);
               *reinterpret_cast<uint4*>(orow + n + 4) = make_uint4(v[e + 4], v[e + 5], v[e + 6], v[e + 7]);
             } else {
@@ -209,7 +210,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (EPI == EPI_GELU) y[q] = gelu_tanh_f<OutT>(y[q]);
           }
           if (EPI == EPI_RESIDUAL) {
-            if (n + 8 <= p.N) {
+            if (p.vec && n + 8 <= p.N) {
               uint4 xv = *reinterpret_cast<const uint4*>(orow + n);
               uint4 gv = grow ? *reinterpret_cast<const uint4*>(grow + n) : make_uint4(0, 0, 0, 0);
               const OutT* xa = reinterpret_cast<const OutT*>(&xv);
@@ -228,7 +229,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
             }
           }
-          if (n + 8 <= p.N) {
+          if (p.vec && n + 8 <= p.N) {
             uint4 w;
             w.x = Cvt<OutT>::pack2(y[0], y[1]);
             w.y = Cvt<OutT>::pack2(y[2], y[3]);
@@ -282,6 +283,11 @@ static int launch_gemm(const void* a, const void* w, int M, int N, int K, const 
   if ((rc = encode_tmap(&ma, t, 2, a, da, sa, ba, CU_TENSOR_MAP_SWIZZLE_128B))) return rc;
   if ((rc = encode_tmap(&mb, t, 2, w, db, sb, bb, CU_TENSOR_MAP_SWIZZLE_128B))) return rc;
   Params p = prm;
+  const int out_esz = std::is_same<OutT, int32_t>::value ? 4 : 2;
+  p.vec = ((p.ldo * out_esz) % 16 == 0 && (reinterpret_cast<uintptr_t>(p.out) & 15) == 0 &&
+           (!p.gate || ((p.gate_stride * 2) % 16 == 0 && (reinterpret_cast<uintptr_t>(p.gate) & 15) == 0)))
+              ? 1
+              : 0;
   p.M = M;
   p.N = N;
   p.K = K;
@@ -313,12 +319,11 @@ static int check_common(const char* what, const void* a, const void* w, const vo
   if (m < 0 || n <= 0 || k <= 0 || m > 0x7fffffff || n > 0x7fffffff || k > 0x7fffffff)
     return set_error(HI3D_ERR_INVALID_ARGUMENT, "%s: bad sizes m=%lld n=%lld k=%lld", what, (long long)m,
                      (long long)n, (long long)k);
-  if (ldo < n || ldo % 4 || !aligned16(a) || !aligned16(w) || !aligned16(out))
-    return set_error(HI3D_ERR_INVALID_ARGUMENT, "%s: ldo must be >= n and 16-byte rows; pointers 16-byte aligned", what);
+  if (ldo < n || !aligned16(a) || !aligned16(w))
+    return set_error(HI3D_ERR_INVALID_ARGUMENT, "%s: ldo must be >= n; A and W 16-byte aligned", what);
   if (epi < 0 || epi > 2) return set_error(HI3D_ERR_INVALID_ARGUMENT, "%s: unknown epilogue %d", what, epi);
-  if (gate && (epi != gemm::EPI_RESIDUAL || rows_per_batch <= 0 || gate_stride % 8 || !aligned16(gate)))
-    return set_error(HI3D_ERR_INVALID_ARGUMENT, "%s: gate needs the residual epilogue, rows_per_batch > 0, aligned",
-                     what);
+  if (gate && (epi != gemm::EPI_RESIDUAL || rows_per_batch <= 0))
+    return set_error(HI3D_ERR_INVALID_ARGUMENT, "%s: gate needs the residual epilogue and rows_per_batch > 0", what);
   return HI3D_OK;
 }
 
@@ -335,8 +340,7 @@ extern "C" int hi3d_gemm_w8a8(const int8_t* a, const int8_t* w, const float* sa,
   if ((!sa || !sw) && out_dtype != HI3D_I32)
     return set_error(HI3D_ERR_INVALID_ARGUMENT, "gemm_w8a8: activation and weight scales are required");
   if (k % 16) return set_error(HI3D_ERR_INVALID_ARGUMENT, "gemm_w8a8: K must be a multiple of 16");
-  if (out_dtype != HI3D_I32 && ldo % 8)
-    return set_error(HI3D_ERR_INVALID_ARGUMENT, "gemm_w8a8: ldo must be a multiple of 8 for 16-bit outputs");
+
   if (m == 0) return HI3D_OK;
   gemm::Params p = {};
   p.out = out;
@@ -366,7 +370,7 @@ extern "C" int hi3d_gemm(const void* a, const void* w, const void* bias, void* o
   int rc = check_common("gemm", a, w, out, m, n, k, ldo, epilogue, gate, rows_per_batch, gate_stride);
   if (rc) return rc;
   if (k % 8) return set_error(HI3D_ERR_INVALID_ARGUMENT, "gemm: K must be a multiple of 8");
-  if (ldo % 8) return set_error(HI3D_ERR_INVALID_ARGUMENT, "gemm: ldo must be a multiple of 8");
+
   if (m == 0) return HI3D_OK;
   gemm::Params p = {};
   p.out = out;

@@ -8,12 +8,14 @@ GPU run can never silently take another code path.
 from __future__ import annotations
 
 import ctypes
+import os
 import threading
 from pathlib import Path
 
 import torch
 
-LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libhi3d_b200.so"
+# HI3D_B200_LIB selects another build of the same library (e.g. a tuning variant).
+LIB_PATH = Path(os.environ.get("HI3D_B200_LIB", Path(__file__).resolve().parent / "_lib" / "libhi3d_b200.so"))
 
 OK = 0
 ERR_INVALID_ARGUMENT = 1
