@@ -157,6 +157,44 @@ HI3D_API int hi3d_gemm_w8a8(const int8_t* a, const int8_t* w, const float* sa, c
 HI3D_API int hi3d_quantize_act_i8(const void* x, const float* multiplier, int8_t* q, float* scale, int64_t rows,
                                   int64_t k, int rotate, int dtype, void* stream);
 
+/* ---- sparse voxel structure and convolution ------------------------------ */
+/* Bytes of workspace hi3d_neighbour_map_build needs for n voxels (hash table). */
+HI3D_API int hi3d_neighbour_map_workspace_size(int64_t n, int64_t* bytes);
+
+/* Replaces sparse.neighbour_table (src/hi3d_mac/mlx_backend/sparse.py:29-43; OFFSETS :20) and the
+ * pair search of the spconv shim (src/hi3d_mac/torch_backend/sparse_conv.py:115-149).
+ * coords [n, 3] int32 (x, y, z) in [0, 2^21); query [nq, 3] (NULL = coords, nq ignored);
+ * table [nq, 27] int32: table[o, k] = row of coords equal to query[o] * stride + d_k, or n
+ * when absent, d_k = (k / 9 - 1, k / 3 % 3 - 1, k % 3 - 1).  stride 1 (submanifold) or 2
+ * (query = downsampled coordinates).  Duplicate coordinates resolve to the last row. */
+HI3D_API int hi3d_neighbour_map_build(const int32_t* coords, int64_t n, const int32_t* query, int64_t nq,
+                                      int stride, int32_t* table, void* workspace, int64_t workspace_bytes,
+                                      void* stream);
+
+/* Bytes of workspace hi3d_downsample_structure needs for n voxels. */
+HI3D_API int hi3d_downsample_workspace_size(int64_t n, int64_t* bytes);
+
+/* Replaces sparse.downsample_structure (src/hi3d_mac/mlx_backend/sparse.py:217-233): unique
+ * coords // 2 in lexicographic (x, y, z) order -> low [num_low, 3], inverse [n] (parent of each
+ * row), counts [num_low] (children per parent); *num_low (device int32) receives the count.
+ * low and counts must hold n rows.  Validates the coordinates with one stream synchronisation. */
+HI3D_API int hi3d_downsample_structure(const int32_t* coords, int64_t n, int32_t* low, int32_t* inverse,
+                                       int32_t* counts, int32_t* num_low, void* workspace, int64_t workspace_bytes,
+                                       void* stream);
+
+/* 27-bit mask per 128-row output tile of the taps with at least one present neighbour
+ * (tap_mask [ceil(n_out / 128)]); hi3d_sparse_conv skips the others. */
+HI3D_API int hi3d_conv_tap_mask(const int32_t* table, int64_t n_out, int64_t n_in, uint32_t* tap_mask, void* stream);
+
+/* Replaces sparse.sparse_conv (src/hi3d_mac/mlx_backend/sparse.py:191-214) and the upstream
+ * SubMConv3d (src/sparc3d/ops/sparse_backend.py:130-148): out[o] = bias + sum_k x[table[o, k]] W_k^T
+ * (rows equal to n_in contribute zero), fp32 accumulation, output rounded once.
+ * x [n_in, cin]; table [n_out, 27] from hi3d_neighbour_map_build; weight [cout, 27, cin]
+ * (spconv's (out, 3, 3, 3, in) layout); bias [cout] or NULL; out [n_out, cout]; cin, cout % 8 == 0. */
+HI3D_API int hi3d_sparse_conv(const void* x, const int32_t* table, const uint32_t* tap_mask, const void* weight,
+                              const void* bias, void* out, int64_t n_in, int64_t n_out, int cin, int cout, int dtype,
+                              void* stream);
+
 /* ---- elementwise epilogues of the block --------------------------------- */
 /* x <- x + y * gate (all in the I/O type, two roundings: round(y*gate), then round(x + .)).
  * Replaces the residual/gate expressions at src/hi3d_mac/mlx_backend/transformer.py:570,588
