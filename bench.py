@@ -1,7 +1,7 @@
 """Benchmark of the sparse-DiT refinement torso on B200 (BASELINE configs[1] by default).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload stack|stack_w8a8|attention|attention262k]
+                    [--workload stack|stack_w8a8|attention|attention262k|conv]
 
 One step = one forward of the 24-block stack (C=1024, 16 heads x 64, GELU MLP 4x,
 1370 condition tokens) over T=32,768 voxel tokens of one object in fp16, inputs
@@ -482,13 +482,89 @@ def run_attention(args, big: bool) -> None:
         dist.destroy_process_group()
 
 
+def run_conv(args) -> None:
+    """cfg5: submanifold 3x3x3 conv, 200,000 shell voxels in 128^3, C_in = C_out = 256, fp16.
+    A step = one convolution over all voxels (the neighbour map is built once per level, as in
+    the reference, and timed separately).  Reports TFLOP/s over the actual neighbour pairs
+    (2 * Cin * Cout per present pair); the dense-equivalent count is in the config."""
+    import torch
+
+    from hi3d_b200 import _lib, sparse, synthetic
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    _lib.load()
+    n, c = 200_000, 256
+    coords = synthetic.shell_coords(n, 128, 48, 4, seed=5)
+    g = torch.Generator(device=dev).manual_seed(3)
+    x = torch.randn((n, c), generator=g, device=dev).half()
+    w = (torch.randn((c, 3, 3, 3, c), generator=g, device=dev) * 0.02).half()
+    b = (torch.randn(c, generator=g, device=dev) * 0.02).half()
+    cdev = torch.from_numpy(coords).to(dev)
+    for _ in range(3):
+        level = sparse.Level(cdev, sparse.neighbour_table(cdev))
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        table = sparse.neighbour_table(cdev)
+    e1.record()
+    torch.cuda.synchronize()
+    map_ms = e0.elapsed_time(e1) / args.steps
+    mask = level.tap_mask
+    pairs = int((level.table < n).sum().item())
+    step = lambda: sparse.conv(x, level.table, w, b, tap_mask=mask)
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    _lib.LAUNCHES[0] = 0
+    with ClockSampler(0) as clocks:
+        e0.record()
+        for _ in range(args.steps):
+            step()
+        e1.record()
+        torch.cuda.synchronize()
+    launches = _lib.LAUNCHES[0]
+    ms = e0.elapsed_time(e1) / args.steps
+    flops = 2.0 * c * c * pairs
+    dense_flops = 2.0 * 27 * n * c * c
+    peaks = _peaks()
+    hx = x.cpu().pin_memory()
+    hout = torch.empty((n, c), dtype=torch.float16).pin_memory()
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(args.steps):
+        hout.copy_(sparse.conv(hx.to(dev, non_blocking=True), level.table, w, b, tap_mask=mask), non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    line = {
+        "metric": "sparse_conv_tflops", "value": flops / (ms / 1e3) / 1e12, "unit": "TFLOP/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "none",
+        "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": {"workload": f"cfg5: submanifold 3x3x3 conv, {n} shell voxels in 128^3, {c}->{c} channels, fp16",
+                   "pairs": pairs, "dense_equivalent_tflops": dense_flops / (ms / 1e3) / 1e12,
+                   "neighbour_map_ms": map_ms, "lookups_per_s": 27 * n / (map_ms / 1e3),
+                   "l2": "inputs larger than L2 (102 MB features + 102 MB output)"},
+        "roofline": {"bound": "tensor", "achieved": flops / (ms / 1e3) / 1e12, "peak": peaks["bf16_tflops"],
+                     "unit": "TFLOP/s", "frac": flops / (ms / 1e3) / 1e12 / peaks["bf16_tflops"],
+                     "traffic": _profile_traffic("sparse_conv_cfg5"),
+                     "peak_source": f"{peaks['source']} bf16_tflops (burst)"},
+        "e2e": {"value": flops / (e2e_ms / 1e3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": n * c * 2,
+                "d2h_bytes_per_step": n * c * 2},
+        "gpu_launches": launches, "clocks": clocks.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["stack", "stack_w8a8", "attention", "attention262k"], default="stack")
+    ap.add_argument("--workload", choices=["stack", "stack_w8a8", "attention", "attention262k", "conv"],
+                    default="stack")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -496,6 +572,8 @@ def main() -> None:
         run_reference(args)
     elif args.workload in ("stack", "stack_w8a8"):
         run_ours(args)
+    elif args.workload == "conv":
+        run_conv(args)
     else:
         run_attention(args, big=args.workload == "attention262k")
 

@@ -410,8 +410,10 @@ extern "C" int hi3d_neighbour_map_workspace_size(int64_t n, int64_t* bytes) {
 extern "C" int hi3d_neighbour_map_build(const int32_t* coords, int64_t n, const int32_t* query, int64_t nq,
                                         int stride, int32_t* table, void* workspace, int64_t workspace_bytes,
                                         void* stream) {
-  if (!coords || !table || !workspace || n < 0 || nq < 0 || (stride != 1 && stride != 2))
+  if (n < 0 || nq < 0 || (stride != 1 && stride != 2) || (n > 0 && !coords) || !workspace)
     return set_error(HI3D_ERR_INVALID_ARGUMENT, "neighbour_map: bad arguments");
+  if ((query ? nq : n) == 0) return HI3D_OK;
+  if (!table) return set_error(HI3D_ERR_INVALID_ARGUMENT, "neighbour_map: null table");
   int64_t need = 0;
   int rc = hi3d_neighbour_map_workspace_size(n, &need);
   if (rc) return rc;
@@ -456,7 +458,7 @@ extern "C" int hi3d_downsample_workspace_size(int64_t n, int64_t* bytes) {
 extern "C" int hi3d_downsample_structure(const int32_t* coords, int64_t n, int32_t* low, int32_t* inverse,
                                          int32_t* counts, int32_t* num_low, void* workspace, int64_t workspace_bytes,
                                          void* stream) {
-  if (!coords || !low || !inverse || !counts || !num_low || !workspace || n < 0)
+  if (n < 0 || !num_low || !workspace || (n > 0 && (!coords || !low || !inverse || !counts)))
     return set_error(HI3D_ERR_INVALID_ARGUMENT, "downsample_structure: bad arguments");
   int64_t need = 0;
   int rc = hi3d_downsample_workspace_size(n, &need);
