@@ -1,7 +1,7 @@
 """Benchmark of the sparse-DiT refinement torso on B200 (BASELINE configs[1] by default).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload stack|stack_w8a8|attention|attention262k|conv]
+                    [--workload stack|stack_w8a8|block|attention|attention262k|conv]
 
 One step = one forward of the 24-block stack (C=1024, 16 heads x 64, GELU MLP 4x,
 1370 condition tokens) over T=32,768 voxel tokens of one object in fp16, inputs
@@ -131,16 +131,16 @@ def make_inputs(seed: int = 0):
     return coords, cos, sin, x, mod, cond
 
 
-def device_weights(device, seed: int = 100) -> list[dict]:
-    """24 blocks of N(0, 0.02) fp16 weights generated on the device (seeded)."""
+def device_weights(device, seed: int = 100, blocks: int = BLOCKS) -> list[dict]:
+    """``blocks`` blocks of N(0, 0.02) fp16 weights generated on the device (seeded)."""
     import torch
 
     from hi3d_b200.synthetic import BLOCK_LINEARS
 
     g = torch.Generator(device=device).manual_seed(seed)
     c, d = CHANNELS, CHANNELS // HEADS
-    blocks = []
-    for _ in range(BLOCKS):
+    out = []
+    for _ in range(blocks):
         w = {}
         for name, i_mult, o_mult in BLOCK_LINEARS:
             w[f"{name}.weight"] = (torch.randn((o_mult * c, i_mult * c), generator=g, device=device) * 0.02).half()
@@ -152,8 +152,8 @@ def device_weights(device, seed: int = 100) -> list[dict]:
         w["norm2.bias"] = torch.zeros(c, device=device)
         w["self_attn.q_rms_norm.gamma"] = torch.ones((HEADS, d), device=device)
         w["self_attn.k_rms_norm.gamma"] = torch.ones((HEADS, d), device=device)
-        blocks.append(w)
-    return blocks
+        out.append(w)
+    return out
 
 
 # ----------------------------------------------------------------------------- CPU baseline
@@ -199,7 +199,7 @@ def run_reference(args) -> None:
     if rank != 0:
         return
     cores = os.cpu_count()
-    if args.workload == "stack":
+    if args.workload in ("stack", "stack_w8a8", "block"):
         sample = 512
         secs = []
         for i in range(args.warmup + args.steps):
@@ -258,7 +258,8 @@ def run_ours(args) -> None:
         raise ValueError("T must divide by the number of GPUs")
     tl = T_TOKENS // world
     rows = slice(rank * tl, (rank + 1) * tl)
-    weights = device_weights(dev)
+    nblocks = 1 if args.workload == "block" else BLOCKS
+    weights = device_weights(dev, blocks=nblocks)
     if args.workload == "stack_w8a8":
         weights = [transformer.to_w8a8(w) for w in weights]
     x_host = torch.from_numpy(x[rows]).pin_memory()
@@ -305,7 +306,7 @@ def run_ours(args) -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     ms_per_step = ms / args.steps
-    value = BLOCKS * T_TOKENS / (ms_per_step / 1e3)
+    value = nblocks * T_TOKENS / (ms_per_step / 1e3)
 
     # ---- end to end through the public API: pinned host input -> stack -> host output
     out_host = torch.empty_like(x_host).pin_memory()
@@ -324,7 +325,7 @@ def run_ours(args) -> None:
         t = torch.tensor([e2e_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
-    e2e_value = BLOCKS * T_TOKENS / (e2e_ms / args.steps / 1e3)
+    e2e_value = nblocks * T_TOKENS / (e2e_ms / args.steps / 1e3)
 
     # ---- roofline of the dominant kernel (self-attention)
     peaks = _peaks()
@@ -347,9 +348,9 @@ def run_ours(args) -> None:
                                 f"weights, int32 accumulate, fp16 dequant), T={T_TOKENS}, C={CHANNELS}, "
                                 f"{HEADS}x{CHANNELS // HEADS} heads, {COND} cond tokens"
                                 if args.workload == "stack_w8a8" else
-                                f"cfg1: {BLOCKS}-block sparse-DiT stack fwd, T={T_TOKENS} shell tokens in {GRID}^3, "
+                                f"cfg1: {nblocks}-block sparse-DiT stack fwd, T={T_TOKENS} shell tokens in {GRID}^3, "
                                 f"C={CHANNELS}, {HEADS}x{CHANNELS // HEADS} heads, {COND} cond tokens, fp16"),
-                   "blocks": BLOCKS, "tokens": T_TOKENS, "parallelism": f"query-sharded x{world}" if world > 1 else "none",
+                   "blocks": nblocks, "tokens": T_TOKENS, "parallelism": f"query-sharded x{world}" if world > 1 else "none",
                    "l2": "inputs larger than L2 (705 MB of weights + activations per step)"},
         "roofline": roofline,
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": x_host.numel() * 2,
@@ -563,14 +564,14 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["stack", "stack_w8a8", "attention", "attention262k", "conv"],
+    ap.add_argument("--workload", choices=["stack", "stack_w8a8", "block", "attention", "attention262k", "conv"],
                     default="stack")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
-    elif args.workload in ("stack", "stack_w8a8"):
+    elif args.workload in ("stack", "stack_w8a8", "block"):
         run_ours(args)
     elif args.workload == "conv":
         run_conv(args)
