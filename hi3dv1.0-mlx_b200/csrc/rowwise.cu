@@ -93,13 +93,20 @@ __global__ void __launch_bounds__(256) ln_mod_kernel(const T* __restrict__ x, T*
       sc = *reinterpret_cast<const Vec8*>(scale + mb + base);
       sh = *reinterpret_cast<const Vec8*>(shift + mb + base);
     }
+    float wv[8], bv[8];
+    if (AFFINE) {
+      *reinterpret_cast<float4*>(&wv[0]) = *reinterpret_cast<const float4*>(weight + base);
+      *reinterpret_cast<float4*>(&wv[4]) = *reinterpret_cast<const float4*>(weight + base + 4);
+      *reinterpret_cast<float4*>(&bv[0]) = *reinterpret_cast<const float4*>(bias + base);
+      *reinterpret_cast<float4*>(&bv[4]) = *reinterpret_cast<const float4*>(bias + base + 4);
+    }
 #pragma unroll
     for (int i = 0; i < 8; i += 2) {
       float y0 = __fmul_rn(__fsub_rn(v[c][i], mean), inv);
       float y1 = __fmul_rn(__fsub_rn(v[c][i + 1], mean), inv);
       if (AFFINE) {
-        y0 = __fadd_rn(__fmul_rn(y0, weight[base + i]), bias[base + i]);
-        y1 = __fadd_rn(__fmul_rn(y1, weight[base + i + 1]), bias[base + i + 1]);
+        y0 = __fadd_rn(__fmul_rn(y0, wv[i]), bv[i]);
+        y1 = __fadd_rn(__fmul_rn(y1, wv[i + 1]), bv[i + 1]);
       }
       T h0 = round_t<T>(y0), h1 = round_t<T>(y1);
       if (MODULATE) {
@@ -174,72 +181,80 @@ static int dispatch_ln(const void* x, void* out, int64_t rows, int C, float eps,
 // nrm = max(sqrt(sum re^2 + im^2), 1e-12); y = re / nrm * g * sqrt(D).
 // ---------------------------------------------------------------------------
 template <typename T, int D>
-__global__ void __launch_bounds__(256) qkv_rope_rms_kernel(const T* __restrict__ qkv, const float* __restrict__ cosv,
-                                                           const float* __restrict__ sinv,
-                                                           const float* __restrict__ gq,
-                                                           const float* __restrict__ gk, T* __restrict__ q,
-                                                           T* __restrict__ k, T* __restrict__ v, int64_t M,
-                                                           int64_t N, int H, int token_major) {
+__global__ void __launch_bounds__(1024) qkv_rope_rms_kernel(const T* __restrict__ qkv, const float* __restrict__ cosv,
+                                                            const float* __restrict__ sinv,
+                                                            const float* __restrict__ gq,
+                                                            const float* __restrict__ gk, T* __restrict__ q,
+                                                            T* __restrict__ k, T* __restrict__ v, int N, int H,
+                                                            int token_major) {
   constexpr int ACTIVE = D / 8;
   constexpr int G = ACTIVE <= 8 ? 8 : (ACTIVE <= 16 ? 16 : 32);
-  constexpr int GROUPS_PER_WARP = 32 / G;
   const int lane = threadIdx.x & 31;
   const int sub = lane % G;
-  const int64_t unit = ((int64_t)blockIdx.x * 8 + (threadIdx.x >> 5)) * GROUPS_PER_WARP + lane / G;
-  const int64_t total = M * 3 * H;
-  // No early exit before the group reduction: every lane of the warp takes part
-  // in the full-mask shuffles, inactive lanes contribute zero.
-  const bool in_range = unit < total;
-  const bool valid = in_range && sub < ACTIVE;
-  const int64_t m = in_range ? unit / (3 * H) : 0;
-  const int ph = in_range ? (int)(unit % (3 * H)) : 0;
-  const int part = ph / H, h = ph % H;
-  const int64_t b = m / N, n = m % N;
-  const T* src = qkv + ((m * 3 + part) * (int64_t)H + h) * D;  // kernels.py:31
-  const int64_t dst_off = token_major ? ((b * N + n) * H + h) * D : ((b * H + h) * N + n) * D;
-  const int c0 = sub * 8;
-  Vec8 raw = {};
-  if (valid) raw = *reinterpret_cast<const Vec8*>(src + c0);
-  float x[8];
-  unpack8<T>(raw, x);
-  float r[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-  float ss = 0.f;
-  if (valid && part != 2) {
-    const float* cs = cosv + n * (D / 2) + c0 / 2;
-    const float* sn = sinv + n * (D / 2) + c0 / 2;
+  const int m = blockIdx.x;  // token row of the [B*N, 3*H*D] projection
+  const int b = m / N, n = m - b * N;
+  const int units = 3 * H;
+  const int per_block = (int)(blockDim.x / G);
+  const T* row = qkv + (int64_t)m * units * D;
+  const float* cs_row = cosv + (int64_t)n * (D / 2);
+  const float* sn_row = sinv + (int64_t)n * (D / 2);
+  // The loop bound is uniform across the block, so every lane reaches every
+  // full-mask shuffle; lanes past the last unit contribute zero.
+  for (int u0 = 0; u0 < units; u0 += per_block) {
+    const int u = u0 + (int)(threadIdx.x / G);
+    const bool in_range = u < units;
+    const bool valid = in_range && sub < ACTIVE;
+    const int part = in_range ? u / H : 0, h = in_range ? u - (u / H) * H : 0;
+    const int c0 = sub * 8;
+    Vec8 raw = {};
+    if (valid) raw = *reinterpret_cast<const Vec8*>(row + (int64_t)u * D + c0);  // ((m*3+part)*H+h)*D, kernels.py:31
+    float x[8];
+    unpack8<T>(raw, x);
+    float r[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    float ss = 0.f;
+    if (valid && part != 2) {
+      const float4 c4 = *reinterpret_cast<const float4*>(cs_row + c0 / 2);
+      const float4 s4 = *reinterpret_cast<const float4*>(sn_row + c0 / 2);
+      const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, sv[4] = {s4.x, s4.y, s4.z, s4.w};
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float c = cs[i], s = sn[i];
-      r[2 * i] = x[2 * i] * c - x[2 * i + 1] * s;
-      r[2 * i + 1] = x[2 * i] * s + x[2 * i + 1] * c;
-      ss += r[2 * i] * r[2 * i] + r[2 * i + 1] * r[2 * i + 1];
+      for (int i = 0; i < 4; ++i) {
+        r[2 * i] = x[2 * i] * cc[i] - x[2 * i + 1] * sv[i];
+        r[2 * i + 1] = x[2 * i] * sv[i] + x[2 * i + 1] * cc[i];
+        ss += r[2 * i] * r[2 * i] + r[2 * i + 1] * r[2 * i + 1];
+      }
     }
-  }
 #pragma unroll
-  for (int o = G / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-  if (!valid) return;
-  if (part == 2) {
-    *reinterpret_cast<Vec8*>(v + dst_off + c0) = raw;
-    return;
-  }
-  const float nrm = fmaxf(sqrtf(ss), 1e-12f);
-  const float scale = sqrtf((float)D);
-  const float* g = (part == 0 ? gq : gk) + h * D + c0;
-  Vec8 o;
+    for (int o = G / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (!valid) continue;
+    const int64_t dst_off = token_major ? (((int64_t)b * N + n) * H + h) * D : (((int64_t)b * H + h) * N + n) * D;
+    if (part == 2) {
+      *reinterpret_cast<Vec8*>(v + dst_off + c0) = raw;
+      continue;
+    }
+    const float nrm = fmaxf(sqrtf(ss), 1e-12f);
+    const float scale = sqrtf((float)D);
+    const float* g = (part == 0 ? gq : gk) + h * D + c0;
+    const float4 g0 = *reinterpret_cast<const float4*>(g), g1 = *reinterpret_cast<const float4*>(g + 4);
+    const float gg[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+    Vec8 o;
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
-    o.w[i] = Cvt<T>::pack2(r[2 * i] / nrm * g[2 * i] * scale, r[2 * i + 1] / nrm * g[2 * i + 1] * scale);
-  *reinterpret_cast<Vec8*>((part == 0 ? q : k) + dst_off + c0) = o;
+    for (int i = 0; i < 4; ++i)
+      o.w[i] = Cvt<T>::pack2(r[2 * i] / nrm * gg[2 * i] * scale, r[2 * i + 1] / nrm * gg[2 * i + 1] * scale);
+    *reinterpret_cast<Vec8*>((part == 0 ? q : k) + dst_off + c0) = o;
+  }
 }
 
 template <typename T>
 static int dispatch_rope(const void* qkv, const float* c, const float* s, const float* gq, const float* gk, void* q,
                          void* k, void* v, int64_t M, int64_t N, int H, int D, int tm, cudaStream_t st) {
-  const int64_t units = M * 3 * H;
-  auto grid_for = [&](int G) { return (unsigned)(((units + (32 / G) - 1) / (32 / G) + 7) / 8); };
-#define HI3D_ROPE(DD, GG)                                                                                            \
-  qkv_rope_rms_kernel<T, DD><<<grid_for(GG), 256, 0, st>>>((const T*)qkv, c, s, gq, gk, (T*)q, (T*)k, (T*)v, M, N, \
-                                                           H, tm)
+  if (M > 0x7fffffff || N > 0x7fffffff) return set_error(HI3D_ERR_INVALID_ARGUMENT, "qkv_rope_rms: too many rows");
+  auto threads_for = [&](int G) {
+    const int t = ((3 * H * G + 31) / 32) * 32;
+    return t > 1024 ? 1024 : t;
+  };
+#define HI3D_ROPE(DD, GG)                                                                                   \
+  qkv_rope_rms_kernel<T, DD><<<(unsigned)M, threads_for(GG), 0, st>>>((const T*)qkv, c, s, gq, gk, (T*)q, (T*)k, \
+                                                                      (T*)v, (int)N, H, tm)
   switch (D) {
     case 32: HI3D_ROPE(32, 8); break;
     case 64: HI3D_ROPE(64, 8); break;
