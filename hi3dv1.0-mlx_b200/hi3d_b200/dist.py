@@ -18,6 +18,24 @@ from . import attention, kernels
 from .transformer import _modulation, linear
 
 
+def shard_slice(total: int, rank: int, world: int) -> slice:
+    """Contiguous query-row slice of ``rank``: the rows ``[rank * total / world, ...)``."""
+    if total % world:
+        raise ValueError(f"{total} rows do not split evenly over {world} ranks")
+    per = total // world
+    return slice(rank * per, (rank + 1) * per)
+
+
+def gather_rows(local: torch.Tensor, group=None, out: torch.Tensor | None = None, async_op: bool = False):
+    """All-gather equal row shards ``[rows, ...]`` of every rank into ``[world * rows, ...]`` in rank
+    order (NCCL over NVLink for CUDA tensors, gloo for CPU tensors)."""
+    world = dist.get_world_size(group)
+    if out is None:
+        out = torch.empty((world * local.shape[0], *local.shape[1:]), dtype=local.dtype, device=local.device)
+    work = dist.all_gather_into_tensor(out, local.contiguous(), group=group, async_op=async_op)
+    return (out, work) if async_op else out
+
+
 def block_forward_sharded(w: dict, x: torch.Tensor, mod: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
                           ck: torch.Tensor, cv: torch.Tensor, heads: int, group=None,
                           kv_buffers: tuple[torch.Tensor, torch.Tensor] | None = None) -> torch.Tensor:
@@ -36,8 +54,8 @@ def block_forward_sharded(w: dict, x: torch.Tensor, mod: torch.Tensor, cos: torc
     if kv_buffers is None:
         kv_buffers = tuple(torch.empty((world * t_local, heads, d), dtype=dt, device=x.device) for _ in range(2))
     k_all, v_all = kv_buffers
-    hk = dist.all_gather_into_tensor(k_all, k[0], group=group, async_op=True)
-    hv = dist.all_gather_into_tensor(v_all, v[0], group=group, async_op=True)
+    _, hk = gather_rows(k[0], group, out=k_all, async_op=True)
+    _, hv = gather_rows(v[0], group, out=v_all, async_op=True)
     hk.wait()
     hv.wait()
     a = attention.flash_attention(q, k_all.permute(1, 0, 2)[None], v_all.permute(1, 0, 2)[None], scale,

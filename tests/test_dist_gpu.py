@@ -1,0 +1,69 @@
+"""Query-sharded block stack on 2 GPUs (NCCL) vs the single-GPU stack.
+
+Every row-wise kernel computes a row independently of the others and each query row's
+attention reads the same K/V blocks in the same order, so the sharded result must be
+bit-identical to the unsharded one.  Needs two GPUs (``gpurun --gpus 2``); skipped otherwise.
+"""
+
+from __future__ import annotations
+
+import datetime
+import os
+import socket
+import sys
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, result_path):
+    sys.path.insert(0, os.path.join(REPO, "hi3dv1.0-mlx_b200"))
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    from hi3d_b200 import dist as hdist
+    from hi3d_b200 import synthetic, transformer
+
+    t, c, heads, L = 2048, 256, 4, 77
+    coords = synthetic.shell_coords(t, 32, 10, 3, seed=1)
+    cos, sin = transformer.rope_tables(coords, c // heads)
+    ws = [transformer.to_device(synthetic.block_weights(c, c, heads, seed=s, gamma_random=True), dev)
+          for s in (2, 3)]
+    x = synthetic.features(t, c, seed=4)
+    mod = synthetic.modulation(c, 0.4, seed=5).astype(np.float16)
+    ctx = torch.from_numpy(synthetic.features(L, c, seed=6)).to(dev)
+    kvs = [transformer.context_kv(w, ctx, heads) for w in ws]
+    rows = hdist.shard_slice(t, rank, world)
+    tt = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    stack = hdist.ShardedBlockStack(ws, heads)
+    y_local = stack(tt(x[rows]), tt(mod), tt(cos[rows]), tt(sin[rows]), kvs)
+    y = hdist.gather_rows(y_local)
+    if rank == 0:
+        ref = transformer.BlockStack(ws, heads)(tt(x)[None], tt(mod), tt(cos), tt(sin), kvs)[0]
+        np.save(result_path, np.array([float(torch.equal(y, ref)), float((y.float() - ref.float()).abs().max())]))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_sharded_stack_matches_single_gpu(tmp_path):
+    out = tmp_path / "r.npy"
+    mp.spawn(_worker, args=(2, _free_port(), str(out)), nprocs=2, join=True)
+    equal, maxdiff = np.load(out)
+    assert equal == 1.0, maxdiff

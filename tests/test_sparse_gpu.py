@@ -146,3 +146,56 @@ def test_config5_conv_sampled_rows():
     wk = w.double().cpu().numpy().reshape(256, 27, 256)
     ref = np.einsum("rkc,okc->ro", xs[tab], wk) + b.double().cpu().numpy()
     assert rel_l2(got[rows].float().cpu().numpy(), ref) < 2e-3
+
+
+def test_spconv_shim_matches_golden_and_dense_conv3d():
+    """The spconv drop-in (tests/test_backends.py:21-67 of the reference): SubMConv3d against the
+    reference shim's fp64 golden, the pair layout coords[dst] == coords[src] + 1 - r, and the
+    k <-> 26 - k count symmetry of submanifold pairs."""
+    from hi3d_b200.torch_backend import sparse_conv as sc
+
+    g = np.load(GOLDEN / "sparse.npz")
+    xyz = g["coords"]
+    indices = _t(np.concatenate([np.zeros((xyz.shape[0], 1), np.int32), xyz], 1))
+    conv = sc.SubMConv3d(8, 8, 3, bias=True, indice_key="subm3").to(DEV)
+    w = np.zeros((8, 3, 3, 3, 8))
+    w[:7, ..., :5] = g["weight"]
+    b = np.zeros(8)
+    b[:7] = g["bias"]
+    with torch.no_grad():
+        conv.weight.copy_(torch.from_numpy(w))
+        conv.bias.copy_(torch.from_numpy(b))
+    conv = conv.half()
+    feats = np.zeros((xyz.shape[0], 8))
+    feats[:, :5] = g["feats"]
+    x = sc.SparseConvTensor(_t(feats, torch.float16), indices, [12, 12, 12], 1)
+    out = conv(x)
+    assert "subm3" in x.indice_dict
+    assert rel_l2(out.features.float().cpu().numpy()[:, :7], g["conv_out"]) < 3e-3
+    _, pairs, counts = sc.get_indice_pairs(indices, 1, [12, 12, 12], sc.ConvAlgo.Native, (3, 3, 3), (1, 1, 1),
+                                           (1, 1, 1), (1, 1, 1), (0, 0, 0), True, False)
+    coords = torch.from_numpy(xyz.astype(np.int64))
+    for k in range(27):
+        r = torch.tensor([k // 9, (k // 3) % 3, k % 3])
+        n = int(counts[k])
+        src, dst = pairs[0, k, :n].cpu(), pairs[1, k, :n].cpu()
+        assert torch.equal(coords[dst], coords[src] + 1 - r)
+        assert n == int(counts[26 - k])
+    with pytest.raises(NotImplementedError):
+        sc.get_indice_pairs(indices, 1, [12] * 3, sc.ConvAlgo.Native, (3, 3, 3), (2, 2, 2), (1, 1, 1), (1, 1, 1),
+                            (0, 0, 0), True, False)
+
+
+def test_spconv_shim_batches_do_not_mix():
+    from hi3d_b200.torch_backend import sparse_conv as sc
+
+    rng = np.random.default_rng(9)
+    xyz = np.argwhere(rng.random((10, 10, 10)) < 0.4).astype(np.int32)
+    n = xyz.shape[0]
+    idx = np.concatenate([np.concatenate([np.zeros((n, 1), np.int32), xyz], 1),
+                          np.concatenate([np.ones((n, 1), np.int32), xyz], 1)])
+    feats = rng.standard_normal((2 * n, 16)).astype(np.float16)
+    conv = sc.SubMConv3d(16, 16, 3).to(DEV).half()
+    both = conv(sc.SparseConvTensor(_t(feats), _t(idx), [10] * 3, 2)).features
+    one = conv(sc.SparseConvTensor(_t(feats[:n]), _t(idx[:n]), [10] * 3, 1)).features
+    assert torch.equal(both[:n], one)
