@@ -329,7 +329,7 @@ def run_ours(args) -> None:
 
     # ---- roofline of the dominant kernel (self-attention)
     peaks = _peaks()
-    self_launches = [r for r in attn if r["kind"] == "self"]
+    self_launches = [r for r in attn if r["nk"] == T_TOKENS]  # self-attention: keys = all tokens
     avg_s = sum(r["ms"] for r in self_launches) / max(1, len(self_launches)) / 1e3
     flops = self_launches[0]["flops"] if self_launches else 0.0
     achieved = flops / avg_s / 1e12 if avg_s > 0 else 0.0

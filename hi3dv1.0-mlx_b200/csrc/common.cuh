@@ -362,14 +362,15 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
 // trick, f = x - n in [-0.5, 0.5]; 2^f by a degree-4 polynomial whose
 // coefficients were fitted for this library (weighted least squares on the
 // relative error over [-0.5, 0.5]; max relative error 2.7e-6 in fp32 Horner);
-// the result's exponent field is then increased by n.  Inputs are clamped to
-// [-125, 127] so the exponent arithmetic stays in the normal range (2^-125
-// rounds to zero in the 16-bit P either way).
+// the result's exponent field is then increased by n.  Inputs must be <= 127;
+// they are clamped below at -125 so the exponent arithmetic stays in the
+// normal range (2^-125 rounds to zero in the 16-bit P either way).
 __device__ __forceinline__ uint64_t f2_exp2_poly(uint64_t x) {
   float x0, x1;
   f2_unpack(x, x0, x1);
-  x0 = fminf(fmaxf(x0, -125.0f), 127.0f);
-  x1 = fminf(fmaxf(x1, -125.0f), 127.0f);
+  // callers guarantee x <= 127 (attention: x <= kRescaleLog2); only the lower clamp is needed
+  x0 = fmaxf(x0, -125.0f);
+  x1 = fmaxf(x1, -125.0f);
   const uint64_t xc = f2_pack(x0, x1);
   const float kMagic = 12582912.0f;  // 1.5 * 2^23
   const uint64_t r = f2_add(xc, f2_pack(kMagic, kMagic));

@@ -38,8 +38,8 @@ class KernelTimer:
     """Optional CUDA-event timing of every attention launch on the launching stream.
 
     ``start()`` arms it, ``stop()`` synchronises and returns one record per launch
-    (``kind``: "self" when queries and keys are the same sequence length, else "cross";
-    ``flops`` = 4 * Nq * Nk * H * D for dense launches, None for varlen ones).
+    (``nq``, ``nk`` rows; ``flops`` = 4 * Nq * Nk * H * D for dense launches, None for varlen
+    ones; ``ms`` the event-timed duration).
     """
 
     def __init__(self):
@@ -69,7 +69,7 @@ def _launch(args: _lib.AttnArgs, dev_tensor: torch.Tensor) -> None:
         e1.record()
         dense = not args.cu_seqlens_q
         flops = 4.0 * args.nq * args.nk * args.heads * args.head_dim * args.num_seqs if dense else None
-        TIMER.records.append({"kind": "self" if args.nq == args.nk else "cross", "flops": flops, "e0": e0, "e1": e1})
+        TIMER.records.append({"nq": args.nq, "nk": args.nk, "flops": flops, "e0": e0, "e1": e1})
 
 
 def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float,
