@@ -17,6 +17,7 @@
 //   source), per-tap weights by TMA, fp32 accumulators in TMEM.  Taps with no
 //   neighbour in the whole tile are skipped (a 27-bit mask per tile).
 #include <cub/cub.cuh>
+#include <mutex>
 
 #include "abi.h"
 #include "common.cuh"
@@ -441,6 +442,91 @@ extern "C" int hi3d_neighbour_map_build(const int32_t* coords, int64_t n, const 
   hash_query_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(query, nq, stride, keys, vals, cap - 1,
                                                                      (int32_t)n, table);
   return check_launch("neighbour_map query");
+}
+
+// ---------------------------------------------------------------------------
+// neighbour map without a caller workspace
+//
+// For callers that cannot allocate device memory: the hash table lives in one
+// file-scope device array sized for HI3D_NEIGHBOUR_MAP_NOALLOC_MAX_VOXELS
+// voxels (6 MiB + 256 B), present on every GPU that loads this library until
+// the process exits.  All calls on a GPU share it, so calls that overlap on
+// that GPU (two streams, two host threads) race.
+// ---------------------------------------------------------------------------
+namespace hi3d {
+namespace sparse {
+
+constexpr uint32_t kNoAllocCap = 1u << 19;  // hash_capacity(HI3D_NEIGHBOUR_MAP_NOALLOC_MAX_VOXELS)
+constexpr size_t kNoAllocValsOff = (size_t)kNoAllocCap * 8;
+constexpr size_t kNoAllocFlagOff = kNoAllocValsOff + (size_t)kNoAllocCap * 4;
+constexpr size_t kNoAllocBytes = kNoAllocFlagOff + 256;
+static_assert(2 * (uint64_t)HI3D_NEIGHBOUR_MAP_NOALLOC_MAX_VOXELS <= kNoAllocCap, "scratch below the voxel limit");
+
+// keys [cap] u64 at 0, vals [cap] i32 at kNoAllocValsOff, overflow flag at kNoAllocFlagOff
+static __device__ __align__(256) uint8_t g_nmap_scratch[kNoAllocBytes];
+
+// In host code `g_nmap_scratch` names a host-side stand-in, not device memory;
+// its device address is looked up once per device and cached here.
+constexpr int kMaxDevices = 64;
+static std::mutex g_nmap_mu;
+static uint8_t* g_nmap_ptr[kMaxDevices] = {};
+
+static int nmap_scratch(uint8_t** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(HI3D_ERR_CUDA, "neighbour_map_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices)
+    return set_error(HI3D_ERR_UNSUPPORTED, "neighbour_map_noalloc: device ordinal %d above %d", dev, kMaxDevices - 1);
+  std::lock_guard<std::mutex> lock(g_nmap_mu);
+  if (!g_nmap_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_nmap_scratch);
+    if (e != cudaSuccess)
+      return set_error(HI3D_ERR_CUDA, "neighbour_map_noalloc: cudaGetSymbolAddress on device %d: %s", dev,
+                       cudaGetErrorString(e));
+    g_nmap_ptr[dev] = static_cast<uint8_t*>(p);
+  }
+  *out = g_nmap_ptr[dev];
+  return HI3D_OK;
+}
+
+}  // namespace sparse
+}  // namespace hi3d
+
+extern "C" int hi3d_neighbour_map_build_noalloc(const int32_t* coords, int64_t n, const int32_t* query, int64_t nq,
+                                                int stride, int32_t* table, void* stream) {
+  if (n < 0 || nq < 0 || (stride != 1 && stride != 2) || (n > 0 && !coords))
+    return set_error(HI3D_ERR_INVALID_ARGUMENT, "neighbour_map_noalloc: bad arguments");
+  if (n > HI3D_NEIGHBOUR_MAP_NOALLOC_MAX_VOXELS)
+    return set_error(HI3D_ERR_CAPACITY,
+                     "neighbour_map_noalloc: %lld voxels exceed the fixed scratch limit of %d; "
+                     "use hi3d_neighbour_map_build with a workspace",
+                     (long long)n, HI3D_NEIGHBOUR_MAP_NOALLOC_MAX_VOXELS);
+  if ((query ? nq : n) == 0) return HI3D_OK;
+  if (!table) return set_error(HI3D_ERR_INVALID_ARGUMENT, "neighbour_map_noalloc: null table");
+  if (!query) {
+    query = coords;
+    nq = n;
+  }
+  uint8_t* ws = nullptr;
+  int rc = nmap_scratch(&ws);
+  if (rc) return rc;
+  cudaStream_t st = as_stream(stream);
+  const uint32_t cap = hash_capacity(n);  // <= kNoAllocCap by the limit above
+  uint64_t* keys = reinterpret_cast<uint64_t*>(ws);
+  int32_t* vals = reinterpret_cast<int32_t*>(ws + kNoAllocValsOff);
+  int* flag = reinterpret_cast<int*>(ws + kNoAllocFlagOff);
+  // the array keeps the previous call's table: clear the slots this call probes
+  cudaError_t e = cudaMemsetAsync(keys, 0xff, (size_t)cap * 8, st);
+  if (e == cudaSuccess) e = cudaMemsetAsync(vals, 0xff, (size_t)cap * 4, st);
+  if (e == cudaSuccess) e = cudaMemsetAsync(flag, 0, sizeof(int), st);
+  if (e != cudaSuccess) return set_error(HI3D_ERR_CUDA, "neighbour_map_noalloc: memset: %s", cudaGetErrorString(e));
+  if (n > 0) hash_insert_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(coords, n, keys, vals, cap - 1, flag);
+  if ((rc = check_launch("neighbour_map_noalloc insert"))) return rc;
+  const int64_t total = nq * 27;
+  hash_query_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(query, nq, stride, keys, vals, cap - 1,
+                                                                     (int32_t)n, table);
+  return check_launch("neighbour_map_noalloc query");
 }
 
 extern "C" int hi3d_downsample_workspace_size(int64_t n, int64_t* bytes) {

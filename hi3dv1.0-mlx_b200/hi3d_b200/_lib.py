@@ -65,6 +65,7 @@ SIGNATURES: dict[str, tuple] = {
     "hi3d_quantize_act_i8": (_i32, [_c_void_p] * 4 + [_i64, _i64, _i32, _i32, _c_void_p]),
     "hi3d_neighbour_map_workspace_size": (_i32, [_i64, ctypes.POINTER(_i64)]),
     "hi3d_neighbour_map_build": (_i32, [_c_void_p, _i64, _c_void_p, _i64, _i32, _c_void_p, _c_void_p, _i64, _c_void_p]),
+    "hi3d_neighbour_map_build_noalloc": (_i32, [_c_void_p, _i64, _c_void_p, _i64, _i32, _c_void_p, _c_void_p]),
     "hi3d_downsample_workspace_size": (_i32, [_i64, ctypes.POINTER(_i64)]),
     "hi3d_downsample_structure": (_i32, [_c_void_p, _i64] + [_c_void_p] * 5 + [_i64, _c_void_p]),
     "hi3d_conv_tap_mask": (_i32, [_c_void_p, _i64, _i64, _c_void_p, _c_void_p]),

@@ -171,6 +171,27 @@ HI3D_API int hi3d_neighbour_map_build(const int32_t* coords, int64_t n, const in
                                       int stride, int32_t* table, void* workspace, int64_t workspace_bytes,
                                       void* stream);
 
+/* No counterpart in the reference: an addition of this library for callers that cannot
+ * allocate device memory, such as a host whose own memory pool has already reserved the
+ * GPU's memory (so a cudaMalloc would fail or compete with it), a C host that binds only this
+ * ABI and has no allocator for a workspace, or a latency-bound caller that cannot accept the
+ * device-wide synchronisation that cudaMalloc and cudaFree imply.
+ *
+ * Same arguments and result as hi3d_neighbour_map_build, without the workspace: the hash table
+ * lives in a fixed device array inside the library, sized for at most
+ * HI3D_NEIGHBOUR_MAP_NOALLOC_MAX_VOXELS voxels (n); 6 MiB + 256 bytes of it are held on every
+ * GPU that loads the library until the process exits.  A larger n returns HI3D_ERR_CAPACITY;
+ * nq is not limited.  Nothing is allocated, at set-up or per call.
+ *
+ * The first call on a device (the one current when it is made) looks up that device's address
+ * of the array; make that first call before any stream capture.  `stream` must belong to the
+ * current device.  Every call on a device shares the one array, and each call clears the part
+ * it uses before building, so calls in sequence are independent, but calls that overlap on the
+ * GPU (on two streams, or from two host threads) race and give wrong tables. */
+#define HI3D_NEIGHBOUR_MAP_NOALLOC_MAX_VOXELS 262144
+HI3D_API int hi3d_neighbour_map_build_noalloc(const int32_t* coords, int64_t n, const int32_t* query, int64_t nq,
+                                              int stride, int32_t* table, void* stream);
+
 /* Bytes of workspace hi3d_downsample_structure needs for n voxels. */
 HI3D_API int hi3d_downsample_workspace_size(int64_t n, int64_t* bytes);
 
