@@ -9,11 +9,13 @@
 // (GELU in fp32, transformer.py:176-179); or update a residual stream in place,
 // x = round(x + round(y * gate)) (transformer.py:570, :588).
 //
-// CTA (192 threads), one per SM, looping over 128 x 256 output tiles:
+// CTA (320 threads), one per SM, looping over 128 x 256 output tiles:
 //   warp 0     TMA producer: A [128 x 128 B] and W [256 x 128 B] per stage
 //   warp 1     MMA issuer (one lane), TMEM owner; two 256-column accumulators
 //              so the epilogue of one tile overlaps the MMAs of the next
-//   warps 2-5  epilogue, one output row per thread (TMEM lane = row)
+//   warps 2-9  epilogue: two warps per TMEM lane quarter (one per 128-column
+//              half), results staged through shared memory for coalesced
+//              16-byte global accesses
 #include <type_traits>
 
 #include "abi.h"
@@ -22,14 +24,16 @@
 namespace hi3d {
 namespace gemm {
 
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;
 constexpr int BM = 128;
 constexpr int BN = 256;
 constexpr int BKB = 128;  // K bytes per stage (one 128-byte swizzle row)
 constexpr int NST = 4;
 constexpr int A_STAGE = BM * BKB;
 constexpr int B_STAGE = BN * BKB;
-constexpr int SMEM = NST * (A_STAGE + B_STAGE) + 1024 + 256;
+constexpr int EPI_WARPS = 8;
+constexpr int STAGE_BYTES = 32 * 64;  // per epilogue warp: 32 rows x 32 16-bit columns
+constexpr int SMEM = NST * (A_STAGE + B_STAGE) + EPI_WARPS * (STAGE_BYTES + 256 * 4) + 1024 + 256;
 
 enum Kind { KIND_F16 = 0, KIND_BF16 = 1, KIND_I8 = 2 };
 enum Epi { EPI_STORE = 0, EPI_GELU = 1, EPI_RESIDUAL = 2 };
@@ -69,7 +73,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + NST * A_STAGE;
-  Barriers* bar = reinterpret_cast<Barriers*>(sB + NST * B_STAGE);
+  uint8_t* sStage = sB + NST * B_STAGE;
+  float* sVec = reinterpret_cast<float*>(sStage + EPI_WARPS * STAGE_BYTES);
+  Barriers* bar = reinterpret_cast<Barriers*>(sVec + EPI_WARPS * 256);
   constexpr int ESZ = KIND == KIND_I8 ? 1 : 2;
   constexpr int BKE = BKB / ESZ;  // K elements per stage
 
@@ -83,7 +89,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&bar->acc_full[a], 1);
-      mbar_init(&bar->acc_empty[a], BM);
+      mbar_init(&bar->acc_empty[a], EPI_WARPS);
     }
     bar->abort = 0;
     fence_barrier_init();
@@ -157,93 +163,156 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int sub = warp & 3;
-    const int r = sub * 32 + lane;
-    const uint32_t lane_addr = (uint32_t)(sub * 32) << 16;
+    // Warp w (2..9) reads TMEM lanes 32 (w % 4) .. +31 (rows q*32.. of the tile)
+    // and columns 128 h .. 128 h + 127 with h = (w - 2) / 4.  Per 32-column chunk:
+    //   phase 1, thread = row: accumulators -> rounded 16-bit y (bias, dequant,
+    //            GELU) -> the warp's swizzled 32 x 64 B staging tile;
+    //   phase 2, coalesced: lane -> (row i*8 + lane/4, 16-byte column group
+    //            lane%4): residual/gate update and 16-byte global stores, eight
+    //            rows x 64 contiguous bytes per instruction.
+    // The residual tile is prefetched with coalesced loads before the
+    // accumulator wait.
+    const int q = warp & 3, h = (warp - 2) >> 2, ew = warp - 2;
+    uint8_t* stage = sStage + ew * STAGE_BYTES;
+    float* vec = sVec + ew * 256;  // [0, 128): bias of this warp's columns; [128, 256): weight scales
+    const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
+    constexpr bool kRaw = std::is_same<OutT, int32_t>::value;
     int local = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
       const int acc = local & 1, use = local >> 1;
+      const int m0 = (tile / p.tiles_n) * BM + q * 32;  // this warp's first row
+      const int nh = (tile % p.tiles_n) * BN + h * 128;  // this warp's first column
+      if constexpr (!kRaw) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int nn = nh + lane * 4 + e;
+          float b = 0.0f, sw = 1.0f;
+          if (nn < p.N) {
+            if (p.bias) b = Cvt<OutT>::to_f(reinterpret_cast<const OutT*>(p.bias)[nn]);
+            if (KIND == KIND_I8) sw = p.sw[nn];
+          }
+          vec[lane * 4 + e] = b;
+          vec[128 + lane * 4 + e] = sw;
+        }
+      }
+      uint4 res[4][4];
+      if constexpr (EPI == EPI_RESIDUAL) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int m = m0 + i * 8 + (lane >> 2), n = nh + c * 32 + (lane & 3) * 8;
+            res[c][i] = make_uint4(0, 0, 0, 0);
+            if (p.vec && m < p.M && n + 8 <= p.N)
+              res[c][i] = *reinterpret_cast<const uint4*>(reinterpret_cast<const OutT*>(p.out) + (int64_t)m * p.ldo + n);
+          }
+      }
+      __syncwarp();
       if (!mbar_wait(&bar->acc_full[acc], use & 1, abort, 120)) break;
       tc_fence_after();
-      const int m = (tile / p.tiles_n) * BM + r;
-      const int n0 = (tile % p.tiles_n) * BN;
-      const bool row_ok = m < p.M;
+      const int mr = m0 + lane;  // phase-1 row
       float sa = 1.0f;
-      if (KIND == KIND_I8 && row_ok) sa = p.sa[m];
-      OutT* orow = reinterpret_cast<OutT*>(p.out) + (int64_t)m * p.ldo;
-      const OutT* grow = nullptr;
-      if (EPI == EPI_RESIDUAL && p.gate) grow = reinterpret_cast<const OutT*>(p.gate) + (m / p.rows_per_batch) * p.gate_stride;
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      if (KIND == KIND_I8 && mr < p.M && !kRaw) sa = p.sa[mr];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
         uint32_t v[32];
-        __syncwarp();
-        tmem_ld32(tmem + lane_addr + acc * BN + c * 32, v);
+        tmem_ld32(tmem + lane_addr + acc * BN + h * 128 + c * 32, v);
         tmem_wait_ld();
-        const int nb = n0 + c * 32;
-        if (!row_ok || nb >= p.N) continue;
+        const int nb = nh + c * 32;
+        if constexpr (kRaw) {
+          // raw exact int32 accumulators (verification / custom dequantisation), thread = row
+          OutT* orow = reinterpret_cast<OutT*>(p.out) + (int64_t)mr * p.ldo;
+          if (mr < p.M) {
 #pragma unroll
-        for (int e = 0; e < 32; e += 8) {
-          const int n = nb + e;
-          if (n >= p.N) break;
-          if constexpr (std::is_same<OutT, int32_t>::value) {
-            // raw exact int32 accumulators (verification / custom dequantisation)
-            if (p.vec && n + 8 <= p.N) {
-              *reinterpret_cast<uint4*>(orow + n) = make_uint4(v[e], v[e + 1], v[e + 2], v[e + 3]);
-              *reinterpret_cast<uint4*>(orow + n + 4) = make_uint4(v[e + 4], v[e + 5], v[e + 6], v[e + 7]);
-            } else {
-              for (int q = 0; q < 8 && n + q < p.N; ++q) orow[n + q] = (int32_t)v[e + q];
-            }
-            continue;
-          } else {
-          float y[8];
-#pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            const int nn = min(n + q, p.N - 1);
-            float t;
-            if (KIND == KIND_I8) {
-              t = __fmul_rn(__fmul_rn(__int2float_rn((int)v[e + q]), sa), p.sw[nn]);
-            } else {
-              t = __uint_as_float(v[e + q]);
-            }
-            if (p.bias) t = __fadd_rn(t, Cvt<OutT>::to_f(reinterpret_cast<const OutT*>(p.bias)[nn]));
-            y[q] = Cvt<OutT>::to_f(Cvt<OutT>::from_f(t));  // round to the output type
-            if (EPI == EPI_GELU) y[q] = gelu_tanh_f<OutT>(y[q]);
-          }
-          if (EPI == EPI_RESIDUAL) {
-            if (p.vec && n + 8 <= p.N) {
-              uint4 xv = *reinterpret_cast<const uint4*>(orow + n);
-              uint4 gv = grow ? *reinterpret_cast<const uint4*>(grow + n) : make_uint4(0, 0, 0, 0);
-              const OutT* xa = reinterpret_cast<const OutT*>(&xv);
-              const OutT* ga = reinterpret_cast<const OutT*>(&gv);
-#pragma unroll
-              for (int q = 0; q < 8; ++q) {
-                float g = y[q];
-                if (grow) g = Cvt<OutT>::to_f(Cvt<OutT>::from_f(__fmul_rn(g, Cvt<OutT>::to_f(ga[q]))));
-                y[q] = __fadd_rn(Cvt<OutT>::to_f(xa[q]), g);
-              }
-            } else {
-              for (int q = 0; q < 8 && n + q < p.N; ++q) {
-                float g = y[q];
-                if (grow) g = Cvt<OutT>::to_f(Cvt<OutT>::from_f(__fmul_rn(g, Cvt<OutT>::to_f(grow[n + q]))));
-                y[q] = __fadd_rn(Cvt<OutT>::to_f(orow[n + q]), g);
+            for (int e = 0; e < 32; e += 8) {
+              const int n = nb + e;
+              if (n >= p.N) break;
+              if (p.vec && n + 8 <= p.N) {
+                *reinterpret_cast<uint4*>(orow + n) = make_uint4(v[e], v[e + 1], v[e + 2], v[e + 3]);
+                *reinterpret_cast<uint4*>(orow + n + 4) = make_uint4(v[e + 4], v[e + 5], v[e + 6], v[e + 7]);
+              } else {
+                for (int qq = 0; qq < 8 && n + qq < p.N; ++qq) orow[n + qq] = (int32_t)v[e + qq];
               }
             }
           }
-          if (p.vec && n + 8 <= p.N) {
+          continue;
+        } else {
+          // phase 1
+#pragma unroll
+          for (int e = 0; e < 32; e += 8) {
+            float y[8];
+#pragma unroll
+            for (int qq = 0; qq < 8; ++qq) {
+              const int col = c * 32 + e + qq;
+              float t;
+              if (KIND == KIND_I8)
+                t = __fmul_rn(__fmul_rn(__int2float_rn((int)v[e + qq]), sa), vec[128 + col]);
+              else
+                t = __uint_as_float(v[e + qq]);
+              if (p.bias) t = __fadd_rn(t, vec[col]);
+              y[qq] = Cvt<OutT>::to_f(Cvt<OutT>::from_f(t));  // round to the output type
+              if (EPI == EPI_GELU) y[qq] = gelu_tanh_f<OutT>(y[qq]);
+            }
             uint4 w;
             w.x = Cvt<OutT>::pack2(y[0], y[1]);
             w.y = Cvt<OutT>::pack2(y[2], y[3]);
             w.z = Cvt<OutT>::pack2(y[4], y[5]);
             w.w = Cvt<OutT>::pack2(y[6], y[7]);
-            *reinterpret_cast<uint4*>(orow + n) = w;
-          } else {
-            for (int q = 0; q < 8 && n + q < p.N; ++q) orow[n + q] = Cvt<OutT>::from_f(y[q]);
+            const int j = e >> 3;
+            *reinterpret_cast<uint4*>(stage + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) = w;
           }
+          __syncwarp();
+          // phase 2
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int rl = i * 8 + (lane >> 2), j = lane & 3;
+            const int m = m0 + rl, n = nb + j * 8;
+            const uint4 yv = *reinterpret_cast<const uint4*>(stage + rl * 64 + ((j ^ ((rl >> 1) & 3)) << 4));
+            if (m >= p.M || n >= p.N) continue;
+            OutT* orow = reinterpret_cast<OutT*>(p.out) + (int64_t)m * p.ldo;
+            const OutT* ya = reinterpret_cast<const OutT*>(&yv);
+            const OutT* grow = nullptr;
+            if (EPI == EPI_RESIDUAL && p.gate)
+              grow = reinterpret_cast<const OutT*>(p.gate) + (m / p.rows_per_batch) * p.gate_stride;
+            if (p.vec && n + 8 <= p.N) {
+              if constexpr (EPI == EPI_RESIDUAL) {
+                const uint4 gv = grow ? __ldg(reinterpret_cast<const uint4*>(grow + n)) : make_uint4(0, 0, 0, 0);
+                const OutT* xa = reinterpret_cast<const OutT*>(&res[c][i]);
+                const OutT* ga = reinterpret_cast<const OutT*>(&gv);
+                float o[8];
+#pragma unroll
+                for (int qq = 0; qq < 8; ++qq) {
+                  float g = Cvt<OutT>::to_f(ya[qq]);
+                  if (grow) g = Cvt<OutT>::to_f(Cvt<OutT>::from_f(__fmul_rn(g, Cvt<OutT>::to_f(ga[qq]))));
+                  o[qq] = __fadd_rn(Cvt<OutT>::to_f(xa[qq]), g);
+                }
+                uint4 w;
+                w.x = Cvt<OutT>::pack2(o[0], o[1]);
+                w.y = Cvt<OutT>::pack2(o[2], o[3]);
+                w.z = Cvt<OutT>::pack2(o[4], o[5]);
+                w.w = Cvt<OutT>::pack2(o[6], o[7]);
+                *reinterpret_cast<uint4*>(orow + n) = w;
+              } else {
+                *reinterpret_cast<uint4*>(orow + n) = yv;
+              }
+            } else {
+              for (int qq = 0; qq < 8 && n + qq < p.N; ++qq) {
+                if (EPI == EPI_RESIDUAL) {
+                  float g = Cvt<OutT>::to_f(ya[qq]);
+                  if (grow) g = Cvt<OutT>::to_f(Cvt<OutT>::from_f(__fmul_rn(g, Cvt<OutT>::to_f(grow[n + qq]))));
+                  orow[n + qq] = Cvt<OutT>::from_f(__fadd_rn(Cvt<OutT>::to_f(orow[n + qq]), g));
+                } else {
+                  orow[n + qq] = ya[qq];
+                }
+              }
+            }
           }
+          __syncwarp();  // the staging tile is rewritten by the next chunk
         }
       }
       tc_fence_before();
-      mbar_arrive(&bar->acc_empty[acc]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar->acc_empty[acc]);
     }
   }
 
