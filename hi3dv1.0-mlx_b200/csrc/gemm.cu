@@ -66,6 +66,24 @@ __device__ __forceinline__ float gelu_tanh_f(float a) {
   return 0.5f * a * (1.0f + tanhf(k0 * (a + 0.044715f * a * a * a)));
 }
 
+// Coalesced residual loads of one 32 x 32 chunk: row group i covers rows
+// m0 + i*8 + lane/4, columns n + (lane%4)*8 .. +7 (zero where not 16-byte loadable;
+// the scalar path reloads those).
+template <typename OutT>
+__device__ __forceinline__ void prefetch_residual(const Params& p, uint4 (&r)[4], int m0, int n, int lane) {
+  if constexpr (std::is_same<OutT, int32_t>::value) {
+    return;
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int m = m0 + i * 8 + (lane >> 2), nn = n + (lane & 3) * 8;
+      r[i] = make_uint4(0, 0, 0, 0);
+      if (p.vec && m < p.M && nn + 8 <= p.N)
+        r[i] = *reinterpret_cast<const uint4*>(reinterpret_cast<const OutT*>(p.out) + (int64_t)m * p.ldo + nn);
+    }
+  }
+}
+
 template <int KIND, int EPI, typename OutT>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Params p) {
@@ -177,6 +195,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     float* vec = sVec + ew * 256;  // [0, 128): bias of this warp's columns; [128, 256): weight scales
     const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
     constexpr bool kRaw = std::is_same<OutT, int32_t>::value;
+    // Residual rows of this warp's strip, [chunk][row group]: loaded for the first
+    // tile before its accumulator wait, and for each next tile chunk by chunk as
+    // the current tile's chunks finish, so the loads overlap the current tile.
+    uint4 res[4][4];
     int local = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
       const int acc = local & 1, use = local >> 1;
@@ -195,17 +217,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           vec[128 + lane * 4 + e] = sw;
         }
       }
-      uint4 res[4][4];
-      if constexpr (EPI == EPI_RESIDUAL) {
+      if (EPI == EPI_RESIDUAL && local == 0) {
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int m = m0 + i * 8 + (lane >> 2), n = nh + c * 32 + (lane & 3) * 8;
-            res[c][i] = make_uint4(0, 0, 0, 0);
-            if (p.vec && m < p.M && n + 8 <= p.N)
-              res[c][i] = *reinterpret_cast<const uint4*>(reinterpret_cast<const OutT*>(p.out) + (int64_t)m * p.ldo + n);
-          }
+        for (int c = 0; c < 4; ++c) prefetch_residual<OutT>(p, res[c], m0, nh + c * 32, lane);
       }
       __syncwarp();
       if (!mbar_wait(&bar->acc_full[acc], use & 1, abort, 120)) break;
@@ -308,6 +322,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
           __syncwarp();  // the staging tile is rewritten by the next chunk
+          if (EPI == EPI_RESIDUAL) {
+            const int nt = tile + gridDim.x;
+            if (nt < num_tiles)
+              prefetch_residual<OutT>(p, res[c], (nt / p.tiles_n) * BM + q * 32,
+                                      (nt % p.tiles_n) * BN + h * 128 + c * 32, lane);
+          }
         }
       }
       tc_fence_before();

@@ -11,9 +11,11 @@
 // Then s = max(max|y|, 1e-8) / 127 and q = clamp(rint(y / s), -127, 127)
 // (round half to even), all in IEEE fp32.
 //
-// Layout: one warp per row; each lane owns 8 consecutive elements (16-byte
-// loads), so bits 0-2 of the element index are in-register stages and bits
-// 3-5 are xor-shuffles across lanes 1, 2 and 4 apart.
+// Layout: one to eight warps per row (by width); each lane owns 8 consecutive
+// elements of a 256-element chunk (16-byte loads, each warp instruction one
+// contiguous 512-byte span), so bits 0-2 of the element index are in-register
+// stages and bits 3-5 are xor-shuffles across lanes 1, 2 and 4 apart.  Warps of
+// one row combine their maxima through shared memory.
 #include "abi.h"
 #include "common.cuh"
 
@@ -33,20 +35,38 @@ __device__ __forceinline__ float butterfly_lane(float v, int dist, bool set) {
   return set ? __fsub_rn(other, v) : __fadd_rn(v, other);
 }
 
-template <typename T, int ITERS, bool ROTATE>
+// rint(y / s) with y / s the correctly rounded IEEE quotient, clamped to
+// [-127, 127] (|y / s| <= 127 for finite rows; NaN gives -127).
+// z = y * rn(1 / s) is within |y / s| * 2^-23 <= 1.6e-5 of the true quotient;
+// when z is farther than 3e-5 from a half-integer, the true quotient and its
+// rounded value lie on the same side of it and rint(z) is the answer.  The few
+// quotients closer to a rounding tie take the exact division.
+__device__ __forceinline__ int quant_code(float y, float s, float inv) {
+  const float z = __fmul_rn(y, inv);
+  float r = rintf(z);
+  if (fabsf(z - r) >= 0.5f - 3e-5f) r = rintf(__fdiv_rn(y, s));
+  return (int)fminf(fmaxf(r, -127.0f), 127.0f);
+}
+
+// One row per WPR warps of a 256-thread block; warp `part` of a row handles the
+// 256-element chunks part, part + WPR, ... (IPW of them).
+template <typename T, int IPW, int WPR, bool ROTATE>
 __global__ void __launch_bounds__(256) quant_h64_kernel(const T* __restrict__ x, const float* __restrict__ sign,
                                                         int8_t* __restrict__ q, float* __restrict__ scale, int64_t rows,
                                                         int K) {
-  const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
-  if (row >= rows) return;  // whole warp leaves together
-  const int lane = threadIdx.x & 31;
-  const T* xr = x + row * K;
-  float y[ITERS][8];
+  constexpr int RPB = 8 / WPR;  // rows per block
+  __shared__ float red[8];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * RPB + warp / WPR;
+  const int part = warp % WPR;
+  const bool row_ok = row < rows;
+  const T* xr = x + (row_ok ? row : 0) * K;
+  float y[IPW][8];
   float amax = 0.f;
 #pragma unroll
-  for (int it = 0; it < ITERS; ++it) {
-    const int base = it * 256 + lane * 8;
-    const bool active = base < K;
+  for (int j = 0; j < IPW; ++j) {
+    const int base = (part + j * WPR) * 256 + lane * 8;
+    const bool active = row_ok && base < K;
     float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     if (active) {
       load8<T>(xr + base, v);
@@ -82,45 +102,67 @@ __global__ void __launch_bounds__(256) quant_h64_kernel(const T* __restrict__ x,
     }
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      y[it][i] = v[i];
+      y[j][i] = v[i];
       if (active) amax = fmaxf(amax, fabsf(v[i]));
     }
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  if (WPR > 1) {
+    if (lane == 0) red[warp] = amax;
+    __syncthreads();
+    const int first = warp - part;
+#pragma unroll
+    for (int w = 0; w < WPR; ++w) amax = fmaxf(amax, red[first + w]);
+  }
+  if (!row_ok) return;
   const float s = __fdiv_rn(fmaxf(amax, 1e-8f), 127.0f);
-  if (lane == 0) scale[row] = s;
+  const float inv = __frcp_rn(s);
+  if (lane == 0 && part == 0) scale[row] = s;
   int8_t* qr = q + row * K;
 #pragma unroll
-  for (int it = 0; it < ITERS; ++it) {
-    const int base = it * 256 + lane * 8;
+  for (int j = 0; j < IPW; ++j) {
+    const int base = (part + j * WPR) * 256 + lane * 8;
     if (base >= K) continue;
     uint32_t w[2] = {0u, 0u};
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      float r = rintf(__fdiv_rn(y[it][i], s));
-      r = fminf(fmaxf(r, -127.0f), 127.0f);
-      w[i >> 2] |= ((uint32_t)(uint8_t)(int8_t)(int)r) << (8 * (i & 3));
-    }
+    for (int i = 0; i < 8; ++i)
+      w[i >> 2] |= ((uint32_t)(uint8_t)(int8_t)quant_code(y[j][i], s, inv)) << (8 * (i & 3));
     *reinterpret_cast<uint2*>(qr + base) = make_uint2(w[0], w[1]);
+  }
+}
+
+template <typename T, int IPW, int WPR, bool ROTATE>
+static void launch_q(const void* x, const float* sign, int8_t* q, float* scale, int64_t rows, int K, cudaStream_t st) {
+  constexpr int RPB = 8 / WPR;
+  quant_h64_kernel<T, IPW, WPR, ROTATE>
+      <<<(unsigned)((rows + RPB - 1) / RPB), 256, 0, st>>>((const T*)x, sign, q, scale, rows, K);
+}
+
+template <typename T, int WPR, bool ROTATE>
+static void launch_w(int ipw, const void* x, const float* sign, int8_t* q, float* scale, int64_t rows, int K,
+                     cudaStream_t st) {
+  switch (ipw) {
+    case 1: launch_q<T, 1, WPR, ROTATE>(x, sign, q, scale, rows, K, st); break;
+    case 2: launch_q<T, 2, WPR, ROTATE>(x, sign, q, scale, rows, K, st); break;
+    case 3: launch_q<T, 3, WPR, ROTATE>(x, sign, q, scale, rows, K, st); break;
+    case 4: launch_q<T, 4, WPR, ROTATE>(x, sign, q, scale, rows, K, st); break;
+    default: launch_q<T, 5, WPR, ROTATE>(x, sign, q, scale, rows, K, st); break;
   }
 }
 
 template <typename T, bool ROTATE>
 static int launch_quant(const void* x, const float* sign, int8_t* q, float* scale, int64_t rows, int K,
                         cudaStream_t st) {
-  const dim3 grid((unsigned)((rows + 7) / 8)), block(256);
-  switch ((K + 255) / 256) {
-#define HI3D_Q(n) \
-  case n: quant_h64_kernel<T, n, ROTATE><<<grid, block, 0, st>>>((const T*)x, sign, q, scale, rows, K); break;
-    HI3D_Q(1) HI3D_Q(2) HI3D_Q(3) HI3D_Q(4) HI3D_Q(5) HI3D_Q(6) HI3D_Q(7) HI3D_Q(8)
-    HI3D_Q(9) HI3D_Q(10) HI3D_Q(11) HI3D_Q(12) HI3D_Q(13) HI3D_Q(14) HI3D_Q(15) HI3D_Q(16)
-    HI3D_Q(17) HI3D_Q(18) HI3D_Q(19) HI3D_Q(20) HI3D_Q(21) HI3D_Q(22) HI3D_Q(23) HI3D_Q(24)
-    HI3D_Q(25) HI3D_Q(26) HI3D_Q(27) HI3D_Q(28) HI3D_Q(29) HI3D_Q(30) HI3D_Q(31) HI3D_Q(32)
-    HI3D_Q(33) HI3D_Q(34)
-#undef HI3D_Q
-    default:
-      return set_error(HI3D_ERR_UNSUPPORTED, "quantize_act_i8: width %d above 8704 not supported", K);
+  const int chunks = (K + 255) / 256;  // 256-element chunks per row
+  if (chunks > 40) return set_error(HI3D_ERR_UNSUPPORTED, "quantize_act_i8: width %d above 10240 not supported", K);
+  const int wpr = chunks <= 4 ? 1 : chunks <= 8 ? 2 : chunks <= 16 ? 4 : 8;
+  const int ipw = (chunks + wpr - 1) / wpr;
+  switch (wpr) {
+    case 1: launch_w<T, 1, ROTATE>(ipw, x, sign, q, scale, rows, K, st); break;
+    case 2: launch_w<T, 2, ROTATE>(ipw, x, sign, q, scale, rows, K, st); break;
+    case 4: launch_w<T, 4, ROTATE>(ipw, x, sign, q, scale, rows, K, st); break;
+    default: launch_w<T, 8, ROTATE>(ipw, x, sign, q, scale, rows, K, st); break;
   }
   return check_launch("quantize_act_i8");
 }
