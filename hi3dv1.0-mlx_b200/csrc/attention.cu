@@ -1,22 +1,28 @@
 // Flash attention forward for sm_100a: tcgen05 MMAs with TMEM accumulators,
-// TMA-fed K/V ring, two 128-row query tiles per CTA so the tensor core works
-// on one tile while the softmax warps process the other.
+// TMA-fed K/V ring, two 128-row query tiles per CTA whose softmax warps run
+// continuously while the tensor core computes the other products.
 //
 // Numerics (attention.py:84-233 of the reference): S = Q K^T in fp32; online
 // softmax in the exp2 domain (scale * log2 e folded into one multiplier);
 // P = exp2(s - m) summed unrounded into l, rounded to the I/O type for the
 // P V product, which accumulates in fp32; output O / l rounded once.
 //
-// CTA layout (320 threads):
+// CTA layout (352 threads):
 //   warp 0      TMA producer (one lane): Q tiles once, then K/V blocks into
 //               an NST-stage ring
-//   warp 1      MMA issuer (one lane); also owns the TMEM allocation
+//   warp 1      MMA issuer of query tile 0 (one lane); owns the TMEM allocation
+//   warp 10     MMA issuer of query tile 1 (one lane)
 //   warps 2-5   softmax + O correction + epilogue of query tile 0
 //   warps 6-9   the same for query tile 1
 // A warp reaches TMEM lanes 32*(warp % 4) .. +31, so each group of four
 // consecutive warps covers the 128 rows of its tile.
 // TMEM (512 columns): tile i at column 256*i holds S [BK cols, fp32],
 // P [BK/2 cols, packed 16-bit pairs] and O [D cols, fp32].
+// Per tile and key block j: the softmax signals s_free once S(j) is in its
+// registers, and the tile's issuer immediately computes S(j+1) into the same
+// columns; P(j) V is issued when the softmax publishes P(j) (p_full).  Each
+// tile's softmax therefore finds its next scores ready, and the two issuers
+// wait only on their own tile, so neither tile's P V queues behind the other.
 #include <type_traits>
 
 #include "abi.h"
@@ -25,7 +31,7 @@
 namespace hi3d {
 namespace attn {
 
-constexpr int kThreads = 320;
+constexpr int kThreads = 352;
 constexpr int kRowsPerTile = 128;
 // Exponentials per 16-pair chunk of a score row evaluated by the FMA-pipe
 // polynomial (the rest use the MUFU ex2 unit), balancing the two pipes.
@@ -69,6 +75,7 @@ struct Barriers {
   uint64_t v_full[4];
   uint64_t kv_empty[4];
   uint64_t s_full[2];
+  uint64_t s_free[2];  // the tile's softmax has read its scores into registers
   uint64_t p_full[2];
   uint64_t o_done[2];
   uint32_t tmem_base;
@@ -115,10 +122,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int s = 0; s < C::NST; ++s) {
       mbar_init(&bar->k_full[s], 1);
       mbar_init(&bar->v_full[s], 1);
-      mbar_init(&bar->kv_empty[s], 1);
+      mbar_init(&bar->kv_empty[s], 2);  // released by both tiles' MMA issuers
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bar->s_full[i], 1);
+      mbar_init(&bar->s_free[i], 4);  // one arrival per softmax warp of the tile
       mbar_init(&bar->p_full[i], kRowsPerTile);
       mbar_init(&bar->o_done[i], 1);
     }
@@ -170,11 +178,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    // Order per block j: PV_0(j), S_0(j+1), PV_1(j), S_1(j+1).  S_i(j+1) is
-    // issued as soon as softmax i has published P_i(j) (it has read S_i(j) by
-    // then), so one tile's softmax overlaps the other tile's MMAs.
+  } else if (warp == 1 || warp == 10) {
+    // ------------------------------------------------------------ MMA issuers
+    // Warp 1 issues tile 0's MMAs, warp 10 tile 1's: each waits (suspended)
+    // only on its own tile's events, so neither tile's P V queues behind the
+    // other tile's softmax.
     if (lane == 0) {
       constexpr uint32_t fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
       constexpr uint32_t idesc_s = make_idesc(1, fmt, 0, 0, kRowsPerTile, C::BK);
@@ -195,29 +203,32 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_commit(&bar->s_full[i]);
       };
+      const int i = warp == 1 ? 0 : 1;
       bool ok = mbar_wait(&bar->q_full, 0, abort, 10) && mbar_wait(&bar->k_full[0], 0, abort, 11);
       if (ok) {
         tc_fence_after();
-        issue_s(0, 0);
-        issue_s(1, 0);
+        issue_s(i, 0);
       }
+      // Per block j: S_i(j+1) as soon as softmax i has read S_i(j) (s_free), then
+      // P_i(j) V once it has published P_i(j).
       for (int j = 0; ok && j < nblk; ++j) {
         const int s = j % C::NST, n = j / C::NST;
         const int s1 = (j + 1) % C::NST, n1 = (j + 1) / C::NST;
-        if (!(ok = mbar_wait(&bar->v_full[s], n & 1, abort, 13))) break;
-        if (j + 1 < nblk && !(ok = mbar_wait(&bar->k_full[s1], n1 & 1, abort, 11))) break;
-        for (int i = 0; i < 2; ++i) {
-          if (!(ok = mbar_wait(&bar->p_full[i], j & 1, abort, 14))) break;
+        if (j + 1 < nblk) {
+          if (!(ok = mbar_wait(&bar->k_full[s1], n1 & 1, abort, 11))) break;
+          if (!(ok = mbar_wait(&bar->s_free[i], j & 1, abort, 15))) break;
           tc_fence_after();
-          const uint64_t dVs = dV + (uint64_t)((s * C::KV_STAGE) >> 4);
-          const uint32_t dO = tmem + 256 * i + C::O_COL, aP = tmem + 256 * i + C::P_COL;
-#pragma unroll
-          for (int ks = 0; ks < C::BK / 16; ++ks)
-            mma_f16_ts(dO, aP + ks * 8, dVs + (uint64_t)(ks * (2048 >> 4)), idesc_pv, (j > 0 || ks > 0) ? 1u : 0u);
-          tc_commit(&bar->o_done[i]);
-          if (j + 1 < nblk) issue_s(i, s1);
+          issue_s(i, s1);
         }
-        if (!ok) break;
+        if (!(ok = mbar_wait(&bar->v_full[s], n & 1, abort, 13))) break;
+        if (!(ok = mbar_wait(&bar->p_full[i], j & 1, abort, 14))) break;
+        tc_fence_after();
+        const uint64_t dVs = dV + (uint64_t)((s * C::KV_STAGE) >> 4);
+        const uint32_t dO = tmem + 256 * i + C::O_COL, aP = tmem + 256 * i + C::P_COL;
+#pragma unroll
+        for (int ks = 0; ks < C::BK / 16; ++ks)
+          mma_f16_ts(dO, aP + ks * 8, dVs + (uint64_t)(ks * (2048 >> 4)), idesc_pv, (j > 0 || ks > 0) ? 1u : 0u);
+        tc_commit(&bar->o_done[i]);
         // Release the stage only when a later block will be loaded into it, so
         // that every commit has a waiter before the CTA exits.
         if (j + C::NST < nblk) tc_commit(&bar->kv_empty[s]);
@@ -243,6 +254,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int c = 0; c < C::BK / 32; ++c) tmem_ld32(tS + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[c * 32]));
       tmem_wait_ld();
+      // scores are in registers: the next block's S may overwrite them
+      if (j + 1 < nblk) {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar->s_free[i]);
+      }
 
       const int klim = (int)(k_len - (int64_t)j * C::BK);  // valid keys in this block
       if (klim < C::BK) {
@@ -267,8 +284,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       // P and in fp32 l), and O needs no correction.  O / l is unchanged.
       const float m_blk = mx * scale2;
       const bool grow = m_blk > m_run + kRescaleLog2;
+      const bool warp_grow = __any_sync(0xffffffffu, grow);
       const float m_new = grow ? m_blk : m_run;
-      const float alpha = grow ? ex2_approx(m_run - m_new) : 1.0f;
+      // the correction factor needs the MUFU unit only in the rare blocks where
+      // a row of this warp moves its maximum
+      float alpha = 1.0f;
+      if (warp_grow) alpha = grow ? ex2_approx(m_run - m_new) : 1.0f;
       const uint64_t negm = f2_pack(-m_new, -m_new);
       uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};  // four independent packed row-sum chains
 #pragma unroll
@@ -301,7 +322,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (!ok) break;
       // O *= alpha, only when a row of this warp moved its maximum
-      if (j > 0 && __any_sync(0xffffffffu, grow)) {
+      if (j > 0 && warp_grow) {
 #pragma unroll
         for (int oc = 0; oc < (D + 31) / 32; ++oc) {
           uint32_t r[32];
@@ -312,14 +333,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_st32(tO + oc * 32, r);
         }
       }
-      float a0, a1, a2, a3;
-      f2_unpack(f2_add(acc[0], acc[1]), a0, a1);
-      f2_unpack(f2_add(acc[2], acc[3]), a2, a3);
-      l_run = l_run * alpha + ((a0 + a1) + (a2 + a3));
       m_run = m_new;
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&bar->p_full[i]);
+      // the row sum is not needed by P V: update it after publishing P
+      float a0, a1, a2, a3;
+      f2_unpack(f2_add(acc[0], acc[1]), a0, a1);
+      f2_unpack(f2_add(acc[2], acc[3]), a2, a3);
+      l_run = l_run * alpha + ((a0 + a1) + (a2 + a3));
     }
     // ---- epilogue: O / l -> out[row, h*D + d]
     if (ok && mbar_wait(&bar->o_done[i], (nblk - 1) & 1, abort, 22)) {
