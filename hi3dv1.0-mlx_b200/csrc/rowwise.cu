@@ -174,21 +174,28 @@ static int dispatch_ln(const void* x, void* out, int64_t rows, int C, float eps,
 }
 
 // ---------------------------------------------------------------------------
-// RoPE + QK RMS norm + split.  A group of G = D/8 lanes (rounded up to a power
-// of two) handles one (row, part, head); each active lane owns 8 consecutive
-// channels = 4 rotation pairs.  Norm reduction by xor-shuffles in the group.
+// RoPE + QK RMS norm + split.  A group of G lanes handles one (row, part,
+// head); each active lane owns 8 W consecutive channels (W 16-byte vectors,
+// 4 W rotation pairs).  Norm reduction by xor-shuffles in the group.
 // kernels.py:22-57 semantics: re = x0 c - x1 s, im = x0 s + x1 c (fp32);
-// nrm = max(sqrt(sum re^2 + im^2), 1e-12); y = re / nrm * g * sqrt(D).
+// nrm = max(sqrt(sum re^2 + im^2), 1e-12); y = re / nrm * g * sqrt(D), the
+// division taken once per head as f = sqrt(D) / nrm (y = re * f * g).
 // ---------------------------------------------------------------------------
-template <typename T, int D>
+// lanes per (row, part, head): D / (8 W) data lanes rounded up to a power of two (>= 2)
+__host__ __device__ constexpr int rope_group(int D, int W) {
+  return D / (8 * W) <= 2 ? 2 : (D / (8 * W) <= 4 ? 4 : (D / (8 * W) <= 8 ? 8 : 16));
+}
+
+template <typename T, int D, int W>
 __global__ void __launch_bounds__(1024) qkv_rope_rms_kernel(const T* __restrict__ qkv, const float* __restrict__ cosv,
                                                             const float* __restrict__ sinv,
                                                             const float* __restrict__ gq,
                                                             const float* __restrict__ gk, T* __restrict__ q,
                                                             T* __restrict__ k, T* __restrict__ v, int N, int H,
                                                             int token_major) {
-  constexpr int ACTIVE = D / 8;
-  constexpr int G = ACTIVE <= 8 ? 8 : (ACTIVE <= 16 ? 16 : 32);
+  constexpr int CH = 8 * W;        // channels per lane (W 16-byte vectors)
+  constexpr int ACTIVE = D / CH;   // lanes per (row, part, head) that hold data
+  constexpr int G = rope_group(D, W);
   const int lane = threadIdx.x & 31;
   const int sub = lane % G;
   const int m = blockIdx.x;  // token row of the [B*N, 3*H*D] projection
@@ -198,6 +205,7 @@ __global__ void __launch_bounds__(1024) qkv_rope_rms_kernel(const T* __restrict_
   const T* row = qkv + (int64_t)m * units * D;
   const float* cs_row = cosv + (int64_t)n * (D / 2);
   const float* sn_row = sinv + (int64_t)n * (D / 2);
+  const int c0 = sub * CH;
   // The loop bound is uniform across the block, so every lane reaches every
   // full-mask shuffle; lanes past the last unit contribute zero.
   for (int u0 = 0; u0 < units; u0 += per_block) {
@@ -205,22 +213,30 @@ __global__ void __launch_bounds__(1024) qkv_rope_rms_kernel(const T* __restrict_
     const bool in_range = u < units;
     const bool valid = in_range && sub < ACTIVE;
     const int part = in_range ? u / H : 0, h = in_range ? u - (u / H) * H : 0;
-    const int c0 = sub * 8;
-    Vec8 raw = {};
-    if (valid) raw = *reinterpret_cast<const Vec8*>(row + (int64_t)u * D + c0);  // ((m*3+part)*H+h)*D, kernels.py:31
-    float x[8];
-    unpack8<T>(raw, x);
-    float r[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    float ss = 0.f;
-    if (valid && part != 2) {
-      const float4 c4 = *reinterpret_cast<const float4*>(cs_row + c0 / 2);
-      const float4 s4 = *reinterpret_cast<const float4*>(sn_row + c0 / 2);
-      const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, sv[4] = {s4.x, s4.y, s4.z, s4.w};
+    Vec8 raw[W];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        r[2 * i] = x[2 * i] * cc[i] - x[2 * i + 1] * sv[i];
-        r[2 * i + 1] = x[2 * i] * sv[i] + x[2 * i + 1] * cc[i];
-        ss += r[2 * i] * r[2 * i] + r[2 * i + 1] * r[2 * i + 1];
+    for (int w = 0; w < W; ++w) {
+      raw[w] = Vec8{};
+      if (valid) raw[w] = *reinterpret_cast<const Vec8*>(row + (int64_t)u * D + c0 + 8 * w);  // ((m*3+part)*H+h)*D, kernels.py:31
+    }
+    float rr[CH];
+    float ss = 0.f;
+#pragma unroll
+    for (int w = 0; w < W; ++w) {
+      float x[8];
+      unpack8<T>(raw[w], x);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) rr[8 * w + i] = 0.f;
+      if (valid && part != 2) {
+        const float4 c4 = *reinterpret_cast<const float4*>(cs_row + (c0 + 8 * w) / 2);
+        const float4 s4 = *reinterpret_cast<const float4*>(sn_row + (c0 + 8 * w) / 2);
+        const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, sv[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          rr[8 * w + 2 * i] = x[2 * i] * cc[i] - x[2 * i + 1] * sv[i];
+          rr[8 * w + 2 * i + 1] = x[2 * i] * sv[i] + x[2 * i + 1] * cc[i];
+          ss += rr[8 * w + 2 * i] * rr[8 * w + 2 * i] + rr[8 * w + 2 * i + 1] * rr[8 * w + 2 * i + 1];
+        }
       }
     }
 #pragma unroll
@@ -228,19 +244,24 @@ __global__ void __launch_bounds__(1024) qkv_rope_rms_kernel(const T* __restrict_
     if (!valid) continue;
     const int64_t dst_off = token_major ? (((int64_t)b * N + n) * H + h) * D : (((int64_t)b * H + h) * N + n) * D;
     if (part == 2) {
-      *reinterpret_cast<Vec8*>(v + dst_off + c0) = raw;
+#pragma unroll
+      for (int w = 0; w < W; ++w) *reinterpret_cast<Vec8*>(v + dst_off + c0 + 8 * w) = raw[w];
       continue;
     }
-    const float nrm = fmaxf(sqrtf(ss), 1e-12f);
-    const float scale = sqrtf((float)D);
+    // y = re / nrm * g * sqrt(D), with one division per head: f = sqrt(D) / nrm
+    const float f = __fdiv_rn(sqrtf((float)D), fmaxf(sqrtf(ss), 1e-12f));
     const float* g = (part == 0 ? gq : gk) + h * D + c0;
-    const float4 g0 = *reinterpret_cast<const float4*>(g), g1 = *reinterpret_cast<const float4*>(g + 4);
-    const float gg[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
-    Vec8 o;
+    T* dst = (part == 0 ? q : k) + dst_off + c0;
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
-      o.w[i] = Cvt<T>::pack2(r[2 * i] / nrm * gg[2 * i] * scale, r[2 * i + 1] / nrm * gg[2 * i + 1] * scale);
-    *reinterpret_cast<Vec8*>((part == 0 ? q : k) + dst_off + c0) = o;
+    for (int w = 0; w < W; ++w) {
+      const float4 g0 = *reinterpret_cast<const float4*>(g + 8 * w), g1 = *reinterpret_cast<const float4*>(g + 8 * w + 4);
+      const float gg[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+      Vec8 o;
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        o.w[i] = Cvt<T>::pack2(rr[8 * w + 2 * i] * f * gg[2 * i], rr[8 * w + 2 * i + 1] * f * gg[2 * i + 1]);
+      *reinterpret_cast<Vec8*>(dst + 8 * w) = o;
+    }
   }
 }
 
@@ -252,14 +273,18 @@ static int dispatch_rope(const void* qkv, const float* c, const float* s, const 
     const int t = ((3 * H * G + 31) / 32) * 32;
     return t > 1024 ? 1024 : t;
   };
-#define HI3D_ROPE(DD, GG)                                                                                   \
-  qkv_rope_rms_kernel<T, DD><<<(unsigned)M, threads_for(GG), 0, st>>>((const T*)qkv, c, s, gq, gk, (T*)q, (T*)k, \
-                                                                      (T*)v, (int)N, H, tm)
+#ifndef HI3D_ROPE_VECS
+#define HI3D_ROPE_VECS 2
+#endif
+  constexpr int W = HI3D_ROPE_VECS;  // 16-byte vectors per lane
+#define HI3D_ROPE(DD)                                                                                      \
+  qkv_rope_rms_kernel<T, DD, W><<<(unsigned)M, threads_for(rope_group(DD, W)), 0, st>>>((const T*)qkv, c, s, gq, gk, (T*)q, (T*)k, \
+                                                                         (T*)v, (int)N, H, tm)
   switch (D) {
-    case 32: HI3D_ROPE(32, 8); break;
-    case 64: HI3D_ROPE(64, 8); break;
-    case 96: HI3D_ROPE(96, 16); break;
-    case 128: HI3D_ROPE(128, 16); break;
+    case 32: HI3D_ROPE(32); break;
+    case 64: HI3D_ROPE(64); break;
+    case 96: HI3D_ROPE(96); break;
+    case 128: HI3D_ROPE(128); break;
     default:
       return set_error(HI3D_ERR_UNSUPPORTED, "qkv_rope_rms: head_dim %d not supported (32, 64, 96, 128)", D);
   }
