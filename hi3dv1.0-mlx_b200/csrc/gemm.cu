@@ -33,10 +33,11 @@ constexpr int A_STAGE = BM * BKB;
 constexpr int B_STAGE = BN * BKB;
 constexpr int EPI_WARPS = 8;
 constexpr int STAGE_BYTES = 32 * 64;  // per epilogue warp: 32 rows x 32 16-bit columns
-constexpr int SMEM = NST * (A_STAGE + B_STAGE) + EPI_WARPS * (STAGE_BYTES + 256 * 4) + 1024 + 256;
+constexpr int VEC = 384;  // per epilogue warp: bias, weight scales, QK-norm gains of its 128 columns
+constexpr int SMEM = NST * (A_STAGE + B_STAGE) + EPI_WARPS * (STAGE_BYTES + VEC * 4) + 1024 + 256;
 
 enum Kind { KIND_F16 = 0, KIND_BF16 = 1, KIND_I8 = 2 };
-enum Epi { EPI_STORE = 0, EPI_GELU = 1, EPI_RESIDUAL = 2 };
+enum Epi { EPI_STORE = 0, EPI_GELU = 1, EPI_RESIDUAL = 2, EPI_QKV_ROPE = 3 };
 
 struct Params {
   void* out;          // [M, ldo] output (or the residual stream for EPI_RESIDUAL)
@@ -49,6 +50,16 @@ struct Params {
   int M, N, K;        // K in elements
   int tiles_m, tiles_n;
   int vec;            // 1 when output rows (and gate rows) allow 16-byte accesses
+  // EPI_QKV_ROPE: the fused projection [B*N, 3*H*D] is split into q, k, v with
+  // RoPE + QK RMS norm on q and k (head_dim 64)
+  const float* cosv;  // [N, D/2]
+  const float* sinv;  // [N, D/2]
+  const float* gq;    // [H, D]
+  const float* gk;    // [H, D]
+  void* q;
+  void* k;
+  void* v;
+  int seq_n, heads, token_major;
 };
 
 struct Barriers {
@@ -93,7 +104,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sB = smem + NST * A_STAGE;
   uint8_t* sStage = sB + NST * B_STAGE;
   float* sVec = reinterpret_cast<float*>(sStage + EPI_WARPS * STAGE_BYTES);
-  Barriers* bar = reinterpret_cast<Barriers*>(sVec + EPI_WARPS * 256);
+  Barriers* bar = reinterpret_cast<Barriers*>(sVec + EPI_WARPS * VEC);
   constexpr int ESZ = KIND == KIND_I8 ? 1 : 2;
   constexpr int BKE = BKB / ESZ;  // K elements per stage
 
@@ -192,7 +203,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // accumulator wait.
     const int q = warp & 3, h = (warp - 2) >> 2, ew = warp - 2;
     uint8_t* stage = sStage + ew * STAGE_BYTES;
-    float* vec = sVec + ew * 256;  // [0, 128): bias of this warp's columns; [128, 256): weight scales
+    // [0, 128): bias of this warp's columns; [128, 256): weight scales; [256, 384): QK-norm gains
+    float* vec = sVec + ew * VEC;
     const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
     constexpr bool kRaw = std::is_same<OutT, int32_t>::value;
     // Residual rows of this warp's strip, [chunk][row group]: loaded for the first
@@ -215,6 +227,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           vec[lane * 4 + e] = b;
           vec[128 + lane * 4 + e] = sw;
+          if (EPI == EPI_QKV_ROPE) {
+            // gain of channel nn: part = nn / (H D) (q, k or v), head channel nn % (H D)
+            const int hd = p.heads * 64, part = nn / hd;
+            vec[256 + lane * 4 + e] = nn < p.N && part < 2 ? (part == 0 ? p.gq : p.gk)[nn - part * hd] : 1.0f;
+          }
         }
       }
       if (EPI == EPI_RESIDUAL && local == 0) {
@@ -227,106 +244,193 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int mr = m0 + lane;  // phase-1 row
       float sa = 1.0f;
       if (KIND == KIND_I8 && mr < p.M && !kRaw) sa = p.sa[mr];
+      if constexpr (EPI == EPI_QKV_ROPE && !kRaw) {
+        // Two 64-channel heads per warp strip.  Phase 1 (thread = row): the
+        // projection output y = round(acc [* sa * sw] + bias) exactly as the
+        // store epilogue writes it, then for q and k heads RoPE on adjacent
+        // pairs and the RMS norm in fp32 (re = y0 c - y1 s, im = y0 s + y1 c,
+        // out = re * (sqrt(64) / max(|r|, 1e-12)) * g); v heads pass through.
+        // Phase 2 stores each 32-channel half through the staging tile into
+        // q/k/v [B, H, N, 64] (or token-major [B, N, H, 64]).
+        const int hd = p.heads * 64;
+        const int tok = mr < p.M ? mr : 0;
+        const int tb = tok / p.seq_n, tn = tok - tb * p.seq_n;
+#pragma unroll 1
+        for (int hh = 0; hh < 2; ++hh) {
+          const int col0 = nh + hh * 64;  // first channel of this head in the projection
+          const int part = col0 / hd, head = (col0 - part * hd) >> 6;
+          float yv[64];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
-        tmem_ld32(tmem + lane_addr + acc * BN + h * 128 + c * 32, v);
-        tmem_wait_ld();
-        const int nb = nh + c * 32;
-        if constexpr (kRaw) {
-          // raw exact int32 accumulators (verification / custom dequantisation), thread = row
-          OutT* orow = reinterpret_cast<OutT*>(p.out) + (int64_t)mr * p.ldo;
-          if (mr < p.M) {
+          for (int c = 0; c < 2; ++c) {
+            uint32_t v[32];
+            tmem_ld32(tmem + lane_addr + acc * BN + h * 128 + hh * 64 + c * 32, v);
+            tmem_wait_ld();
 #pragma unroll
-            for (int e = 0; e < 32; e += 8) {
-              const int n = nb + e;
-              if (n >= p.N) break;
-              if (p.vec && n + 8 <= p.N) {
-                *reinterpret_cast<uint4*>(orow + n) = make_uint4(v[e], v[e + 1], v[e + 2], v[e + 3]);
-                *reinterpret_cast<uint4*>(orow + n + 4) = make_uint4(v[e + 4], v[e + 5], v[e + 6], v[e + 7]);
-              } else {
-                for (int qq = 0; qq < 8 && n + qq < p.N; ++qq) orow[n + qq] = (int32_t)v[e + qq];
-              }
-            }
-          }
-          continue;
-        } else {
-          // phase 1
-#pragma unroll
-          for (int e = 0; e < 32; e += 8) {
-            float y[8];
-#pragma unroll
-            for (int qq = 0; qq < 8; ++qq) {
-              const int col = c * 32 + e + qq;
+            for (int e = 0; e < 32; ++e) {
+              const int col = hh * 64 + c * 32 + e;
               float t;
               if (KIND == KIND_I8)
-                t = __fmul_rn(__fmul_rn(__int2float_rn((int)v[e + qq]), sa), vec[128 + col]);
+                t = __fmul_rn(__fmul_rn(__int2float_rn((int)v[e]), sa), vec[128 + col]);
               else
-                t = __uint_as_float(v[e + qq]);
+                t = __uint_as_float(v[e]);
               if (p.bias) t = __fadd_rn(t, vec[col]);
-              y[qq] = Cvt<OutT>::to_f(Cvt<OutT>::from_f(t));  // round to the output type
-              if (EPI == EPI_GELU) y[qq] = gelu_tanh_f<OutT>(y[qq]);
+              yv[c * 32 + e] = Cvt<OutT>::to_f(Cvt<OutT>::from_f(t));
             }
-            uint4 w;
-            w.x = Cvt<OutT>::pack2(y[0], y[1]);
-            w.y = Cvt<OutT>::pack2(y[2], y[3]);
-            w.z = Cvt<OutT>::pack2(y[4], y[5]);
-            w.w = Cvt<OutT>::pack2(y[6], y[7]);
-            const int j = e >> 3;
-            *reinterpret_cast<uint4*>(stage + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) = w;
           }
-          __syncwarp();
-          // phase 2
+          uint32_t outw[32];  // 64 rounded outputs as 16-bit pairs
+          if (part < 2) {
+            const float4* cs4 = reinterpret_cast<const float4*>(p.cosv + (int64_t)tn * 32);
+            const float4* sn4 = reinterpret_cast<const float4*>(p.sinv + (int64_t)tn * 32);
+            float ss = 0.f;
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int rl = i * 8 + (lane >> 2), j = lane & 3;
-            const int m = m0 + rl, n = nb + j * 8;
-            const uint4 yv = *reinterpret_cast<const uint4*>(stage + rl * 64 + ((j ^ ((rl >> 1) & 3)) << 4));
-            if (m >= p.M || n >= p.N) continue;
-            OutT* orow = reinterpret_cast<OutT*>(p.out) + (int64_t)m * p.ldo;
-            const OutT* ya = reinterpret_cast<const OutT*>(&yv);
-            const OutT* grow = nullptr;
-            if (EPI == EPI_RESIDUAL && p.gate)
-              grow = reinterpret_cast<const OutT*>(p.gate) + (m / p.rows_per_batch) * p.gate_stride;
-            if (p.vec && n + 8 <= p.N) {
-              if constexpr (EPI == EPI_RESIDUAL) {
-                const uint4 gv = grow ? __ldg(reinterpret_cast<const uint4*>(grow + n)) : make_uint4(0, 0, 0, 0);
-                const OutT* xa = reinterpret_cast<const OutT*>(&res[c][i]);
-                const OutT* ga = reinterpret_cast<const OutT*>(&gv);
-                float o[8];
+            for (int i4 = 0; i4 < 8; ++i4) {
+              const float4 c4 = __ldg(cs4 + i4), s4 = __ldg(sn4 + i4);
+              const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, sv[4] = {s4.x, s4.y, s4.z, s4.w};
 #pragma unroll
-                for (int qq = 0; qq < 8; ++qq) {
-                  float g = Cvt<OutT>::to_f(ya[qq]);
-                  if (grow) g = Cvt<OutT>::to_f(Cvt<OutT>::from_f(__fmul_rn(g, Cvt<OutT>::to_f(ga[qq]))));
-                  o[qq] = __fadd_rn(Cvt<OutT>::to_f(xa[qq]), g);
-                }
-                uint4 w;
-                w.x = Cvt<OutT>::pack2(o[0], o[1]);
-                w.y = Cvt<OutT>::pack2(o[2], o[3]);
-                w.z = Cvt<OutT>::pack2(o[4], o[5]);
-                w.w = Cvt<OutT>::pack2(o[6], o[7]);
-                *reinterpret_cast<uint4*>(orow + n) = w;
-              } else {
-                *reinterpret_cast<uint4*>(orow + n) = yv;
+              for (int i = 0; i < 4; ++i) {
+                const int pi = i4 * 4 + i;
+                const float x0 = yv[2 * pi], x1 = yv[2 * pi + 1];
+                const float re = x0 * cc[i] - x1 * sv[i], im = x0 * sv[i] + x1 * cc[i];
+                yv[2 * pi] = re;
+                yv[2 * pi + 1] = im;
+                ss += re * re + im * im;
               }
-            } else {
-              for (int qq = 0; qq < 8 && n + qq < p.N; ++qq) {
-                if (EPI == EPI_RESIDUAL) {
-                  float g = Cvt<OutT>::to_f(ya[qq]);
-                  if (grow) g = Cvt<OutT>::to_f(Cvt<OutT>::from_f(__fmul_rn(g, Cvt<OutT>::to_f(grow[n + qq]))));
-                  orow[n + qq] = Cvt<OutT>::from_f(__fadd_rn(Cvt<OutT>::to_f(orow[n + qq]), g));
+            }
+            const float f = __fdiv_rn(8.0f, fmaxf(sqrtf(ss), 1e-12f));  // sqrt(64) / nrm
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              outw[i] = Cvt<OutT>::pack2(yv[2 * i] * f * vec[256 + hh * 64 + 2 * i],
+                                         yv[2 * i + 1] * f * vec[256 + hh * 64 + 2 * i + 1]);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) outw[i] = Cvt<OutT>::pack2(yv[2 * i], yv[2 * i + 1]);
+          }
+          OutT* dst_base = reinterpret_cast<OutT*>(part == 0 ? p.q : part == 1 ? p.k : p.v);
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              *reinterpret_cast<uint4*>(stage + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) =
+                  make_uint4(outw[half * 16 + 4 * j], outw[half * 16 + 4 * j + 1], outw[half * 16 + 4 * j + 2],
+                             outw[half * 16 + 4 * j + 3]);
+            __syncwarp();
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int rl = i * 8 + (lane >> 2), j = lane & 3;
+              const int m = m0 + rl;
+              const uint4 yq = *reinterpret_cast<const uint4*>(stage + rl * 64 + ((j ^ ((rl >> 1) & 3)) << 4));
+              if (m < p.M) {
+                const int b2 = m / p.seq_n, n2 = m - b2 * p.seq_n;
+                const int64_t row = p.token_major ? ((int64_t)b2 * p.seq_n + n2) * p.heads + head
+                                                  : ((int64_t)b2 * p.heads + head) * p.seq_n + n2;
+                *reinterpret_cast<uint4*>(dst_base + row * 64 + half * 32 + j * 8) = yq;
+              }
+            }
+            __syncwarp();
+          }
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t v[32];
+          tmem_ld32(tmem + lane_addr + acc * BN + h * 128 + c * 32, v);
+          tmem_wait_ld();
+          const int nb = nh + c * 32;
+          if constexpr (kRaw) {
+            // raw exact int32 accumulators (verification / custom dequantisation), thread = row
+            OutT* orow = reinterpret_cast<OutT*>(p.out) + (int64_t)mr * p.ldo;
+            if (mr < p.M) {
+#pragma unroll
+              for (int e = 0; e < 32; e += 8) {
+                const int n = nb + e;
+                if (n >= p.N) break;
+                if (p.vec && n + 8 <= p.N) {
+                  *reinterpret_cast<uint4*>(orow + n) = make_uint4(v[e], v[e + 1], v[e + 2], v[e + 3]);
+                  *reinterpret_cast<uint4*>(orow + n + 4) = make_uint4(v[e + 4], v[e + 5], v[e + 6], v[e + 7]);
                 } else {
-                  orow[n + qq] = ya[qq];
+                  for (int qq = 0; qq < 8 && n + qq < p.N; ++qq) orow[n + qq] = (int32_t)v[e + qq];
                 }
               }
             }
-          }
-          __syncwarp();  // the staging tile is rewritten by the next chunk
-          if (EPI == EPI_RESIDUAL) {
-            const int nt = tile + gridDim.x;
-            if (nt < num_tiles)
-              prefetch_residual<OutT>(p, res[c], (nt / p.tiles_n) * BM + q * 32,
-                                      (nt % p.tiles_n) * BN + h * 128 + c * 32, lane);
+            continue;
+          } else {
+            // phase 1
+#pragma unroll
+            for (int e = 0; e < 32; e += 8) {
+              float y[8];
+#pragma unroll
+              for (int qq = 0; qq < 8; ++qq) {
+                const int col = c * 32 + e + qq;
+                float t;
+                if (KIND == KIND_I8)
+                  t = __fmul_rn(__fmul_rn(__int2float_rn((int)v[e + qq]), sa), vec[128 + col]);
+                else
+                  t = __uint_as_float(v[e + qq]);
+                if (p.bias) t = __fadd_rn(t, vec[col]);
+                y[qq] = Cvt<OutT>::to_f(Cvt<OutT>::from_f(t));  // round to the output type
+                if (EPI == EPI_GELU) y[qq] = gelu_tanh_f<OutT>(y[qq]);
+              }
+              uint4 w;
+              w.x = Cvt<OutT>::pack2(y[0], y[1]);
+              w.y = Cvt<OutT>::pack2(y[2], y[3]);
+              w.z = Cvt<OutT>::pack2(y[4], y[5]);
+              w.w = Cvt<OutT>::pack2(y[6], y[7]);
+              const int j = e >> 3;
+              *reinterpret_cast<uint4*>(stage + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) = w;
+            }
+            __syncwarp();
+            // phase 2
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int rl = i * 8 + (lane >> 2), j = lane & 3;
+              const int m = m0 + rl, n = nb + j * 8;
+              const uint4 yv = *reinterpret_cast<const uint4*>(stage + rl * 64 + ((j ^ ((rl >> 1) & 3)) << 4));
+              if (m >= p.M || n >= p.N) continue;
+              OutT* orow = reinterpret_cast<OutT*>(p.out) + (int64_t)m * p.ldo;
+              const OutT* ya = reinterpret_cast<const OutT*>(&yv);
+              const OutT* grow = nullptr;
+              if (EPI == EPI_RESIDUAL && p.gate)
+                grow = reinterpret_cast<const OutT*>(p.gate) + (m / p.rows_per_batch) * p.gate_stride;
+              if (p.vec && n + 8 <= p.N) {
+                if constexpr (EPI == EPI_RESIDUAL) {
+                  const uint4 gv = grow ? __ldg(reinterpret_cast<const uint4*>(grow + n)) : make_uint4(0, 0, 0, 0);
+                  const OutT* xa = reinterpret_cast<const OutT*>(&res[c][i]);
+                  const OutT* ga = reinterpret_cast<const OutT*>(&gv);
+                  float o[8];
+#pragma unroll
+                  for (int qq = 0; qq < 8; ++qq) {
+                    float g = Cvt<OutT>::to_f(ya[qq]);
+                    if (grow) g = Cvt<OutT>::to_f(Cvt<OutT>::from_f(__fmul_rn(g, Cvt<OutT>::to_f(ga[qq]))));
+                    o[qq] = __fadd_rn(Cvt<OutT>::to_f(xa[qq]), g);
+                  }
+                  uint4 w;
+                  w.x = Cvt<OutT>::pack2(o[0], o[1]);
+                  w.y = Cvt<OutT>::pack2(o[2], o[3]);
+                  w.z = Cvt<OutT>::pack2(o[4], o[5]);
+                  w.w = Cvt<OutT>::pack2(o[6], o[7]);
+                  *reinterpret_cast<uint4*>(orow + n) = w;
+                } else {
+                  *reinterpret_cast<uint4*>(orow + n) = yv;
+                }
+              } else {
+                for (int qq = 0; qq < 8 && n + qq < p.N; ++qq) {
+                  if (EPI == EPI_RESIDUAL) {
+                    float g = Cvt<OutT>::to_f(ya[qq]);
+                    if (grow) g = Cvt<OutT>::to_f(Cvt<OutT>::from_f(__fmul_rn(g, Cvt<OutT>::to_f(grow[n + qq]))));
+                    orow[n + qq] = Cvt<OutT>::from_f(__fadd_rn(Cvt<OutT>::to_f(orow[n + qq]), g));
+                  } else {
+                    orow[n + qq] = ya[qq];
+                  }
+                }
+              }
+            }
+            __syncwarp();  // the staging tile is rewritten by the next chunk
+            if (EPI == EPI_RESIDUAL) {
+              const int nt = tile + gridDim.x;
+              if (nt < num_tiles)
+                prefetch_residual<OutT>(p, res[c], (nt / p.tiles_n) * BM + q * 32,
+                                        (nt % p.tiles_n) * BN + h * 128 + c * 32, lane);
+            }
           }
         }
       }
@@ -398,6 +502,7 @@ static int dispatch_epi(int epi, const void* a, const void* w, int M, int N, int
     case gemm::EPI_STORE: return launch_gemm<KIND, gemm::EPI_STORE, OutT>(a, w, M, N, K, p, st);
     case gemm::EPI_GELU: return launch_gemm<KIND, gemm::EPI_GELU, OutT>(a, w, M, N, K, p, st);
     case gemm::EPI_RESIDUAL: return launch_gemm<KIND, gemm::EPI_RESIDUAL, OutT>(a, w, M, N, K, p, st);
+    case gemm::EPI_QKV_ROPE: return launch_gemm<KIND, gemm::EPI_QKV_ROPE, OutT>(a, w, M, N, K, p, st);
   }
   return set_error(HI3D_ERR_INVALID_ARGUMENT, "gemm: unknown epilogue %d", epi);
 }
@@ -473,4 +578,80 @@ extern "C" int hi3d_gemm(const void* a, const void* w, const void* bias, void* o
   if (dtype == HI3D_BF16)
     return dispatch_epi<gemm::KIND_BF16, __nv_bfloat16>(epilogue, a, w, (int)m, (int)n, (int)k, p, st);
   return set_error(HI3D_ERR_INVALID_ARGUMENT, "gemm: dtype must be f16 or bf16");
+}
+
+// ---------------------------------------------------------------------------
+// QKV projection with RoPE + QK RMS norm + head split in the epilogue
+// ---------------------------------------------------------------------------
+static int qkv_rope_params(const char* what, const void* a, const void* w, const void* cosv, const void* sinv,
+                           const float* gq, const float* gk, void* q, void* k, void* v, int64_t m, int64_t n_seq,
+                           int heads, int head_dim, int64_t kdim, int token_major, gemm::Params* p) {
+  if (!a || !w || !cosv || !sinv || !gq || !gk || !q || !k || !v)
+    return set_error(HI3D_ERR_INVALID_ARGUMENT, "%s: null pointer", what);
+  if (m < 0 || n_seq <= 0 || heads <= 0 || kdim <= 0 || m > 0x7fffffff || kdim > 0x7fffffff || m % n_seq)
+    return set_error(HI3D_ERR_INVALID_ARGUMENT, "%s: bad sizes (rows must be batch * n_seq)", what);
+  if (head_dim != 64 || (heads * 64) % gemm::BN)
+    return set_error(HI3D_ERR_UNSUPPORTED, "%s: needs head_dim 64 and heads * 64 divisible by %d", what, gemm::BN);
+  if (!aligned16(a) || !aligned16(w) || !aligned16(cosv) || !aligned16(sinv) || !aligned16(q) || !aligned16(k) ||
+      !aligned16(v))
+    return set_error(HI3D_ERR_INVALID_ARGUMENT, "%s: pointers must be 16-byte aligned", what);
+  *p = gemm::Params{};
+  p->out = q;
+  p->ldo = 3 * (int64_t)heads * 64;
+  p->rows_per_batch = m > 0 ? m : 1;
+  p->cosv = static_cast<const float*>(cosv);
+  p->sinv = static_cast<const float*>(sinv);
+  p->gq = gq;
+  p->gk = gk;
+  p->q = q;
+  p->k = k;
+  p->v = v;
+  p->seq_n = (int)n_seq;
+  p->heads = heads;
+  p->token_major = token_major ? 1 : 0;
+  return HI3D_OK;
+}
+
+extern "C" int hi3d_gemm_qkv_rope(const void* a, const void* w, const void* bias, const float* cosv,
+                                  const float* sinv, const float* gamma_q, const float* gamma_k, void* q, void* k,
+                                  void* v, int64_t m, int64_t n_seq, int heads, int head_dim, int64_t kdim,
+                                  int token_major, int dtype, void* stream) {
+  gemm::Params p;
+  int rc = qkv_rope_params("gemm_qkv_rope", a, w, cosv, sinv, gamma_q, gamma_k, q, k, v, m, n_seq, heads, head_dim,
+                           kdim, token_major, &p);
+  if (rc) return rc;
+  if (kdim % 8) return set_error(HI3D_ERR_INVALID_ARGUMENT, "gemm_qkv_rope: K must be a multiple of 8");
+  if (m == 0) return HI3D_OK;
+  p.bias = bias;
+  const int n = 3 * heads * 64;
+  cudaStream_t st = as_stream(stream);
+  if (dtype == HI3D_F16)
+    return launch_gemm<gemm::KIND_F16, gemm::EPI_QKV_ROPE, __half>(a, w, (int)m, n, (int)kdim, p, st);
+  if (dtype == HI3D_BF16)
+    return launch_gemm<gemm::KIND_BF16, gemm::EPI_QKV_ROPE, __nv_bfloat16>(a, w, (int)m, n, (int)kdim, p, st);
+  return set_error(HI3D_ERR_INVALID_ARGUMENT, "gemm_qkv_rope: dtype must be f16 or bf16");
+}
+
+extern "C" int hi3d_gemm_w8a8_qkv_rope(const int8_t* a, const int8_t* w, const float* sa, const float* sw,
+                                       const void* bias, const float* cosv, const float* sinv, const float* gamma_q,
+                                       const float* gamma_k, void* q, void* k, void* v, int64_t m, int64_t n_seq,
+                                       int heads, int head_dim, int64_t kdim, int token_major, int out_dtype,
+                                       void* stream) {
+  gemm::Params p;
+  int rc = qkv_rope_params("gemm_w8a8_qkv_rope", a, w, cosv, sinv, gamma_q, gamma_k, q, k, v, m, n_seq, heads,
+                           head_dim, kdim, token_major, &p);
+  if (rc) return rc;
+  if (!sa || !sw) return set_error(HI3D_ERR_INVALID_ARGUMENT, "gemm_w8a8_qkv_rope: scales are required");
+  if (kdim % 16) return set_error(HI3D_ERR_INVALID_ARGUMENT, "gemm_w8a8_qkv_rope: K must be a multiple of 16");
+  if (m == 0) return HI3D_OK;
+  p.bias = bias;
+  p.sa = sa;
+  p.sw = sw;
+  const int n = 3 * heads * 64;
+  cudaStream_t st = as_stream(stream);
+  if (out_dtype == HI3D_F16)
+    return launch_gemm<gemm::KIND_I8, gemm::EPI_QKV_ROPE, __half>(a, w, (int)m, n, (int)kdim, p, st);
+  if (out_dtype == HI3D_BF16)
+    return launch_gemm<gemm::KIND_I8, gemm::EPI_QKV_ROPE, __nv_bfloat16>(a, w, (int)m, n, (int)kdim, p, st);
+  return set_error(HI3D_ERR_INVALID_ARGUMENT, "gemm_w8a8_qkv_rope: out dtype must be f16 or bf16");
 }

@@ -15,7 +15,7 @@ import torch
 import torch.distributed as dist
 
 from . import attention, kernels
-from .transformer import _modulation, linear
+from .transformer import _modulation, linear, qkv_rope
 
 
 def shard_slice(total: int, rank: int, world: int) -> slice:
@@ -48,9 +48,7 @@ def block_forward_sharded(w: dict, x: torch.Tensor, mod: torch.Tensor, cos: torc
     shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp = _modulation(w, mod, c, dt)
 
     h = kernels.layer_norm_modulate(x, 1e-6, scale=scale_msa, shift=shift_msa)
-    qkv = linear(h, w, "self_attn.to_qkv")
-    q, k, v = kernels.qkv_rope_rms(qkv, cos, sin, w["self_attn.q_rms_norm.gamma"],
-                                   w["self_attn.k_rms_norm.gamma"], 1, heads, d, token_major=True)
+    q, k, v = qkv_rope(h, w, cos, sin, 1, heads, d, token_major=True)
     if kv_buffers is None:
         kv_buffers = tuple(torch.empty((world * t_local, heads, d), dtype=dt, device=x.device) for _ in range(2))
     k_all, v_all = kv_buffers

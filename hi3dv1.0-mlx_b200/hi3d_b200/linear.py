@@ -57,3 +57,54 @@ def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = No
                                _lib.ptr(g), rpb, gs, _lib.dtype_code(x), _lib.stream(x))
     _lib.check(rc, "linear")
     return out
+
+
+def qkv_rope_supported(heads: int, head_dim: int) -> bool:
+    """Whether :func:`linear_qkv_rope` handles this head layout (head dim 64, ``heads * 64``
+    a multiple of the 256-column GEMM tile)."""
+    return head_dim == 64 and (heads * 64) % 256 == 0
+
+
+def _qkv_rope_args(x, cos, sin, gamma_q, gamma_k, batch, heads, head_dim, token_major, dtype):
+    k = x.shape[-1]
+    a = x.reshape(-1, k)
+    if not a.is_contiguous():
+        a = a.contiguous()
+    m = a.shape[0]
+    if m % batch:
+        raise ValueError("rows must be batch * n")
+    n = m // batch
+    cos = cos.float().contiguous()
+    sin = sin.float().contiguous()
+    if cos.shape != (n, head_dim // 2) or sin.shape != (n, head_dim // 2):
+        raise ValueError(f"cos/sin must be [N, D/2] = [{n}, {head_dim // 2}]")
+    gq = gamma_q.float().reshape(heads, head_dim).contiguous()
+    gk = gamma_k.float().reshape(heads, head_dim).contiguous()
+    shape = (batch, n, heads, head_dim) if token_major else (batch, heads, n, head_dim)
+    q = torch.empty(shape, dtype=dtype, device=x.device)
+    return a, m, n, cos, sin, gq, gk, q, torch.empty_like(q), torch.empty_like(q)
+
+
+def linear_qkv_rope(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None, cos: torch.Tensor,
+                    sin: torch.Tensor, gamma_q: torch.Tensor, gamma_k: torch.Tensor, batch: int, heads: int,
+                    head_dim: int, token_major: bool = False):
+    """The attention input projection ``x @ W^T + bias`` (``W [3 H D, K]``) split into
+    ``q, k, v [B, H, N, D]`` with RoPE + QK RMS norm applied in the GEMM epilogue: the same
+    result as :func:`linear` followed by :func:`hi3d_b200.kernels.qkv_rope_rms`
+    (transformer.py:501-516, kernels.py:22-90) without writing the projection to memory.
+    ``token_major=True`` returns ``[B, N, H, D]``.  Raises ``NotImplementedError`` unless
+    :func:`qkv_rope_supported`."""
+    _lib.require_cuda(x, weight, bias, cos, sin, gamma_q, gamma_k)
+    if x.dtype not in (torch.float16, torch.bfloat16) or weight.dtype != x.dtype:
+        raise ValueError("linear_qkv_rope takes float16/bfloat16 activations and weights of one dtype")
+    if weight.shape != (3 * heads * head_dim, x.shape[-1]):
+        raise ValueError(f"weight must be [3*H*D, K], got {tuple(weight.shape)}")
+    a, m, n, cos, sin, gq, gk, q, k, v = _qkv_rope_args(x, cos, sin, gamma_q, gamma_k, batch, heads, head_dim,
+                                                        token_major, x.dtype)
+    b = None if bias is None else bias.to(x.dtype).contiguous()
+    rc = _lib.load().hi3d_gemm_qkv_rope(a.data_ptr(), weight.contiguous().data_ptr(), _lib.ptr(b), cos.data_ptr(),
+                                        sin.data_ptr(), gq.data_ptr(), gk.data_ptr(), q.data_ptr(), k.data_ptr(),
+                                        v.data_ptr(), m, n, heads, head_dim, a.shape[1], int(token_major),
+                                        _lib.dtype_code(x), _lib.stream(x))
+    _lib.check(rc, "linear_qkv_rope")
+    return q, k, v

@@ -89,6 +89,23 @@ def linear(x: torch.Tensor, w: dict, name: str, epilogue: str = "store", residua
     return _linear.linear(x, w[f"{name}.weight"], w[f"{name}.bias"], epilogue=epilogue, residual=residual, gate=gate)
 
 
+def qkv_rope(h: torch.Tensor, w: dict, cos: torch.Tensor, sin: torch.Tensor, batch: int, heads: int, d: int,
+             token_major: bool = False):
+    """``q, k, v`` of the self-attention: the ``self_attn.to_qkv`` projection with RoPE + QK RMS
+    norm (transformer.py:501-516 then kernels.py:22-90).  Fused into the GEMM epilogue when the
+    head layout allows it (head dim 64), else the projection followed by the row kernel."""
+    name = "self_attn.to_qkv"
+    gq, gk = w["self_attn.q_rms_norm.gamma"], w["self_attn.k_rms_norm.gamma"]
+    if _linear.qkv_rope_supported(heads, d):
+        if f"{name}.w8_scale" in w:
+            return _w8a8.linear_qkv_rope(h, w[f"{name}.weight"], w[f"{name}.w8_scale"], w[f"{name}.bias"], cos, sin,
+                                         gq, gk, batch, heads, d, token_major)
+        return _linear.linear_qkv_rope(h, w[f"{name}.weight"], w[f"{name}.bias"], cos, sin, gq, gk, batch, heads, d,
+                                       token_major)
+    qkv = linear(h, w, name)
+    return kernels.qkv_rope_rms(qkv, cos, sin, gq, gk, batch, heads, d, token_major=token_major)
+
+
 BLOCK_PROJECTIONS = ("self_attn.to_qkv", "self_attn.to_out", "cross_attn.to_q", "cross_attn.to_out", "mlp.mlp.0",
                      "mlp.mlp.2")
 
@@ -149,9 +166,7 @@ def block_forward(w: dict, x: torch.Tensor, mod: torch.Tensor, cos: torch.Tensor
 
     # self-attention
     h = kernels.layer_norm_modulate(x, 1e-6, scale=scale_msa, shift=shift_msa)
-    qkv = linear(h.view(-1, c), w, "self_attn.to_qkv")
-    q, k, v = kernels.qkv_rope_rms(qkv, cos, sin, w["self_attn.q_rms_norm.gamma"],
-                                   w["self_attn.k_rms_norm.gamma"], batch, heads, d)
+    q, k, v = qkv_rope(h.view(-1, c), w, cos, sin, batch, heads, d)
     a = attention.flash_attention(q, k, v, scale)
     linear(a, w, "self_attn.to_out", epilogue="residual", residual=x, gate=gate_msa)
 
@@ -188,9 +203,7 @@ def block_forward_packed(w: dict, x: torch.Tensor, mod: torch.Tensor, cos: torch
     shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp = _modulation(w, mod, c, dt)
 
     h = kernels.layer_norm_modulate(x, 1e-6, scale=scale_msa, shift=shift_msa)
-    qkv = linear(h, w, "self_attn.to_qkv")
-    q, k, v = kernels.qkv_rope_rms(qkv, cos, sin, w["self_attn.q_rms_norm.gamma"],
-                                   w["self_attn.k_rms_norm.gamma"], 1, heads, d)
+    q, k, v = qkv_rope(h, w, cos, sin, 1, heads, d)
     tr = lambda z: z[0].permute(1, 0, 2)  # [1, H, T, D] -> [T, H, D] view
     a = attention.flash_attn_varlen(tr(q), tr(k), tr(v), cu_seqlens, cu_seqlens, max_seqlen, scale)
     linear(a.view(t, c), w, "self_attn.to_out", epilogue="residual", residual=x, gate=gate_msa)

@@ -113,3 +113,30 @@ def linear(x: torch.Tensor, w: torch.Tensor, sw: torch.Tensor, bias: torch.Tenso
                                     _lib.dtype_code(out), _lib.stream(x))
     _lib.check(rc, "w8a8.linear")
     return out
+
+
+def linear_qkv_rope(x: torch.Tensor, w: torch.Tensor, sw: torch.Tensor, bias: torch.Tensor, cos: torch.Tensor,
+                    sin: torch.Tensor, gamma_q: torch.Tensor, gamma_k: torch.Tensor, batch: int, heads: int,
+                    head_dim: int, token_major: bool = False, multiplier: torch.Tensor | None = None,
+                    rotate: bool = True):
+    """The attention input projection through int8 (as :func:`linear`, w8a8.py:105-119) with
+    RoPE + QK RMS norm + head split in the GEMM epilogue (as ``hi3d_b200.linear.linear_qkv_rope``)."""
+    from .linear import _qkv_rope_args
+
+    _lib.require_cuda(x, w, sw, bias, cos, sin, gamma_q, gamma_k)
+    if w.dtype != torch.int8 or sw.dtype != torch.float32:
+        raise ValueError("W8A8 requires int8 weights and float32 scales")
+    if w.shape != (3 * heads * head_dim, x.shape[-1]) or sw.shape != (w.shape[0],) or bias.shape != (w.shape[0],):
+        raise ValueError("incompatible W8A8 projection shapes")
+    out_dtype = x.dtype if x.dtype in (torch.float16, torch.bfloat16) else torch.float16
+    aq, sa = quantize_activation(x.to(out_dtype), multiplier, rotate)
+    _, m, n, cos, sin, gq, gk, q, k, v = _qkv_rope_args(x, cos, sin, gamma_q, gamma_k, batch, heads, head_dim,
+                                                        token_major, out_dtype)
+    b = bias.to(out_dtype).contiguous()
+    rc = _lib.load().hi3d_gemm_w8a8_qkv_rope(aq.data_ptr(), w.contiguous().data_ptr(), sa.data_ptr(),
+                                             sw.contiguous().data_ptr(), b.data_ptr(), cos.data_ptr(), sin.data_ptr(),
+                                             gq.data_ptr(), gk.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(), m,
+                                             n, heads, head_dim, aq.shape[1], int(token_major),
+                                             _lib.dtype_code(q), _lib.stream(x))
+    _lib.check(rc, "w8a8.linear_qkv_rope")
+    return q, k, v

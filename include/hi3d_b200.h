@@ -149,6 +149,29 @@ HI3D_API int hi3d_gemm_w8a8(const int8_t* a, const int8_t* w, const float* sa, c
                             const void* gate, int64_t rows_per_batch, int64_t gate_stride, int out_dtype,
                             void* stream);
 
+/* The attention input projection with RoPE + QK RMS norm + head split in its epilogue: replaces
+ * the fused QKV mx.addmm (src/hi3d_mac/mlx_backend/transformer.py:501-516) followed by
+ * kernels.qkv_rope_rms (src/hi3d_mac/mlx_backend/kernels.py:22-90).  The projection
+ * y = round(A W^T + bias) ([m, 3 * heads * 64], channel = part * H * 64 + h * 64 + d) is not
+ * written out: q and k get the rotation of adjacent pairs with cos/sin [n_seq, 32] of the row's
+ * position and r / max(|r|, 1e-12) * gamma * 8 in fp32 (gamma_q/gamma_k [heads, 64] fp32), v the
+ * rounded projection itself.  Outputs [batch, heads, n_seq, 64] (token_major 0) or
+ * [batch, n_seq, heads, 64] (token_major 1); m = batch * n_seq.  head_dim must be 64 and
+ * heads * 64 a multiple of 256 (HI3D_ERR_UNSUPPORTED otherwise: use hi3d_gemm + hi3d_qkv_rope_rms). */
+HI3D_API int hi3d_gemm_qkv_rope(const void* a, const void* w, const void* bias, const float* cos, const float* sin,
+                                const float* gamma_q, const float* gamma_k, void* q, void* k, void* v, int64_t m,
+                                int64_t n_seq, int heads, int head_dim, int64_t k_dim, int token_major, int dtype,
+                                void* stream);
+
+/* The same through int8: activation codes and scales from hi3d_quantize_act_i8, int8 weights with
+ * per-channel scales, y = round(float(acc) * sa * sw + bias) as in hi3d_gemm_w8a8
+ * (src/hi3d_mac/mlx_backend/w8a8.py:105-119), then the epilogue of hi3d_gemm_qkv_rope. */
+HI3D_API int hi3d_gemm_w8a8_qkv_rope(const int8_t* a, const int8_t* w, const float* sa, const float* sw,
+                                     const void* bias, const float* cos, const float* sin, const float* gamma_q,
+                                     const float* gamma_k, void* q, void* k, void* v, int64_t m, int64_t n_seq,
+                                     int heads, int head_dim, int64_t k_dim, int token_major, int out_dtype,
+                                     void* stream);
+
 /* Replaces w8a8.quantize_activation (src/hi3d_mac/mlx_backend/w8a8.py:25-58, :95-102):
  * per row of x [rows, k] (k % 64 == 0), y = H64(x * multiplier) / 8 per 64-block (signed
  * natural-order Walsh-Hadamard, rotate != 0) or y = x (rotate == 0); s = max(max|y|, 1e-8) / 127;

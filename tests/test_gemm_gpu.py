@@ -128,3 +128,66 @@ def test_w8a8_projection_close_to_fp16():
     y16 = (x.astype(np.float32) @ w.astype(np.float32).T + b.astype(np.float32))
     err = np.linalg.norm(y8 - y16) / np.linalg.norm(y16)
     assert err < 2e-2, err
+
+
+def _rope_inputs(rng, batch, n, heads, k_dim, dtype):
+    d = 64
+    x = _t(rng.standard_normal((batch * n, k_dim)).astype(np.float32), dtype)
+    w = _t((rng.standard_normal((3 * heads * d, k_dim)) * 0.05).astype(np.float32), dtype)
+    b = _t((rng.standard_normal(3 * heads * d) * 0.1).astype(np.float32), dtype)
+    ang = rng.uniform(0, 6.3, (n, d // 2)).astype(np.float32)
+    cos, sin = _t(np.cos(ang)), _t(np.sin(ang))
+    gq = _t(rng.uniform(0.5, 1.5, (heads, d)).astype(np.float32))
+    gk = _t(rng.uniform(0.5, 1.5, (heads, d)).astype(np.float32))
+    return x, w, b, cos, sin, gq, gk
+
+
+@pytest.mark.parametrize("batch,n,heads,k_dim", [(1, 1000, 16, 1024), (2, 300, 4, 256), (3, 129, 8, 512)])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("token_major", [False, True])
+def test_linear_qkv_rope_matches_projection_then_rope(batch, n, heads, k_dim, dtype, token_major):
+    """Fused QKV projection + RoPE + QK norm vs the unfused pair (linear then qkv_rope_rms) and the
+    float64 rotation oracle: v bit-exact (both are the rounded projection), q/k within the rope
+    kernel's own float64 bound."""
+    from hi3d_b200 import kernels
+    from conftest import rel_l2
+
+    rng = np.random.default_rng(n + heads)
+    x, w, b, cos, sin, gq, gk = _rope_inputs(rng, batch, n, heads, k_dim, dtype)
+    q, k, v = lin.linear_qkv_rope(x, w, b, cos, sin, gq, gk, batch, heads, 64, token_major)
+    qkv = lin.linear(x, w, b)
+    q0, k0, v0 = kernels.qkv_rope_rms(qkv, cos, sin, gq, gk, batch, heads, 64, token_major=token_major)
+    assert torch.equal(v, v0)
+    qf, kf = ops.qkv_rope_rms_f64(qkv.float().cpu().numpy(), cos.cpu().numpy(), sin.cpu().numpy(),
+                                  gq.cpu().numpy(), gk.cpu().numpy(), batch, heads, 64)
+    perm = (0, 2, 1, 3) if token_major else (0, 1, 2, 3)
+    tol = 2.2e-4 if dtype == torch.float16 else 2e-3
+    for got, ref, unfused in ((q, qf, q0), (k, kf, k0)):
+        g = got.permute(*perm).float().cpu().numpy()
+        assert rel_l2(g, ref) < tol
+        assert (got == unfused).float().mean() > 0.98
+
+
+def test_w8a8_linear_qkv_rope_matches_projection_then_rope():
+    from hi3d_b200 import kernels
+
+    rng = np.random.default_rng(7)
+    batch, n, heads, k_dim = 2, 200, 4, 512
+    x, w, b, cos, sin, gq, gk = _rope_inputs(rng, batch, n, heads, k_dim, torch.float16)
+    wq, sw = w8a8.quantize_weight(w)
+    q, k, v = w8a8.linear_qkv_rope(x, wq, sw, b, cos, sin, gq, gk, batch, heads, 64)
+    qkv = w8a8.linear(x, wq, sw, b)
+    q0, k0, v0 = kernels.qkv_rope_rms(qkv, cos, sin, gq, gk, batch, heads, 64)
+    assert torch.equal(v, v0)
+    for got, ref in ((q, q0), (k, k0)):
+        assert (got == ref).float().mean() > 0.98
+        assert (got.float() - ref.float()).abs().max().item() <= 2 ** -8 * ref.float().abs().max().item()
+
+
+def test_linear_qkv_rope_rejects_unsupported_layouts():
+    x = torch.zeros(64, 256, device=DEV, dtype=torch.float16)
+    w = torch.zeros(3 * 2 * 64, 256, device=DEV, dtype=torch.float16)   # heads * 64 = 128: not a tile multiple
+    cos = torch.zeros(64, 32, device=DEV)
+    g = torch.ones(2, 64, device=DEV)
+    with pytest.raises(NotImplementedError):
+        lin.linear_qkv_rope(x, w, None, cos, cos, g, g, 1, 2, 64)
