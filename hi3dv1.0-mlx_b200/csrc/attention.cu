@@ -67,6 +67,15 @@ struct Params {
   int num_seqs, heads, tiles_per_seq;
   int kv_batched;  // 0: one K/V set shared by all sequences
   float scale2;  // softmax scale * log2(e)
+  // Key-split mode (k_splits > 1): CTA `split` covers key blocks
+  // [split * nb / k_splits, (split + 1) * nb / k_splits) of its sequence and writes
+  // O / l (fp32) to part_o[split][row][head][d] and log2-sum-exp m + log2(l) (in
+  // units of scale2 * s) to part_lse[split][row][head]; row = packed query row
+  // (varlen) or b * nq + query row (dense).
+  int k_splits;
+  float* part_o;
+  float* part_lse;
+  int64_t part_rows;
 };
 
 struct Barriers {
@@ -94,8 +103,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sV = sK + C::NST * C::KV_STAGE;    // [NST][NCH][BK][128 B]
   Barriers* bar = reinterpret_cast<Barriers*>(sV + C::NST * C::KV_STAGE);
 
-  // ---- work decode: (head, sequence, 256-row query block) ----
-  const int bid = blockIdx.x;
+  // ---- work decode: (head, sequence, 256-row query block[, key split]) ----
+  const int split = blockIdx.x % p.k_splits;
+  const int bid = blockIdx.x / p.k_splits;
   const int t = bid % p.tiles_per_seq;
   const int rest = bid / p.tiles_per_seq;
   const int b = rest % p.num_seqs;
@@ -113,8 +123,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     bk = 0;
   }
   const int64_t q_row0 = (int64_t)t * 2 * kRowsPerTile;
-  if (q_row0 >= q_len || k_len <= 0) return;  // uniform across the CTA
-  const int nblk = (int)((k_len + C::BK - 1) / C::BK);
+  if (q_row0 >= q_len) return;  // uniform across the CTA
+  const int nblk_all = k_len > 0 ? (int)((k_len + C::BK - 1) / C::BK) : 0;
+  const int kb0 = (int)((int64_t)split * nblk_all / p.k_splits);
+  const int nblk = (int)((int64_t)(split + 1) * nblk_all / p.k_splits) - kb0;  // key blocks of this CTA
+  if (nblk <= 0) {
+    // no keys for this CTA: a split part marks its rows empty (log2-sum-exp -inf)
+    if (p.k_splits > 1) {
+      for (int e = threadIdx.x; e < 2 * kRowsPerTile; e += blockDim.x) {
+        const int64_t qr = q_row0 + e;
+        if (qr >= q_len) continue;
+        const int64_t prow = p.cu_q ? q_start + qr : (int64_t)b * p.nq + qr;
+        p.part_lse[((int64_t)split * p.part_rows + prow) * p.heads + h] = -INFINITY;
+      }
+    }
+    return;
+  }
+  // key blocks are numbered from the first block of this CTA's range
+  k_start += (int64_t)kb0 * C::BK;
+  k_len -= (int64_t)kb0 * C::BK;
 
   const int warp = warp_id(), lane = lane_id();
   if (threadIdx.x == 0) {
@@ -348,6 +375,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int64_t qrow = q_row0 + i * kRowsPerTile + row;
       const float inv = 1.0f / l_run;
+      if (p.k_splits > 1) {
+        // partial result of this key range: O / l in fp32 and the log2-sum-exp
+        const int64_t prow = p.cu_q ? q_start + qrow : (int64_t)b * p.nq + qrow;
+        float* po = p.part_o + (((int64_t)split * p.part_rows + prow) * p.heads + h) * D;
+        if (qrow < q_len) p.part_lse[((int64_t)split * p.part_rows + prow) * p.heads + h] = m_run + log2f(l_run);
+#pragma unroll
+        for (int oc = 0; oc < (D + 31) / 32; ++oc) {
+          uint32_t r[32];
+          __syncwarp();
+          tmem_ld32(tO + oc * 32, r);
+          tmem_wait_ld();
+          if (qrow < q_len) {
+#pragma unroll
+            for (int e = 0; e < 32 && oc * 32 + e < D; e += 4)
+              *reinterpret_cast<float4*>(po + oc * 32 + e) =
+                  make_float4(__uint_as_float(r[e]) * inv, __uint_as_float(r[e + 1]) * inv,
+                              __uint_as_float(r[e + 2]) * inv, __uint_as_float(r[e + 3]) * inv);
+          }
+        }
+      } else {
       T* dst = reinterpret_cast<T*>(p.out) + (int64_t)(p.cu_q ? 0 : b) * p.o_batch + (q_start + qrow) * p.o_row +
                (int64_t)h * p.o_head;
 #pragma unroll
@@ -368,6 +415,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
+      }
     }
   }
 
@@ -377,6 +425,41 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
+}
+
+// Combines the key-split partials of one (row, head) per warp:
+// out = sum_s 2^(lse_s - max) O_s / sum_s 2^(lse_s - max), rounded once.  Rows
+// whose splits all saw no keys are left untouched, as in the single-pass kernel.
+template <typename T, int D>
+__global__ void __launch_bounds__(256) merge_kernel(const float* __restrict__ part_o,
+                                                    const float* __restrict__ part_lse, T* __restrict__ out,
+                                                    int64_t rows, int heads, int splits, int64_t nq, int dense,
+                                                    int64_t o_row, int64_t o_head, int64_t o_batch) {
+  constexpr int E = D / 32;  // elements per lane
+  const int64_t wid = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (wid >= rows * heads) return;
+  const int64_t r = wid / heads;
+  const int h = (int)(wid - r * heads);
+  float mx = -INFINITY;
+  for (int s = 0; s < splits; ++s) mx = fmaxf(mx, part_lse[((int64_t)s * rows + r) * heads + h]);
+  if (mx == -INFINITY) return;
+  float acc[E] = {};
+  float wsum = 0.f;
+  for (int s = 0; s < splits; ++s) {
+    const float ls = part_lse[((int64_t)s * rows + r) * heads + h];
+    if (ls == -INFINITY) continue;
+    const float wgt = exp2f(ls - mx);
+    wsum += wgt;
+    const float* po = part_o + (((int64_t)s * rows + r) * heads + h) * D + lane * E;
+#pragma unroll
+    for (int e = 0; e < E; ++e) acc[e] += wgt * po[e];
+  }
+  const float inv = 1.0f / wsum;
+  const int64_t b = dense ? r / nq : 0, qr = dense ? r - b * nq : r;
+  T* dst = out + b * o_batch + qr * o_row + (int64_t)h * o_head + lane * E;
+#pragma unroll
+  for (int e = 0; e < E; ++e) dst[e] = Cvt<T>::from_f(acc[e] * inv);
 }
 
 }  // namespace attn
@@ -393,7 +476,8 @@ static int make_attn_map(CUtensorMap* map, const void* base, int dtype, int D, i
 }
 
 template <typename T, int D>
-static int launch_attn(const hi3d_attn_args* a, cudaStream_t st) {
+static int launch_attn(const hi3d_attn_args* a, cudaStream_t st, int k_splits = 1, float* part_o = nullptr,
+                       float* part_lse = nullptr) {
   using C = attn::Cfg<D>;
   const bool varlen_q = a->cu_seqlens_q != nullptr, varlen_k = a->cu_seqlens_k != nullptr;
   const int64_t qb = varlen_q ? 1 : a->num_seqs;
@@ -422,21 +506,34 @@ static int launch_attn(const hi3d_attn_args* a, cudaStream_t st) {
   const int64_t qlen_max = varlen_q ? a->max_seqlen_q : a->nq;
   p.tiles_per_seq = (int)((qlen_max + 2 * attn::kRowsPerTile - 1) / (2 * attn::kRowsPerTile));
   p.scale2 = a->scale * 1.4426950408889634f;
-  const int64_t grid = (int64_t)p.tiles_per_seq * a->num_seqs * a->heads;
+  p.k_splits = k_splits;
+  p.part_o = part_o;
+  p.part_lse = part_lse;
+  p.part_rows = varlen_q ? a->nq : (int64_t)a->num_seqs * a->nq;
+  const int64_t grid = (int64_t)p.tiles_per_seq * a->num_seqs * a->heads * k_splits;
   if (grid == 0) return HI3D_OK;
   if (grid > 0x7fffffff) return set_error(HI3D_ERR_INVALID_ARGUMENT, "flash_attn: too many tiles");
   auto kern = attn::flash_fwd_kernel<T, D>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (e != cudaSuccess) return set_error(HI3D_ERR_CUDA, "flash_attn: smem attribute: %s", cudaGetErrorString(e));
   kern<<<(unsigned)grid, attn::kThreads, C::SMEM, st>>>(mq, mk, mv, p);
-  return check_launch("flash_attn_fwd");
+  if ((rc = check_launch("flash_attn_fwd"))) return rc;
+  if (k_splits > 1) {
+    const int64_t warps = p.part_rows * a->heads;
+    attn::merge_kernel<T, D><<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(
+        part_o, part_lse, static_cast<T*>(a->out), p.part_rows, a->heads, k_splits, a->nq, varlen_q ? 0 : 1, a->o_row,
+        a->o_head, a->o_batch);
+    return check_launch("flash_attn_merge");
+  }
+  return HI3D_OK;
 }
 
-}  // namespace hi3d
+static int64_t split_part_bytes(const hi3d_attn_args* a, int k_splits) {
+  const int64_t rows = a->cu_seqlens_q ? a->nq : (int64_t)a->num_seqs * a->nq;
+  return (int64_t)k_splits * rows * a->heads * a->head_dim * 4;
+}
 
-using namespace hi3d;
-
-extern "C" int hi3d_flash_attn_fwd(const hi3d_attn_args* a, void* stream) {
+static int check_attn_args(const hi3d_attn_args* a) {
   if (!a || !a->q || !a->k || !a->v || !a->out)
     return set_error(HI3D_ERR_INVALID_ARGUMENT, "flash_attn: null pointer");
   if (a->dtype != HI3D_F16 && a->dtype != HI3D_BF16)
@@ -453,14 +550,59 @@ extern "C" int hi3d_flash_attn_fwd(const hi3d_attn_args* a, void* stream) {
     if (s < 0 || s % 8) return set_error(HI3D_ERR_INVALID_ARGUMENT, "flash_attn: strides must be multiples of 8");
   if (a->cu_seqlens_q && a->max_seqlen_q <= 0 && a->nq > 0)
     return set_error(HI3D_ERR_INVALID_ARGUMENT, "flash_attn: varlen needs max_seqlen_q");
-  if (a->nq == 0 || a->num_seqs == 0) return HI3D_OK;
   if (a->nq > 0x7fffffff || a->nk > 0x7fffffff)
     return set_error(HI3D_ERR_INVALID_ARGUMENT, "flash_attn: more than 2^31 rows");
-  cudaStream_t st = as_stream(stream);
-  const bool bf = a->dtype == HI3D_BF16;
+  return HI3D_OK;
+}
+
+template <typename T>
+static int dispatch_attn(const hi3d_attn_args* a, cudaStream_t st, int k_splits, float* part_o, float* part_lse) {
   switch (a->head_dim) {
-    case 64: return bf ? launch_attn<__nv_bfloat16, 64>(a, st) : launch_attn<__half, 64>(a, st);
-    case 96: return bf ? launch_attn<__nv_bfloat16, 96>(a, st) : launch_attn<__half, 96>(a, st);
-    default: return bf ? launch_attn<__nv_bfloat16, 128>(a, st) : launch_attn<__half, 128>(a, st);
+    case 64: return launch_attn<T, 64>(a, st, k_splits, part_o, part_lse);
+    case 96: return launch_attn<T, 96>(a, st, k_splits, part_o, part_lse);
+    default: return launch_attn<T, 128>(a, st, k_splits, part_o, part_lse);
   }
+}
+
+}  // namespace hi3d
+
+using namespace hi3d;
+
+extern "C" int hi3d_flash_attn_fwd(const hi3d_attn_args* a, void* stream) {
+  int rc = check_attn_args(a);
+  if (rc) return rc;
+  if (a->nq == 0 || a->num_seqs == 0) return HI3D_OK;
+  cudaStream_t st = as_stream(stream);
+  return a->dtype == HI3D_BF16 ? dispatch_attn<__nv_bfloat16>(a, st, 1, nullptr, nullptr)
+                               : dispatch_attn<__half>(a, st, 1, nullptr, nullptr);
+}
+
+extern "C" int hi3d_flash_attn_split_workspace_size(const hi3d_attn_args* a, int k_splits, int64_t* bytes) {
+  int rc = check_attn_args(a);
+  if (rc) return rc;
+  if (!bytes || k_splits < 1 || k_splits > 64)
+    return set_error(HI3D_ERR_INVALID_ARGUMENT, "flash_attn_split: k_splits must be in [1, 64]");
+  const int64_t po = split_part_bytes(a, k_splits);
+  *bytes = ((po + 255) & ~int64_t(255)) + po / a->head_dim + 256;
+  return HI3D_OK;
+}
+
+extern "C" int hi3d_flash_attn_fwd_split(const hi3d_attn_args* a, int k_splits, void* workspace,
+                                         int64_t workspace_bytes, void* stream) {
+  int64_t need = 0;
+  int rc = hi3d_flash_attn_split_workspace_size(a, k_splits, &need);
+  if (rc) return rc;
+  if (a->nq == 0 || a->num_seqs == 0) return HI3D_OK;
+  cudaStream_t st = as_stream(stream);
+  if (k_splits == 1)
+    return a->dtype == HI3D_BF16 ? dispatch_attn<__nv_bfloat16>(a, st, 1, nullptr, nullptr)
+                                 : dispatch_attn<__half>(a, st, 1, nullptr, nullptr);
+  if (!workspace || !aligned16(workspace) || workspace_bytes < need)
+    return set_error(HI3D_ERR_CAPACITY, "flash_attn_split: workspace %lld bytes, need %lld (16-byte aligned)",
+                     (long long)workspace_bytes, (long long)need);
+  float* part_o = static_cast<float*>(workspace);
+  float* part_lse = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) +
+                                             ((split_part_bytes(a, k_splits) + 255) & ~int64_t(255)));
+  return a->dtype == HI3D_BF16 ? dispatch_attn<__nv_bfloat16>(a, st, k_splits, part_o, part_lse)
+                               : dispatch_attn<__half>(a, st, k_splits, part_o, part_lse);
 }

@@ -13,6 +13,8 @@ online softmax in fp32 in the exp2 domain, ``P`` rounded to the input dtype for
 from __future__ import annotations
 
 import ctypes
+import functools
+import math
 
 import torch
 
@@ -57,13 +59,50 @@ class KernelTimer:
 TIMER = KernelTimer()
 
 
-def _launch(args: _lib.AttnArgs, dev_tensor: torch.Tensor) -> None:
+@functools.lru_cache(maxsize=None)
+def _sm_count(device_index: int) -> int:
+    return torch.cuda.get_device_properties(device_index).multi_processor_count
+
+
+def auto_splits(ctas: int, key_blocks: int, sms: int, max_splits: int = 8) -> int:
+    """Key splits per query block that fill the waves of ``sms`` CTAs (one per SM): the s
+    minimising ceil(ctas * s / sms) / s, taken only when it beats no split by more than 3 %
+    (the merge costs a little) and leaves at least two key blocks per split."""
+    best, best_t = 1, float(math.ceil(ctas / sms))
+    for s in range(2, max_splits + 1):
+        if key_blocks < 2 * s:
+            break
+        t = math.ceil(ctas * s / sms) / s
+        if t < best_t * 0.97:
+            best, best_t = s, t
+    return best
+
+
+def _resolve_splits(k_splits, args: _lib.AttnArgs, dev_tensor: torch.Tensor) -> int:
+    if k_splits != "auto":
+        return int(k_splits)
+    tiles = math.ceil(args.max_seqlen_q / 256)
+    bk = 128 if args.head_dim == 64 else 64
+    longest_k = args.nk if not args.cu_seqlens_k else args.nk  # packed: bounded by the total
+    return auto_splits(tiles * args.num_seqs * args.heads, math.ceil(longest_k / bk), _sm_count(dev_tensor.device.index))
+
+
+def _launch(args: _lib.AttnArgs, dev_tensor: torch.Tensor, k_splits=1) -> None:
     stream = _lib.stream(dev_tensor)
+    splits = _resolve_splits(k_splits, args, dev_tensor)
     rec = TIMER.records is not None
     if rec:
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-    rc = _lib.load().hi3d_flash_attn_fwd(ctypes.byref(args), stream)
+    lib = _lib.load()
+    if splits > 1:
+        nbytes = ctypes.c_int64()
+        _lib.check(lib.hi3d_flash_attn_split_workspace_size(ctypes.byref(args), splits, ctypes.byref(nbytes)),
+                   "flash_attention split workspace", launched=False)
+        ws = torch.empty(nbytes.value, dtype=torch.uint8, device=dev_tensor.device)
+        rc = lib.hi3d_flash_attn_fwd_split(ctypes.byref(args), splits, ws.data_ptr(), ws.numel(), stream)
+    else:
+        rc = lib.hi3d_flash_attn_fwd(ctypes.byref(args), stream)
     _lib.check(rc, "flash_attention")
     if rec:
         e1.record()
@@ -73,13 +112,16 @@ def _launch(args: _lib.AttnArgs, dev_tensor: torch.Tensor) -> None:
 
 
 def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float,
-                    q_layout: str = "bhnd") -> torch.Tensor:
+                    q_layout: str = "bhnd", k_splits: int | str = "auto") -> torch.Tensor:
     """``softmax(q k^T * scale) v`` for fp16/bf16 inputs, returned as ``[B, Nq, H * D]``.
 
     Args:
         q: ``[B, H, Nq, D]`` (``q_layout="bhnd"``) or ``[B, Nq, H, D]`` (``"bnhd"``).
         k, v: ``[B, H, Nk, D]``, or ``[1, H, Nk, D]`` shared by every batch element.
         scale: softmax scale applied to ``q k^T``.
+        k_splits: key ranges per query block computed by separate CTAs and merged
+            (``hi3d_flash_attn_fwd_split``); ``"auto"`` splits only when the query blocks alone
+            leave a partial last wave (e.g. one query shard per GPU).
     """
     _lib.require_cuda(q, k, v)
     if q_layout == "bhnd":
@@ -110,16 +152,17 @@ def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: fl
         o_row=heads * dim, o_head=dim, o_batch=nq * heads * dim,
         cu_seqlens_q=None, cu_seqlens_k=None, nq=nq, nk=nk, max_seqlen_q=nq,
         num_seqs=batch, heads=heads, head_dim=dim, dtype=_lib.dtype_code(q), scale=float(scale))
-    _launch(args, q)
+    _launch(args, q, k_splits)
     return out
 
 
 def flash_attn_varlen(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqlens_q: torch.Tensor,
                       cu_seqlens_k: torch.Tensor | None, max_seqlen_q: int, scale: float,
-                      out: torch.Tensor | None = None) -> torch.Tensor:
+                      out: torch.Tensor | None = None, k_splits: int | str = "auto") -> torch.Tensor:
     """Packed variable-length attention: ``q [Tq, H, D]``, ``k, v [Tk, H, D]`` (any row
     stride, contiguous head dim), ``cu_seqlens_*`` int32 ``[num_seqs + 1]`` on the device.
     ``cu_seqlens_k=None`` shares all ``Tk`` keys with every sequence.  Returns ``[Tq, H, D]``.
+    ``k_splits`` as in :func:`flash_attention`.
     """
     _lib.require_cuda(q, k, v, cu_seqlens_q, cu_seqlens_k)
     tq, heads, dim = q.shape
@@ -147,5 +190,5 @@ def flash_attn_varlen(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seql
         cu_seqlens_q=cu_q.data_ptr(), cu_seqlens_k=None if cu_k is None else cu_k.data_ptr(),
         nq=tq, nk=tk, max_seqlen_q=int(max_seqlen_q), num_seqs=num_seqs, heads=heads, head_dim=dim,
         dtype=_lib.dtype_code(q), scale=float(scale))
-    _launch(args, q)
+    _launch(args, q, k_splits)
     return out

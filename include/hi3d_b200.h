@@ -124,6 +124,17 @@ typedef struct hi3d_attn_args {
 
 HI3D_API int hi3d_flash_attn_fwd(const hi3d_attn_args* args, void* stream);
 
+/* The same attention with each (sequence, head, 256-row query block) split into k_splits key
+ * ranges processed by separate CTAs, then merged: out = sum_s 2^(lse_s - max) O_s / sum_s
+ * 2^(lse_s - max) with O_s = O / l and lse_s the log2-sum-exp of key range s (fp32), rounded
+ * once.  Same contract as hi3d_flash_attn_fwd (attention.py:238-277 of the reference); splitting
+ * keeps all SMs busy when the query blocks alone do not fill whole waves (a query shard per GPU).
+ * Results agree with the single-pass kernel to within 16-bit output rounding.  The workspace
+ * (partials, fp32) comes from the caller; k_splits in [1, 64]. */
+HI3D_API int hi3d_flash_attn_split_workspace_size(const hi3d_attn_args* args, int k_splits, int64_t* bytes);
+HI3D_API int hi3d_flash_attn_fwd_split(const hi3d_attn_args* args, int k_splits, void* workspace,
+                                       int64_t workspace_bytes, void* stream);
+
 /* ---- projections (tcgen05 GEMM with fused epilogues) --------------------- */
 /* out = epilogue(A W^T): A [m, k] and W [n, k] row-major (K-major, as nn.Linear weights),
  * out [m, ldo] row-major.  Epilogues act on y = round(acc + bias) (bias [n] in the output

@@ -107,3 +107,44 @@ def test_long_sequence_sampled_rows_and_determinism():
     exact = ops.attention_f64(q[:, :, rows], k, v, d ** -0.5)
     got = out[:, rows].float().cpu().numpy()
     assert rel_rms(got, exact) < 3e-4
+
+
+@pytest.mark.parametrize("splits", [2, 3, 4, 7])
+@pytest.mark.parametrize("h,d,dtype", [(16, 64, torch.float16), (4, 128, torch.bfloat16), (6, 96, torch.float16)])
+def test_key_split_attention_matches_single_pass_and_float64(splits, h, d, dtype):
+    """Key ranges on separate CTAs merged by log2-sum-exp weights: within the float64 bound and
+    within output rounding of the single-pass kernel (dense, batch 2, keys not a multiple of the
+    key block)."""
+    rng = np.random.default_rng(splits + d)
+    q = (rng.standard_normal((2, h, 300, d)) * 2).astype(np.float32)
+    k = (rng.standard_normal((2, h, 1111, d)) * 2).astype(np.float32)
+    v = rng.standard_normal((2, h, 1111, d)).astype(np.float32)
+    qt, kt, vt = (_t(a, dtype) for a in (q, k, v))
+    exact = ops.attention_f64(*(t.float().cpu().numpy() for t in (qt, kt, vt)), d ** -0.5)
+    one = attention.flash_attention(qt, kt, vt, d ** -0.5, k_splits=1)
+    got = attention.flash_attention(qt, kt, vt, d ** -0.5, k_splits=splits)
+    tol = 3e-4 if dtype == torch.float16 else 4e-3
+    assert rel_rms(got.float().cpu().numpy(), exact) < tol
+    ulp = 2.0 ** (-10 if dtype == torch.float16 else -7)
+    assert (got.float() - one.float()).abs().max().item() <= 2 * ulp * one.float().abs().max().item()
+
+
+def test_key_split_varlen_with_short_and_empty_sequences():
+    """More splits than some sequences have key blocks (those splits are empty) and an empty
+    sequence: still exact to the float64 bound."""
+    rng = np.random.default_rng(9)
+    h, d = 16, 64
+    cu = np.array([0, 100, 100, 357, 1700, 1701], np.int32)
+    qkv = (rng.standard_normal((1701, 3, h, d)) * 2).astype(np.float16)
+    exact = ops.attention_varlen(qkv[:, 0], qkv[:, 1], qkv[:, 2], cu, cu, d ** -0.5)
+    t = _t(qkv, torch.float16)
+    cut = _t(cu, torch.int32)
+    got = attention.flash_attn_varlen(t[:, 0], t[:, 1], t[:, 2], cut, cut, 1343, d ** -0.5, k_splits=6)
+    assert rel_rms(got.float().cpu().numpy(), exact) < 3e-4
+
+
+def test_auto_splits_fill_waves():
+    assert attention.auto_splits(2048, 256, 148) == 1   # cfg1 on one GPU: 13.8 waves already
+    assert attention.auto_splits(256, 256, 148) == 4    # one eighth of the queries per GPU
+    assert attention.auto_splits(512, 256, 148) == 2
+    assert attention.auto_splits(256, 3, 148) == 1      # too few key blocks to split
