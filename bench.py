@@ -329,9 +329,12 @@ def run_ours(args) -> None:
 
     # ---- roofline of the dominant kernel (self-attention)
     peaks = _peaks()
-    self_launches = [r for r in attn if r["nk"] == T_TOKENS]  # self-attention: keys = all tokens
-    avg_s = sum(r["ms"] for r in self_launches) / max(1, len(self_launches)) / 1e3
-    flops = self_launches[0]["flops"] if self_launches else 0.0
+    # Self-attention: one launch per block over all keys, or (sharded) the partial launches over the
+    # rank's own and the gathered keys; every block has exactly one cross-attention launch.
+    self_launches = [r for r in attn if r["nk"] != COND and r["flops"]]
+    n_blocks_seen = max(1, sum(1 for r in attn if r["nk"] == COND))
+    avg_s = sum(r["ms"] for r in self_launches) / n_blocks_seen / 1e3
+    flops = sum(r["flops"] for r in self_launches) / n_blocks_seen
     achieved = flops / avg_s / 1e12 if avg_s > 0 else 0.0
     peak = peaks["bf16_tflops_sustained"]
     attn_share = sum(r["ms"] for r in attn) / ms if ms > 0 else None

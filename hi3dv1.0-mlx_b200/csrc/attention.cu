@@ -67,12 +67,14 @@ struct Params {
   int num_seqs, heads, tiles_per_seq;
   int kv_batched;  // 0: one K/V set shared by all sequences
   float scale2;  // softmax scale * log2(e)
-  // Key-split mode (k_splits > 1): CTA `split` covers key blocks
+  // Partial mode (part_o set): CTA `split` covers key blocks
   // [split * nb / k_splits, (split + 1) * nb / k_splits) of its sequence and writes
-  // O / l (fp32) to part_o[split][row][head][d] and log2-sum-exp m + log2(l) (in
-  // units of scale2 * s) to part_lse[split][row][head]; row = packed query row
-  // (varlen) or b * nq + query row (dense).
+  // O / l (fp32) to part_o[slot0 + split][row][head][d] and the log2-sum-exp
+  // m + log2(l) (in units of scale2 * s) to part_lse[slot0 + split][row][head];
+  // row = packed query row (varlen) or b * nq + query row (dense).  Without
+  // part_o there is one key range and O / l is written to `out`.
   int k_splits;
+  int slot0;  // partial slot of split 0 (several launches can fill one partial buffer)
   float* part_o;
   float* part_lse;
   int64_t part_rows;
@@ -129,12 +131,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int nblk = (int)((int64_t)(split + 1) * nblk_all / p.k_splits) - kb0;  // key blocks of this CTA
   if (nblk <= 0) {
     // no keys for this CTA: a split part marks its rows empty (log2-sum-exp -inf)
-    if (p.k_splits > 1) {
+    if (p.part_o) {
       for (int e = threadIdx.x; e < 2 * kRowsPerTile; e += blockDim.x) {
         const int64_t qr = q_row0 + e;
         if (qr >= q_len) continue;
         const int64_t prow = p.cu_q ? q_start + qr : (int64_t)b * p.nq + qr;
-        p.part_lse[((int64_t)split * p.part_rows + prow) * p.heads + h] = -INFINITY;
+        p.part_lse[((int64_t)(p.slot0 + split) * p.part_rows + prow) * p.heads + h] = -INFINITY;
       }
     }
     return;
@@ -375,11 +377,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int64_t qrow = q_row0 + i * kRowsPerTile + row;
       const float inv = 1.0f / l_run;
-      if (p.k_splits > 1) {
+      if (p.part_o) {
         // partial result of this key range: O / l in fp32 and the log2-sum-exp
         const int64_t prow = p.cu_q ? q_start + qrow : (int64_t)b * p.nq + qrow;
-        float* po = p.part_o + (((int64_t)split * p.part_rows + prow) * p.heads + h) * D;
-        if (qrow < q_len) p.part_lse[((int64_t)split * p.part_rows + prow) * p.heads + h] = m_run + log2f(l_run);
+        float* po = p.part_o + (((int64_t)(p.slot0 + split) * p.part_rows + prow) * p.heads + h) * D;
+        if (qrow < q_len) p.part_lse[((int64_t)(p.slot0 + split) * p.part_rows + prow) * p.heads + h] = m_run + log2f(l_run);
 #pragma unroll
         for (int oc = 0; oc < (D + 31) / 32; ++oc) {
           uint32_t r[32];
@@ -475,9 +477,11 @@ static int make_attn_map(CUtensorMap* map, const void* base, int dtype, int D, i
   return encode_tmap(map, t, 4, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
+// Single pass (part_o == nullptr) or partial results of k_splits key ranges into
+// slots [slot0, slot0 + k_splits) of part_o / part_lse (no merge).
 template <typename T, int D>
 static int launch_attn(const hi3d_attn_args* a, cudaStream_t st, int k_splits = 1, float* part_o = nullptr,
-                       float* part_lse = nullptr) {
+                       float* part_lse = nullptr, int slot0 = 0) {
   using C = attn::Cfg<D>;
   const bool varlen_q = a->cu_seqlens_q != nullptr, varlen_k = a->cu_seqlens_k != nullptr;
   const int64_t qb = varlen_q ? 1 : a->num_seqs;
@@ -507,6 +511,7 @@ static int launch_attn(const hi3d_attn_args* a, cudaStream_t st, int k_splits = 
   p.tiles_per_seq = (int)((qlen_max + 2 * attn::kRowsPerTile - 1) / (2 * attn::kRowsPerTile));
   p.scale2 = a->scale * 1.4426950408889634f;
   p.k_splits = k_splits;
+  p.slot0 = slot0;
   p.part_o = part_o;
   p.part_lse = part_lse;
   p.part_rows = varlen_q ? a->nq : (int64_t)a->num_seqs * a->nq;
@@ -517,15 +522,20 @@ static int launch_attn(const hi3d_attn_args* a, cudaStream_t st, int k_splits = 
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (e != cudaSuccess) return set_error(HI3D_ERR_CUDA, "flash_attn: smem attribute: %s", cudaGetErrorString(e));
   kern<<<(unsigned)grid, attn::kThreads, C::SMEM, st>>>(mq, mk, mv, p);
-  if ((rc = check_launch("flash_attn_fwd"))) return rc;
-  if (k_splits > 1) {
-    const int64_t warps = p.part_rows * a->heads;
-    attn::merge_kernel<T, D><<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(
-        part_o, part_lse, static_cast<T*>(a->out), p.part_rows, a->heads, k_splits, a->nq, varlen_q ? 0 : 1, a->o_row,
-        a->o_head, a->o_batch);
-    return check_launch("flash_attn_merge");
-  }
-  return HI3D_OK;
+  return check_launch("flash_attn_fwd");
+}
+
+template <typename T, int D>
+static int launch_merge(const hi3d_attn_args* a, cudaStream_t st, int num_slots, const float* part_o,
+                        const float* part_lse) {
+  const bool varlen_q = a->cu_seqlens_q != nullptr;
+  const int64_t rows = varlen_q ? a->nq : (int64_t)a->num_seqs * a->nq;
+  const int64_t warps = rows * a->heads;
+  if (warps == 0) return HI3D_OK;
+  attn::merge_kernel<T, D><<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(
+      part_o, part_lse, static_cast<T*>(a->out), rows, a->heads, num_slots, a->nq, varlen_q ? 0 : 1, a->o_row,
+      a->o_head, a->o_batch);
+  return check_launch("flash_attn_merge");
 }
 
 static int64_t split_part_bytes(const hi3d_attn_args* a, int k_splits) {
@@ -556,11 +566,22 @@ static int check_attn_args(const hi3d_attn_args* a) {
 }
 
 template <typename T>
-static int dispatch_attn(const hi3d_attn_args* a, cudaStream_t st, int k_splits, float* part_o, float* part_lse) {
+static int dispatch_attn(const hi3d_attn_args* a, cudaStream_t st, int k_splits, float* part_o, float* part_lse,
+                         int slot0) {
   switch (a->head_dim) {
-    case 64: return launch_attn<T, 64>(a, st, k_splits, part_o, part_lse);
-    case 96: return launch_attn<T, 96>(a, st, k_splits, part_o, part_lse);
-    default: return launch_attn<T, 128>(a, st, k_splits, part_o, part_lse);
+    case 64: return launch_attn<T, 64>(a, st, k_splits, part_o, part_lse, slot0);
+    case 96: return launch_attn<T, 96>(a, st, k_splits, part_o, part_lse, slot0);
+    default: return launch_attn<T, 128>(a, st, k_splits, part_o, part_lse, slot0);
+  }
+}
+
+template <typename T>
+static int dispatch_merge(const hi3d_attn_args* a, cudaStream_t st, int num_slots, const float* part_o,
+                          const float* part_lse) {
+  switch (a->head_dim) {
+    case 64: return launch_merge<T, 64>(a, st, num_slots, part_o, part_lse);
+    case 96: return launch_merge<T, 96>(a, st, num_slots, part_o, part_lse);
+    default: return launch_merge<T, 128>(a, st, num_slots, part_o, part_lse);
   }
 }
 
@@ -573,8 +594,8 @@ extern "C" int hi3d_flash_attn_fwd(const hi3d_attn_args* a, void* stream) {
   if (rc) return rc;
   if (a->nq == 0 || a->num_seqs == 0) return HI3D_OK;
   cudaStream_t st = as_stream(stream);
-  return a->dtype == HI3D_BF16 ? dispatch_attn<__nv_bfloat16>(a, st, 1, nullptr, nullptr)
-                               : dispatch_attn<__half>(a, st, 1, nullptr, nullptr);
+  return a->dtype == HI3D_BF16 ? dispatch_attn<__nv_bfloat16>(a, st, 1, nullptr, nullptr, 0)
+                               : dispatch_attn<__half>(a, st, 1, nullptr, nullptr, 0);
 }
 
 extern "C" int hi3d_flash_attn_split_workspace_size(const hi3d_attn_args* a, int k_splits, int64_t* bytes) {
@@ -595,14 +616,47 @@ extern "C" int hi3d_flash_attn_fwd_split(const hi3d_attn_args* a, int k_splits, 
   if (a->nq == 0 || a->num_seqs == 0) return HI3D_OK;
   cudaStream_t st = as_stream(stream);
   if (k_splits == 1)
-    return a->dtype == HI3D_BF16 ? dispatch_attn<__nv_bfloat16>(a, st, 1, nullptr, nullptr)
-                                 : dispatch_attn<__half>(a, st, 1, nullptr, nullptr);
+    return a->dtype == HI3D_BF16 ? dispatch_attn<__nv_bfloat16>(a, st, 1, nullptr, nullptr, 0)
+                                 : dispatch_attn<__half>(a, st, 1, nullptr, nullptr, 0);
   if (!workspace || !aligned16(workspace) || workspace_bytes < need)
     return set_error(HI3D_ERR_CAPACITY, "flash_attn_split: workspace %lld bytes, need %lld (16-byte aligned)",
                      (long long)workspace_bytes, (long long)need);
   float* part_o = static_cast<float*>(workspace);
   float* part_lse = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) +
                                              ((split_part_bytes(a, k_splits) + 255) & ~int64_t(255)));
-  return a->dtype == HI3D_BF16 ? dispatch_attn<__nv_bfloat16>(a, st, k_splits, part_o, part_lse)
-                               : dispatch_attn<__half>(a, st, k_splits, part_o, part_lse);
+  rc = a->dtype == HI3D_BF16 ? dispatch_attn<__nv_bfloat16>(a, st, k_splits, part_o, part_lse, 0)
+                             : dispatch_attn<__half>(a, st, k_splits, part_o, part_lse, 0);
+  if (rc) return rc;
+  return a->dtype == HI3D_BF16 ? dispatch_merge<__nv_bfloat16>(a, st, k_splits, part_o, part_lse)
+                               : dispatch_merge<__half>(a, st, k_splits, part_o, part_lse);
+}
+
+extern "C" int hi3d_flash_attn_fwd_partial(const hi3d_attn_args* a, int k_splits, int slot0, float* part_o,
+                                           float* part_lse, int64_t part_rows, void* stream) {
+  int rc = check_attn_args(a);
+  if (rc) return rc;
+  if (k_splits < 1 || k_splits > 64 || slot0 < 0)
+    return set_error(HI3D_ERR_INVALID_ARGUMENT, "flash_attn_partial: k_splits in [1, 64] and slot0 >= 0");
+  if (!part_o || !part_lse || !aligned16(part_o))
+    return set_error(HI3D_ERR_INVALID_ARGUMENT, "flash_attn_partial: partial buffers (part_o 16-byte aligned)");
+  const int64_t rows = a->cu_seqlens_q ? a->nq : (int64_t)a->num_seqs * a->nq;
+  if (part_rows != rows)
+    return set_error(HI3D_ERR_INVALID_ARGUMENT, "flash_attn_partial: part_rows %lld, the query rows are %lld",
+                     (long long)part_rows, (long long)rows);
+  if (a->nq == 0 || a->num_seqs == 0) return HI3D_OK;
+  cudaStream_t st = as_stream(stream);
+  return a->dtype == HI3D_BF16 ? dispatch_attn<__nv_bfloat16>(a, st, k_splits, part_o, part_lse, slot0)
+                               : dispatch_attn<__half>(a, st, k_splits, part_o, part_lse, slot0);
+}
+
+extern "C" int hi3d_flash_attn_merge(const hi3d_attn_args* a, int num_slots, const float* part_o,
+                                     const float* part_lse, void* stream) {
+  int rc = check_attn_args(a);
+  if (rc) return rc;
+  if (num_slots < 1 || !part_o || !part_lse)
+    return set_error(HI3D_ERR_INVALID_ARGUMENT, "flash_attn_merge: num_slots >= 1 and partial buffers required");
+  if (a->nq == 0 || a->num_seqs == 0) return HI3D_OK;
+  cudaStream_t st = as_stream(stream);
+  return a->dtype == HI3D_BF16 ? dispatch_merge<__nv_bfloat16>(a, st, num_slots, part_o, part_lse)
+                               : dispatch_merge<__half>(a, st, num_slots, part_o, part_lse);
 }

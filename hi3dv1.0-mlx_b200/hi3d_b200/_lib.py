@@ -65,6 +65,9 @@ SIGNATURES: dict[str, tuple] = {
     "hi3d_quantize_act_i8": (_i32, [_c_void_p] * 4 + [_i64, _i64, _i32, _i32, _c_void_p]),
     "hi3d_flash_attn_split_workspace_size": (_i32, [ctypes.POINTER(AttnArgs), _i32, ctypes.POINTER(_i64)]),
     "hi3d_flash_attn_fwd_split": (_i32, [ctypes.POINTER(AttnArgs), _i32, _c_void_p, _i64, _c_void_p]),
+    "hi3d_flash_attn_fwd_partial": (_i32, [ctypes.POINTER(AttnArgs), _i32, _i32, _c_void_p, _c_void_p, _i64,
+                                           _c_void_p]),
+    "hi3d_flash_attn_merge": (_i32, [ctypes.POINTER(AttnArgs), _i32, _c_void_p, _c_void_p, _c_void_p]),
     "hi3d_gemm_qkv_rope": (_i32, [_c_void_p] * 10 + [_i64, _i64, _i32, _i32, _i64, _i32, _i32, _c_void_p]),
     "hi3d_gemm_w8a8_qkv_rope": (_i32, [_c_void_p] * 12 + [_i64, _i64, _i32, _i32, _i64, _i32, _i32, _c_void_p]),
     "hi3d_neighbour_map_workspace_size": (_i32, [_i64, ctypes.POINTER(_i64)]),

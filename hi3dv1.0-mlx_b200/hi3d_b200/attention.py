@@ -141,19 +141,94 @@ def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: fl
     out = torch.empty((batch, nq, heads * dim), dtype=q.dtype, device=q.device)
     if nq == 0 or batch == 0:
         return out
+    _launch(_dense_args(q, k, v, out, scale, q_layout), q, k_splits)
+    return out
+
+
+def _dense_args(q, k, v, out, scale: float, q_layout: str) -> _lib.AttnArgs:
+    if q_layout == "bhnd":
+        batch, heads, nq, dim = q.shape
+    else:
+        batch, nq, heads, dim = q.shape
     qr, qh, qb = _strides3(q, q_layout)
     kr, kh, kb = _strides3(k, "bhnd")
     vr, vh, vb = _strides3(v, "bhnd")
     if k.shape[0] == 1:
         kb = vb = 0
-    args = _lib.AttnArgs(
+    return _lib.AttnArgs(
         q=q.data_ptr(), k=k.data_ptr(), v=v.data_ptr(), out=out.data_ptr(),
         q_row=qr, q_head=qh, q_batch=qb, k_row=kr, k_head=kh, k_batch=kb, v_row=vr, v_head=vh, v_batch=vb,
         o_row=heads * dim, o_head=dim, o_batch=nq * heads * dim,
-        cu_seqlens_q=None, cu_seqlens_k=None, nq=nq, nk=nk, max_seqlen_q=nq,
+        cu_seqlens_q=None, cu_seqlens_k=None, nq=nq, nk=k.shape[2], max_seqlen_q=nq,
         num_seqs=batch, heads=heads, head_dim=dim, dtype=_lib.dtype_code(q), scale=float(scale))
-    _launch(args, q, k_splits)
-    return out
+
+
+def auto_key_splits(q_rows: int, k_rows: int, heads: int, head_dim: int, batch: int = 1, device=None) -> int:
+    """The key splits :func:`flash_attention` picks with ``k_splits="auto"`` for these sizes."""
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    bk = 128 if head_dim == 64 else 64
+    return auto_splits(math.ceil(q_rows / 256) * batch * heads, math.ceil(k_rows / bk), _sm_count(dev.index))
+
+
+class AttentionParts:
+    """Attention of one set of queries over several disjoint key sets, combined exactly by their
+    log-sum-exp weights: :meth:`add` one key set at a time (``hi3d_flash_attn_fwd_partial``), then
+    :meth:`merge` (``hi3d_flash_attn_merge``).  The sharded block attends its own key shard while
+    the other ranks' keys are still being gathered.  Queries and keys as in
+    :func:`flash_attention`; ``slots`` bounds the total key splits of all ``add`` calls."""
+
+    def __init__(self, q: torch.Tensor, scale: float, slots: int, q_layout: str = "bhnd"):
+        _lib.require_cuda(q)
+        if q_layout not in ("bhnd", "bnhd"):
+            raise ValueError(f"unknown q layout {q_layout!r}")
+        _check_inner(q, "q")
+        self.q, self.scale, self.layout = q, float(scale), q_layout
+        if q_layout == "bhnd":
+            self.batch, self.heads, self.nq, self.dim = q.shape
+        else:
+            self.batch, self.nq, self.heads, self.dim = q.shape
+        rows = self.batch * self.nq
+        self.part_o = torch.empty((slots, rows, self.heads, self.dim), dtype=torch.float32, device=q.device)
+        self.part_lse = torch.empty((slots, rows, self.heads), dtype=torch.float32, device=q.device)
+        self.slots, self.used = slots, 0
+
+    def add(self, k: torch.Tensor, v: torch.Tensor, k_splits: int | str = "auto") -> None:
+        _lib.require_cuda(k, v)
+        if k.shape[1] != self.heads or k.shape[3] != self.dim or v.shape != k.shape or k.dtype != self.q.dtype:
+            raise ValueError(f"keys {tuple(k.shape)} do not match the queries")
+        for t, n in ((k, "k"), (v, "v")):
+            _check_inner(t, n)
+        if k.shape[2] == 0 or self.nq == 0 or self.batch == 0:
+            return
+        args = _dense_args(self.q, k, v, self.part_o, self.scale, self.layout)
+        splits = _resolve_splits(k_splits, args, self.q)
+        if self.used + splits > self.slots:
+            raise ValueError(f"{self.used + splits} key splits exceed the {self.slots} partial slots")
+        rec = TIMER.records is not None
+        if rec:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+        rc = _lib.load().hi3d_flash_attn_fwd_partial(ctypes.byref(args), splits, self.used, self.part_o.data_ptr(),
+                                                     self.part_lse.data_ptr(), self.batch * self.nq,
+                                                     _lib.stream(self.q))
+        _lib.check(rc, "flash_attention partial")
+        if rec:
+            e1.record()
+            flops = 4.0 * args.nq * args.nk * args.heads * args.head_dim * args.num_seqs
+            TIMER.records.append({"nq": args.nq, "nk": args.nk, "flops": flops, "e0": e0, "e1": e1, "part": True})
+        self.used += splits
+
+    def merge(self) -> torch.Tensor:
+        """``[B, Nq, H * D]`` from all key sets added so far."""
+        out = torch.empty((self.batch, self.nq, self.heads * self.dim), dtype=self.q.dtype, device=self.q.device)
+        if self.used == 0 or self.nq == 0 or self.batch == 0:
+            return out
+        args = _dense_args(self.q, self.q if self.layout == "bhnd" else self.q.transpose(1, 2),
+                           self.q if self.layout == "bhnd" else self.q.transpose(1, 2), out, self.scale, self.layout)
+        rc = _lib.load().hi3d_flash_attn_merge(ctypes.byref(args), self.used, self.part_o.data_ptr(),
+                                               self.part_lse.data_ptr(), _lib.stream(self.q))
+        _lib.check(rc, "flash_attention merge")
+        return out
 
 
 def flash_attn_varlen(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqlens_q: torch.Tensor,

@@ -54,10 +54,23 @@ def block_forward_sharded(w: dict, x: torch.Tensor, mod: torch.Tensor, cos: torc
     k_all, v_all = kv_buffers
     _, hk = gather_rows(k[0], group, out=k_all, async_op=True)
     _, hv = gather_rows(v[0], group, out=v_all, async_op=True)
+    # Attend to this rank's own keys while the others are being gathered, then to the keys
+    # before and after the local shard; the partials are merged by their log-sum-exp weights.
+    rank = dist.get_rank(group)
+    bhnd = lambda t: t.permute(1, 0, 2)[None]  # [rows, H, D] token-major -> [1, H, rows, D] view
+    key_sets = [(0, rank * t_local), ((rank + 1) * t_local, world * t_local)]
+    splits = [attention.auto_key_splits(t_local, t_local, heads, d, device=x.device)]
+    splits += [attention.auto_key_splits(t_local, hi - lo, heads, d, device=x.device) for lo, hi in key_sets if hi > lo]
+    parts = attention.AttentionParts(q, scale, sum(splits), q_layout="bnhd")
+    parts.add(bhnd(k[0]), bhnd(v[0]), splits[0])
     hk.wait()
     hv.wait()
-    a = attention.flash_attention(q, k_all.permute(1, 0, 2)[None], v_all.permute(1, 0, 2)[None], scale,
-                                  q_layout="bnhd")
+    i = 1
+    for lo, hi in key_sets:
+        if hi > lo:
+            parts.add(bhnd(k_all[lo:hi]), bhnd(v_all[lo:hi]), splits[i])
+            i += 1
+    a = parts.merge()
     linear(a[0], w, "self_attn.to_out", epilogue="residual", residual=x, gate=gate_msa)
 
     h = kernels.layer_norm_modulate(x, 1e-6, weight=w["norm2.weight"], bias=w["norm2.bias"])

@@ -135,6 +135,19 @@ HI3D_API int hi3d_flash_attn_split_workspace_size(const hi3d_attn_args* args, in
 HI3D_API int hi3d_flash_attn_fwd_split(const hi3d_attn_args* args, int k_splits, void* workspace,
                                        int64_t workspace_bytes, void* stream);
 
+/* Partial results for combining attention over disjoint key sets of the same queries (a query
+ * shard against its own keys first, other ranks' keys once gathered): k_splits key ranges of
+ * args' keys, written as O / l (fp32) to part_o[slot0 + s][row][head][head_dim] and the
+ * log2-sum-exp to part_lse[slot0 + s][row][head], row = query row (dense: b * nq + row;
+ * varlen: packed row) with part_rows the number of query rows.  args->out is not touched.
+ * hi3d_flash_attn_merge then writes args->out from slots [0, num_slots) as in
+ * hi3d_flash_attn_fwd_split.  No counterpart in the reference (attention.py:238-277 computes all
+ * keys in one pass); it serves the sharded block. */
+HI3D_API int hi3d_flash_attn_fwd_partial(const hi3d_attn_args* args, int k_splits, int slot0, float* part_o,
+                                         float* part_lse, int64_t part_rows, void* stream);
+HI3D_API int hi3d_flash_attn_merge(const hi3d_attn_args* args, int num_slots, const float* part_o,
+                                   const float* part_lse, void* stream);
+
 /* ---- projections (tcgen05 GEMM with fused epilogues) --------------------- */
 /* out = epilogue(A W^T): A [m, k] and W [n, k] row-major (K-major, as nn.Linear weights),
  * out [m, ldo] row-major.  Epilogues act on y = round(acc + bias) (bias [n] in the output

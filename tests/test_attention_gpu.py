@@ -148,3 +148,22 @@ def test_auto_splits_fill_waves():
     assert attention.auto_splits(256, 256, 148) == 4    # one eighth of the queries per GPU
     assert attention.auto_splits(512, 256, 148) == 2
     assert attention.auto_splits(256, 3, 148) == 1      # too few key blocks to split
+
+
+def test_attention_parts_over_disjoint_key_sets_match_single_pass():
+    """Keys split into three disjoint sets added one at a time (as the sharded block does) and
+    merged: within output rounding of one pass over all keys, and within the float64 bound."""
+    rng = np.random.default_rng(11)
+    h, d = 8, 64
+    q = (rng.standard_normal((1, 500, h, d)) * 2).astype(np.float16)      # token-major queries
+    k = (rng.standard_normal((1, h, 3000, d)) * 2).astype(np.float16)
+    v = rng.standard_normal((1, h, 3000, d)).astype(np.float16)
+    qt, kt, vt = _t(q, torch.float16), _t(k, torch.float16), _t(v, torch.float16)
+    one = attention.flash_attention(qt, kt, vt, d ** -0.5, q_layout="bnhd", k_splits=1)
+    parts = attention.AttentionParts(qt, d ** -0.5, slots=8, q_layout="bnhd")
+    for lo, hi in ((1000, 2000), (0, 1000), (2000, 3000)):
+        parts.add(kt[:, :, lo:hi], vt[:, :, lo:hi], k_splits=2 if lo == 0 else 1)
+    got = parts.merge()
+    assert (got.float() - one.float()).abs().max().item() <= 2 * 2 ** -10 * one.float().abs().max().item()
+    exact = ops.attention_f64(q.transpose(0, 2, 1, 3), k, v, d ** -0.5)
+    assert rel_rms(got.float().cpu().numpy(), exact) < 3e-4  # both [1, Nq, H * D]

@@ -1,8 +1,11 @@
 """Query-sharded block stack on 2 GPUs (NCCL) vs the single-GPU stack.
 
-Every row-wise kernel computes a row independently of the others and each query row's
-attention reads the same K/V blocks in the same order, so the sharded result must be
-bit-identical to the unsharded one.  Needs two GPUs (``gpurun --gpus 2``); skipped otherwise.
+Every row-wise kernel computes a row independently of the others; the sharded attention
+combines the rank's own keys (attended while the other rank's are gathered) and the gathered
+keys by their log-sum-exp weights, which agrees with the single pass to within 16-bit output
+rounding.  So the stack output must match the unsharded one to the block tolerance (relative
+L2 1e-3 over two blocks) with most elements bit-identical.  Needs two GPUs
+(``gpurun --gpus 2``); skipped otherwise.
 """
 
 from __future__ import annotations
@@ -56,7 +59,9 @@ def _worker(rank, world, port, result_path):
     y = hdist.gather_rows(y_local)
     if rank == 0:
         ref = transformer.BlockStack(ws, heads)(tt(x)[None], tt(mod), tt(cos), tt(sin), kvs)[0]
-        np.save(result_path, np.array([float(torch.equal(y, ref)), float((y.float() - ref.float()).abs().max())]))
+        yf, rf = y.float(), ref.float()
+        rel = float((yf - rf).norm() / rf.norm())
+        np.save(result_path, np.array([rel, float((y == ref).float().mean())]))
     dist.barrier()
     dist.destroy_process_group()
 
@@ -65,5 +70,6 @@ def _worker(rank, world, port, result_path):
 def test_sharded_stack_matches_single_gpu(tmp_path):
     out = tmp_path / "r.npy"
     mp.spawn(_worker, args=(2, _free_port(), str(out)), nprocs=2, join=True)
-    equal, maxdiff = np.load(out)
-    assert equal == 1.0, maxdiff
+    rel, same = np.load(out)
+    assert rel < 1e-3, rel
+    assert same > 0.9, same
