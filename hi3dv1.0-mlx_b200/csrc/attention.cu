@@ -397,26 +397,26 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       } else {
-      T* dst = reinterpret_cast<T*>(p.out) + (int64_t)(p.cu_q ? 0 : b) * p.o_batch + (q_start + qrow) * p.o_row +
-               (int64_t)h * p.o_head;
+        T* dst = reinterpret_cast<T*>(p.out) + (int64_t)(p.cu_q ? 0 : b) * p.o_batch + (q_start + qrow) * p.o_row +
+                 (int64_t)h * p.o_head;
 #pragma unroll
-      for (int oc = 0; oc < (D + 31) / 32; ++oc) {
-        uint32_t r[32];
-        __syncwarp();
-        tmem_ld32(tO + oc * 32, r);
-        tmem_wait_ld();
-        if (qrow < q_len) {
+        for (int oc = 0; oc < (D + 31) / 32; ++oc) {
+          uint32_t r[32];
+          __syncwarp();
+          tmem_ld32(tO + oc * 32, r);
+          tmem_wait_ld();
+          if (qrow < q_len) {
 #pragma unroll
-          for (int e = 0; e < 32 && oc * 32 + e < D; e += 8) {
-            uint4 w;
-            w.x = Cvt<T>::pack2(__uint_as_float(r[e]) * inv, __uint_as_float(r[e + 1]) * inv);
-            w.y = Cvt<T>::pack2(__uint_as_float(r[e + 2]) * inv, __uint_as_float(r[e + 3]) * inv);
-            w.z = Cvt<T>::pack2(__uint_as_float(r[e + 4]) * inv, __uint_as_float(r[e + 5]) * inv);
-            w.w = Cvt<T>::pack2(__uint_as_float(r[e + 6]) * inv, __uint_as_float(r[e + 7]) * inv);
-            *reinterpret_cast<uint4*>(dst + oc * 32 + e) = w;
+            for (int e = 0; e < 32 && oc * 32 + e < D; e += 8) {
+              uint4 w;
+              w.x = Cvt<T>::pack2(__uint_as_float(r[e]) * inv, __uint_as_float(r[e + 1]) * inv);
+              w.y = Cvt<T>::pack2(__uint_as_float(r[e + 2]) * inv, __uint_as_float(r[e + 3]) * inv);
+              w.z = Cvt<T>::pack2(__uint_as_float(r[e + 4]) * inv, __uint_as_float(r[e + 5]) * inv);
+              w.w = Cvt<T>::pack2(__uint_as_float(r[e + 6]) * inv, __uint_as_float(r[e + 7]) * inv);
+              *reinterpret_cast<uint4*>(dst + oc * 32 + e) = w;
+            }
           }
         }
-      }
       }
     }
   }
