@@ -15,6 +15,9 @@ int set_error(int code, const char* fmt, ...);
 // HI3D_OK, or HI3D_ERR_CUDA with the launch error recorded.
 int check_launch(const char* what);
 
+// Streaming multiprocessors of the current device (cached per device).
+int sm_count();
+
 // Encode a tiled TMA descriptor (dims/strides innermost first; strides are
 // given for dims 1..rank-1 in bytes).
 int encode_tmap(CUtensorMap* map, CUtensorMapDataType type, int rank, const void* base, const uint64_t* dims,

@@ -57,86 +57,94 @@ __global__ void __launch_bounds__(256) quant_h64_kernel(const T* __restrict__ x,
   constexpr int RPB = 8 / WPR;  // rows per block
   __shared__ float red[8];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t row = (int64_t)blockIdx.x * RPB + warp / WPR;
   const int part = warp % WPR;
-  const bool row_ok = row < rows;
-  const T* xr = x + (row_ok ? row : 0) * K;
-  float y[IPW][8];
-  float amax = 0.f;
+  // grid-stride over groups of RPB rows (the grid is sized to whole waves); the trip
+  // count is uniform across the block, so every thread reaches the block barriers
+  for (int64_t g = blockIdx.x; g * RPB < rows; g += gridDim.x) {
+    const int64_t row = g * RPB + warp / WPR;
+    const bool row_ok = row < rows;
+    const T* xr = x + (row_ok ? row : 0) * K;
+    float y[IPW][8];
+    float amax = 0.f;
 #pragma unroll
-  for (int j = 0; j < IPW; ++j) {
-    const int base = (part + j * WPR) * 256 + lane * 8;
-    const bool active = row_ok && base < K;
-    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    if (active) {
-      load8<T>(xr + base, v);
-      if (ROTATE) {
-        const float4 s0 = *reinterpret_cast<const float4*>(sign + base);
-        const float4 s1 = *reinterpret_cast<const float4*>(sign + base + 4);
-        v[0] = __fmul_rn(v[0], s0.x); v[1] = __fmul_rn(v[1], s0.y);
-        v[2] = __fmul_rn(v[2], s0.z); v[3] = __fmul_rn(v[3], s0.w);
-        v[4] = __fmul_rn(v[4], s1.x); v[5] = __fmul_rn(v[5], s1.y);
-        v[6] = __fmul_rn(v[6], s1.z); v[7] = __fmul_rn(v[7], s1.w);
-      }
-    }
-    if (ROTATE) {
-      // element bits 0, 1, 2: in registers
-#pragma unroll
-      for (int d = 1; d < 8; d <<= 1) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          if (i & d) continue;
-          const float u = v[i], w = v[i | d];
-          v[i] = __fadd_rn(u, w);
-          v[i | d] = __fsub_rn(u, w);
+    for (int j = 0; j < IPW; ++j) {
+      const int base = (part + j * WPR) * 256 + lane * 8;
+      const bool active = row_ok && base < K;
+      float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      if (active) {
+        load8<T>(xr + base, v);
+        if (ROTATE) {
+          const float4 s0 = *reinterpret_cast<const float4*>(sign + base);
+          const float4 s1 = *reinterpret_cast<const float4*>(sign + base + 4);
+          v[0] = __fmul_rn(v[0], s0.x); v[1] = __fmul_rn(v[1], s0.y);
+          v[2] = __fmul_rn(v[2], s0.z); v[3] = __fmul_rn(v[3], s0.w);
+          v[4] = __fmul_rn(v[4], s1.x); v[5] = __fmul_rn(v[5], s1.y);
+          v[6] = __fmul_rn(v[6], s1.z); v[7] = __fmul_rn(v[7], s1.w);
         }
       }
-      // element bits 3, 4: lanes 1 and 2 apart; bit 5: lanes 4 apart, with the 1/8 scale
-      const int g = lane & 7;
+      if (ROTATE) {
+        // element bits 0, 1, 2: in registers
 #pragma unroll
-      for (int i = 0; i < 8; ++i) v[i] = butterfly_lane(v[i], 1, g & 1);
+        for (int d = 1; d < 8; d <<= 1) {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) v[i] = butterfly_lane(v[i], 2, g & 2);
+          for (int i = 0; i < 8; ++i) {
+            if (i & d) continue;
+            const float u = v[i], w = v[i | d];
+            v[i] = __fadd_rn(u, w);
+            v[i | d] = __fsub_rn(u, w);
+          }
+        }
+        // element bits 3, 4: lanes 1 and 2 apart; bit 5: lanes 4 apart, with the 1/8 scale
+        const int g = lane & 7;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(butterfly_lane(v[i], 4, g & 4), 0.125f);
+        for (int i = 0; i < 8; ++i) v[i] = butterfly_lane(v[i], 1, g & 1);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = butterfly_lane(v[i], 2, g & 2);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(butterfly_lane(v[i], 4, g & 4), 0.125f);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        y[j][i] = v[i];
+        if (active) amax = fmaxf(amax, fabsf(v[i]));
+      }
     }
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      y[j][i] = v[i];
-      if (active) amax = fmaxf(amax, fabsf(v[i]));
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if (WPR > 1) {
+      if (lane == 0) red[warp] = amax;
+      __syncthreads();
+      const int first = warp - part;
+#pragma unroll
+      for (int w = 0; w < WPR; ++w) amax = fmaxf(amax, red[first + w]);
     }
-  }
+    if (row_ok) {
+      const float s = __fdiv_rn(fmaxf(amax, 1e-8f), 127.0f);
+      const float inv = __frcp_rn(s);
+      if (lane == 0 && part == 0) scale[row] = s;
+      int8_t* qr = q + row * K;
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-  if (WPR > 1) {
-    if (lane == 0) red[warp] = amax;
-    __syncthreads();
-    const int first = warp - part;
+      for (int j = 0; j < IPW; ++j) {
+        const int base = (part + j * WPR) * 256 + lane * 8;
+        if (base >= K) continue;
+        uint32_t w[2] = {0u, 0u};
 #pragma unroll
-    for (int w = 0; w < WPR; ++w) amax = fmaxf(amax, red[first + w]);
-  }
-  if (!row_ok) return;
-  const float s = __fdiv_rn(fmaxf(amax, 1e-8f), 127.0f);
-  const float inv = __frcp_rn(s);
-  if (lane == 0 && part == 0) scale[row] = s;
-  int8_t* qr = q + row * K;
-#pragma unroll
-  for (int j = 0; j < IPW; ++j) {
-    const int base = (part + j * WPR) * 256 + lane * 8;
-    if (base >= K) continue;
-    uint32_t w[2] = {0u, 0u};
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-      w[i >> 2] |= ((uint32_t)(uint8_t)(int8_t)quant_code(y[j][i], s, inv)) << (8 * (i & 3));
-    *reinterpret_cast<uint2*>(qr + base) = make_uint2(w[0], w[1]);
+        for (int i = 0; i < 8; ++i)
+          w[i >> 2] |= ((uint32_t)(uint8_t)(int8_t)quant_code(y[j][i], s, inv)) << (8 * (i & 3));
+        *reinterpret_cast<uint2*>(qr + base) = make_uint2(w[0], w[1]);
+      }
+    }
+    if (WPR > 1) __syncthreads();  // red[] is rewritten by the next group
   }
 }
 
 template <typename T, int IPW, int WPR, bool ROTATE>
 static void launch_q(const void* x, const float* sign, int8_t* q, float* scale, int64_t rows, int K, cudaStream_t st) {
   constexpr int RPB = 8 / WPR;
+  // at most 8 resident 256-thread blocks per SM: a grid of whole waves
+  const int64_t blocks = (rows + RPB - 1) / RPB, cap = (int64_t)sm_count() * 8;
   quant_h64_kernel<T, IPW, WPR, ROTATE>
-      <<<(unsigned)((rows + RPB - 1) / RPB), 256, 0, st>>>((const T*)x, sign, q, scale, rows, K);
+      <<<(unsigned)(blocks < cap ? blocks : cap), 256, 0, st>>>((const T*)x, sign, q, scale, rows, K);
 }
 
 template <typename T, int WPR, bool ROTATE>

@@ -45,89 +45,92 @@ __global__ void __launch_bounds__(256) ln_mod_kernel(const T* __restrict__ x, T*
                                                      const float* __restrict__ bias, const T* __restrict__ scale,
                                                      const T* __restrict__ shift, int64_t rows_per_batch,
                                                      int64_t mod_stride) {
-  const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
-  if (row >= rows) return;
   const int lane = threadIdx.x & 31;
-  const T* xr = x + row * C;
-  T* yr = out + row * C;
+  // grid-stride over rows (the grid is sized to whole waves), one warp per row
+  for (int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5); row < rows; row += (int64_t)gridDim.x * 8) {
+    const T* xr = x + row * C;
+    T* yr = out + row * C;
 
-  // chunk c covers channels [c*256, c*256+256); only the last chunk can be partial
-  float v[NCH][8];
+    // chunk c covers channels [c*256, c*256+256); only the last chunk can be partial
+    float v[NCH][8];
 #pragma unroll
-  for (int c = 0; c < NCH; ++c) {
-    Vec8 raw = {};
-    if (c * 256 + lane * 8 < C) raw = *reinterpret_cast<const Vec8*>(xr + c * 256 + lane * 8);
-    unpack8<T>(raw, v[c]);
-  }
-  float sum = 0.f;
+    for (int c = 0; c < NCH; ++c) {
+      Vec8 raw = {};
+      if (c * 256 + lane * 8 < C) raw = *reinterpret_cast<const Vec8*>(xr + c * 256 + lane * 8);
+      unpack8<T>(raw, v[c]);
+    }
+    float sum = 0.f;
 #pragma unroll
-  for (int c = 0; c < NCH; ++c)
+    for (int c = 0; c < NCH; ++c)
 #pragma unroll
-    for (int i = 0; i < 8; ++i) sum += v[c][i];
+      for (int i = 0; i < 8; ++i) sum += v[c][i];
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-  const float mean = __fdiv_rn(sum, (float)C);
-  float sq = 0.f;
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    const float mean = __fdiv_rn(sum, (float)C);
+    float sq = 0.f;
 #pragma unroll
-  for (int c = 0; c < NCH; ++c) {
-    if (c * 256 + lane * 8 < C) {
+    for (int c = 0; c < NCH; ++c) {
+      if (c * 256 + lane * 8 < C) {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        float d = __fsub_rn(v[c][i], mean);
-        sq = __fmaf_rn(d, d, sq);
+        for (int i = 0; i < 8; ++i) {
+          float d = __fsub_rn(v[c][i], mean);
+          sq = __fmaf_rn(d, d, sq);
+        }
       }
     }
-  }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
-  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sq, (float)C), eps)));
+    for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sq, (float)C), eps)));
 
-  const int64_t mb = MODULATE ? (row / rows_per_batch) * mod_stride : 0;
+    const int64_t mb = MODULATE ? (row / rows_per_batch) * mod_stride : 0;
 #pragma unroll
-  for (int c = 0; c < NCH; ++c) {
-    const int base = c * 256 + lane * 8;
-    if (base >= C) continue;
-    Vec8 o;
-    Vec8 sc, sh;
-    if (MODULATE) {
-      sc = *reinterpret_cast<const Vec8*>(scale + mb + base);
-      sh = *reinterpret_cast<const Vec8*>(shift + mb + base);
-    }
-    float wv[8], bv[8];
-    if (AFFINE) {
-      *reinterpret_cast<float4*>(&wv[0]) = *reinterpret_cast<const float4*>(weight + base);
-      *reinterpret_cast<float4*>(&wv[4]) = *reinterpret_cast<const float4*>(weight + base + 4);
-      *reinterpret_cast<float4*>(&bv[0]) = *reinterpret_cast<const float4*>(bias + base);
-      *reinterpret_cast<float4*>(&bv[4]) = *reinterpret_cast<const float4*>(bias + base + 4);
-    }
-#pragma unroll
-    for (int i = 0; i < 8; i += 2) {
-      float y0 = __fmul_rn(__fsub_rn(v[c][i], mean), inv);
-      float y1 = __fmul_rn(__fsub_rn(v[c][i + 1], mean), inv);
-      if (AFFINE) {
-        y0 = __fadd_rn(__fmul_rn(y0, wv[i]), bv[i]);
-        y1 = __fadd_rn(__fmul_rn(y1, wv[i + 1]), bv[i + 1]);
-      }
-      T h0 = round_t<T>(y0), h1 = round_t<T>(y1);
+    for (int c = 0; c < NCH; ++c) {
+      const int base = c * 256 + lane * 8;
+      if (base >= C) continue;
+      Vec8 o;
+      Vec8 sc, sh;
       if (MODULATE) {
-        const T* s2 = reinterpret_cast<const T*>(&sc.w[i / 2]);
-        const T* t2 = reinterpret_cast<const T*>(&sh.w[i / 2]);
-        h0 = round_t<T>(__fmul_rn(Cvt<T>::to_f(h0), Cvt<T>::to_f(s2[0])));
-        h1 = round_t<T>(__fmul_rn(Cvt<T>::to_f(h1), Cvt<T>::to_f(s2[1])));
-        h0 = round_t<T>(__fadd_rn(Cvt<T>::to_f(h0), Cvt<T>::to_f(t2[0])));
-        h1 = round_t<T>(__fadd_rn(Cvt<T>::to_f(h1), Cvt<T>::to_f(t2[1])));
+        sc = *reinterpret_cast<const Vec8*>(scale + mb + base);
+        sh = *reinterpret_cast<const Vec8*>(shift + mb + base);
       }
-      T pair[2] = {h0, h1};
-      o.w[i / 2] = *reinterpret_cast<uint32_t*>(pair);
+      float wv[8], bv[8];
+      if (AFFINE) {
+        *reinterpret_cast<float4*>(&wv[0]) = *reinterpret_cast<const float4*>(weight + base);
+        *reinterpret_cast<float4*>(&wv[4]) = *reinterpret_cast<const float4*>(weight + base + 4);
+        *reinterpret_cast<float4*>(&bv[0]) = *reinterpret_cast<const float4*>(bias + base);
+        *reinterpret_cast<float4*>(&bv[4]) = *reinterpret_cast<const float4*>(bias + base + 4);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; i += 2) {
+        float y0 = __fmul_rn(__fsub_rn(v[c][i], mean), inv);
+        float y1 = __fmul_rn(__fsub_rn(v[c][i + 1], mean), inv);
+        if (AFFINE) {
+          y0 = __fadd_rn(__fmul_rn(y0, wv[i]), bv[i]);
+          y1 = __fadd_rn(__fmul_rn(y1, wv[i + 1]), bv[i + 1]);
+        }
+        T h0 = round_t<T>(y0), h1 = round_t<T>(y1);
+        if (MODULATE) {
+          const T* s2 = reinterpret_cast<const T*>(&sc.w[i / 2]);
+          const T* t2 = reinterpret_cast<const T*>(&sh.w[i / 2]);
+          h0 = round_t<T>(__fmul_rn(Cvt<T>::to_f(h0), Cvt<T>::to_f(s2[0])));
+          h1 = round_t<T>(__fmul_rn(Cvt<T>::to_f(h1), Cvt<T>::to_f(s2[1])));
+          h0 = round_t<T>(__fadd_rn(Cvt<T>::to_f(h0), Cvt<T>::to_f(t2[0])));
+          h1 = round_t<T>(__fadd_rn(Cvt<T>::to_f(h1), Cvt<T>::to_f(t2[1])));
+        }
+        T pair[2] = {h0, h1};
+        o.w[i / 2] = *reinterpret_cast<uint32_t*>(pair);
+      }
+      *reinterpret_cast<Vec8*>(yr + base) = o;
     }
-    *reinterpret_cast<Vec8*>(yr + base) = o;
   }
 }
 
 template <typename T, int NCH>
 static void launch_ln(const void* x, void* out, int64_t rows, int C, float eps, const float* w, const float* b,
                       const void* sc, const void* sh, int64_t rpb, int64_t ms, cudaStream_t st) {
-  dim3 grid((unsigned)((rows + 7) / 8)), block(256);
+  // at most 8 resident 256-thread blocks per SM: a grid of whole waves, rows by grid stride
+  const int64_t blocks = (rows + 7) / 8, cap = (int64_t)sm_count() * 8;
+  dim3 grid((unsigned)(blocks < cap ? blocks : cap)), block(256);
   const T* xt = (const T*)x;
   T* ot = (T*)out;
   const T* s = (const T*)sc;
