@@ -55,7 +55,7 @@ def build(force: bool = False, jobs: int | None = None, verbose: bool = True) ->
         objs = list(pool.map(lambda s: _compile(s, force), sources))
     newest = max(o.stat().st_mtime for o in objs)
     if force or not LIB.exists() or LIB.stat().st_mtime < newest:
-        cmd = [NVCC, *ARCH, "-shared", *[str(o) for o in objs], "-o", str(LIB)]
+        cmd = [NVCC, *ARCH, "-shared", *[str(o) for o in objs], "-ldl", "-o", str(LIB)]
         proc = subprocess.run(cmd, capture_output=True, text=True)
         if proc.returncode != 0:
             raise RuntimeError(f"link failed:\n{proc.stderr}")

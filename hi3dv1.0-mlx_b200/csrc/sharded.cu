@@ -1,0 +1,256 @@
+// Query-sharded self-attention over the GPUs of one node, one process per GPU.
+//
+// Each rank holds a contiguous slice of S rows of one sequence: its queries, keys
+// and values ([S, H, D], token-major).  The K/V slices of all ranks are
+// all-gathered over NCCL on a side stream while the caller's stream attends the
+// rank's own keys; the caller's stream then waits for the gather, attends the
+// keys before and after its own slice, and merges the partial results by their
+// log2-sum-exp weights (hi3d_flash_attn_fwd_partial / hi3d_flash_attn_merge).
+//
+// NCCL is loaded at run time (dlopen of libnccl.so.2), so the library has no link
+// dependency on it; inside a process that already loaded NCCL (e.g. through
+// PyTorch) the same copy is used.
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <cmath>
+#include <cstring>
+#include <mutex>
+
+#include "abi.h"
+
+namespace hi3d {
+namespace {
+
+struct NcclApi {
+  ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*group_start)() = nullptr;
+  ncclResult_t (*group_end)() = nullptr;
+  const char* (*error_string)(ncclResult_t) = nullptr;
+  bool ok = false;
+};
+
+const NcclApi& nccl() {
+  static NcclApi api;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) return;
+    api.get_unique_id = reinterpret_cast<decltype(api.get_unique_id)>(dlsym(h, "ncclGetUniqueId"));
+    api.comm_init_rank = reinterpret_cast<decltype(api.comm_init_rank)>(dlsym(h, "ncclCommInitRank"));
+    api.comm_destroy = reinterpret_cast<decltype(api.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
+    api.all_gather = reinterpret_cast<decltype(api.all_gather)>(dlsym(h, "ncclAllGather"));
+    api.group_start = reinterpret_cast<decltype(api.group_start)>(dlsym(h, "ncclGroupStart"));
+    api.group_end = reinterpret_cast<decltype(api.group_end)>(dlsym(h, "ncclGroupEnd"));
+    api.error_string = reinterpret_cast<decltype(api.error_string)>(dlsym(h, "ncclGetErrorString"));
+    api.ok = api.get_unique_id && api.comm_init_rank && api.comm_destroy && api.all_gather && api.group_start &&
+             api.group_end && api.error_string;
+  });
+  return api;
+}
+
+int nccl_error(const char* what, ncclResult_t r) {
+  return set_error(HI3D_ERR_NCCL, "%s: %s", what, nccl().error_string ? nccl().error_string(r) : "NCCL error");
+}
+
+// A communicator with the side stream and events of the K/V gather.
+struct Comm {
+  ncclComm_t comm = nullptr;
+  int rank = 0, world = 1, device = 0;
+  cudaStream_t side = nullptr;
+  cudaEvent_t inputs_ready = nullptr, gathered = nullptr;
+};
+
+// Key splits per query block that fill whole waves of `sms` one-CTA-per-SM blocks:
+// the s minimising ceil(ctas * s / sms) / s, taken only when it beats no split by
+// more than 3 % and leaves at least two key blocks per split (as the Python side).
+int auto_splits(int64_t ctas, int64_t key_blocks, int sms) {
+  int best = 1;
+  double best_t = std::ceil((double)ctas / sms);
+  for (int s = 2; s <= 8; ++s) {
+    if (key_blocks < 2 * s) break;
+    const double t = std::ceil((double)ctas * s / sms) / s;
+    if (t < best_t * 0.97) {
+      best = s;
+      best_t = t;
+    }
+  }
+  return best;
+}
+
+struct Plan {
+  int64_t ranges[3][2];  // key row ranges: own slice, before it, after it
+  int splits[3];
+  int slots;
+};
+
+Plan make_plan(int rank, int world, int64_t s_rows, int heads, int head_dim) {
+  Plan p{};
+  const int64_t total = s_rows * world;
+  p.ranges[0][0] = rank * s_rows;
+  p.ranges[0][1] = (rank + 1) * s_rows;
+  p.ranges[1][0] = 0;
+  p.ranges[1][1] = rank * s_rows;
+  p.ranges[2][0] = (rank + 1) * s_rows;
+  p.ranges[2][1] = total;
+  const int bk = head_dim == 64 ? 128 : 64;
+  const int64_t ctas = (s_rows + 255) / 256 * heads;
+  p.slots = 0;
+  for (int r = 0; r < 3; ++r) {
+    const int64_t n = p.ranges[r][1] - p.ranges[r][0];
+    p.splits[r] = n > 0 ? auto_splits(ctas, (n + bk - 1) / bk, sm_count()) : 0;
+    p.slots += p.splits[r];
+  }
+  return p;
+}
+
+int64_t part_bytes(int slots, int64_t s_rows, int heads, int head_dim) {
+  return (int64_t)slots * s_rows * heads * head_dim * 4;
+}
+
+}  // namespace
+}  // namespace hi3d
+
+using namespace hi3d;
+
+extern "C" int hi3d_nccl_unique_id(void* id) {
+  if (!id) return set_error(HI3D_ERR_INVALID_ARGUMENT, "nccl_unique_id: null pointer");
+  if (!nccl().ok) return set_error(HI3D_ERR_NCCL, "nccl_unique_id: libnccl.so.2 could not be loaded");
+  ncclUniqueId u;
+  ncclResult_t r = nccl().get_unique_id(&u);
+  if (r != ncclSuccess) return nccl_error("ncclGetUniqueId", r);
+  memcpy(id, &u, sizeof(u));
+  return HI3D_OK;
+}
+
+extern "C" int hi3d_nccl_comm_init(const void* id, int world, int rank, void** comm) {
+  if (!id || !comm || world < 1 || rank < 0 || rank >= world)
+    return set_error(HI3D_ERR_INVALID_ARGUMENT, "nccl_comm_init: bad arguments");
+  if (!nccl().ok) return set_error(HI3D_ERR_NCCL, "nccl_comm_init: libnccl.so.2 could not be loaded");
+  Comm* c = new Comm;
+  c->rank = rank;
+  c->world = world;
+  cudaGetDevice(&c->device);
+  ncclUniqueId u;
+  memcpy(&u, id, sizeof(u));
+  ncclResult_t r = nccl().comm_init_rank(&c->comm, world, u, rank);
+  if (r != ncclSuccess) {
+    delete c;
+    return nccl_error("ncclCommInitRank", r);
+  }
+  cudaError_t e = cudaStreamCreateWithFlags(&c->side, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->inputs_ready, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->gathered, cudaEventDisableTiming);
+  if (e != cudaSuccess) {
+    nccl().comm_destroy(c->comm);
+    delete c;
+    return set_error(HI3D_ERR_CUDA, "nccl_comm_init: stream/event: %s", cudaGetErrorString(e));
+  }
+  *comm = c;
+  return HI3D_OK;
+}
+
+extern "C" int hi3d_nccl_comm_destroy(void* comm) {
+  if (!comm) return HI3D_OK;
+  Comm* c = static_cast<Comm*>(comm);
+  cudaStreamSynchronize(c->side);
+  if (c->inputs_ready) cudaEventDestroy(c->inputs_ready);
+  if (c->gathered) cudaEventDestroy(c->gathered);
+  if (c->side) cudaStreamDestroy(c->side);
+  ncclResult_t r = c->comm ? nccl().comm_destroy(c->comm) : ncclSuccess;
+  delete c;
+  return r == ncclSuccess ? HI3D_OK : nccl_error("ncclCommDestroy", r);
+}
+
+extern "C" int hi3d_sharded_attn_workspace_size(void* comm, int64_t s_rows, int heads, int head_dim,
+                                                int64_t* bytes) {
+  if (!comm || !bytes || s_rows < 0 || heads <= 0)
+    return set_error(HI3D_ERR_INVALID_ARGUMENT, "sharded_attn_workspace_size: bad arguments");
+  const Comm* c = static_cast<const Comm*>(comm);
+  const Plan p = make_plan(c->rank, c->world, s_rows, heads, head_dim);
+  const int64_t po = part_bytes(p.slots, s_rows, heads, head_dim);
+  *bytes = ((po + 255) & ~int64_t(255)) + po / head_dim + 256;
+  return HI3D_OK;
+}
+
+extern "C" int hi3d_sharded_attn(void* comm, const void* q, const void* k, const void* v, void* k_all, void* v_all,
+                                 void* out, int64_t s_rows, int heads, int head_dim, float scale, int dtype,
+                                 void* workspace, int64_t workspace_bytes, void* stream) {
+  if (!comm || !q || !k || !v || !k_all || !v_all || !out || s_rows < 0 || heads <= 0)
+    return set_error(HI3D_ERR_INVALID_ARGUMENT, "sharded_attn: bad arguments");
+  if (dtype != HI3D_F16 && dtype != HI3D_BF16)
+    return set_error(HI3D_ERR_INVALID_ARGUMENT, "sharded_attn: dtype must be f16 or bf16");
+  Comm* c = static_cast<Comm*>(comm);
+  int64_t need = 0;
+  int rc = hi3d_sharded_attn_workspace_size(comm, s_rows, heads, head_dim, &need);
+  if (rc) return rc;
+  if (s_rows == 0) return HI3D_OK;
+  if (!workspace || workspace_bytes < need || !aligned16(workspace))
+    return set_error(HI3D_ERR_CAPACITY, "sharded_attn: workspace %lld bytes, need %lld (16-byte aligned)",
+                     (long long)workspace_bytes, (long long)need);
+  const Plan p = make_plan(c->rank, c->world, s_rows, heads, head_dim);
+  float* part_o = static_cast<float*>(workspace);
+  float* part_lse = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) +
+                                             ((part_bytes(p.slots, s_rows, heads, head_dim) + 255) & ~int64_t(255)));
+  cudaStream_t st = as_stream(stream);
+  const int64_t row = (int64_t)heads * head_dim;  // elements per token row
+  const size_t esz = 2;
+
+  // K/V gather on the side stream, after the caller's stream has produced k and v
+  cudaError_t e = cudaEventRecord(c->inputs_ready, st);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(c->side, c->inputs_ready, 0);
+  if (e != cudaSuccess) return set_error(HI3D_ERR_CUDA, "sharded_attn: %s", cudaGetErrorString(e));
+  const ncclDataType_t nt = dtype == HI3D_BF16 ? ncclBfloat16 : ncclFloat16;
+  ncclResult_t r = nccl().group_start();
+  if (r == ncclSuccess) r = nccl().all_gather(k, k_all, (size_t)(s_rows * row), nt, c->comm, c->side);
+  if (r == ncclSuccess) r = nccl().all_gather(v, v_all, (size_t)(s_rows * row), nt, c->comm, c->side);
+  ncclResult_t r2 = nccl().group_end();
+  if (r != ncclSuccess) return nccl_error("ncclAllGather", r);
+  if (r2 != ncclSuccess) return nccl_error("ncclGroupEnd", r2);
+  e = cudaEventRecord(c->gathered, c->side);
+  if (e != cudaSuccess) return set_error(HI3D_ERR_CUDA, "sharded_attn: %s", cudaGetErrorString(e));
+
+  // one dense sequence: queries [S, H, D] token-major against a key range
+  auto args_for = [&](const void* kp, const void* vp, int64_t nk) {
+    hi3d_attn_args a{};
+    a.q = q;
+    a.k = kp;
+    a.v = vp;
+    a.out = out;
+    a.q_row = a.k_row = a.v_row = a.o_row = row;
+    a.q_head = a.k_head = a.v_head = a.o_head = head_dim;
+    a.q_batch = a.o_batch = s_rows * row;
+    a.k_batch = a.v_batch = 0;
+    a.nq = s_rows;
+    a.nk = nk;
+    a.max_seqlen_q = s_rows;
+    a.num_seqs = 1;
+    a.heads = heads;
+    a.head_dim = head_dim;
+    a.dtype = dtype;
+    a.scale = scale;
+    return a;
+  };
+  int slot = 0;
+  // own keys while the gather runs
+  hi3d_attn_args own = args_for(k, v, s_rows);
+  if ((rc = hi3d_flash_attn_fwd_partial(&own, p.splits[0], slot, part_o, part_lse, s_rows, st))) return rc;
+  slot += p.splits[0];
+  e = cudaStreamWaitEvent(st, c->gathered, 0);
+  if (e != cudaSuccess) return set_error(HI3D_ERR_CUDA, "sharded_attn: %s", cudaGetErrorString(e));
+  for (int i = 1; i < 3; ++i) {
+    const int64_t lo = p.ranges[i][0], n = p.ranges[i][1] - lo;
+    if (n <= 0) continue;
+    const uint8_t* kb = static_cast<const uint8_t*>(k_all) + lo * row * esz;
+    const uint8_t* vb = static_cast<const uint8_t*>(v_all) + lo * row * esz;
+    hi3d_attn_args a = args_for(kb, vb, n);
+    if ((rc = hi3d_flash_attn_fwd_partial(&a, p.splits[i], slot, part_o, part_lse, s_rows, st))) return rc;
+    slot += p.splits[i];
+  }
+  hi3d_attn_args m = args_for(k, v, s_rows);
+  return hi3d_flash_attn_merge(&m, slot, part_o, part_lse, st);
+}

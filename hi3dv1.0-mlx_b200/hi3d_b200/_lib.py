@@ -23,6 +23,7 @@ ERR_UNSUPPORTED = 2
 ERR_CUDA = 3
 ERR_DEVICE_TIMEOUT = 4
 ERR_CAPACITY = 5
+ERR_NCCL = 6
 
 F16, BF16, F32, I32 = 0, 1, 2, 3
 EPI_STORE, EPI_GELU, EPI_RESIDUAL = 0, 1, 2
@@ -68,6 +69,12 @@ SIGNATURES: dict[str, tuple] = {
     "hi3d_flash_attn_fwd_partial": (_i32, [ctypes.POINTER(AttnArgs), _i32, _i32, _c_void_p, _c_void_p, _i64,
                                            _c_void_p]),
     "hi3d_flash_attn_merge": (_i32, [ctypes.POINTER(AttnArgs), _i32, _c_void_p, _c_void_p, _c_void_p]),
+    "hi3d_nccl_unique_id": (_i32, [_c_void_p]),
+    "hi3d_nccl_comm_init": (_i32, [_c_void_p, _i32, _i32, ctypes.POINTER(_c_void_p)]),
+    "hi3d_nccl_comm_destroy": (_i32, [_c_void_p]),
+    "hi3d_sharded_attn_workspace_size": (_i32, [_c_void_p, _i64, _i32, _i32, ctypes.POINTER(_i64)]),
+    "hi3d_sharded_attn": (_i32, [_c_void_p] * 7 + [_i64, _i32, _i32, ctypes.c_float, _i32, _c_void_p, _i64,
+                                                   _c_void_p]),
     "hi3d_gemm_qkv_rope": (_i32, [_c_void_p] * 10 + [_i64, _i64, _i32, _i32, _i64, _i32, _i32, _c_void_p]),
     "hi3d_gemm_w8a8_qkv_rope": (_i32, [_c_void_p] * 12 + [_i64, _i64, _i32, _i32, _i64, _i32, _i32, _c_void_p]),
     "hi3d_neighbour_map_workspace_size": (_i32, [_i64, ctypes.POINTER(_i64)]),

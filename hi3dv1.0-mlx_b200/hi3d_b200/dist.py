@@ -104,3 +104,64 @@ class ShardedBlockStack:
         for i, w in enumerate(self.weights):
             block_forward_sharded(w, x, mod, cos, sin, kvs[i][0], kvs[i][1], self.heads, self.group, self._kv)
         return x
+
+
+class NcclComm:
+    """The library's own NCCL communicator (``hi3d_nccl_comm_init``) over the ranks of a
+    torch.distributed group: rank 0 creates the id, which is broadcast through the group."""
+
+    def __init__(self, group=None):
+        import ctypes
+
+        from . import _lib
+
+        lib = _lib.load()
+        self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        buf = ctypes.create_string_buffer(128)
+        if self.rank == 0:
+            _lib.check(lib.hi3d_nccl_unique_id(buf), "nccl_unique_id", launched=False)
+        obj = [buf.raw if self.rank == 0 else None]
+        dist.broadcast_object_list(obj, src=dist.get_global_rank(group, 0) if group is not None else 0, group=group)
+        self._id = ctypes.create_string_buffer(obj[0], 128)
+        handle = ctypes.c_void_p()
+        _lib.check(lib.hi3d_nccl_comm_init(self._id, self.world, self.rank, ctypes.byref(handle)), "nccl_comm_init",
+                   launched=False)
+        self.handle = handle
+
+    def close(self) -> None:
+        from . import _lib
+
+        if self.handle:
+            _lib.check(_lib.load().hi3d_nccl_comm_destroy(self.handle), "nccl_comm_destroy", launched=False)
+            self.handle = None
+
+
+def sharded_attention(comm: NcclComm, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float,
+                      kv_buffers: tuple[torch.Tensor, torch.Tensor] | None = None) -> torch.Tensor:
+    """Self-attention of this rank's rows through the native ``hi3d_sharded_attn``: ``q, k, v
+    [S, H, D]`` (token-major slices of one sequence, rank order); K/V gathered over the library's
+    NCCL communicator while the own keys are attended.  Returns ``[S, H * D]``."""
+    import ctypes
+
+    from . import _lib
+
+    _lib.require_cuda(q, k, v)
+    s_rows, heads, d = q.shape
+    if k.shape != q.shape or v.shape != q.shape or k.dtype != q.dtype or v.dtype != q.dtype:
+        raise ValueError("q, k, v must be [S, H, D] slices of one dtype")
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    if kv_buffers is None:
+        kv_buffers = tuple(torch.empty((comm.world * s_rows, heads, d), dtype=q.dtype, device=q.device)
+                           for _ in range(2))
+    k_all, v_all = kv_buffers
+    lib = _lib.load()
+    nbytes = ctypes.c_int64()
+    _lib.check(lib.hi3d_sharded_attn_workspace_size(comm.handle, s_rows, heads, d, ctypes.byref(nbytes)),
+               "sharded_attn workspace", launched=False)
+    ws = torch.empty(nbytes.value, dtype=torch.uint8, device=q.device)
+    out = torch.empty((s_rows, heads * d), dtype=q.dtype, device=q.device)
+    rc = lib.hi3d_sharded_attn(comm.handle, q.data_ptr(), k.data_ptr(), v.data_ptr(), k_all.data_ptr(),
+                               v_all.data_ptr(), out.data_ptr(), s_rows, heads, d, float(scale), _lib.dtype_code(q),
+                               ws.data_ptr(), ws.numel(), _lib.stream(q))
+    _lib.check(rc, "sharded_attention")
+    return out

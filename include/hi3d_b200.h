@@ -38,6 +38,7 @@ extern "C" {
 #define HI3D_ERR_CUDA 3             /* a CUDA runtime/driver call failed */
 #define HI3D_ERR_DEVICE_TIMEOUT 4   /* a bounded device-side wait ran out */
 #define HI3D_ERR_CAPACITY 5         /* a caller-provided workspace is too small */
+#define HI3D_ERR_NCCL 6             /* an NCCL call failed (or libnccl.so.2 is not available) */
 
 /* ---- element types ----------------------------------------------------- */
 #define HI3D_F16 0
@@ -147,6 +148,28 @@ HI3D_API int hi3d_flash_attn_fwd_partial(const hi3d_attn_args* args, int k_split
                                          float* part_lse, int64_t part_rows, void* stream);
 HI3D_API int hi3d_flash_attn_merge(const hi3d_attn_args* args, int num_slots, const float* part_o,
                                    const float* part_lse, void* stream);
+
+/* ---- query-sharded self-attention over NCCL ------------------------------ */
+/* One process per GPU.  hi3d_nccl_unique_id fills a 128-byte id on one rank, which the caller
+ * hands to the others; hi3d_nccl_comm_init creates the communicator on the current device
+ * (NCCL is loaded at run time from libnccl.so.2).  It is the one entry that allocates: NCCL's
+ * own buffers, plus a side stream and two events for the gather, released by
+ * hi3d_nccl_comm_destroy.
+ *
+ * hi3d_sharded_attn: the partitioned self-attention of the sharded block (the reference runs
+ * one GPU and has no counterpart; it replaces attention.flash_attention, attention.py:238-277,
+ * over all T rows).  This rank holds rows [rank * s_rows, (rank + 1) * s_rows) of one sequence:
+ * q, k, v [s_rows, heads, head_dim] token-major.  The K/V slices of all ranks are all-gathered
+ * into k_all, v_all [world * s_rows, heads, head_dim] on a side stream while the stream attends
+ * the rank's own keys; then the keys before and after its slice; the partials are merged into
+ * out [s_rows, heads * head_dim].  Same numerics as hi3d_flash_attn_fwd_split. */
+HI3D_API int hi3d_nccl_unique_id(void* id);
+HI3D_API int hi3d_nccl_comm_init(const void* id, int world, int rank, void** comm);
+HI3D_API int hi3d_nccl_comm_destroy(void* comm);
+HI3D_API int hi3d_sharded_attn_workspace_size(void* comm, int64_t s_rows, int heads, int head_dim, int64_t* bytes);
+HI3D_API int hi3d_sharded_attn(void* comm, const void* q, const void* k, const void* v, void* k_all, void* v_all,
+                               void* out, int64_t s_rows, int heads, int head_dim, float scale, int dtype,
+                               void* workspace, int64_t workspace_bytes, void* stream);
 
 /* ---- projections (tcgen05 GEMM with fused epilogues) --------------------- */
 /* out = epilogue(A W^T): A [m, k] and W [n, k] row-major (K-major, as nn.Linear weights),

@@ -73,3 +73,42 @@ def test_sharded_stack_matches_single_gpu(tmp_path):
     rel, same = np.load(out)
     assert rel < 1e-3, rel
     assert same > 0.9, same
+
+
+def _worker_native(rank, world, port, result_path):
+    sys.path.insert(0, os.path.join(REPO, "hi3dv1.0-mlx_b200"))
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    from hi3d_b200 import attention
+    from hi3d_b200 import dist as hdist
+
+    t, heads, d = 4096, 16, 64
+    g = torch.Generator(device=dev).manual_seed(3)
+    q, k, v = (torch.randn((t, heads, d), generator=g, device=dev).half() for _ in range(3))
+    rows = hdist.shard_slice(t, rank, world)
+    comm = hdist.NcclComm()
+    out_local = hdist.sharded_attention(comm, q[rows], k[rows], v[rows], d ** -0.5)
+    out = hdist.gather_rows(out_local)
+    comm.close()
+    if rank == 0:
+        bhnd = lambda z: z.permute(1, 0, 2)[None]
+        ref = attention.flash_attention(bhnd(q), bhnd(k), bhnd(v), d ** -0.5, k_splits=1)[0]
+        rel = float(((out.float() - ref.float()).abs().max() / ref.float().abs().max()).item())
+        np.save(result_path, np.array([rel]))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_native_sharded_attention_matches_single_gpu(tmp_path):
+    """hi3d_sharded_attn over the library's own NCCL communicator (gather on a side stream,
+    own keys first, merge) vs one pass over all keys on one GPU: within 16-bit output rounding."""
+    out = tmp_path / "r.npy"
+    mp.spawn(_worker_native, args=(2, _free_port(), str(out)), nprocs=2, join=True)
+    (rel,) = np.load(out)
+    assert rel <= 2 * 2 ** -10, rel
