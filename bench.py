@@ -339,7 +339,7 @@ def run_ours(args) -> None:
     peak = peaks["bf16_tflops_sustained"]
     attn_share = sum(r["ms"] for r in attn) / ms if ms > 0 else None
     roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-                "traffic": _profile_traffic("flash_attn_fwd_cfg1"), "kernel": "hi3d::attn::flash_fwd_kernel<half,64>",
+                "traffic": _profile_traffic("flash_attn_fwd_cfg1"), "kernel": "hi3d::attn::flash_fwd_kernel<half,64,false>",
                 "peak_source": f"{peaks['source']} bf16_tflops_sustained (burst {peaks['bf16_tflops']})",
                 "flops_per_launch": flops, "avg_launch_ms": avg_s * 1e3, "attention_time_share": attn_share}
 

@@ -93,7 +93,10 @@ struct Barriers {
   int abort;
 };
 
-template <typename T, int D>
+// PARTIAL: key-split launch writing partial O / l and log2-sum-exp (Params::part_o);
+// otherwise one pass over all keys writing `out`.  Two instantiations keep the
+// single-pass kernel free of the split bookkeeping.
+template <typename T, int D, bool PARTIAL>
 __global__ void __launch_bounds__(kThreads, 1)
     flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, const Params p) {
@@ -106,8 +109,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   Barriers* bar = reinterpret_cast<Barriers*>(sV + C::NST * C::KV_STAGE);
 
   // ---- work decode: (head, sequence, 256-row query block[, key split]) ----
-  const int split = blockIdx.x % p.k_splits;
-  const int bid = blockIdx.x / p.k_splits;
+  const int split = PARTIAL ? (int)(blockIdx.x % p.k_splits) : 0;
+  const int bid = PARTIAL ? (int)(blockIdx.x / p.k_splits) : (int)blockIdx.x;
   const int t = bid % p.tiles_per_seq;
   const int rest = bid / p.tiles_per_seq;
   const int b = rest % p.num_seqs;
@@ -126,24 +129,28 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   const int64_t q_row0 = (int64_t)t * 2 * kRowsPerTile;
   if (q_row0 >= q_len) return;  // uniform across the CTA
-  const int nblk_all = k_len > 0 ? (int)((k_len + C::BK - 1) / C::BK) : 0;
-  const int kb0 = (int)((int64_t)split * nblk_all / p.k_splits);
-  const int nblk = (int)((int64_t)(split + 1) * nblk_all / p.k_splits) - kb0;  // key blocks of this CTA
-  if (nblk <= 0) {
-    // no keys for this CTA: a split part marks its rows empty (log2-sum-exp -inf)
-    if (p.part_o) {
+  int nblk;  // key blocks of this CTA
+  if constexpr (PARTIAL) {
+    const int nblk_all = k_len > 0 ? (int)((k_len + C::BK - 1) / C::BK) : 0;
+    const int kb0 = (int)((int64_t)split * nblk_all / p.k_splits);
+    nblk = (int)((int64_t)(split + 1) * nblk_all / p.k_splits) - kb0;
+    if (nblk <= 0) {
+      // no keys for this CTA: its rows are marked empty (log2-sum-exp -inf)
       for (int e = threadIdx.x; e < 2 * kRowsPerTile; e += blockDim.x) {
         const int64_t qr = q_row0 + e;
         if (qr >= q_len) continue;
         const int64_t prow = p.cu_q ? q_start + qr : (int64_t)b * p.nq + qr;
         p.part_lse[((int64_t)(p.slot0 + split) * p.part_rows + prow) * p.heads + h] = -INFINITY;
       }
+      return;
     }
-    return;
+    // key blocks are numbered from the first block of this CTA's range
+    k_start += (int64_t)kb0 * C::BK;
+    k_len -= (int64_t)kb0 * C::BK;
+  } else {
+    if (k_len <= 0) return;
+    nblk = (int)((k_len + C::BK - 1) / C::BK);
   }
-  // key blocks are numbered from the first block of this CTA's range
-  k_start += (int64_t)kb0 * C::BK;
-  k_len -= (int64_t)kb0 * C::BK;
 
   const int warp = warp_id(), lane = lane_id();
   if (threadIdx.x == 0) {
@@ -377,7 +384,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int64_t qrow = q_row0 + i * kRowsPerTile + row;
       const float inv = 1.0f / l_run;
-      if (p.part_o) {
+      if constexpr (PARTIAL) {
         // partial result of this key range: O / l in fp32 and the log2-sum-exp
         const int64_t prow = p.cu_q ? q_start + qrow : (int64_t)b * p.nq + qrow;
         float* po = p.part_o + (((int64_t)(p.slot0 + split) * p.part_rows + prow) * p.heads + h) * D;
@@ -518,7 +525,7 @@ static int launch_attn(const hi3d_attn_args* a, cudaStream_t st, int k_splits = 
   const int64_t grid = (int64_t)p.tiles_per_seq * a->num_seqs * a->heads * k_splits;
   if (grid == 0) return HI3D_OK;
   if (grid > 0x7fffffff) return set_error(HI3D_ERR_INVALID_ARGUMENT, "flash_attn: too many tiles");
-  auto kern = attn::flash_fwd_kernel<T, D>;
+  auto kern = part_o ? attn::flash_fwd_kernel<T, D, true> : attn::flash_fwd_kernel<T, D, false>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (e != cudaSuccess) return set_error(HI3D_ERR_CUDA, "flash_attn: smem attribute: %s", cudaGetErrorString(e));
   kern<<<(unsigned)grid, attn::kThreads, C::SMEM, st>>>(mq, mk, mv, p);

@@ -39,15 +39,17 @@ __device__ __forceinline__ T round_t(float v) {
 // NCH = ceil(channels / 256) chunks of 8 elements per lane held in registers
 // (channels % 8 == 0, <= 4096).
 // ---------------------------------------------------------------------------
+constexpr int kLnRowsPerBlock = 4;  // one warp per row: 128-thread blocks, 16 resident per SM
+
 template <typename T, int NCH, bool AFFINE, bool MODULATE>
-__global__ void __launch_bounds__(256) ln_mod_kernel(const T* __restrict__ x, T* __restrict__ out, int64_t rows,
-                                                     int C, float eps, const float* __restrict__ weight,
-                                                     const float* __restrict__ bias, const T* __restrict__ scale,
-                                                     const T* __restrict__ shift, int64_t rows_per_batch,
-                                                     int64_t mod_stride) {
+__global__ void __launch_bounds__(kLnRowsPerBlock * 32)
+    ln_mod_kernel(const T* __restrict__ x, T* __restrict__ out, int64_t rows, int C, float eps,
+                  const float* __restrict__ weight, const float* __restrict__ bias, const T* __restrict__ scale,
+                  const T* __restrict__ shift, int64_t rows_per_batch, int64_t mod_stride) {
   const int lane = threadIdx.x & 31;
   // grid-stride over rows (the grid is sized to whole waves), one warp per row
-  for (int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5); row < rows; row += (int64_t)gridDim.x * 8) {
+  for (int64_t row = (int64_t)blockIdx.x * kLnRowsPerBlock + (threadIdx.x >> 5); row < rows;
+       row += (int64_t)gridDim.x * kLnRowsPerBlock) {
     const T* xr = x + row * C;
     T* yr = out + row * C;
 
@@ -128,9 +130,11 @@ __global__ void __launch_bounds__(256) ln_mod_kernel(const T* __restrict__ x, T*
 template <typename T, int NCH>
 static void launch_ln(const void* x, void* out, int64_t rows, int C, float eps, const float* w, const float* b,
                       const void* sc, const void* sh, int64_t rpb, int64_t ms, cudaStream_t st) {
-  // at most 8 resident 256-thread blocks per SM: a grid of whole waves, rows by grid stride
-  const int64_t blocks = (rows + 7) / 8, cap = (int64_t)sm_count() * 8;
-  dim3 grid((unsigned)(blocks < cap ? blocks : cap)), block(256);
+  // at most 16 resident 128-thread blocks per SM (2048 threads): a grid of whole
+  // waves, rows by grid stride
+  const int64_t blocks = (rows + kLnRowsPerBlock - 1) / kLnRowsPerBlock,
+                cap = (int64_t)sm_count() * (2048 / (kLnRowsPerBlock * 32));
+  dim3 grid((unsigned)(blocks < cap ? blocks : cap)), block(kLnRowsPerBlock * 32);
   const T* xt = (const T*)x;
   T* ot = (T*)out;
   const T* s = (const T*)sc;
