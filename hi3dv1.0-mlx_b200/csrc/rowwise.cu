@@ -53,36 +53,47 @@ __global__ void __launch_bounds__(kLnRowsPerBlock * 32)
     const T* xr = x + row * C;
     T* yr = out + row * C;
 
-    // chunk c covers channels [c*256, c*256+256); only the last chunk can be partial
-    float v[NCH][8];
+    // chunk c covers channels [c*256, c*256+256); only the last chunk can be partial.
+    // Pairs of channels travel as f32x2: one instruction per pair for each step.
+    Vec8 raw[NCH];
 #pragma unroll
     for (int c = 0; c < NCH; ++c) {
-      Vec8 raw = {};
-      if (c * 256 + lane * 8 < C) raw = *reinterpret_cast<const Vec8*>(xr + c * 256 + lane * 8);
-      unpack8<T>(raw, v[c]);
+      raw[c] = Vec8{};
+      if (c * 256 + lane * 8 < C) raw[c] = *reinterpret_cast<const Vec8*>(xr + c * 256 + lane * 8);
     }
-    float sum = 0.f;
+    uint64_t d[NCH][4];
+    uint64_t s2 = 0;  // (0.f, 0.f)
 #pragma unroll
     for (int c = 0; c < NCH; ++c)
 #pragma unroll
-      for (int i = 0; i < 8; ++i) sum += v[c][i];
+      for (int i = 0; i < 4; ++i) {
+        d[c][i] = Cvt<T>::to_f2(raw[c].w[i]);
+        s2 = f2_add(s2, d[c][i]);
+      }
+    float slo, shi;
+    f2_unpack(s2, slo, shi);
+    float sum = slo + shi;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
     const float mean = __fdiv_rn(sum, (float)C);
-    float sq = 0.f;
+    const uint64_t neg_mean = f2_splat(-mean);
+    uint64_t q2 = 0;
 #pragma unroll
     for (int c = 0; c < NCH; ++c) {
       if (c * 256 + lane * 8 < C) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          float d = __fsub_rn(v[c][i], mean);
-          sq = __fmaf_rn(d, d, sq);
+        for (int i = 0; i < 4; ++i) {
+          d[c][i] = f2_add(d[c][i], neg_mean);  // x - mean, exact as the scalar subtraction
+          q2 = f2_fma(d[c][i], d[c][i], q2);
         }
       }
     }
+    float qlo, qhi;
+    f2_unpack(q2, qlo, qhi);
+    float sq = qlo + qhi;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
-    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sq, (float)C), eps)));
+    const uint64_t inv2 = f2_splat(__fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sq, (float)C), eps))));
 
     const int64_t mb = MODULATE ? (row / rows_per_batch) * mod_stride : 0;
 #pragma unroll
@@ -95,32 +106,26 @@ __global__ void __launch_bounds__(kLnRowsPerBlock * 32)
         sc = *reinterpret_cast<const Vec8*>(scale + mb + base);
         sh = *reinterpret_cast<const Vec8*>(shift + mb + base);
       }
-      float wv[8], bv[8];
+      uint64_t wv[4], bv[4];
       if (AFFINE) {
-        *reinterpret_cast<float4*>(&wv[0]) = *reinterpret_cast<const float4*>(weight + base);
-        *reinterpret_cast<float4*>(&wv[4]) = *reinterpret_cast<const float4*>(weight + base + 4);
-        *reinterpret_cast<float4*>(&bv[0]) = *reinterpret_cast<const float4*>(bias + base);
-        *reinterpret_cast<float4*>(&bv[4]) = *reinterpret_cast<const float4*>(bias + base + 4);
+        const float4 w0 = *reinterpret_cast<const float4*>(weight + base);
+        const float4 w1 = *reinterpret_cast<const float4*>(weight + base + 4);
+        const float4 b0 = *reinterpret_cast<const float4*>(bias + base);
+        const float4 b1 = *reinterpret_cast<const float4*>(bias + base + 4);
+        wv[0] = f2_pack(w0.x, w0.y), wv[1] = f2_pack(w0.z, w0.w), wv[2] = f2_pack(w1.x, w1.y),
+        wv[3] = f2_pack(w1.z, w1.w);
+        bv[0] = f2_pack(b0.x, b0.y), bv[1] = f2_pack(b0.z, b0.w), bv[2] = f2_pack(b1.x, b1.y),
+        bv[3] = f2_pack(b1.z, b1.w);
       }
 #pragma unroll
-      for (int i = 0; i < 8; i += 2) {
-        float y0 = __fmul_rn(__fsub_rn(v[c][i], mean), inv);
-        float y1 = __fmul_rn(__fsub_rn(v[c][i + 1], mean), inv);
-        if (AFFINE) {
-          y0 = __fadd_rn(__fmul_rn(y0, wv[i]), bv[i]);
-          y1 = __fadd_rn(__fmul_rn(y1, wv[i + 1]), bv[i + 1]);
-        }
-        T h0 = round_t<T>(y0), h1 = round_t<T>(y1);
-        if (MODULATE) {
-          const T* s2 = reinterpret_cast<const T*>(&sc.w[i / 2]);
-          const T* t2 = reinterpret_cast<const T*>(&sh.w[i / 2]);
-          h0 = round_t<T>(__fmul_rn(Cvt<T>::to_f(h0), Cvt<T>::to_f(s2[0])));
-          h1 = round_t<T>(__fmul_rn(Cvt<T>::to_f(h1), Cvt<T>::to_f(s2[1])));
-          h0 = round_t<T>(__fadd_rn(Cvt<T>::to_f(h0), Cvt<T>::to_f(t2[0])));
-          h1 = round_t<T>(__fadd_rn(Cvt<T>::to_f(h1), Cvt<T>::to_f(t2[1])));
-        }
-        T pair[2] = {h0, h1};
-        o.w[i / 2] = *reinterpret_cast<uint32_t*>(pair);
+      for (int i = 0; i < 4; ++i) {
+        uint64_t y = f2_mul(d[c][i], inv2);
+        if (AFFINE) y = f2_add(f2_mul(y, wv[i]), bv[i]);
+        uint32_t h = Cvt<T>::from_f2(y);
+        // fp16/bf16 pair multiply and add are correctly rounded, so they equal
+        // rounding the fp32 product / sum of the two rounded operands
+        if (MODULATE) h = Cvt<T>::add2(Cvt<T>::mul2(h, sc.w[i]), sh.w[i]);
+        o.w[i] = h;
       }
       *reinterpret_cast<Vec8*>(yr + base) = o;
     }
