@@ -1,7 +1,7 @@
 """Benchmark of the sparse-DiT refinement torso on B200 (BASELINE configs[1] by default).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload stack|stack_w8a8|block|attention|attention262k|conv]
+                    [--workload stack|stack_w8a8|block|attention|attention262k|conv|forward]
 
 One step = one forward of the 24-block stack (C=1024, 16 heads x 64, GELU MLP 4x,
 1370 condition tokens) over T=32,768 voxel tokens of one object in fp16, inputs
@@ -13,6 +13,11 @@ slices and every block all-gathers K/V over NCCL (strong scaling).
 (T=32,768, 16x64 heads, fp16); ``--workload attention262k`` the high-resolution
 config (262,144 tokens packed as 4 objects of 65,536, bf16, varlen), query-sharded
 over the GPUs.  Both report attention TFLOP/s (4 * Nq * Nk * H * D per object).
+
+``--workload conv`` times the cfg5 submanifold convolution; ``--workload forward`` the whole
+refinement transformer around the same stack (input layer, two fine/low res blocks, the
+24 blocks, the upsampling and output res blocks, LayerNorm + output layer) on a fine shell
+whose downsampled level holds ~34k tokens, reporting transformer tokens/s.
 
 Rank 0 prints one JSON line.  ``--impl reference`` times the CPU path instead: the
 oracle port of the reference block (the reference itself is Python that cannot travel
@@ -44,6 +49,8 @@ HEADS = 16
 COND = 1370
 BLOCKS = 24
 GRID, RADIUS, THICK = 64, 24.0, 3.0
+# whole-transformer workload: fine voxels on a shell in 128^3 (R=48 +-4) -> 34,316 low tokens
+FWD_FINE, FWD_GRID, FWD_RADIUS, FWD_THICK, FWD_IO, FWD_T = 120000, 128, 48.0, 4.0, 256, 0.37
 
 
 def _peaks() -> dict:
@@ -194,6 +201,66 @@ def cpu_attention_tflops(big: bool, sample: int = 256) -> tuple[float, str]:
     return 4.0 * sample * per * HEADS * d / secs / 1e12, f"{sample} query rows x {per} keys x {HEADS} heads, fp32"
 
 
+def forward_inputs():
+    from hi3d_b200 import synthetic
+
+    if "fwd" not in _CPU_CACHE:
+        coords = synthetic.shell_coords(FWD_FINE, FWD_GRID, FWD_RADIUS, FWD_THICK, seed=1)
+        feats = synthetic.features(coords.shape[0], 32, seed=4, dtype=np.float32)
+        cond = synthetic.features(COND, CHANNELS, seed=5, dtype=np.float32)
+        _CPU_CACHE["fwd"] = (coords, feats, cond)
+    return _CPU_CACHE["fwd"]
+
+
+def cpu_forward_seconds(sample: int = 512) -> tuple[float, str]:
+    """One fp32 CPU forward of the whole transformer (oracle port): the embedding and I/O stages
+    run in full at the workload size; the 24 blocks are the row-sampled block estimate on the
+    low level, times 24."""
+    from hi3d_b200 import synthetic
+    from oracle import ops
+
+    coords, feats, cond = forward_inputs()
+    w = synthetic.model_weights(CHANNELS, CHANNELS, HEADS, 1, io_channels=FWD_IO, seed=3)
+    io_only = {k: v for k, v in w.items() if not k.startswith("blocks.")}
+    t0 = time.perf_counter()
+    ops.forward_f32(io_only, feats, coords, FWD_T, cond, HEADS)
+    io_s = time.perf_counter() - t0
+    low, _, _ = ops.downsample_structure(coords)
+    cos, sin = ops.rope_tables(low, CHANNELS // HEADS)
+    x = synthetic.features(low.shape[0], CHANNELS, seed=6, dtype=np.float32)
+    mod = synthetic.modulation(CHANNELS, FWD_T, seed=7)
+    bw = {k[len("blocks.0."):]: v for k, v in w.items() if k.startswith("blocks.0.")}
+    blk_s, _ = ops.block_seconds_sampled(bw, x, mod, cos, sin, cond, HEADS, sample=sample, seed=0)
+    desc = (f"whole transformer fp32 (numpy oracle port): embedding + I/O stages in full on {coords.shape[0]} fine "
+            f"voxels ({io_s:.1f} s), plus {BLOCKS} x one block on {low.shape[0]} low tokens estimated from "
+            f"{sample} sampled query rows ({blk_s:.1f} s each)")
+    return io_s + BLOCKS * blk_s, desc
+
+
+def cpu_conv_tflops(sample: int = 20000) -> tuple[float, str]:
+    """fp32 numpy gather-GEMM of ``sample`` output rows of the cfg5 convolution (TFLOP/s over the
+    present neighbour pairs, as the GPU arm counts them)."""
+    from hi3d_b200 import synthetic
+    from oracle import ops
+
+    if "conv" not in _CPU_CACHE:
+        n, c = 200_000, 256
+        coords = synthetic.shell_coords(n, 128, 48, 4, seed=5)
+        rng = np.random.default_rng(3)
+        table = ops.neighbour_table(coords)[:sample]
+        x = np.concatenate([rng.standard_normal((n, c)).astype(np.float32), np.zeros((1, c), np.float32)])
+        wt = (rng.standard_normal((27, c, c)) * 0.02).astype(np.float32)
+        _CPU_CACHE["conv"] = (table, x, wt, n)
+    table, x, wt, n = _CPU_CACHE["conv"]
+    t0 = time.perf_counter()
+    out = np.zeros((table.shape[0], wt.shape[2]), np.float32)
+    for k in range(27):
+        out += x[table[:, k]] @ wt[k]
+    secs = time.perf_counter() - t0
+    pairs = int((table < n).sum())
+    return 2.0 * wt.shape[1] * wt.shape[2] * pairs / secs / 1e12, f"{sample} output rows of cfg5, fp32 gather-GEMM"
+
+
 def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -212,6 +279,26 @@ def run_reference(args) -> None:
         desc = (f"one fp32 block at T={T_TOKENS} per step (numpy oracle port of the reference block): K/V side on "
                 f"all rows, {sample} sampled query rows for the rest, scaled by T/{sample}")
         workload = f"cfg1 block on CPU: T={T_TOKENS}, C={CHANNELS}, H={HEADS}x64, L={COND}"
+    elif args.workload == "forward":
+        secs = []
+        for i in range(args.warmup + args.steps):
+            sec, desc = cpu_forward_seconds()
+            if i >= args.warmup:
+                secs.append(sec)
+        from oracle import ops
+
+        n_low = ops.downsample_structure(forward_inputs()[0])[0].shape[0]
+        per = statistics.median(secs)
+        value, unit, metric, ms_step = n_low / per, "tokens/s", "forward_tokens_per_s", per * 1e3
+        workload = f"whole transformer on CPU: {FWD_FINE} fine voxels, {n_low} low tokens, {BLOCKS} blocks"
+    elif args.workload == "conv":
+        vals = []
+        for i in range(args.warmup + args.steps):
+            v, desc = cpu_conv_tflops()
+            if i >= args.warmup:
+                vals.append(v)
+        value, unit, metric, ms_step = statistics.median(vals), "TFLOP/s", "sparse_conv_tflops", None
+        workload = "cfg5 submanifold conv on CPU"
     else:
         big = args.workload == "attention262k"
         vals = []
@@ -561,14 +648,98 @@ def run_conv(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_forward(args) -> None:
+    """The whole refinement transformer (one conditioned branch) on one GPU: a step is one
+    velocity evaluation, inputs resident; ``value`` = low-level tokens / step time."""
+    import torch
+
+    from hi3d_b200 import _lib, attention, model, synthetic
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    _lib.load()
+    coords, feats, cond = forward_inputs()
+    cfg = model.ModelConfig(model_channels=CHANNELS, cond_channels=CHANNELS, num_heads=HEADS, num_blocks=BLOCKS,
+                            io_channels=FWD_IO)
+    m = model.Sparc3DTransformer(cfg, synthetic.model_weights(CHANNELS, CHANNELS, HEADS, BLOCKS, io_channels=FWD_IO,
+                                                              seed=3), device=dev)
+    geo = model.Geometry(coords, cfg.head_dim, device=dev)
+    n_low = geo.low.n
+    kvs = m.prepare(torch.from_numpy(cond).to(dev))
+    f_host = torch.from_numpy(feats).pin_memory()
+    f_dev = f_host.to(dev)
+    step = lambda f: m(f, FWD_T, geo, kvs)[0]
+    for _ in range(args.warmup):
+        step(f_dev)
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    attention.TIMER.start()
+    _lib.LAUNCHES[0] = 0
+    with ClockSampler(0) as clocks:
+        e0.record(stream)
+        for _ in range(args.steps):
+            step(f_dev)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    launches = _lib.LAUNCHES[0]
+    attn = attention.TIMER.stop()
+    ms = e0.elapsed_time(e1) / args.steps
+    # the I/O stages alone (same calls as inside a step), for the split of the step time
+    emb, _ = m.embed(FWD_T)
+    e0.record(stream)
+    for _ in range(args.steps):
+        h, skip0 = m.input_stage(f_dev, emb, geo)
+        m.output_stage(h, h, skip0, emb, geo)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    io_ms = e0.elapsed_time(e1) / args.steps
+    out_host = torch.empty((coords.shape[0], 32), dtype=torch.float32).pin_memory()
+    e0.record(stream)
+    for _ in range(args.steps):
+        out_host.copy_(step(f_host.to(dev, non_blocking=True)), non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+
+    peaks = _peaks()
+    self_launches = [r for r in attn if r["nk"] == n_low and r["flops"]]
+    avg_s = sum(r["ms"] for r in self_launches) / max(1, len(self_launches)) / 1e3
+    flops = sum(r["flops"] for r in self_launches) / max(1, len(self_launches))
+    achieved = flops / avg_s / 1e12 if avg_s > 0 else 0.0
+    peak = peaks["bf16_tflops_sustained"]
+    line = {
+        "metric": "forward_tokens_per_s", "value": n_low / (ms / 1e3), "unit": "tokens/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "none",
+        "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": {"workload": (f"whole refinement transformer fwd: {coords.shape[0]} fine shell voxels in "
+                                f"{FWD_GRID}^3 -> {n_low} low tokens, I/O stage {FWD_IO} channels, {BLOCKS} blocks "
+                                f"C={CHANNELS} {HEADS}x{CHANNELS // HEADS} heads, {COND} cond tokens, fp16 torso"),
+                   "fine_voxels": int(coords.shape[0]), "low_tokens": n_low, "io_stages_ms": io_ms,
+                   "stack_ms": ms - io_ms, "l2": "inputs larger than L2 (705 MB of weights per step)"},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak, "traffic": None,
+                     "kernel": "hi3d::attn::flash_fwd_kernel<half,64,false>",
+                     "peak_source": f"{peaks['source']} bf16_tflops_sustained", "flops_per_launch": flops,
+                     "avg_launch_ms": avg_s * 1e3},
+        "e2e": {"value": n_low / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": f_host.numel() * 4,
+                "d2h_bytes_per_step": out_host.numel() * 4},
+        "gpu_launches": launches, "clocks": clocks.summary(),
+    }
+    secs, desc = cpu_forward_seconds()
+    line["cpu_baseline"] = {"value": n_low / secs, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+                            "sample": desc}
+    print(json.dumps(line), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["stack", "stack_w8a8", "block", "attention", "attention262k", "conv"],
-                    default="stack")
+    ap.add_argument("--workload", choices=["stack", "stack_w8a8", "block", "attention", "attention262k", "conv",
+                                           "forward"], default="stack")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -578,6 +749,8 @@ def main() -> None:
         run_ours(args)
     elif args.workload == "conv":
         run_conv(args)
+    elif args.workload == "forward":
+        run_forward(args)
     else:
         run_attention(args, big=args.workload == "attention262k")
 

@@ -29,19 +29,29 @@ __device__ __forceinline__ T round_t(float v) {
   return Cvt<T>::from_f(v);
 }
 
+// SiLU of a rounded pair, evaluated in fp32 and rounded once (F.silu on fp16,
+// the activation after the res-block norms: sparc3d_transformer.py:137-141).
+__device__ __forceinline__ float silu_f(float v) { return v / (1.0f + __expf(-v)); }
+template <typename T>
+__device__ __forceinline__ uint32_t silu2(uint32_t h) {
+  const T* e = reinterpret_cast<const T*>(&h);
+  return Cvt<T>::pack2(silu_f(Cvt<T>::to_f(e[0])), silu_f(Cvt<T>::to_f(e[1])));
+}
+
 // ---------------------------------------------------------------------------
-// LayerNorm32 (+ affine) (+ modulation), one warp per row.
+// LayerNorm32 (+ affine) (+ modulation) (+ SiLU), one warp per row.
 //
 // Semantics of kernels.py:162-201: fp32 sum -> mean = sum / C; fp32 sum of
 // squared deviations; inv = 1 / sqrt(sumsq / C + eps) (IEEE sqrt and divide);
 // y = (x - mean) * inv; affine y = y * w + b without contraction; h = T(y);
-// modulation h = T(float(h) * float(scale)); h = T(float(h) + float(shift)).
+// modulation h = T(float(h) * float(scale)); h = T(float(h) + float(shift));
+// act: h = T(silu(float(h))).
 // NCH = ceil(channels / 256) chunks of 8 elements per lane held in registers
-// (channels % 8 == 0, <= 4096).
+// (channels % 8 == 0, <= 4352).
 // ---------------------------------------------------------------------------
 constexpr int kLnRowsPerBlock = 4;  // one warp per row: 128-thread blocks, 16 resident per SM
 
-template <typename T, int NCH, bool AFFINE, bool MODULATE>
+template <typename T, int NCH, bool AFFINE, bool MODULATE, bool ACT>
 __global__ void __launch_bounds__(kLnRowsPerBlock * 32)
     ln_mod_kernel(const T* __restrict__ x, T* __restrict__ out, int64_t rows, int C, float eps,
                   const float* __restrict__ weight, const float* __restrict__ bias, const T* __restrict__ scale,
@@ -125,6 +135,7 @@ __global__ void __launch_bounds__(kLnRowsPerBlock * 32)
         // fp16/bf16 pair multiply and add are correctly rounded, so they equal
         // rounding the fp32 product / sum of the two rounded operands
         if (MODULATE) h = Cvt<T>::add2(Cvt<T>::mul2(h, sc.w[i]), sh.w[i]);
+        if (ACT) h = silu2<T>(h);
         o.w[i] = h;
       }
       *reinterpret_cast<Vec8*>(yr + base) = o;
@@ -134,7 +145,7 @@ __global__ void __launch_bounds__(kLnRowsPerBlock * 32)
 
 template <typename T, int NCH>
 static void launch_ln(const void* x, void* out, int64_t rows, int C, float eps, const float* w, const float* b,
-                      const void* sc, const void* sh, int64_t rpb, int64_t ms, cudaStream_t st) {
+                      const void* sc, const void* sh, int64_t rpb, int64_t ms, int act, cudaStream_t st) {
   // at most 16 resident 128-thread blocks per SM (2048 threads): a grid of whole
   // waves, rows by grid stride
   const int64_t blocks = (rows + kLnRowsPerBlock - 1) / kLnRowsPerBlock,
@@ -144,23 +155,27 @@ static void launch_ln(const void* x, void* out, int64_t rows, int C, float eps, 
   T* ot = (T*)out;
   const T* s = (const T*)sc;
   const T* t = (const T*)sh;
-  if (w && sc)
-    ln_mod_kernel<T, NCH, true, true><<<grid, block, 0, st>>>(xt, ot, rows, C, eps, w, b, s, t, rpb, ms);
+  if (act && w)  // the res-block norm1: affine, then SiLU
+    ln_mod_kernel<T, NCH, true, false, true><<<grid, block, 0, st>>>(xt, ot, rows, C, eps, w, b, s, t, rpb, ms);
+  else if (act)  // the res-block norm2: modulation, then SiLU
+    ln_mod_kernel<T, NCH, false, true, true><<<grid, block, 0, st>>>(xt, ot, rows, C, eps, w, b, s, t, rpb, ms);
+  else if (w && sc)
+    ln_mod_kernel<T, NCH, true, true, false><<<grid, block, 0, st>>>(xt, ot, rows, C, eps, w, b, s, t, rpb, ms);
   else if (w)
-    ln_mod_kernel<T, NCH, true, false><<<grid, block, 0, st>>>(xt, ot, rows, C, eps, w, b, s, t, rpb, ms);
+    ln_mod_kernel<T, NCH, true, false, false><<<grid, block, 0, st>>>(xt, ot, rows, C, eps, w, b, s, t, rpb, ms);
   else if (sc)
-    ln_mod_kernel<T, NCH, false, true><<<grid, block, 0, st>>>(xt, ot, rows, C, eps, w, b, s, t, rpb, ms);
+    ln_mod_kernel<T, NCH, false, true, false><<<grid, block, 0, st>>>(xt, ot, rows, C, eps, w, b, s, t, rpb, ms);
   else
-    ln_mod_kernel<T, NCH, false, false><<<grid, block, 0, st>>>(xt, ot, rows, C, eps, w, b, s, t, rpb, ms);
+    ln_mod_kernel<T, NCH, false, false, false><<<grid, block, 0, st>>>(xt, ot, rows, C, eps, w, b, s, t, rpb, ms);
 }
 
 template <typename T>
 static int dispatch_ln(const void* x, void* out, int64_t rows, int C, float eps, const float* w, const float* b,
-                       const void* sc, const void* sh, int64_t rpb, int64_t ms, cudaStream_t st) {
+                       const void* sc, const void* sh, int64_t rpb, int64_t ms, int act, cudaStream_t st) {
   switch ((C + 255) / 256) {
 #define HI3D_LN_CASE(n) \
   case n:               \
-    launch_ln<T, n>(x, out, rows, C, eps, w, b, sc, sh, rpb, ms, st); break;
+    launch_ln<T, n>(x, out, rows, C, eps, w, b, sc, sh, rpb, ms, act, st); break;
     HI3D_LN_CASE(1)
     HI3D_LN_CASE(2)
     HI3D_LN_CASE(3)
@@ -177,9 +192,10 @@ static int dispatch_ln(const void* x, void* out, int64_t rows, int C, float eps,
     HI3D_LN_CASE(14)
     HI3D_LN_CASE(15)
     HI3D_LN_CASE(16)
+    HI3D_LN_CASE(17)
 #undef HI3D_LN_CASE
     default:
-      return set_error(HI3D_ERR_UNSUPPORTED, "layer_norm_modulate: channels %d not supported (multiple of 8, <= 4096)",
+      return set_error(HI3D_ERR_UNSUPPORTED, "layer_norm_modulate: channels %d not supported (multiple of 8, <= 4352)",
                        C);
   }
   return check_launch("layer_norm_modulate");
@@ -359,16 +375,18 @@ __global__ void gelu_kernel(const T* __restrict__ x, T* __restrict__ out, int64_
 
 using namespace hi3d;
 
-extern "C" int hi3d_layer_norm_modulate(const void* x, void* out, int64_t rows, int64_t channels, float eps,
-                                        const float* weight, const float* bias, const void* scale,
-                                        const void* shift, int64_t rows_per_batch, int64_t mod_stride, int dtype,
-                                        void* stream) {
+static int layer_norm_entry(const void* x, void* out, int64_t rows, int64_t channels, float eps, const float* weight,
+                            const float* bias, const void* scale, const void* shift, int64_t rows_per_batch,
+                            int64_t mod_stride, int act, int dtype, void* stream) {
   if (!x || !out || rows < 0 || channels <= 0)
     return set_error(HI3D_ERR_INVALID_ARGUMENT, "layer_norm_modulate: bad pointers or sizes");
-  if (channels % 8 || channels > 4096)
-    return set_error(HI3D_ERR_UNSUPPORTED, "layer_norm_modulate: channels must be a multiple of 8 and <= 4096");
+  if (channels % 8 || channels > 4352)
+    return set_error(HI3D_ERR_UNSUPPORTED, "layer_norm_modulate: channels must be a multiple of 8 and <= 4352");
   if ((weight == nullptr) != (bias == nullptr) || (scale == nullptr) != (shift == nullptr))
     return set_error(HI3D_ERR_INVALID_ARGUMENT, "layer_norm_modulate: weight/bias and scale/shift come in pairs");
+  if (act != 0 && act != 1) return set_error(HI3D_ERR_INVALID_ARGUMENT, "layer_norm: act must be 0 or 1 (SiLU)");
+  if (act && (weight != nullptr) == (scale != nullptr))
+    return set_error(HI3D_ERR_UNSUPPORTED, "layer_norm: SiLU follows either the affine or the modulation, not both");
   if (!aligned16(x) || !aligned16(out) || (scale && (!aligned16(scale) || !aligned16(shift))))
     return set_error(HI3D_ERR_INVALID_ARGUMENT, "layer_norm_modulate: pointers must be 16-byte aligned");
   if (scale && (rows_per_batch <= 0 || mod_stride % 8))
@@ -378,11 +396,26 @@ extern "C" int hi3d_layer_norm_modulate(const void* x, void* out, int64_t rows, 
   cudaStream_t st = as_stream(stream);
   if (dtype == HI3D_F16)
     return dispatch_ln<__half>(x, out, rows, (int)channels, eps, weight, bias, scale, shift, rows_per_batch,
-                               mod_stride, st);
+                               mod_stride, act, st);
   if (dtype == HI3D_BF16)
     return dispatch_ln<__nv_bfloat16>(x, out, rows, (int)channels, eps, weight, bias, scale, shift, rows_per_batch,
-                                      mod_stride, st);
+                                      mod_stride, act, st);
   return set_error(HI3D_ERR_INVALID_ARGUMENT, "layer_norm_modulate: dtype must be f16 or bf16");
+}
+
+extern "C" int hi3d_layer_norm_modulate(const void* x, void* out, int64_t rows, int64_t channels, float eps,
+                                        const float* weight, const float* bias, const void* scale,
+                                        const void* shift, int64_t rows_per_batch, int64_t mod_stride, int dtype,
+                                        void* stream) {
+  return layer_norm_entry(x, out, rows, channels, eps, weight, bias, scale, shift, rows_per_batch, mod_stride, 0,
+                          dtype, stream);
+}
+
+extern "C" int hi3d_layer_norm_act(const void* x, void* out, int64_t rows, int64_t channels, float eps,
+                                   const float* weight, const float* bias, const void* scale, const void* shift,
+                                   int64_t rows_per_batch, int64_t mod_stride, int act, int dtype, void* stream) {
+  return layer_norm_entry(x, out, rows, channels, eps, weight, bias, scale, shift, rows_per_batch, mod_stride,
+                          act, dtype, stream);
 }
 
 extern "C" int hi3d_qkv_rope_rms(const void* qkv, const float* cos, const float* sin, const float* gamma_q,

@@ -112,22 +112,127 @@ __global__ void unique_flags_kernel(const uint64_t* __restrict__ sorted, int64_t
 }
 
 // group[i] = inclusive_scan(flags)[i] - 1 is the low index of sorted element i
+// The radix sort is stable, so `rows` lists the children of each low voxel
+// together and in ascending row order: with `children` set it is copied out and
+// offsets[g] .. offsets[g + 1] delimit the children of low voxel g.
 __global__ void downsample_scatter_kernel(const uint64_t* __restrict__ sorted, const int32_t* __restrict__ rows,
                                           const int32_t* __restrict__ scan, int64_t n, int32_t* __restrict__ low,
                                           int32_t* __restrict__ inverse, int32_t* __restrict__ counts,
-                                          int32_t* __restrict__ num_low) {
+                                          int32_t* __restrict__ num_low, int32_t* __restrict__ children,
+                                          int32_t* __restrict__ offsets) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
   const int g = scan[i] - 1;
   inverse[rows[i]] = g;
   atomicAdd(counts + g, 1);
+  if (children) children[i] = rows[i];
   if (i == 0 || sorted[i] != sorted[i - 1]) {
     const uint64_t k = sorted[i];
     low[3 * g] = (int32_t)(k >> (2 * kCoordBits));
     low[3 * g + 1] = (int32_t)((k >> kCoordBits) & kCoordMax);
     low[3 * g + 2] = (int32_t)(k & kCoordMax);
+    if (offsets) offsets[g] = (int32_t)i;
   }
-  if (i == n - 1) *num_low = g + 1;
+  if (i == n - 1) {
+    *num_low = g + 1;
+    if (offsets) offsets[g + 1] = (int32_t)n;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Resampling between the fine and the downsampled level (the I/O stages of the
+// transformer).  One thread per (row, 8-channel vector): consecutive threads read
+// consecutive 16-byte pieces of a row.
+// ---------------------------------------------------------------------------
+struct alignas(16) Vec8h {
+  uint32_t w[4];
+};
+
+template <typename T>
+__device__ __forceinline__ void add8(float (&acc)[8], const Vec8h& v) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const T* e = reinterpret_cast<const T*>(&v.w[i]);
+    acc[2 * i] += Cvt<T>::to_f(e[0]);
+    acc[2 * i + 1] += Cvt<T>::to_f(e[1]);
+  }
+}
+
+// out[g] = T(sum_{children i of g, ascending} float(x[i]) / (count_g + 1)):
+// Geometry.downsample (transformer.py:261-263), whose scatter-add starts from the
+// zero row and whose mean divides by children + 1 (upstream scatter_reduce(mean)
+// includes the zero-initialised output, transformer.py:249-251).
+template <typename T>
+__global__ void downsample_mean_kernel(const T* __restrict__ x, const int32_t* __restrict__ children,
+                                       const int32_t* __restrict__ offsets, int64_t m, int vecs,
+                                       T* __restrict__ out) {
+  const int64_t total = m * vecs;
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t g = t / vecs;
+    const int v = (int)(t - g * vecs);
+    const int b = offsets[g], e = offsets[g + 1];
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int i = b; i < e; ++i)
+      add8<T>(acc, *reinterpret_cast<const Vec8h*>(x + ((int64_t)children[i] * vecs + v) * 8));
+    const float div = (float)(e - b + 1);
+    Vec8h o;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) o.w[i] = Cvt<T>::pack2(acc[2 * i] / div, acc[2 * i + 1] / div);
+    *reinterpret_cast<Vec8h*>(out + (g * vecs + v) * 8) = o;
+  }
+}
+
+// out[o] = T(sum_{k: table[o][k] present} float(proj[inverse[table[o][k]] * 27 + k]) + float(bias)):
+// the convolution of the upsampled features without materialising them
+// (Sparc3DTransformerMLX._up_conv, transformer.py:449-475): proj holds every low
+// voxel projected through all 27 taps, rows p * 27 + k.
+template <typename T>
+__global__ void upconv_gather_kernel(const T* __restrict__ proj, const int32_t* __restrict__ table,
+                                     const int32_t* __restrict__ inverse, int64_t n_fine, int vecs,
+                                     const T* __restrict__ bias, T* __restrict__ out) {
+  const int64_t total = n_fine * vecs;
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t o = t / vecs;
+    const int v = (int)(t - o * vecs);
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    const int32_t* row = table + o * 27;
+#pragma unroll 1
+    for (int k = 0; k < 27; ++k) {
+      const int32_t j = row[k];
+      if (j >= n_fine) continue;  // absent neighbour (sentinel n_fine)
+      const int64_t pr = (int64_t)inverse[j] * 27 + k;
+      add8<T>(acc, *reinterpret_cast<const Vec8h*>(proj + (pr * vecs + v) * 8));
+    }
+    if (bias) {
+      const Vec8h bv = *reinterpret_cast<const Vec8h*>(bias + v * 8);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const T* e = reinterpret_cast<const T*>(&bv.w[i]);
+        acc[2 * i] = __fadd_rn(acc[2 * i], Cvt<T>::to_f(e[0]));
+        acc[2 * i + 1] = __fadd_rn(acc[2 * i + 1], Cvt<T>::to_f(e[1]));
+      }
+    }
+    Vec8h ov;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) ov.w[i] = Cvt<T>::pack2(acc[2 * i], acc[2 * i + 1]);
+    *reinterpret_cast<Vec8h*>(out + (o * vecs + v) * 8) = ov;
+  }
+}
+
+// out[o] = src[index[o]] (Geometry.upsample, transformer.py:265-266)
+__global__ void gather_rows_kernel(const uint4* __restrict__ src, const int32_t* __restrict__ index, int64_t rows,
+                                   int vecs, uint4* __restrict__ out) {
+  const int64_t total = rows * vecs;
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t o = t / vecs;
+    const int v = (int)(t - o * vecs);
+    out[t] = src[(int64_t)index[o] * vecs + v];
+  }
+}
+
+static unsigned stride_grid(int64_t total) {
+  const int64_t blocks = (total + 255) / 256, cap = (int64_t)sm_count() * 8;
+  return (unsigned)(blocks < cap ? blocks : cap);
 }
 
 __global__ void check_coords_kernel(const int32_t* __restrict__ coords, int64_t n, int* __restrict__ bad) {
@@ -158,6 +263,7 @@ struct ConvParams {
   void* out;
   int n_in, n_out, cin, cout;
   int tiles_m, tiles_n, kchunks;
+  int act;  // 1: SiLU of the rounded output, rounded again (the conv2 -> SiLU of a res block)
 };
 
 struct ConvBarriers {
@@ -360,6 +466,10 @@ __global__ void __launch_bounds__(CV_THREADS, 1)
             const int nn = min(n + q, p.cout - 1);
             float a = any_tap ? __uint_as_float(v[e + q]) : 0.0f;
             if (bias) a = __fadd_rn(a, Cvt<T>::to_f(bias[nn]));
+            if (p.act) {
+              a = Cvt<T>::to_f(Cvt<T>::from_f(a));
+              a = a / (1.0f + __expf(-a));
+            }
             y[q] = a;
           }
           if (n + 8 <= p.cout) {
@@ -541,9 +651,9 @@ extern "C" int hi3d_downsample_workspace_size(int64_t n, int64_t* bytes) {
   return HI3D_OK;
 }
 
-extern "C" int hi3d_downsample_structure(const int32_t* coords, int64_t n, int32_t* low, int32_t* inverse,
-                                         int32_t* counts, int32_t* num_low, void* workspace, int64_t workspace_bytes,
-                                         void* stream) {
+static int downsample_impl(const int32_t* coords, int64_t n, int32_t* low, int32_t* inverse, int32_t* counts,
+                           int32_t* children, int32_t* offsets, int32_t* num_low, void* workspace,
+                           int64_t workspace_bytes, void* stream) {
   if (n < 0 || !num_low || !workspace || (n > 0 && (!coords || !low || !inverse || !counts)))
     return set_error(HI3D_ERR_INVALID_ARGUMENT, "downsample_structure: bad arguments");
   int64_t need = 0;
@@ -583,8 +693,94 @@ extern "C" int hi3d_downsample_structure(const int32_t* coords, int64_t n, int32
   if (e != cudaSuccess) return set_error(HI3D_ERR_CUDA, "downsample_structure: scan: %s", cudaGetErrorString(e));
   e = cudaMemsetAsync(counts, 0, nn * sizeof(int32_t), st);
   if (e != cudaSuccess) return set_error(HI3D_ERR_CUDA, "downsample_structure: %s", cudaGetErrorString(e));
-  downsample_scatter_kernel<<<g, 256, 0, st>>>(k_out, r_out, scan, n, low, inverse, counts, num_low);
+  downsample_scatter_kernel<<<g, 256, 0, st>>>(k_out, r_out, scan, n, low, inverse, counts, num_low, children,
+                                               offsets);
   return check_launch("downsample_structure");
+}
+
+extern "C" int hi3d_downsample_structure(const int32_t* coords, int64_t n, int32_t* low, int32_t* inverse,
+                                         int32_t* counts, int32_t* num_low, void* workspace, int64_t workspace_bytes,
+                                         void* stream) {
+  return downsample_impl(coords, n, low, inverse, counts, nullptr, nullptr, num_low, workspace, workspace_bytes,
+                         stream);
+}
+
+extern "C" int hi3d_downsample_structure_children(const int32_t* coords, int64_t n, int32_t* low, int32_t* inverse,
+                                                  int32_t* counts, int32_t* children, int32_t* offsets,
+                                                  int32_t* num_low, void* workspace, int64_t workspace_bytes,
+                                                  void* stream) {
+  if (n > 0 && (!children || !offsets))
+    return set_error(HI3D_ERR_INVALID_ARGUMENT, "downsample_structure_children: children and offsets required");
+  if (n == 0 && offsets) {
+    cudaError_t e = cudaMemsetAsync(offsets, 0, sizeof(int32_t), as_stream(stream));
+    if (e != cudaSuccess) return set_error(HI3D_ERR_CUDA, "downsample_structure_children: %s", cudaGetErrorString(e));
+  }
+  return downsample_impl(coords, n, low, inverse, counts, children, offsets, num_low, workspace, workspace_bytes,
+                         stream);
+}
+
+static int resample_args(const char* what, const void* a, const void* b, const void* out, int64_t rows,
+                         int64_t channels, int dtype) {
+  if (!a || !b || !out || rows < 0 || channels <= 0)
+    return set_error(HI3D_ERR_INVALID_ARGUMENT, "%s: bad pointers or sizes", what);
+  if (channels % 8) return set_error(HI3D_ERR_INVALID_ARGUMENT, "%s: channels must be a multiple of 8", what);
+  if (channels / 8 > 0x7fffffff || rows > ((int64_t)1 << 40) / channels)
+    return set_error(HI3D_ERR_INVALID_ARGUMENT, "%s: too many elements", what);
+  if (!aligned16(a) || !aligned16(out))
+    return set_error(HI3D_ERR_INVALID_ARGUMENT, "%s: feature pointers must be 16-byte aligned", what);
+  if (dtype != HI3D_F16 && dtype != HI3D_BF16)
+    return set_error(HI3D_ERR_INVALID_ARGUMENT, "%s: dtype must be f16 or bf16", what);
+  return HI3D_OK;
+}
+
+extern "C" int hi3d_downsample_mean(const void* x, const int32_t* children, const int32_t* offsets, int64_t num_low,
+                                    int64_t channels, void* out, int dtype, void* stream) {
+  int rc = resample_args("downsample_mean", x, children, out, num_low, channels, dtype);
+  if (rc) return rc;
+  if (!offsets) return set_error(HI3D_ERR_INVALID_ARGUMENT, "downsample_mean: offsets required");
+  if (num_low == 0) return HI3D_OK;
+  const int vecs = (int)(channels / 8);
+  const unsigned grid = stride_grid(num_low * vecs);
+  cudaStream_t st = as_stream(stream);
+  if (dtype == HI3D_F16)
+    downsample_mean_kernel<__half><<<grid, 256, 0, st>>>((const __half*)x, children, offsets, num_low, vecs,
+                                                         (__half*)out);
+  else
+    downsample_mean_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>((const __nv_bfloat16*)x, children, offsets, num_low,
+                                                                vecs, (__nv_bfloat16*)out);
+  return check_launch("downsample_mean");
+}
+
+extern "C" int hi3d_upconv_gather_sum(const void* proj, const int32_t* table, const int32_t* inverse, int64_t n_fine,
+                                      int64_t channels, const void* bias, void* out, int dtype, void* stream) {
+  int rc = resample_args("upconv_gather_sum", proj, table, out, n_fine, channels, dtype);
+  if (rc) return rc;
+  if (!inverse) return set_error(HI3D_ERR_INVALID_ARGUMENT, "upconv_gather_sum: inverse required");
+  if (bias && !aligned16(bias))
+    return set_error(HI3D_ERR_INVALID_ARGUMENT, "upconv_gather_sum: bias must be 16-byte aligned");
+  if (n_fine == 0) return HI3D_OK;
+  const int vecs = (int)(channels / 8);
+  const unsigned grid = stride_grid(n_fine * vecs);
+  cudaStream_t st = as_stream(stream);
+  if (dtype == HI3D_F16)
+    upconv_gather_kernel<__half><<<grid, 256, 0, st>>>((const __half*)proj, table, inverse, n_fine, vecs,
+                                                       (const __half*)bias, (__half*)out);
+  else
+    upconv_gather_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>((const __nv_bfloat16*)proj, table, inverse, n_fine,
+                                                              vecs, (const __nv_bfloat16*)bias,
+                                                              (__nv_bfloat16*)out);
+  return check_launch("upconv_gather_sum");
+}
+
+extern "C" int hi3d_gather_rows(const void* src, const int32_t* index, int64_t rows, int64_t channels, void* out,
+                                int dtype, void* stream) {
+  int rc = resample_args("gather_rows", src, index, out, rows, channels, dtype);
+  if (rc) return rc;
+  if (rows == 0) return HI3D_OK;
+  const int vecs = (int)(channels / 8);
+  gather_rows_kernel<<<stride_grid(rows * vecs), 256, 0, as_stream(stream)>>>(
+      static_cast<const uint4*>(src), index, rows, vecs, static_cast<uint4*>(out));
+  return check_launch("gather_rows");
 }
 
 extern "C" int hi3d_conv_tap_mask(const int32_t* table, int64_t n_out, int64_t n_in, uint32_t* tap_mask,
@@ -604,11 +800,12 @@ static int num_sms_conv() {
   return n > 0 ? n : 148;
 }
 
-extern "C" int hi3d_sparse_conv(const void* x, const int32_t* table, const uint32_t* tap_mask, const void* weight,
-                                const void* bias, void* out, int64_t n_in, int64_t n_out, int cin, int cout, int dtype,
-                                void* stream) {
+extern "C" int hi3d_sparse_conv_act(const void* x, const int32_t* table, const uint32_t* tap_mask, const void* weight,
+                                    const void* bias, void* out, int64_t n_in, int64_t n_out, int cin, int cout,
+                                    int act, int dtype, void* stream) {
   if (!x || !table || !tap_mask || !weight || !out || n_in < 0 || n_out < 0 || cin <= 0 || cout <= 0)
     return set_error(HI3D_ERR_INVALID_ARGUMENT, "sparse_conv: bad arguments");
+  if (act != 0 && act != 1) return set_error(HI3D_ERR_INVALID_ARGUMENT, "sparse_conv: act must be 0 or 1 (SiLU)");
   if (cin % 8 || cout % 8)
     return set_error(HI3D_ERR_INVALID_ARGUMENT, "sparse_conv: channels must be multiples of 8");
   if (!aligned16(x) || !aligned16(weight) || !aligned16(out))
@@ -639,6 +836,7 @@ extern "C" int hi3d_sparse_conv(const void* x, const int32_t* table, const uint3
   p.tiles_m = (int)((n_out + CV_BM - 1) / CV_BM);
   p.tiles_n = (cout + CV_BN - 1) / CV_BN;
   p.kchunks = (cin + CV_BKE - 1) / CV_BKE;
+  p.act = act;
   const int tiles = p.tiles_m * p.tiles_n;
   const int grid = tiles < num_sms_conv() ? tiles : num_sms_conv();
   cudaStream_t st = as_stream(stream);
@@ -653,4 +851,10 @@ extern "C" int hi3d_sparse_conv(const void* x, const int32_t* table, const uint3
     conv_kernel<__nv_bfloat16><<<grid, CV_THREADS, CV_SMEM, st>>>(mw, p);
   }
   return check_launch("sparse_conv");
+}
+
+extern "C" int hi3d_sparse_conv(const void* x, const int32_t* table, const uint32_t* tap_mask, const void* weight,
+                                const void* bias, void* out, int64_t n_in, int64_t n_out, int cin, int cout, int dtype,
+                                void* stream) {
+  return hi3d_sparse_conv_act(x, table, tap_mask, weight, bias, out, n_in, n_out, cin, cout, 0, dtype, stream);
 }

@@ -84,6 +84,14 @@ SIGNATURES: dict[str, tuple] = {
     "hi3d_downsample_structure": (_i32, [_c_void_p, _i64] + [_c_void_p] * 5 + [_i64, _c_void_p]),
     "hi3d_conv_tap_mask": (_i32, [_c_void_p, _i64, _i64, _c_void_p, _c_void_p]),
     "hi3d_sparse_conv": (_i32, [_c_void_p] * 6 + [_i64, _i64, _i32, _i32, _i32, _c_void_p]),
+    "hi3d_layer_norm_act": (_i32, [_c_void_p, _c_void_p, _i64, _i64, _f32, _c_void_p, _c_void_p, _c_void_p,
+                                   _c_void_p, _i64, _i64, _i32, _i32, _c_void_p]),
+    "hi3d_sparse_conv_act": (_i32, [_c_void_p] * 6 + [_i64, _i64, _i32, _i32, _i32, _i32, _c_void_p]),
+    "hi3d_downsample_structure_children": (_i32, [_c_void_p, _i64] + [_c_void_p] * 7 + [_i64, _c_void_p]),
+    "hi3d_downsample_mean": (_i32, [_c_void_p, _c_void_p, _c_void_p, _i64, _i64, _c_void_p, _i32, _c_void_p]),
+    "hi3d_upconv_gather_sum": (_i32, [_c_void_p, _c_void_p, _c_void_p, _i64, _i64, _c_void_p, _c_void_p, _i32,
+                                      _c_void_p]),
+    "hi3d_gather_rows": (_i32, [_c_void_p, _c_void_p, _i64, _i64, _c_void_p, _i32, _c_void_p]),
 }
 
 _lib = None

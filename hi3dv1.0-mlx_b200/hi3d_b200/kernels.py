@@ -15,13 +15,16 @@ from . import _lib
 
 def layer_norm_modulate(x: torch.Tensor, eps: float, weight: torch.Tensor | None = None,
                         bias: torch.Tensor | None = None, scale: torch.Tensor | None = None,
-                        shift: torch.Tensor | None = None) -> torch.Tensor:
+                        shift: torch.Tensor | None = None, act: str | None = None) -> torch.Tensor:
     """``LayerNorm32`` of fp16/bf16 rows (fp32 statistics), then optionally the adaLN
     modulation ``h * scale + shift`` with two roundings, in one pass over ``x``.
 
     ``weight``/``bias`` are fp32 ``[C]`` (affine, as ``norm2``); ``scale``/``shift`` are
     ``[C]``, ``[1, C]`` or ``[B, C]`` in the dtype of ``x`` (``[B, C]`` modulates batch
     element ``b`` of ``x [B, N, C]`` with row ``b``).  Reference: kernels.py:162-237.
+    ``act="silu"`` appends the SiLU of the transformer's res-block norms
+    (src/hi3d_mac/mlx_backend/transformer.py:418-437); it follows either the affine or the
+    modulation.
     """
     _lib.require_cuda(x, weight, bias, scale, shift)
     c = x.shape[-1]
@@ -47,9 +50,16 @@ def layer_norm_modulate(x: torch.Tensor, eps: float, weight: torch.Tensor | None
         weight = weight.float().contiguous()
         bias = bias.float().contiguous()
     lib = _lib.load()
-    rc = lib.hi3d_layer_norm_modulate(x.data_ptr(), out.data_ptr(), rows, c, float(eps), _lib.ptr(weight),
-                                      _lib.ptr(bias), _lib.ptr(scale), _lib.ptr(shift), rows_per_batch, mod_stride,
-                                      _lib.dtype_code(x), _lib.stream(x))
+    if act is None:
+        rc = lib.hi3d_layer_norm_modulate(x.data_ptr(), out.data_ptr(), rows, c, float(eps), _lib.ptr(weight),
+                                          _lib.ptr(bias), _lib.ptr(scale), _lib.ptr(shift), rows_per_batch,
+                                          mod_stride, _lib.dtype_code(x), _lib.stream(x))
+    elif act == "silu":
+        rc = lib.hi3d_layer_norm_act(x.data_ptr(), out.data_ptr(), rows, c, float(eps), _lib.ptr(weight),
+                                     _lib.ptr(bias), _lib.ptr(scale), _lib.ptr(shift), rows_per_batch, mod_stride, 1,
+                                     _lib.dtype_code(x), _lib.stream(x))
+    else:
+        raise ValueError(f"unknown activation {act!r}")
     _lib.check(rc, "layer_norm_modulate")
     return out
 

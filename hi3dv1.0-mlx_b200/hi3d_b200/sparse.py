@@ -79,6 +79,79 @@ def downsample_structure(coords):
     return low[:m], inverse, counts[:m]
 
 
+def downsample_groups(coords):
+    """``(low, inverse, counts, children, offsets)``: :func:`downsample_structure` plus the fine
+    rows of each low voxel, ``children[offsets[g]:offsets[g + 1]]`` in ascending row order (the
+    rows Geometry.downsample averages, transformer.py:261-263).  Synchronises once."""
+    c = _coords_dev(coords)
+    n = c.shape[0]
+    low = torch.empty((max(n, 1), 3), dtype=torch.int32, device=c.device)
+    inverse = torch.empty(n, dtype=torch.int32, device=c.device)
+    counts = torch.empty(max(n, 1), dtype=torch.int32, device=c.device)
+    children = torch.empty(max(n, 1), dtype=torch.int32, device=c.device)
+    offsets = torch.empty(n + 1, dtype=torch.int32, device=c.device)
+    num = torch.zeros(1, dtype=torch.int32, device=c.device)
+    lib = _lib.load()
+    ws = _workspace(lib.hi3d_downsample_workspace_size, n, c.device)
+    rc = lib.hi3d_downsample_structure_children(c.data_ptr(), n, low.data_ptr(), inverse.data_ptr(),
+                                                counts.data_ptr(), children.data_ptr(), offsets.data_ptr(),
+                                                num.data_ptr(), ws.data_ptr(), ws.numel(), _lib.stream(c))
+    _lib.check(rc, "downsample_structure_children")
+    m = int(num.item())
+    return low[:m], inverse, counts[:m], children[:n], offsets[:m + 1]
+
+
+def downsample_mean(x: torch.Tensor, children: torch.Tensor, offsets: torch.Tensor) -> torch.Tensor:
+    """Mean of each low voxel's children with the reference's ``children + 1`` divisor
+    (Geometry.downsample, transformer.py:261-263), fp32 sums in ascending row order."""
+    _lib.require_cuda(x, children, offsets)
+    if x.dtype not in (torch.float16, torch.bfloat16):
+        raise ValueError("downsample_mean takes float16/bfloat16 features")
+    x = x.contiguous()
+    m = offsets.shape[0] - 1
+    out = torch.empty((m, x.shape[1]), dtype=x.dtype, device=x.device)
+    rc = _lib.load().hi3d_downsample_mean(x.data_ptr(), children.data_ptr(), offsets.data_ptr(), m, x.shape[1],
+                                          out.data_ptr(), _lib.dtype_code(x), _lib.stream(x))
+    _lib.check(rc, "downsample_mean")
+    return out
+
+
+def upsample(x: torch.Tensor, inverse: torch.Tensor) -> torch.Tensor:
+    """Rows of the low level copied to their fine children (Geometry.upsample,
+    transformer.py:265-266)."""
+    _lib.require_cuda(x, inverse)
+    x = x.contiguous()
+    out = torch.empty((inverse.shape[0], x.shape[1]), dtype=x.dtype, device=x.device)
+    rc = _lib.load().hi3d_gather_rows(x.data_ptr(), inverse.data_ptr(), inverse.shape[0], x.shape[1], out.data_ptr(),
+                                      _lib.dtype_code(x), _lib.stream(x))
+    _lib.check(rc, "upsample")
+    return out
+
+
+def up_conv(h_low: torch.Tensor, fine_table: torch.Tensor, inverse: torch.Tensor, weight: torch.Tensor,
+            bias: torch.Tensor | None = None) -> torch.Tensor:
+    """3x3x3 convolution at the fine level of the upsampled ``h_low`` without materialising the
+    upsampled rows (Sparc3DTransformerMLX._up_conv, transformer.py:449-475): every low voxel is
+    projected through the 27 taps by one GEMM, ``proj [N_low * 27, Cout]``, then each fine voxel
+    sums the projections of its neighbours' parents.  ``weight`` in spconv layout
+    ``[Cout, 3, 3, 3, Cin]``."""
+    from . import linear as _linear
+
+    _lib.require_cuda(h_low, fine_table, inverse, weight, bias)
+    cout = weight.shape[0]
+    # [Cout, 27, Cin] -> [27 * Cout, Cin]: GEMM row k * Cout + o is tap k of output channel o
+    w_taps = weight.reshape(cout, 27, -1).to(h_low.dtype).permute(1, 0, 2).reshape(27 * cout, -1).contiguous()
+    proj = _linear.linear(h_low.contiguous(), w_taps)
+    n_fine = fine_table.shape[0]
+    out = torch.empty((n_fine, cout), dtype=h_low.dtype, device=h_low.device)
+    b = None if bias is None else bias.to(h_low.dtype).contiguous()
+    rc = _lib.load().hi3d_upconv_gather_sum(proj.data_ptr(), fine_table.data_ptr(), inverse.data_ptr(), n_fine, cout,
+                                            _lib.ptr(b), out.data_ptr(), _lib.dtype_code(h_low),
+                                            _lib.stream(h_low))
+    _lib.check(rc, "up_conv")
+    return out
+
+
 class Level:
     """One coordinate set and its convolution gather table (``N`` marks absent)."""
 
@@ -124,9 +197,12 @@ def _kernel_weight_from_gemm(weight_t: torch.Tensor) -> torch.Tensor:
 
 
 def conv(x: torch.Tensor, table: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None,
-         n_in: int | None = None, tap_mask: torch.Tensor | None = None) -> torch.Tensor:
+         n_in: int | None = None, tap_mask: torch.Tensor | None = None, act: str | None = None) -> torch.Tensor:
     """Gathered 3x3x3 convolution with the spconv weight layout ``weight [out, 3, 3, 3, in]``
-    (or ``[out, 27, in]``): ``out[o] = bias + sum_k x[table[o, k]] W_k^T``."""
+    (or ``[out, 27, in]``): ``out[o] = bias + sum_k x[table[o, k]] W_k^T``; ``act="silu"``
+    applies SiLU to the rounded output (the conv2 -> SiLU of a res block)."""
+    if act not in (None, "silu"):
+        raise ValueError(f"unknown activation {act!r}")
     _lib.require_cuda(x, table, weight, bias)
     if x.dtype not in (torch.float16, torch.bfloat16):
         raise ValueError("sparse conv takes float16/bfloat16 features")
@@ -142,8 +218,9 @@ def conv(x: torch.Tensor, table: torch.Tensor, weight: torch.Tensor, bias: torch
         tap_mask = conv_tap_mask(table, n_in)
     out = torch.empty((n_out, cout), dtype=x.dtype, device=x.device)
     b = None if bias is None else bias.to(x.dtype).contiguous()
-    rc = _lib.load().hi3d_sparse_conv(x.data_ptr(), table.data_ptr(), tap_mask.data_ptr(), w.data_ptr(), _lib.ptr(b),
-                                      out.data_ptr(), n_in, n_out, cin, cout, _lib.dtype_code(x), _lib.stream(x))
+    rc = _lib.load().hi3d_sparse_conv_act(x.data_ptr(), table.data_ptr(), tap_mask.data_ptr(), w.data_ptr(),
+                                          _lib.ptr(b), out.data_ptr(), n_in, n_out, cin, cout,
+                                          1 if act == "silu" else 0, _lib.dtype_code(x), _lib.stream(x))
     _lib.check(rc, "sparse_conv")
     return out
 

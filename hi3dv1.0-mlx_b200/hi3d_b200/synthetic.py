@@ -104,3 +104,65 @@ def block_weights(channels: int, ctx_channels: int, heads: int, seed: int, gamma
 
 def features(rows: int, channels: int, seed: int, dtype=np.float16) -> np.ndarray:
     return np.random.default_rng(seed).standard_normal((rows, channels)).astype(np.float32).astype(dtype)
+
+
+def resblock_shapes(channels: int, out_channels: int, emb_channels: int) -> dict:
+    """Parameter shapes of one sparse res block (``SparseResBlock3d``,
+    src/sparc3d/models/transformers/sparc3d_transformer.py:80-130): hidden = out // 2."""
+    hid = out_channels // 2
+    shapes = {
+        "norm1.weight": (channels,), "norm1.bias": (channels,),
+        "conv1.conv.weight": (hid, 3, 3, 3, channels), "conv1.conv.bias": (hid,),
+        "conv2.conv.weight": (hid, 3, 3, 3, hid), "conv2.conv.bias": (hid,),
+        "linear.weight": (out_channels, hid), "linear.bias": (out_channels,),
+        "emb_layers.1.weight": (2 * hid, emb_channels), "emb_layers.1.bias": (2 * hid,),
+    }
+    if channels != out_channels:
+        shapes.update({"skip_connection.weight": (out_channels, channels), "skip_connection.bias": (out_channels,)})
+    return shapes
+
+
+def model_weights(channels: int, ctx_channels: int, heads: int, num_blocks: int, io_channels: int = 256,
+                  in_channels: int = 32, out_channels: int = 32, seed: int = 0, std: float | None = 0.02) -> dict:
+    """Random parameters of the whole refinement transformer, named as the upstream state dict
+    (``Sparc3DTransformer``, sparc3d_transformer.py:149-230) for one I/O stage of two res blocks.
+
+    Linear and convolution parameters of the fp16 torso (I/O res blocks and blocks) are rounded
+    to fp16, as ``convert_to_fp16`` stores them; the timestep embedder, adaLN, input/output
+    layers and the norms stay fp32.  ``std`` is the weight standard deviation (BASELINE: 0.02);
+    ``None`` scales each weight by 1/sqrt(fan-in) and randomises the norm affines, which keeps
+    activations O(1) through the stack for parity tests.
+    """
+    rng = np.random.default_rng(seed)
+
+    def weight(shape, fan_in):
+        s = std if std is not None else 1.0 / math.sqrt(fan_in)
+        return rng.normal(0, s, shape).astype(np.float32)
+
+    w: dict[str, np.ndarray] = {}
+    c = channels
+    for name, (o, i) in (("t_embedder.mlp.0", (c, 256)), ("t_embedder.mlp.2", (c, c)),
+                         ("adaLN_modulation.1", (6 * c, c)), ("input_layer", (io_channels, in_channels))):
+        w[f"{name}.weight"] = weight((o, i), i)
+        w[f"{name}.bias"] = rng.normal(0, 0.02, o).astype(np.float32)
+    stages = (("input_blocks.0", io_channels, io_channels), ("input_blocks.1", io_channels, c),
+              ("out_blocks.0", 2 * c, io_channels), ("out_blocks.1", 2 * io_channels, io_channels))
+    for name, cin, cout in stages:
+        for key, shape in resblock_shapes(cin, cout, c).items():
+            full = f"{name}.{key}"
+            if key == "norm1.weight":
+                w[full] = (np.ones(shape, np.float32) if std is not None else
+                           rng.uniform(0.5, 1.5, shape).astype(np.float32))
+            elif key == "norm1.bias":
+                w[full] = (np.zeros(shape, np.float32) if std is not None else
+                           rng.normal(0, 0.1, shape).astype(np.float32))
+            elif key.endswith("bias"):
+                w[full] = rng.normal(0, 0.02, shape).astype(np.float16)
+            else:
+                w[full] = weight(shape, int(np.prod(shape[1:]))).astype(np.float16)
+    for i in range(num_blocks):
+        for k, v in block_weights(c, ctx_channels, heads, seed=seed * 1000 + i + 1, gamma_random=std is None).items():
+            w[f"blocks.{i}.{k}"] = v
+    w["out_layer.weight"] = weight((out_channels, io_channels), io_channels)
+    w["out_layer.bias"] = rng.normal(0, 0.02, out_channels).astype(np.float32)
+    return w

@@ -68,6 +68,17 @@ HI3D_API int hi3d_layer_norm_modulate(const void* x, void* out, int64_t rows, in
                              const float* weight, const float* bias, const void* scale, const void* shift,
                              int64_t rows_per_batch, int64_t mod_stride, int dtype, void* stream);
 
+/* hi3d_layer_norm_modulate followed by SiLU (act = 1; act = 0 is the plain form): the norms of
+ * the transformer's sparse res blocks, h = silu(LN32(x; weight, bias)) (norm1) and
+ * h = silu(LN(x) * (1 + scale) + shift) (norm2; pass the rounded 1 + scale as `scale`)
+ * (src/hi3d_mac/mlx_backend/transformer.py:418-437; upstream SparseResBlock3d.forward,
+ * src/sparc3d/models/transformers/sparc3d_transformer.py:132-144).  SiLU is evaluated in fp32 on
+ * the rounded value and rounded once.  With act = 1 exactly one of weight/bias and scale/shift
+ * is given.  Channels up to 4352 (the 2 x 2112-channel input of the upsampling block). */
+HI3D_API int hi3d_layer_norm_act(const void* x, void* out, int64_t rows, int64_t channels, float eps,
+                                 const float* weight, const float* bias, const void* scale, const void* shift,
+                                 int64_t rows_per_batch, int64_t mod_stride, int act, int dtype, void* stream);
+
 /* ---- RoPE + per-head QK RMS norm + head split --------------------------- */
 /* Replaces kernels.qkv_rope_rms / qkv_rope_rms_simd
  * (src/hi3d_mac/mlx_backend/kernels.py:62-90, :137-157; kernels :22-57, :93-133) and the upstream
@@ -273,6 +284,39 @@ HI3D_API int hi3d_downsample_structure(const int32_t* coords, int64_t n, int32_t
                                        int32_t* counts, int32_t* num_low, void* workspace, int64_t workspace_bytes,
                                        void* stream);
 
+/* hi3d_downsample_structure that also lists the children of every low voxel: children [n] holds
+ * the fine rows grouped by parent, each group in ascending row order, and offsets [n + 1]
+ * delimits group g as children[offsets[g] .. offsets[g + 1]) (offsets[num_low] = n).  This is the
+ * row set the reference's scatter-add visits for each parent (Geometry.downsample,
+ * src/hi3d_mac/mlx_backend/transformer.py:261-263), kept so the mean is summed in a fixed order. */
+HI3D_API int hi3d_downsample_structure_children(const int32_t* coords, int64_t n, int32_t* low, int32_t* inverse,
+                                                int32_t* counts, int32_t* children, int32_t* offsets,
+                                                int32_t* num_low, void* workspace, int64_t workspace_bytes,
+                                                void* stream);
+
+/* Replaces Geometry.downsample (src/hi3d_mac/mlx_backend/transformer.py:261-263; upstream
+ * SparseDownsample, src/sparc3d/nn/sparse/spatial.py:34-82): out[g] = round(sum of x over the
+ * children of g, fp32 in ascending row order, / (children + 1)) -- the upstream mean includes the
+ * zero-initialised output row.  x [n, channels]; out [num_low, channels]; channels % 8 == 0. */
+HI3D_API int hi3d_downsample_mean(const void* x, const int32_t* children, const int32_t* offsets, int64_t num_low,
+                                  int64_t channels, void* out, int dtype, void* stream);
+
+/* Replaces the gather-sum of Sparc3DTransformerMLX._up_conv (src/hi3d_mac/mlx_backend/transformer.py:
+ * 449-475): the 3x3x3 convolution of upsampled features computed from the low level.
+ * proj [num_low * 27, channels] holds every low voxel projected through each tap (row p * 27 + k,
+ * a GEMM of the low features with the taps' weights); for each fine voxel o
+ * out[o] = round(sum_k proj[inverse[table[o, k]] * 27 + k] + bias) over the present taps k
+ * (table [n_fine, 27] of the fine level, sentinel n_fine), fp32 in tap order, bias [channels] or
+ * NULL.  Upstream this is SparseUpsample followed by the conv (sparc3d_transformer.py:135-139). */
+HI3D_API int hi3d_upconv_gather_sum(const void* proj, const int32_t* table, const int32_t* inverse, int64_t n_fine,
+                                    int64_t channels, const void* bias, void* out, int dtype, void* stream);
+
+/* Replaces Geometry.upsample (src/hi3d_mac/mlx_backend/transformer.py:265-266; upstream
+ * SparseUpsample, src/sparc3d/nn/sparse/spatial.py:85-124): out[o] = src[index[o]] for
+ * rows o of out [rows, channels]; channels % 8 == 0. */
+HI3D_API int hi3d_gather_rows(const void* src, const int32_t* index, int64_t rows, int64_t channels, void* out,
+                              int dtype, void* stream);
+
 /* 27-bit mask per 128-row output tile of the taps with at least one present neighbour
  * (tap_mask [ceil(n_out / 128)]); hi3d_sparse_conv skips the others. */
 HI3D_API int hi3d_conv_tap_mask(const int32_t* table, int64_t n_out, int64_t n_in, uint32_t* tap_mask, void* stream);
@@ -285,6 +329,13 @@ HI3D_API int hi3d_conv_tap_mask(const int32_t* table, int64_t n_out, int64_t n_i
 HI3D_API int hi3d_sparse_conv(const void* x, const int32_t* table, const uint32_t* tap_mask, const void* weight,
                               const void* bias, void* out, int64_t n_in, int64_t n_out, int cin, int cout, int dtype,
                               void* stream);
+
+/* hi3d_sparse_conv with an activation: act = 1 applies SiLU to the rounded output (fp32, rounded
+ * again), the conv2 -> SiLU of the transformer's sparse res blocks
+ * (src/hi3d_mac/mlx_backend/transformer.py:418-424; upstream sparc3d_transformer.py:142-143). */
+HI3D_API int hi3d_sparse_conv_act(const void* x, const int32_t* table, const uint32_t* tap_mask, const void* weight,
+                                  const void* bias, void* out, int64_t n_in, int64_t n_out, int cin, int cout, int act,
+                                  int dtype, void* stream);
 
 /* ---- elementwise epilogues of the block --------------------------------- */
 /* x <- x + y * gate (all in the I/O type, two roundings: round(y*gate), then round(x + .)).

@@ -348,6 +348,130 @@ def block_forward_f32(w: dict, x: np.ndarray, mod: np.ndarray, cos: np.ndarray, 
     return (x + lin(h, "mlp.mlp.2") * gate_mlp).astype(f)
 
 
+# ----------------------------------------------------------------------------- full transformer (fp32)
+
+
+def silu_f32(x: np.ndarray) -> np.ndarray:
+    """``x * sigmoid(x)`` (transformer.py:172-173)."""
+    x = x.astype(F32)
+    return (x / (F32(1) + np.exp(-x))).astype(F32)
+
+
+def timestep_embedding_f32(t: np.ndarray, dim: int = 256, max_period: int = 10000) -> np.ndarray:
+    """Sinusoidal embedding ``[cos, sin]`` (transformer.py:182-186)."""
+    half = dim // 2
+    freqs = np.exp(-math.log(max_period) * np.arange(half, dtype=F32) / half).astype(F32)
+    args = t[:, None].astype(F32) * freqs[None]
+    return np.concatenate([np.cos(args), np.sin(args)], axis=-1).astype(F32)
+
+
+def downsample_mean_f32(x: np.ndarray, inverse: np.ndarray, counts: np.ndarray) -> np.ndarray:
+    """Geometry.downsample (transformer.py:261-263): scatter-add of the children from a zero row,
+    divided by ``counts + 1`` (transformer.py:249-251)."""
+    sums = np.zeros((counts.shape[0], x.shape[1]), F32)
+    np.add.at(sums, inverse, x.astype(F32))
+    return (sums / (counts.astype(F32) + 1)[:, None]).astype(F32)
+
+
+def up_conv_f32(h_low: np.ndarray, weight: np.ndarray, bias: np.ndarray, fine_table: np.ndarray,
+                inverse: np.ndarray) -> np.ndarray:
+    """Sparc3DTransformerMLX._up_conv (transformer.py:449-475) with the gather table of
+    Geometry.__post_init__ (transformer.py:253-259): every low voxel projected through the 27
+    taps, then each fine voxel sums the projections of its neighbours' parents."""
+    n_low, cin = h_low.shape
+    cout = weight.shape[0]
+    w_taps = weight.astype(F32).reshape(cout, 27, cin).transpose(2, 1, 0).reshape(cin, 27 * cout)
+    proj = (h_low.astype(F32) @ w_taps).reshape(-1, cout)
+    proj = np.concatenate([proj, np.zeros((1, cout), F32)], 0)
+    parent_of = np.append(inverse, n_low).astype(np.int64)
+    nb_parent = parent_of[fine_table]
+    flat = nb_parent * 27 + np.arange(27)[None, :]
+    flat[nb_parent == n_low] = n_low * 27
+    return (proj[flat].sum(axis=1) + bias.astype(F32)).astype(F32)
+
+
+def _lin(w: dict, name: str, x: np.ndarray) -> np.ndarray:
+    return (x.astype(F32) @ w[f"{name}.weight"].astype(F32).T + w[f"{name}.bias"].astype(F32)).astype(F32)
+
+
+def _conv(w: dict, name: str, x: np.ndarray, table: np.ndarray) -> np.ndarray:
+    out = subm_conv(x, table, conv_weight(w[f"{name}.conv.weight"]), w[f"{name}.conv.bias"], dtype=np.float64)
+    return out.astype(F32)
+
+
+def _emb_scale_shift(w: dict, name: str, emb: np.ndarray):
+    """transformer.py:413-416"""
+    y = _lin(w, f"{name}.emb_layers.1", silu_f32(emb))
+    return np.split(y, 2, axis=1)
+
+
+def _resblock_tail(w: dict, name: str, h: np.ndarray, table: np.ndarray, scale, shift) -> np.ndarray:
+    """norm2 -> modulate -> SiLU -> conv2 -> SiLU -> linear (transformer.py:418-424)."""
+    h = layer_norm32_f32(h) * (1 + scale) + shift
+    h = _conv(w, f"{name}.conv2", silu_f32(h), table)
+    return _lin(w, f"{name}.linear", silu_f32(h))
+
+
+def resblock_f32(w: dict, name: str, x: np.ndarray, emb: np.ndarray, table: np.ndarray) -> np.ndarray:
+    """A res block without resampling (transformer.py:426-437)."""
+    scale, shift = _emb_scale_shift(w, name, emb)
+    h = silu_f32(layer_norm32_f32(x, w[f"{name}.norm1.weight"].astype(F32), w[f"{name}.norm1.bias"].astype(F32)))
+    h = _resblock_tail(w, name, _conv(w, f"{name}.conv1", h, table), table, scale, shift)
+    skip = _lin(w, f"{name}.skip_connection", x) if f"{name}.skip_connection.weight" in w else x.astype(F32)
+    return (h + skip).astype(F32)
+
+
+def forward_f32(w: dict, feats: np.ndarray, coords: np.ndarray, t: float, cond: np.ndarray | None,
+                heads: int) -> np.ndarray:
+    """Velocity of Sparc3DTransformerMLX.__call__ for one conditioned branch, in fp32
+    (transformer.py:606-668; upstream Sparc3DTransformer.forward,
+    src/sparc3d/models/transformers/sparc3d_transformer.py:252-290).
+
+    ``w``: parameters named as the upstream state dict; ``feats [N, in]`` on fine ``coords [N, 3]``;
+    the network sees ``1000 t``; ``cond [L, Cc]``.  One I/O stage (patch size 2, two res blocks
+    per stage), as the reference's ``input_stage``/``output_stage`` hard-code.
+    """
+    coords = np.asarray(coords, np.int32)
+    full_table = neighbour_table(coords)
+    low, inverse, counts = downsample_structure(coords)
+    low_table = neighbour_table(low)
+    # embed (transformer.py:606-617)
+    temb = timestep_embedding_f32(np.array([F32(1000.0) * F32(t)], F32))
+    emb = _lin(w, "t_embedder.mlp.2", silu_f32(_lin(w, "t_embedder.mlp.0", temb)))
+    mod = _lin(w, "adaLN_modulation.1", silu_f32(emb))
+    # input stage (transformer.py:619-625, :439-447)
+    h = _lin(w, "input_layer", feats)
+    h = resblock_f32(w, "input_blocks.0", h, emb, full_table)
+    skip0 = h
+    name = "input_blocks.1"
+    scale, shift = _emb_scale_shift(w, name, emb)
+    xd = downsample_mean_f32(h, inverse, counts)
+    hd = silu_f32(layer_norm32_f32(xd, w[f"{name}.norm1.weight"].astype(F32), w[f"{name}.norm1.bias"].astype(F32)))
+    hd = _resblock_tail(w, name, _conv(w, f"{name}.conv1", hd, low_table), low_table, scale, shift)
+    h = hd + _lin(w, f"{name}.skip_connection", xd)
+    skip_low = h
+    # torso (transformer.py:656-667)
+    c = h.shape[1]
+    cos, sin = rope_tables(low, c // heads)
+    for i in sorted({int(k.split(".")[1]) for k in w if k.startswith("blocks.")}):
+        bw = {k[len(f"blocks.{i}."):]: v for k, v in w.items() if k.startswith(f"blocks.{i}.")}
+        h = block_forward_f32(bw, h, mod, cos, sin, cond, heads)
+    # output stage (transformer.py:627-634, :477-485)
+    name = "out_blocks.0"
+    xl = np.concatenate([h, skip_low], axis=1)
+    scale, shift = _emb_scale_shift(w, name, emb)
+    hl = silu_f32(layer_norm32_f32(xl, w[f"{name}.norm1.weight"].astype(F32), w[f"{name}.norm1.bias"].astype(F32)))
+    hf = up_conv_f32(hl, w[f"{name}.conv1.conv.weight"], w[f"{name}.conv1.conv.bias"], full_table, inverse)
+    hf = _resblock_tail(w, name, hf, full_table, scale, shift)
+    h = hf + _lin(w, f"{name}.skip_connection", xl)[inverse]
+    h = resblock_f32(w, "out_blocks.1", np.concatenate([h, skip0], axis=1), emb, full_table)
+    xf = h.astype(F32)
+    mean = xf.mean(-1, keepdims=True)
+    var = ((xf - mean) ** 2).mean(-1, keepdims=True)
+    h = (xf - mean) / np.sqrt(var + F32(1e-5))
+    return _lin(w, "out_layer", h)
+
+
 # ----------------------------------------------------------------------------- CPU baseline timing
 
 

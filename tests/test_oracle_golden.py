@@ -82,6 +82,44 @@ def test_block_forward_matches_upstream_module():
     assert rel_l2(y, g["y"]) < 1e-5
 
 
+def forward_case():
+    """Inputs, weights and the upstream velocity of the whole-transformer fixture."""
+    from hi3d_b200 import synthetic
+
+    g = _load("forward")
+    c, cc, heads, nblk, io, seed = (int(v) for v in g["config"])
+    w = synthetic.model_weights(c, cc, heads, nblk, io_channels=io, seed=seed, std=None)
+    checksum = sum(float(np.abs(v.astype(np.float64)).sum()) for v in w.values())
+    assert checksum == float(g["weight_checksum"]), "the seeded weight generator changed"
+    return g, w, heads
+
+
+def test_forward_matches_upstream_transformer():
+    """The whole refinement transformer (fp32): oracle vs the upstream Sparc3DTransformer."""
+    g, w, heads = forward_case()
+    vel = ops.forward_f32(w, g["feats"], g["coords"], float(g["t"]), g["cond"], heads)
+    assert vel.shape == g["velocity"].shape
+    assert rel_l2(vel, g["velocity"]) < 1e-5
+
+
+def test_resampling_oracle_identities():
+    """The restructured up-convolution equals upsample-then-conv, and the mean divides by
+    children + 1 (transformer.py:249-251, :449-475)."""
+    rng = np.random.default_rng(5)
+    coords = np.unique(rng.integers(0, 12, (300, 3)), axis=0).astype(np.int32)
+    low, inverse, counts = ops.downsample_structure(coords)
+    x = rng.standard_normal((coords.shape[0], 8)).astype(np.float32)
+    mean = ops.downsample_mean_f32(x, inverse, counts)
+    j = int(inverse[0])
+    assert np.allclose(mean[j], x[inverse == j].sum(0) / (counts[j] + 1), rtol=1e-6)
+    h = rng.standard_normal((low.shape[0], 16)).astype(np.float32)
+    wt = rng.standard_normal((8, 3, 3, 3, 16)).astype(np.float32)
+    b = rng.standard_normal(8).astype(np.float32)
+    table = ops.neighbour_table(coords)
+    direct = ops.subm_conv(h[inverse], table, ops.conv_weight(wt), b)
+    assert rel_l2(ops.up_conv_f32(h, wt, b, table, inverse), direct) < 1e-6
+
+
 @pytest.mark.parametrize("k", [64, 1024, 2112, 4096])
 def test_w8a8_signs_bit_exact(k):
     assert np.array_equal(ops.signs(k), _load("w8a8")[f"signs{k}"])
