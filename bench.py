@@ -694,6 +694,13 @@ def run_forward(args) -> None:
     e1.record(stream)
     torch.cuda.synchronize()
     io_ms = e0.elapsed_time(e1) / args.steps
+    # a guided evaluation: the [condition, zero condition] batch, first block's self-attention shared
+    e0.record(stream)
+    for _ in range(args.steps):
+        m(f_dev, FWD_T, geo, kvs, negative=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    guided_ms = e0.elapsed_time(e1) / args.steps
     out_host = torch.empty((coords.shape[0], 32), dtype=torch.float32).pin_memory()
     e0.record(stream)
     for _ in range(args.steps):
@@ -716,7 +723,8 @@ def run_forward(args) -> None:
                                 f"{FWD_GRID}^3 -> {n_low} low tokens, I/O stage {FWD_IO} channels, {BLOCKS} blocks "
                                 f"C={CHANNELS} {HEADS}x{CHANNELS // HEADS} heads, {COND} cond tokens, fp16 torso"),
                    "fine_voxels": int(coords.shape[0]), "low_tokens": n_low, "io_stages_ms": io_ms,
-                   "stack_ms": ms - io_ms, "l2": "inputs larger than L2 (705 MB of weights per step)"},
+                   "stack_ms": ms - io_ms, "guided_batch2_ms": guided_ms,
+                   "l2": "inputs larger than L2 (705 MB of weights per step)"},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak, "traffic": None,
                      "kernel": "hi3d::attn::flash_fwd_kernel<half,64,false>",

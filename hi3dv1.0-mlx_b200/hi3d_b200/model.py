@@ -220,5 +220,6 @@ class Sparc3DTransformer:
             raise ValueError("branches must be [condition], [condition, None] or [None]")
         negatives = [transformer.negative_cross(w) for w in self.stack.weights] if negative else None
         x = h[None].expand(batch, *h.shape).contiguous()
-        x = self.stack(x, mod, geo.rope_cos, geo.rope_sin, kvs, negatives, n_pos=n_pos)
+        x = self.stack(x, mod, geo.rope_cos, geo.rope_sin, kvs, negatives, n_pos=n_pos,
+                       shared_input=batch > 1)
         return [self.output_stage(x[b], skip_low, skip0, emb, geo) for b in range(batch)]

@@ -149,12 +149,16 @@ def _modulation(w: dict, mod: torch.Tensor, c: int, dt: torch.dtype):
 
 def block_forward(w: dict, x: torch.Tensor, mod: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
                   ck: torch.Tensor | None, cv: torch.Tensor | None, negative: torch.Tensor | None, heads: int,
-                  n_pos: int = 1, inplace: bool = False) -> torch.Tensor:
+                  n_pos: int = 1, inplace: bool = False, shared_self: bool = False) -> torch.Tensor:
     """One block on ``x [B, N, C]`` (the MLX form, transformer.py:543-588): ``B`` branches of one
     object, ``n_pos`` conditioned by the cached condition K/V ``(ck, cv) [1, H, L, D]`` and the
     rest by the zero condition (constant ``negative [1, C]``).
 
     ``inplace=True`` updates ``x`` (the stack does this to avoid a copy per block).
+    ``shared_self=True`` states that every branch holds the same ``x`` (the first block of a
+    guided evaluation): the self-attention sub-layer then runs once and its result is copied to
+    the other branches, which is bit-identical because rows of every kernel are independent
+    (the reference's shared first-block attention, transformer.py:550-569, 656-664).
     """
     batch, n, c = x.shape
     dt = x.dtype
@@ -165,10 +169,13 @@ def block_forward(w: dict, x: torch.Tensor, mod: torch.Tensor, cos: torch.Tensor
     shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp = _modulation(w, mod, c, dt)
 
     # self-attention
-    h = kernels.layer_norm_modulate(x, 1e-6, scale=scale_msa, shift=shift_msa)
-    q, k, v = qkv_rope(h.view(-1, c), w, cos, sin, batch, heads, d)
+    xs = x[:1] if shared_self and batch > 1 else x
+    h = kernels.layer_norm_modulate(xs, 1e-6, scale=scale_msa, shift=shift_msa)
+    q, k, v = qkv_rope(h.view(-1, c), w, cos, sin, xs.shape[0], heads, d)
     a = attention.flash_attention(q, k, v, scale)
-    linear(a, w, "self_attn.to_out", epilogue="residual", residual=x, gate=gate_msa)
+    linear(a, w, "self_attn.to_out", epilogue="residual", residual=xs, gate=gate_msa)
+    if xs.shape[0] != batch:
+        x[1:].copy_(xs.expand(batch - 1, n, c))
 
     # cross-attention (positive branches), constant for the zero-condition branch
     h = kernels.layer_norm_modulate(x, 1e-6, weight=w["norm2.weight"], bias=w["norm2.bias"])
@@ -233,10 +240,13 @@ class BlockStack:
 
     def __call__(self, x: torch.Tensor, mod: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
                  kvs: list[tuple[torch.Tensor, torch.Tensor]], negatives: list[torch.Tensor] | None = None,
-                 n_pos: int = 1) -> torch.Tensor:
+                 n_pos: int = 1, shared_input: bool = False) -> torch.Tensor:
+        """``shared_input=True``: every branch of ``x`` holds the same rows (a guided evaluation),
+        so the first block's self-attention runs once."""
         x = x.clone()
         for i, w in enumerate(self.weights):
             ck, cv = kvs[i] if kvs is not None else (None, None)
             neg = None if negatives is None else negatives[i]
-            block_forward(w, x, mod, cos, sin, ck, cv, neg, self.heads, n_pos=n_pos, inplace=True)
+            block_forward(w, x, mod, cos, sin, ck, cv, neg, self.heads, n_pos=n_pos, inplace=True,
+                          shared_self=shared_input and i == 0)
         return x

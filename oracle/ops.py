@@ -472,6 +472,44 @@ def forward_f32(w: dict, feats: np.ndarray, coords: np.ndarray, t: float, cond: 
     return _lin(w, "out_layer", h)
 
 
+def guidance_scale_f32(t) -> float:
+    """Zero-condition guidance scale in float32 (pipeline.py:75-82)."""
+    t32 = F32(t)
+    if t32 >= 1.0:
+        return 4.0
+    if t32 >= 0.7:
+        return float(F32(10.0) * (t32 * t32))
+    return 1.0
+
+
+def sample_f32(w: dict, noise: np.ndarray, coords: np.ndarray, cond: np.ndarray, heads: int,
+               sigmas: np.ndarray, sigma_hats: np.ndarray, scheduler: str = "heun") -> np.ndarray:
+    """Hi3DPipelineMLX.sample (pipeline.py:156-229) on the fp32 forward: guided velocity
+    ``neg + s (pos - neg)`` with the all-zero condition as the negative branch (its cross-attention
+    reduces to the value bias, as the reference's negative branch computes directly), then Heun
+    (predictor at the next sigma, averaged slopes) or Euler updates."""
+    zeros = np.zeros_like(cond)
+
+    def velocity(x, t):
+        pos = forward_f32(w, x, coords, float(t), cond, heads)
+        if F32(t) < 0.7:
+            return pos
+        neg = forward_f32(w, x, coords, float(t), zeros, heads)
+        return (neg + F32(guidance_scale_f32(t)) * (pos - neg)).astype(F32)
+
+    x = noise.astype(F32)
+    for i in range(sigma_hats.shape[0]):
+        t, t_next = F32(sigma_hats[i]), F32(sigmas[i + 1])
+        dt = F32(t - t_next)
+        v1 = velocity(x, t)
+        if scheduler == "heun":
+            v2 = velocity((x - dt * v1).astype(F32), t_next)
+            x = (x - dt * (F32(0.5) * (v1 + v2))).astype(F32)
+        else:
+            x = (x - dt * v1).astype(F32)
+    return x
+
+
 # ----------------------------------------------------------------------------- CPU baseline timing
 
 

@@ -178,6 +178,22 @@ def main() -> None:
     np.savez_compressed(HERE / "forward.npz", coords=fine, feats=feats, cond=cond, t=t, velocity=vel,
                         config=np.array([c, cc, heads, nblk, io, 21]), weight_checksum=checksum)
 
+    # ---- the upstream flow-matching schedule and guidance (sparc3d.schedulers)
+    from sparc3d.schedulers.flow_match_heun import FlowMatchHeunScheduler
+    from sparc3d.schedulers.schedule import effective_guidance_scale
+
+    sched = {}
+    for steps, tokens in ((25, 34316), (12, 4000), (25, 1000), (3, 1500), (40, 262144)):
+        sch = FlowMatchHeunScheduler()
+        hats = sch.set_timesteps(steps, num_tokens=tokens)
+        sched[f"sigmas_{steps}_{tokens}"] = sch.sigmas.numpy()
+        sched[f"hats_{steps}_{tokens}"] = hats.numpy()
+    ts = np.array([1.2, 1.0, 0.99, 0.85, 0.7, 0.69999, 0.3], np.float32)
+    sched["guidance_t"] = ts
+    # the pipelines pass float32 model times: the tensor form compares and squares in float32
+    sched["guidance"] = effective_guidance_scale(torch.from_numpy(ts)).numpy().astype(np.float64)
+    np.savez_compressed(HERE / "schedule.npz", **sched)
+
     # ---- W8A8 sign tables of the signed H64 rotation
     from hi3d_mac.mlx_backend import w8a8 as ref_w8a8
 
