@@ -337,6 +337,65 @@ HI3D_API int hi3d_sparse_conv_act(const void* x, const int32_t* table, const uin
                                   const void* bias, void* out, int64_t n_in, int64_t n_out, int cin, int cout, int act,
                                   int dtype, void* stream);
 
+/* ---- sparse VAE decoder ---------------------------------------------------- */
+/* Bytes of workspace hi3d_group_norm_stats needs. */
+HI3D_API int hi3d_group_norm_stats_workspace_size(int64_t n, int64_t channels, int64_t* bytes);
+
+/* Replaces SparconvVAEDecoderMLX.group_stats (src/hi3d_mac/mlx_backend/vae.py:142-164; upstream
+ * PointGroupNorm): per-channel fp32 sums S1, S2 of x [n, channels] (f16 or f32), then per group of
+ * channels / groups channels mean = S1 / (count + eps), var = S2 / (count + eps) - mean^2,
+ * inv = 1 / sqrt(var + eps) with count = n * width; mean, inv [channels] (each group's values
+ * repeated over its channels).  Deterministic (fixed summation order). */
+HI3D_API int hi3d_group_norm_stats(const void* x, int64_t n, int64_t channels, int groups, float eps, float* mean,
+                                   float* inv, void* workspace, int64_t workspace_bytes, int dtype, void* stream);
+
+/* Replaces the normalise + swish part of kernels.gather_group_norm_swish
+ * (src/hi3d_mac/mlx_backend/kernels.py:242-296): out = swish(u), u = (x - mean) * inv * weight + bias
+ * in fp32, swish(u) = u * sigmoid(u) with sigmoid from e = 1 / (1 + exp(|u|)), rounded once to
+ * out_dtype (f16 or f32).  The convolution then gathers `out` (hi3d_sparse_conv): the activated
+ * features are written once instead of once per gathered neighbour. */
+HI3D_API int hi3d_group_norm_swish(const void* x, int64_t n, int64_t channels, const float* mean, const float* inv,
+                                   const float* weight, const float* bias, void* out, int in_dtype, int out_dtype,
+                                   void* stream);
+
+/* Bytes of workspace hi3d_child_structure / hi3d_child_table need for num_parents parents. */
+HI3D_API int hi3d_child_table_workspace_size(int64_t num_parents, int64_t* bytes);
+
+/* First half of sparse.child_neighbour_table (src/hi3d_mac/mlx_backend/sparse.py:64-95): from the
+ * occupancy mask [num_parents, 8] (uint8, nonzero = kept) the kept children in parent-major,
+ * slot-minor order: parent, slot [capacity >= 8 * num_parents] and *num_children (device int32).
+ * Fills `workspace` with the child lookup hi3d_child_table reads. */
+HI3D_API int hi3d_child_structure(const uint8_t* mask, int64_t num_parents, int32_t* parent, int32_t* slot,
+                                  int32_t* num_children, void* workspace, int64_t workspace_bytes, void* stream);
+
+/* Second half of sparse.child_neighbour_table (sparse.py:64-95, offsets :46-58): table [num_children, 27]
+ * of the children from the parent table [num_parents, 27] (sentinel num_parents): the neighbour of
+ * child (p, s) at offset k is child (parent_table[p][pk], s') with t = bits(s) + d_k,
+ * pk = offset of floor(t / 2), s' = slot of t mod 2; absent -> num_children.  `workspace` as filled
+ * by hi3d_child_structure. */
+HI3D_API int hi3d_child_table(const int32_t* parent_table, int64_t num_parents, const int32_t* parent,
+                              const int32_t* slot, int64_t num_children, const void* workspace, int32_t* table,
+                              void* stream);
+
+/* Bytes of workspace hi3d_serialize needs for n points. */
+HI3D_API int hi3d_serialize_workspace_size(int64_t n, int64_t* bytes);
+
+/* Replaces vae.serialization for one order (src/hi3d_mac/mlx_backend/vae.py:49-69; upstream
+ * Point.serialization): Morton keys of coords [n, 3] with `depth` bits per axis (x -> key bit
+ * 3i + 2, y -> 3i + 1, z -> 3i; swap_xy = 1 for the "z-trans" order), perm = the stable argsort of
+ * the keys, inverse[perm[i]] = i. */
+HI3D_API int hi3d_serialize(const int32_t* coords, int64_t n, int depth, int swap_xy, int32_t* perm,
+                            int32_t* inverse, void* workspace, int64_t workspace_bytes, void* stream);
+
+/* Replaces the windowed attention of SparconvVAEDecoderMLX.attention_block
+ * (src/hi3d_mac/mlx_backend/vae.py:249-266, windows :72-88; upstream SerializedAttention): qkv
+ * [n, 3, heads, head_dim] (f16 or f32); gather [n_pad] = the rows in padded window order
+ * (window_index); each window of `window` rows attends within itself (softmax(q k^T * scale) v,
+ * fp32), and the result of window position p < n is written to out[gather[p]] ([n, heads *
+ * head_dim]).  n <= window: one window of all rows (n_pad = n).  head_dim 16, 32 or 64. */
+HI3D_API int hi3d_window_attention(const void* qkv, const int32_t* gather, int64_t n, int64_t n_pad, int window,
+                                   int heads, int head_dim, float scale, void* out, int dtype, void* stream);
+
 /* ---- elementwise epilogues of the block --------------------------------- */
 /* x <- x + y * gate (all in the I/O type, two roundings: round(y*gate), then round(x + .)).
  * Replaces the residual/gate expressions at src/hi3d_mac/mlx_backend/transformer.py:570,588

@@ -80,6 +80,111 @@ def conv_weight(weight: np.ndarray) -> np.ndarray:
     return weight.reshape(weight.shape[0], -1).T
 
 
+# ----------------------------------------------------------------------------- VAE decoder
+
+
+def group_stats_f64(x: np.ndarray, eps: float = 1e-6):
+    """PointGroupNorm statistics (vae.py:142-164): groups of ``c / groups`` channels, 32 groups
+    (``c // 4`` below 128 channels); mean = S1 / (count + eps), var = S2 / (count + eps) - mean^2,
+    inv = 1 / sqrt(var + eps), count = n * width; repeated per channel."""
+    n, c = x.shape
+    groups = 32 if 4 * 32 <= c else c // 4
+    width = c // groups
+    xf = x.astype(np.float64)
+    s1 = xf.sum(0).reshape(groups, width).sum(1)
+    s2 = (xf * xf).sum(0).reshape(groups, width).sum(1)
+    count = n * width + eps
+    mean = s1 / count
+    inv = 1.0 / np.sqrt(s2 / count - mean * mean + eps)
+    return np.repeat(mean, width), np.repeat(inv, width)
+
+
+def group_norm_swish(x: np.ndarray, mean, inv, w, b) -> np.ndarray:
+    """``u * sigmoid(u)``, ``u = (x - mean) * inv * w + b`` in float64 (kernels.py:242-260)."""
+    u = (x.astype(np.float64) - mean) * inv * w + b
+    return u / (1.0 + np.exp(-u))
+
+
+def child_offset_tables():
+    """Parent-neighbourhood offset and child slot of every (slot, offset) (sparse.py:46-58)."""
+    pk = np.zeros((8, 27), np.int32)
+    ss = np.zeros((8, 27), np.int32)
+    for s in range(8):
+        bits = np.array([(s >> 2) & 1, (s >> 1) & 1, s & 1])
+        for k, d in enumerate(OFFSETS):
+            t = bits + d
+            pd, cb = t >> 1, t & 1
+            pk[s, k] = (pd[0] + 1) * 9 + (pd[1] + 1) * 3 + (pd[2] + 1)
+            ss[s, k] = cb[0] * 4 + cb[1] * 2 + cb[2]
+    return pk, ss
+
+
+def child_neighbour_table(parent_table: np.ndarray, child_mask: np.ndarray):
+    """Children of an octree upsampling and their neighbour table (sparse.py:64-95)."""
+    pk, ss = child_offset_tables()
+    p = child_mask.shape[0]
+    ids = np.flatnonzero(child_mask.reshape(-1))
+    nc = ids.size
+    lookup = np.full(p * 8 + 8, nc, np.int64)
+    lookup[ids] = np.arange(nc)
+    parent, slot = ids // 8, ids % 8
+    rows = parent_table[parent]
+    nbp = np.take_along_axis(rows, pk[slot], axis=1).astype(np.int64)
+    table = lookup[nbp * 8 + ss[slot]]
+    return table.astype(np.int32), parent.astype(np.int32), slot.astype(np.int32)
+
+
+def morton(coords: np.ndarray, depth: int) -> np.ndarray:
+    """Interleaved keys, x highest (vae.py:49-55)."""
+    x, y, z = (coords[:, i].astype(np.int64) for i in range(3))
+    key = np.zeros_like(x)
+    for i in range(depth):
+        key |= ((x >> i) & 1) << (3 * i + 2) | ((y >> i) & 1) << (3 * i + 1) | ((z >> i) & 1) << (3 * i)
+    return key
+
+
+def serialization(coords: np.ndarray):
+    """``[(perm, inverse)]`` for the orders z and z-trans (vae.py:58-69)."""
+    depth = int(coords.max()).bit_length()
+    out = []
+    for order in ("z", "z-trans"):
+        c = coords if order == "z" else coords[:, [1, 0, 2]]
+        perm = np.argsort(morton(c, depth), kind="stable")
+        inverse = np.empty_like(perm)
+        inverse[perm] = np.arange(perm.shape[0])
+        out.append((perm.astype(np.int32), inverse.astype(np.int32)))
+    return out
+
+
+def window_index(perm: np.ndarray, patch: int = 48) -> np.ndarray:
+    """Rows in padded window order (vae.py:72-88)."""
+    n = perm.shape[0]
+    if n <= patch:
+        return perm
+    n_pad = -(-n // patch) * patch
+    pad = np.arange(n_pad)
+    rem = n % patch
+    if rem:
+        pad[n_pad - patch + rem:] = pad[n_pad - 2 * patch + rem:n_pad - patch]
+    return perm[pad]
+
+
+def window_attention_f64(qkv: np.ndarray, gather: np.ndarray, inverse: np.ndarray, heads: int,
+                         patch: int = 48) -> np.ndarray:
+    """Attention within windows of ``patch`` rows of ``qkv [n, 3, heads, D]`` taken in ``gather``
+    order, scattered back by ``inverse`` (vae.py:249-266), float64."""
+    n = qkv.shape[0]
+    length = patch if gather.shape[0] >= patch else gather.shape[0]
+    d = qkv.shape[1] // 3 // heads
+    g = qkv.astype(np.float64)[gather].reshape(-1, length, 3, heads, d)
+    q, k, v = (g[:, :, i].transpose(0, 2, 1, 3) for i in range(3))
+    s = q @ k.transpose(0, 1, 3, 2) * d ** -0.5
+    p = np.exp(s - s.max(-1, keepdims=True))
+    o = (p / p.sum(-1, keepdims=True)) @ v
+    o = o.transpose(0, 2, 1, 3).reshape(-1, heads * d)
+    return o[inverse]
+
+
 # ----------------------------------------------------------------------------- rope
 
 

@@ -194,6 +194,28 @@ def main() -> None:
     sched["guidance"] = effective_guidance_scale(torch.from_numpy(ts)).numpy().astype(np.float64)
     np.savez_compressed(HERE / "schedule.npz", **sched)
 
+    # ---- VAE decoder index structures: the MLX helpers (octree child table, serialization, windows)
+    core = sys.modules["mlx.core"]
+    core.take = np.take
+    core.take_along_axis = np.take_along_axis
+    core.eval = lambda *a, **k: None
+    from hi3d_mac.mlx_backend import vae as ref_vae
+
+    occ = rng.random((10, 10, 10)) < 0.35
+    pc = np.argwhere(occ).astype(np.int32)
+    pc = pc[rng.permutation(pc.shape[0])]
+    ptable = ref_sparse.neighbour_table(pc)
+    cmask = rng.random((pc.shape[0], 8)) < 0.4
+    ctable, cparent, cslot = ref_sparse.child_neighbour_table(ptable, cmask)
+    scoords = synthetic.shell_coords(1000, 40, 12, 3, seed=41)
+    serial = ref_vae.serialization(scoords)
+    vae_out = dict(parent_coords=pc, parent_table=ptable, child_mask=cmask, child_table=np.asarray(ctable),
+                   child_parent=np.asarray(cparent), child_slot=np.asarray(cslot), serial_coords=scoords)
+    for i, (perm, inverse) in enumerate(serial):
+        gather, scatter = ref_vae.window_index(perm, inverse)
+        vae_out.update({f"perm{i}": perm, f"inverse{i}": inverse, f"gather{i}": gather, f"scatter{i}": scatter})
+    np.savez_compressed(HERE / "vae.npz", **vae_out)
+
     # ---- W8A8 sign tables of the signed H64 rotation
     from hi3d_mac.mlx_backend import w8a8 as ref_w8a8
 

@@ -120,6 +120,27 @@ def test_resampling_oracle_identities():
     assert rel_l2(ops.up_conv_f32(h, wt, b, table, inverse), direct) < 1e-6
 
 
+def test_vae_index_structures_bit_exact():
+    """Octree child table, serialization and window index vs the reference's MLX helpers."""
+    g = _load("vae")
+    table, parent, slot = ops.child_neighbour_table(g["parent_table"], g["child_mask"])
+    assert np.array_equal(table, g["child_table"])
+    assert np.array_equal(parent, g["child_parent"]) and np.array_equal(slot, g["child_slot"])
+    for i, (perm, inverse) in enumerate(ops.serialization(g["serial_coords"])):
+        assert np.array_equal(perm, g[f"perm{i}"]) and np.array_equal(inverse, g[f"inverse{i}"])
+        assert np.array_equal(ops.window_index(perm), g[f"gather{i}"])
+        assert np.array_equal(inverse, g[f"scatter{i}"])
+
+
+def test_child_table_geometry():
+    """A child's neighbour rows are the children at its coordinate + offset."""
+    g = _load("vae")
+    table, parent, slot = ops.child_neighbour_table(g["parent_table"], g["child_mask"])
+    bits = np.stack([(slot >> 2) & 1, (slot >> 1) & 1, slot & 1], 1)
+    coords = g["parent_coords"][parent] * 2 + bits
+    assert np.array_equal(table, ops.neighbour_table(coords))
+
+
 @pytest.mark.parametrize("k", [64, 1024, 2112, 4096])
 def test_w8a8_signs_bit_exact(k):
     assert np.array_equal(ops.signs(k), _load("w8a8")[f"signs{k}"])
