@@ -1,7 +1,7 @@
 """Benchmark of the sparse-DiT refinement torso on B200 (BASELINE configs[1] by default).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload stack|stack_w8a8|block|attention|attention262k|conv|forward]
+                    [--workload stack|stack_w8a8|block|attention|attention262k|conv|forward|vae]
 
 One step = one forward of the 24-block stack (C=1024, 16 heads x 64, GELU MLP 4x,
 1370 condition tokens) over T=32,768 voxel tokens of one object in fp16, inputs
@@ -291,14 +291,15 @@ def run_reference(args) -> None:
         per = statistics.median(secs)
         value, unit, metric, ms_step = n_low / per, "tokens/s", "forward_tokens_per_s", per * 1e3
         workload = f"whole transformer on CPU: {FWD_FINE} fine voxels, {n_low} low tokens, {BLOCKS} blocks"
-    elif args.workload == "conv":
+    elif args.workload in ("conv", "vae"):
         vals = []
         for i in range(args.warmup + args.steps):
             v, desc = cpu_conv_tflops()
             if i >= args.warmup:
                 vals.append(v)
-        value, unit, metric, ms_step = statistics.median(vals), "TFLOP/s", "sparse_conv_tflops", None
-        workload = "cfg5 submanifold conv on CPU"
+        value, unit, ms_step = statistics.median(vals), "TFLOP/s", None
+        metric = "sparse_conv_tflops" if args.workload == "conv" else "vae_conv_gn_swish_tflops"
+        workload = "cfg5 submanifold conv on CPU (the convolution that dominates both workloads)"
     else:
         big = args.workload == "attention262k"
         vals = []
@@ -740,6 +741,79 @@ def run_forward(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_vae(args) -> None:
+    """The VAE decoder's kernels at decoder sizes (one line; value = conv(swish(GN(x))) TFLOP/s):
+    a 256-channel level of 200,000 voxels (cfg5's shell) through GroupNorm statistics + swish +
+    the 3x3x3 conv; the octree child table of that level at 40 % occupancy; serialization and
+    48-point window attention over 32,768 latent points with 512 channels in 32 heads (fp16)."""
+    import torch
+
+    from hi3d_b200 import _lib, sparse, synthetic, vae
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    _lib.load()
+    n, c = 200_000, 256
+    coords = synthetic.shell_coords(n, 128, 48, 4, seed=5)
+    level = sparse.Level.from_coords(coords)
+    g = torch.Generator(device=dev).manual_seed(3)
+    x = (torch.randn((n, c), generator=g, device=dev) * 2).half()
+    nw, nb = torch.rand(c, device=dev) + 0.5, torch.randn(c, device=dev) * 0.1
+    w = (torch.randn((c, 3, 3, 3, c), generator=g, device=dev) * 0.02).half()
+    b = (torch.randn(c, generator=g, device=dev) * 0.02).half()
+    mask = torch.rand((n, 8), device=dev) < 0.4
+    lat = synthetic.shell_coords(32768, 64, 24, 3, seed=6)
+    lat_d = torch.from_numpy(lat).to(dev)
+    qkv = torch.randn((lat.shape[0], 3 * 512), generator=g, device=dev).half()
+    pairs = int((level.table < n).sum().item())
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(args.steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / args.steps
+
+    _lib.LAUNCHES[0] = 0
+    with ClockSampler(0) as clocks:
+        conv_ms = timed(lambda: vae.conv_gn_swish(x, level, nw, nb, w, b))
+        stats_ms = timed(lambda: vae.group_stats(x))
+        mean, inv = vae.group_stats(x)
+        swish_ms = timed(lambda: vae.group_norm_swish(x, mean, inv, nw, nb))
+        child_ms = timed(lambda: vae.child_neighbour_table(level.table, mask))
+        serial_ms = timed(lambda: vae.serialization(lat_d))
+        gather = vae.window_index(vae.serialization(lat_d)[0][0])
+        win_ms = timed(lambda: vae.window_attention(qkv, gather, 32))
+    launches = _lib.LAUNCHES[0]
+    flops = 2.0 * c * c * pairs
+    peaks = _peaks()
+    win_flops = 4.0 * gather.shape[0] * vae.PATCH * 512  # QK^T + PV over each window, all heads
+    line = {
+        "metric": "vae_conv_gn_swish_tflops", "value": flops / (conv_ms / 1e3) / 1e12, "unit": "TFLOP/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": conv_ms, "higher_is_better": True,
+        "scaling": "none", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": {"workload": f"VAE decoder kernels: conv(swish(GN(x))) on {n} voxels x {c} channels; child "
+                               f"table at 40 % occupancy; window attention over {lat.shape[0]} points, 512 ch, "
+                               f"32 heads, windows of {vae.PATCH}",
+                   "group_stats_ms": stats_ms, "group_norm_swish_ms": swish_ms,
+                   "group_norm_swish_gbs": n * c * 4 / (swish_ms / 1e3) / 1e9,
+                   "child_table_ms": child_ms, "serialization_ms": serial_ms, "window_attention_ms": win_ms,
+                   "window_attention_tflops": win_flops / (win_ms / 1e3) / 1e12,
+                   "l2": "inputs larger than L2 (102 MB features + weights per step)"},
+        "roofline": {"bound": "tensor", "achieved": flops / (conv_ms / 1e3) / 1e12, "peak": peaks["bf16_tflops"],
+                     "unit": "TFLOP/s", "frac": flops / (conv_ms / 1e3) / 1e12 / peaks["bf16_tflops"],
+                     "traffic": None, "peak_source": f"{peaks['source']} bf16_tflops (burst)",
+                     "note": "whole conv_gn_swish step (stats + swish + conv) against the conv's FLOPs"},
+        "gpu_launches": launches, "clocks": clocks.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -747,7 +821,7 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["stack", "stack_w8a8", "block", "attention", "attention262k", "conv",
-                                           "forward"], default="stack")
+                                           "forward", "vae"], default="stack")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -759,6 +833,8 @@ def main() -> None:
         run_conv(args)
     elif args.workload == "forward":
         run_forward(args)
+    elif args.workload == "vae":
+        run_vae(args)
     else:
         run_attention(args, big=args.workload == "attention262k")
 

@@ -114,6 +114,100 @@ __global__ void __launch_bounds__(256) gn_swish_kernel(const X* __restrict__ x, 
   }
 }
 
+// 8 consecutive channels of one row as fp32 (16 bytes of fp16, 32 bytes of fp32)
+template <typename X>
+__device__ __forceinline__ void load8f(const X* p, float (&v)[8]);
+template <>
+__device__ __forceinline__ void load8f<__half>(const __half* p, float (&v)[8]) {
+  const uint4 r = *reinterpret_cast<const uint4*>(p);
+  const __half2* h = reinterpret_cast<const __half2*>(&r);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __half22float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+template <>
+__device__ __forceinline__ void load8f<float>(const float* p, float (&v)[8]) {
+  const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
+  v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+}
+template <typename T>
+__device__ __forceinline__ void store8(T* p, const float (&v)[8]);
+template <>
+__device__ __forceinline__ void store8<__half>(__half* p, const float (&v)[8]) {
+  uint4 r;
+  __half2* h = reinterpret_cast<__half2*>(&r);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+  *reinterpret_cast<uint4*>(p) = r;
+}
+template <>
+__device__ __forceinline__ void store8<float>(float* p, const float (&v)[8]) {
+  *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+  *reinterpret_cast<float4*>(p + 4) = make_float4(v[4], v[5], v[6], v[7]);
+}
+
+// Stage 1 with 8-channel vectors (channels % 8 == 0, <= 2048): thread (rr, v) of the block
+// sums channels 8v .. 8v + 7 over rows r0 + rr, r0 + rr + R, ...; the R row lanes are then
+// added in lane order through shared memory.
+template <typename X>
+__global__ void __launch_bounds__(256) gn_partial_v8_kernel(const X* __restrict__ x, int64_t n, int c, int64_t chunk,
+                                                            float* __restrict__ partial) {
+  extern __shared__ float red[];  // [R][2 c]
+  const int vecs = c / 8, lanes = blockDim.x / vecs;
+  const int v = threadIdx.x % vecs, rr = threadIdx.x / vecs;
+  const int64_t r0 = (int64_t)blockIdx.x * chunk;
+  const int64_t r1 = min(n, r0 + chunk);
+  if (rr < lanes) {
+    float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, b[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int64_t r = r0 + rr; r < r1; r += lanes) {
+      float xv[8];
+      load8f<X>(x + r * c + v * 8, xv);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        a[i] = __fadd_rn(a[i], xv[i]);
+        b[i] = __fmaf_rn(xv[i], xv[i], b[i]);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      red[rr * 2 * c + v * 8 + i] = a[i];
+      red[rr * 2 * c + c + v * 8 + i] = b[i];
+    }
+  }
+  __syncthreads();
+  float* out = partial + (int64_t)blockIdx.x * 2 * c;
+  for (int e = threadIdx.x; e < 2 * c; e += blockDim.x) {
+    float acc = 0.f;
+    for (int l = 0; l < lanes; ++l) acc = __fadd_rn(acc, red[l * 2 * c + e]);
+    out[e] = acc;
+  }
+}
+
+template <typename X, typename T>
+__global__ void __launch_bounds__(256) gn_swish_v8_kernel(const X* __restrict__ x, int64_t n, int c,
+                                                          const float* __restrict__ mean,
+                                                          const float* __restrict__ inv, const float* __restrict__ w,
+                                                          const float* __restrict__ b, T* __restrict__ out) {
+  const int vecs = c / 8;
+  const int64_t total = n * vecs;
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+    const int ch = (int)(t % vecs) * 8;
+    float xv[8], o[8];
+    load8f<X>(x + t * 8, xv);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float u = __fadd_rn(
+          __fmul_rn(__fmul_rn(__fsub_rn(xv[i], mean[ch + i]), inv[ch + i]), w[ch + i]), b[ch + i]);
+      const float e = 1.0f / (1.0f + expf(fabsf(u)));
+      o[i] = u < 0.0f ? u * e : u * (1.0f - e);
+    }
+    store8<T>(out + t * 8, o);
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Octree child neighbour table.  Child (p, s) sits at 2 p + bits(s), bits(s) =
 // (s >> 2 & 1, s >> 1 & 1, s & 1); its neighbour at offset d = r_k - 1 is child
@@ -282,12 +376,22 @@ extern "C" int hi3d_group_norm_stats(const void* x, int64_t n, int64_t channels,
   float* partial = static_cast<float*>(workspace);
   cudaStream_t st = as_stream(stream);
   const int c = (int)channels;
-  if (dtype == HI3D_F16)
-    gn_partial_kernel<__half><<<blocks, 256, 0, st>>>((const __half*)x, n, c, chunk, partial);
-  else if (dtype == HI3D_F32)
-    gn_partial_kernel<float><<<blocks, 256, 0, st>>>((const float*)x, n, c, chunk, partial);
-  else
+  if (dtype != HI3D_F16 && dtype != HI3D_F32)
     return set_error(HI3D_ERR_INVALID_ARGUMENT, "group_norm_stats: dtype must be f16 or f32");
+  const bool vec = c % 8 == 0 && c <= 2048 && aligned16(x);
+  if (vec) {
+    const int vecs = c / 8, lanes = 256 / vecs;
+    const int threads = lanes * vecs;
+    const size_t red = (size_t)lanes * 2 * c * sizeof(float);  // <= 16 KB
+    if (dtype == HI3D_F16)
+      gn_partial_v8_kernel<__half><<<blocks, threads, red, st>>>((const __half*)x, n, c, chunk, partial);
+    else
+      gn_partial_v8_kernel<float><<<blocks, threads, red, st>>>((const float*)x, n, c, chunk, partial);
+  } else if (dtype == HI3D_F16) {
+    gn_partial_kernel<__half><<<blocks, 256, 0, st>>>((const __half*)x, n, c, chunk, partial);
+  } else {
+    gn_partial_kernel<float><<<blocks, 256, 0, st>>>((const float*)x, n, c, chunk, partial);
+  }
   const size_t smem = (size_t)2 * c * sizeof(float);
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(gn_finish_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -305,10 +409,27 @@ extern "C" int hi3d_group_norm_swish(const void* x, int64_t n, int64_t channels,
   if ((in_dtype != HI3D_F16 && in_dtype != HI3D_F32) || (out_dtype != HI3D_F16 && out_dtype != HI3D_F32))
     return set_error(HI3D_ERR_INVALID_ARGUMENT, "group_norm_swish: dtypes must be f16 or f32");
   if (n == 0) return HI3D_OK;
-  const int64_t total = n * channels, blocks = (total + 255) / 256, cap = (int64_t)sm_count() * 8;
-  const unsigned grid = (unsigned)(blocks < cap ? blocks : cap);
   cudaStream_t st = as_stream(stream);
   const int c = (int)channels;
+  if (c % 8 == 0 && aligned16(x) && aligned16(out)) {
+    const int64_t total = n * (c / 8), blocks = (total + 255) / 256, cap = (int64_t)sm_count() * 8;
+    const unsigned grid = (unsigned)(blocks < cap ? blocks : cap);
+    if (in_dtype == HI3D_F16 && out_dtype == HI3D_F16)
+      gn_swish_v8_kernel<__half, __half>
+          <<<grid, 256, 0, st>>>((const __half*)x, n, c, mean, inv, weight, bias, (__half*)out);
+    else if (in_dtype == HI3D_F16)
+      gn_swish_v8_kernel<__half, float>
+          <<<grid, 256, 0, st>>>((const __half*)x, n, c, mean, inv, weight, bias, (float*)out);
+    else if (out_dtype == HI3D_F16)
+      gn_swish_v8_kernel<float, __half>
+          <<<grid, 256, 0, st>>>((const float*)x, n, c, mean, inv, weight, bias, (__half*)out);
+    else
+      gn_swish_v8_kernel<float, float>
+          <<<grid, 256, 0, st>>>((const float*)x, n, c, mean, inv, weight, bias, (float*)out);
+    return check_launch("group_norm_swish");
+  }
+  const int64_t total = n * channels, blocks = (total + 255) / 256, cap = (int64_t)sm_count() * 8;
+  const unsigned grid = (unsigned)(blocks < cap ? blocks : cap);
   if (in_dtype == HI3D_F16 && out_dtype == HI3D_F16)
     gn_swish_kernel<__half, __half><<<grid, 256, 0, st>>>((const __half*)x, n, c, mean, inv, weight, bias, (__half*)out);
   else if (in_dtype == HI3D_F16)
