@@ -9,7 +9,8 @@
 // (GELU in fp32, transformer.py:176-179); or update a residual stream in place,
 // x = round(x + round(y * gate)) (transformer.py:570, :588).
 //
-// CTA (320 threads), one per SM, looping over 128 x 256 output tiles:
+// CTA (320 threads), one per SM, looping over 128 x 256 output tiles (16-bit GEMMs run
+// as CTA pairs, cta_group::2, over 256 x 256 tiles: see PAIR below):
 //   warp 0     TMA producer: A [128 x 128 B] and W [256 x 128 B] per stage
 //   warp 1     MMA issuer (one lane), TMEM owner; two 256-column accumulators
 //              so the epilogue of one tile overlaps the MMAs of the next
@@ -35,6 +36,10 @@ constexpr int EPI_WARPS = 8;
 constexpr int STAGE_BYTES = 32 * 64;  // per epilogue warp: 32 rows x 32 16-bit columns
 constexpr int VEC = 384;  // per epilogue warp: bias, weight scales, QK-norm gains of its 128 columns
 constexpr int SMEM = NST * (A_STAGE + B_STAGE) + EPI_WARPS * (STAGE_BYTES + VEC * 4) + 1024 + 256;
+// CTA pairs (cta_group::2): a 256 x 256 output tile per pair, each CTA holding 128 rows of A,
+// 128 rows of W and its 128 x 256 accumulator rows; a 32 KB stage allows a 6-deep ring.
+constexpr int NST_PAIR = 6;
+constexpr int SMEM_PAIR = NST_PAIR * (A_STAGE + B_STAGE / 2) + EPI_WARPS * (STAGE_BYTES + VEC * 4) + 1024 + 256;
 
 enum Kind { KIND_F16 = 0, KIND_BF16 = 1, KIND_I8 = 2 };
 enum Epi { EPI_STORE = 0, EPI_GELU = 1, EPI_RESIDUAL = 2, EPI_QKV_ROPE = 3 };
@@ -63,8 +68,8 @@ struct Params {
 };
 
 struct Barriers {
-  uint64_t full[NST];
-  uint64_t empty[NST];
+  uint64_t full[NST_PAIR];
+  uint64_t empty[NST_PAIR];
   uint64_t acc_full[2];
   uint64_t acc_empty[2];
   uint32_t tmem_base;
@@ -95,14 +100,25 @@ __device__ __forceinline__ void prefetch_residual(const Params& p, uint4 (&r)[4]
   }
 }
 
-template <int KIND, int EPI, typename OutT>
+// PAIR: launched as clusters of two CTAs.  Both CTAs load their halves of the operands
+// (completion counted on the first CTA's barriers); the first CTA's MMA warp issues the
+// cta_group::2 MMAs and releases stages and accumulators to both CTAs with one commit;
+// each CTA runs the epilogue of its 128 accumulator rows and hands the accumulator back to
+// the first CTA.
+template <int KIND, int EPI, typename OutT, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Params p) {
+  constexpr int NSTX = PAIR ? NST_PAIR : NST;
+  constexpr int B_STAGE_L = PAIR ? B_STAGE / 2 : B_STAGE;  // W rows per CTA: BN / 2 or BN
+  constexpr int TM = PAIR ? 2 * BM : BM;                   // output rows per tile
+  const uint32_t rank = PAIR ? cluster_rank() : 0u;
+  const int tile0 = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int tstep = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
-  uint8_t* sB = smem + NST * A_STAGE;
-  uint8_t* sStage = sB + NST * B_STAGE;
+  uint8_t* sB = smem + NSTX * A_STAGE;
+  uint8_t* sStage = sB + NSTX * B_STAGE_L;
   float* sVec = reinterpret_cast<float*>(sStage + EPI_WARPS * STAGE_BYTES);
   Barriers* bar = reinterpret_cast<Barriers*>(sVec + EPI_WARPS * VEC);
   constexpr int ESZ = KIND == KIND_I8 ? 1 : 2;
@@ -112,23 +128,31 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int num_tiles = p.tiles_m * p.tiles_n;
   const int kblocks = (p.K + BKE - 1) / BKE;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < NST; ++s) {
+    for (int s = 0; s < NSTX; ++s) {
       mbar_init(&bar->full[s], 1);
       mbar_init(&bar->empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&bar->acc_full[a], 1);
-      mbar_init(&bar->acc_empty[a], EPI_WARPS);
+      mbar_init(&bar->acc_empty[a], PAIR ? 2 * EPI_WARPS : EPI_WARPS);
     }
     bar->abort = 0;
     fence_barrier_init();
   }
   if (warp == 1) {
-    tmem_alloc(&bar->tmem_base, 512);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(&bar->tmem_base, 512);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(&bar->tmem_base, 512);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR)
+    cluster_sync();  // both CTAs' barriers are initialised before any cross-CTA signal
+  else
+    __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bar->tmem_base;
   volatile int* abort = &bar->abort;
@@ -139,55 +163,82 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_prefetch_desc(&tmB);
       int it = 0;  // global k-block counter (ring position)
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
-        const int m0 = (tile / p.tiles_n) * BM, n0 = (tile % p.tiles_n) * BN;
+      for (int tile = tile0; ok && tile < num_tiles; tile += tstep) {
+        const int m0 = (tile / p.tiles_n) * TM + (int)rank * BM;
+        const int n0 = (tile % p.tiles_n) * BN + (int)rank * (BN / 2) * (PAIR ? 1 : 0);
         for (int kb = 0; kb < kblocks; ++kb, ++it) {
-          const int s = it % NST, n = it / NST;
+          const int s = it % NSTX, n = it / NSTX;
           if (!(ok = mbar_wait(&bar->empty[s], (n & 1) ^ 1, abort, 101))) break;
-          mbar_arrive_expect_tx(&bar->full[s], A_STAGE + B_STAGE);
-          tma_load_2d(sA + s * A_STAGE, &tmA, &bar->full[s], kb * BKE, m0);
-          tma_load_2d(sB + s * B_STAGE, &tmB, &bar->full[s], kb * BKE, n0);
+          if constexpr (PAIR) {
+            // the first CTA expects both CTAs' bytes on its barrier
+            if (rank == 0) mbar_arrive_expect_tx(&bar->full[s], 2 * (A_STAGE + B_STAGE_L));
+            const uint32_t fb = cluster_addr(&bar->full[s], 0);
+            tma_load_2d_pair(sA + s * A_STAGE, &tmA, fb, kb * BKE, m0);
+            tma_load_2d_pair(sB + s * B_STAGE_L, &tmB, fb, kb * BKE, n0);
+          } else {
+            mbar_arrive_expect_tx(&bar->full[s], A_STAGE + B_STAGE);
+            tma_load_2d(sA + s * A_STAGE, &tmA, &bar->full[s], kb * BKE, m0);
+            tma_load_2d(sB + s * B_STAGE, &tmB, &bar->full[s], kb * BKE, n0);
+          }
         }
       }
       volatile int no_abort = 0;
       if (!ok) {
-        // drain the copies already in flight before leaving
-        for (int j = (it > NST ? it - NST : 0); j < it; ++j) mbar_wait(&bar->full[j % NST], (j / NST) & 1, &no_abort, 102);
+        // drain the copies already in flight before leaving (in a pair the first CTA's
+        // barriers count both CTAs' copies, and the final cluster barrier holds the second)
+        if (!PAIR || rank == 0)
+          for (int j = (it > NSTX ? it - NSTX : 0); j < it; ++j)
+            mbar_wait(&bar->full[j % NSTX], (j / NSTX) & 1, &no_abort, 102);
       } else {
         // producer tail: wait for the MMA warp's last releases of each stage, so
         // no barrier arrive is still in flight when the CTA exits
-        for (int j = (it > NST ? it - NST : 0); j < it; ++j) mbar_wait(&bar->empty[j % NST], (j / NST) & 1, abort, 103);
+        for (int j = (it > NSTX ? it - NSTX : 0); j < it; ++j)
+          mbar_wait(&bar->empty[j % NSTX], (j / NSTX) & 1, abort, 103);
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      constexpr uint32_t idesc = KIND == KIND_I8 ? make_idesc(2, 1, 0, 0, BM, BN)
-                                                 : make_idesc(1, KIND == KIND_BF16 ? 1 : 0, 0, 0, BM, BN);
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = KIND == KIND_I8 ? make_idesc(2, 1, 0, 0, TM, BN)
+                                                 : make_idesc(1, KIND == KIND_BF16 ? 1 : 0, 0, 0, TM, BN);
       const uint32_t sAa = smem_u32(sA), sBa = smem_u32(sB);
       int it = 0, local = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x, ++local) {
+      for (int tile = tile0; ok && tile < num_tiles; tile += tstep, ++local) {
         const int acc = local & 1, use = local >> 1;
         if (!(ok = mbar_wait(&bar->acc_empty[acc], (use & 1) ^ 1, abort, 110))) break;
         tc_fence_after();
         const uint32_t d = tmem + acc * BN;
         for (int kb = 0; kb < kblocks; ++kb, ++it) {
-          const int s = it % NST, n = it / NST;
+          const int s = it % NSTX, n = it / NSTX;
           if (!(ok = mbar_wait(&bar->full[s], n & 1, abort, 111))) break;
           tc_fence_after();
 #pragma unroll
           for (int k = 0; k < BKB / 32; ++k) {
             const uint64_t da = smem_desc(sAa + s * A_STAGE + k * 32, 16, 1024, kLayoutSW128);
-            const uint64_t db = smem_desc(sBa + s * B_STAGE + k * 32, 16, 1024, kLayoutSW128);
-            if (KIND == KIND_I8)
-              mma_i8_ss(d, da, db, idesc, (kb > 0 || k > 0) ? 1u : 0u);
-            else
-              mma_f16_ss(d, da, db, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+            const uint64_t db = smem_desc(sBa + s * B_STAGE_L + k * 32, 16, 1024, kLayoutSW128);
+            const uint32_t accum = (kb > 0 || k > 0) ? 1u : 0u;
+            if constexpr (PAIR) {
+              if (KIND == KIND_I8)
+                mma_i8_ss_pair(d, da, db, idesc, accum);
+              else
+                mma_f16_ss_pair(d, da, db, idesc, accum);
+            } else {
+              if (KIND == KIND_I8)
+                mma_i8_ss(d, da, db, idesc, accum);
+              else
+                mma_f16_ss(d, da, db, idesc, accum);
+            }
           }
-          tc_commit(&bar->empty[s]);
+          if constexpr (PAIR)
+            tc_commit_pair(&bar->empty[s], 3);
+          else
+            tc_commit(&bar->empty[s]);
         }
         if (!ok) break;
-        tc_commit(&bar->acc_full[acc]);
+        if constexpr (PAIR)
+          tc_commit_pair(&bar->acc_full[acc], 3);
+        else
+          tc_commit(&bar->acc_full[acc]);
       }
     }
   } else {
@@ -212,9 +263,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     // the current tile's chunks finish, so the loads overlap the current tile.
     uint4 res[4][4];
     int local = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+    for (int tile = tile0; tile < num_tiles; tile += tstep, ++local) {
       const int acc = local & 1, use = local >> 1;
-      const int m0 = (tile / p.tiles_n) * BM + q * 32;  // this warp's first row
+      const int m0 = (tile / p.tiles_n) * TM + (int)rank * BM + q * 32;  // this warp's first row
       const int nh = (tile % p.tiles_n) * BN + h * 128;  // this warp's first column
       if constexpr (!kRaw) {
 #pragma unroll
@@ -426,9 +477,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             __syncwarp();  // the staging tile is rewritten by the next chunk
             if (EPI == EPI_RESIDUAL) {
-              const int nt = tile + gridDim.x;
+              const int nt = tile + tstep;
               if (nt < num_tiles)
-                prefetch_residual<OutT>(p, res[c], (nt / p.tiles_n) * BM + q * 32,
+                prefetch_residual<OutT>(p, res[c], (nt / p.tiles_n) * TM + (int)rank * BM + q * 32,
                                         (nt % p.tiles_n) * BN + h * 128 + c * 32, lane);
             }
           }
@@ -436,15 +487,30 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bar->acc_empty[acc]);
+      if (lane == 0) {
+        // the accumulator belongs to the first CTA's MMA warp
+        if (PAIR && rank != 0)
+          mbar_arrive_remote(cluster_addr(&bar->acc_empty[acc], 0));
+        else
+          mbar_arrive(&bar->acc_empty[acc]);
+      }
     }
   }
 
   tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc(tmem, 512);
+  if constexpr (PAIR) {
+    // no CTA of the pair leaves while the other may still signal its barriers
+    cluster_sync();
+    if (warp == 1) {
+      tc_fence_after();
+      tmem_dealloc_pair(tmem, 512);
+    }
+  } else {
+    __syncthreads();
+    if (warp == 1) {
+      tc_fence_after();
+      tmem_dealloc(tmem, 512);
+    }
   }
 }
 
@@ -461,17 +527,25 @@ static int num_sms() {
   return n;
 }
 
+#ifndef HI3D_GEMM_PAIR
+#define HI3D_GEMM_PAIR 1
+#endif
+
 template <int KIND, int EPI, typename OutT>
 static int launch_gemm(const void* a, const void* w, int M, int N, int K, const gemm::Params& prm, cudaStream_t st) {
   using namespace gemm;
   const int esz = KIND == KIND_I8 ? 1 : 2;
+  // CTA pairs for the 16-bit GEMMs with at least two 128-row blocks: each SM reads 32 KB of
+  // operands per 64-deep K step instead of 48 KB (block projections 927 -> 902 us at
+  // T = 32768, bit-identical).  The int8 GEMM measured slower in pairs (199 -> 208 us).
+  const bool pair = HI3D_GEMM_PAIR && KIND != KIND_I8 && M > BM;
   const CUtensorMapDataType t = KIND == KIND_I8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8
                                 : KIND == KIND_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                                     : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUtensorMap ma, mb;
   uint64_t da[2] = {(uint64_t)K, (uint64_t)M}, db[2] = {(uint64_t)K, (uint64_t)N};
   uint64_t sa[1] = {(uint64_t)K * esz}, sb[1] = {(uint64_t)K * esz};
-  uint32_t ba[2] = {(uint32_t)(BKB / esz), BM}, bb[2] = {(uint32_t)(BKB / esz), BN};
+  uint32_t ba[2] = {(uint32_t)(BKB / esz), BM}, bb[2] = {(uint32_t)(BKB / esz), (uint32_t)(pair ? BN / 2 : BN)};
   int rc;
   if ((rc = encode_tmap(&ma, t, 2, a, da, sa, ba, CU_TENSOR_MAP_SWIZZLE_128B))) return rc;
   if ((rc = encode_tmap(&mb, t, 2, w, db, sb, bb, CU_TENSOR_MAP_SWIZZLE_128B))) return rc;
@@ -484,14 +558,43 @@ static int launch_gemm(const void* a, const void* w, int M, int N, int K, const 
   p.M = M;
   p.N = N;
   p.K = K;
-  p.tiles_m = (M + BM - 1) / BM;
+  const int tm = pair ? 2 * BM : BM;
+  p.tiles_m = (M + tm - 1) / tm;
   p.tiles_n = (N + BN - 1) / BN;
   const int tiles = p.tiles_m * p.tiles_n;
-  const int grid = tiles < num_sms() ? tiles : num_sms();
-  auto kern = gemm_kernel<KIND, EPI, OutT>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+  if (!pair) {
+    const int grid = tiles < num_sms() ? tiles : num_sms();
+    auto kern = gemm_kernel<KIND, EPI, OutT, false>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+    if (e != cudaSuccess) return set_error(HI3D_ERR_CUDA, "gemm: smem attribute: %s", cudaGetErrorString(e));
+    kern<<<grid, kThreads, SMEM, st>>>(ma, mb, p);
+    return check_launch("gemm");
+  }
+  auto kern = gemm_kernel<KIND, EPI, OutT, true>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_PAIR);
   if (e != cudaSuccess) return set_error(HI3D_ERR_CUDA, "gemm: smem attribute: %s", cudaGetErrorString(e));
-  kern<<<grid, kThreads, SMEM, st>>>(ma, mb, p);
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = SMEM_PAIR;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  static int max_pairs = 0;  // co-resident pairs (one CTA per SM)
+  if (max_pairs == 0) {
+    cfg.gridDim = dim3(2 * (num_sms() / 2));
+    int n = 0;
+    e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
+    max_pairs = (e == cudaSuccess && n > 0) ? n : num_sms() / 2;
+  }
+  const int pairs = tiles < max_pairs ? tiles : max_pairs;
+  cfg.gridDim = dim3(2 * pairs);
+  e = cudaLaunchKernelEx(&cfg, kern, ma, mb, p);
+  if (e != cudaSuccess) return set_error(HI3D_ERR_CUDA, "gemm: pair launch: %s", cudaGetErrorString(e));
   return check_launch("gemm");
 }
 
