@@ -147,9 +147,19 @@ def _modulation(w: dict, mod: torch.Tensor, c: int, dt: torch.dtype):
     return shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp
 
 
+def modulation_all(mod_w: torch.Tensor, mod: torch.Tensor, c: int, dt: torch.dtype) -> list[tuple]:
+    """:func:`_modulation` of every block at once: ``mod_w [blocks, 6C]`` stacked block
+    parameters; same element-wise operations, so the values are identical."""
+    parts = (mod_w + mod.float().reshape(1, -1)).view(mod_w.shape[0], 6, c)
+    sg = parts[:, [0, 2, 3, 5]].to(dt)
+    sc = (1 + parts[:, [1, 4]]).to(dt)
+    return [(sg[i, 0], sc[i, 0], sg[i, 1], sg[i, 2], sc[i, 1], sg[i, 3]) for i in range(mod_w.shape[0])]
+
+
 def block_forward(w: dict, x: torch.Tensor, mod: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
                   ck: torch.Tensor | None, cv: torch.Tensor | None, negative: torch.Tensor | None, heads: int,
-                  n_pos: int = 1, inplace: bool = False, shared_self: bool = False) -> torch.Tensor:
+                  n_pos: int = 1, inplace: bool = False, shared_self: bool = False,
+                  mods: tuple | None = None) -> torch.Tensor:
     """One block on ``x [B, N, C]`` (the MLX form, transformer.py:543-588): ``B`` branches of one
     object, ``n_pos`` conditioned by the cached condition K/V ``(ck, cv) [1, H, L, D]`` and the
     rest by the zero condition (constant ``negative [1, C]``).
@@ -159,6 +169,7 @@ def block_forward(w: dict, x: torch.Tensor, mod: torch.Tensor, cos: torch.Tensor
     guided evaluation): the self-attention sub-layer then runs once and its result is copied to
     the other branches, which is bit-identical because rows of every kernel are independent
     (the reference's shared first-block attention, transformer.py:550-569, 656-664).
+    ``mods``: this block's modulation vectors precomputed by :func:`modulation_all`.
     """
     batch, n, c = x.shape
     dt = x.dtype
@@ -166,7 +177,8 @@ def block_forward(w: dict, x: torch.Tensor, mod: torch.Tensor, cos: torch.Tensor
     scale = d ** -0.5
     if not inplace:
         x = x.clone()
-    shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp = _modulation(w, mod, c, dt)
+    shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp = mods if mods is not None else \
+        _modulation(w, mod, c, dt)
 
     # self-attention
     xs = x[:1] if shared_self and batch > 1 else x
@@ -233,6 +245,7 @@ class BlockStack:
     def __init__(self, weights: list[dict], heads: int):
         self.weights = weights
         self.heads = heads
+        self._mod_w = None  # [blocks, 6C] stacked modulation parameters (built on first use)
 
     def prepare(self, cond: torch.Tensor) -> list[tuple[torch.Tensor, torch.Tensor]]:
         """Per-block condition K/V for a ``[L, Cc]`` condition (once per sampling pass)."""
@@ -244,9 +257,12 @@ class BlockStack:
         """``shared_input=True``: every branch of ``x`` holds the same rows (a guided evaluation),
         so the first block's self-attention runs once."""
         x = x.clone()
+        if self._mod_w is None:
+            self._mod_w = torch.stack([w["modulation"].reshape(-1).float() for w in self.weights])
+        mods = modulation_all(self._mod_w, mod, x.shape[-1], x.dtype)
         for i, w in enumerate(self.weights):
             ck, cv = kvs[i] if kvs is not None else (None, None)
             neg = None if negatives is None else negatives[i]
             block_forward(w, x, mod, cos, sin, ck, cv, neg, self.heads, n_pos=n_pos, inplace=True,
-                          shared_self=shared_input and i == 0)
+                          shared_self=shared_input and i == 0, mods=mods[i])
         return x
