@@ -138,6 +138,205 @@ __global__ void __launch_bounds__(256) quant_h64_kernel(const T* __restrict__ x,
   }
 }
 
+// ---------------------------------------------------------------------------
+// LayerNorm-modulate fused with the signed-H64 quantiser: the input of the W8A8
+// projections that follow a norm (QKV, cross-attention Q, MLP in).  Per row, one warp:
+// the LayerNorm32 + affine / modulation of ln_mod_kernel (rowwise.cu; kernels.py:162-201)
+// to the rounded 16-bit h, then exactly the quantiser above on h: sign, H64 (three
+// in-register butterfly stages, three across lanes 1, 2 and 4 apart, / 8), row maximum,
+// codes.  The 16-bit h is never written: bit-identical to quantize(layer_norm_modulate(x)).
+// Lane l of the warp holds channels c * 256 + 8 l .. + 7 of chunk c (channels % 64 == 0).
+// ---------------------------------------------------------------------------
+constexpr int kLnqRowsPerBlock = 4;
+
+template <typename T, int NCH, bool AFFINE, bool MODULATE>
+__global__ void __launch_bounds__(kLnqRowsPerBlock * 32)
+    ln_quant_kernel(const T* __restrict__ x, int64_t rows, int C, float eps, const float* __restrict__ weight,
+                    const float* __restrict__ bias, const T* __restrict__ scale, const T* __restrict__ shift,
+                    int64_t rows_per_batch, int64_t mod_stride, const float* __restrict__ sign,
+                    int8_t* __restrict__ q, float* __restrict__ qscale) {
+  const int lane = threadIdx.x & 31;
+  const int g = lane & 7;
+  for (int64_t row = (int64_t)blockIdx.x * kLnqRowsPerBlock + (threadIdx.x >> 5); row < rows;
+       row += (int64_t)gridDim.x * kLnqRowsPerBlock) {
+    const T* xr = x + row * C;
+    // ---- LayerNorm statistics (as ln_mod_kernel)
+    uint4 raw[NCH];
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      raw[c] = make_uint4(0, 0, 0, 0);
+      if (c * 256 + lane * 8 < C) raw[c] = *reinterpret_cast<const uint4*>(xr + c * 256 + lane * 8);
+    }
+    uint64_t d[NCH][4];
+    uint64_t s2 = 0;
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      const uint32_t* rw = reinterpret_cast<const uint32_t*>(&raw[c]);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        d[c][i] = Cvt<T>::to_f2(rw[i]);
+        s2 = f2_add(s2, d[c][i]);
+      }
+    }
+    float slo, shi;
+    f2_unpack(s2, slo, shi);
+    float sum = slo + shi;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    const float mean = __fdiv_rn(sum, (float)C);
+    const uint64_t neg_mean = f2_splat(-mean);
+    uint64_t q2 = 0;
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      if (c * 256 + lane * 8 < C) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          d[c][i] = f2_add(d[c][i], neg_mean);
+          q2 = f2_fma(d[c][i], d[c][i], q2);
+        }
+      }
+    }
+    float qlo, qhi;
+    f2_unpack(q2, qlo, qhi);
+    float sq = qlo + qhi;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+    const uint64_t inv2 = f2_splat(__fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sq, (float)C), eps))));
+    const int64_t mb = MODULATE ? (row / rows_per_batch) * mod_stride : 0;
+
+    // ---- h (rounded as the separate kernel rounds it), then the rotation per 64-block
+    float y[NCH][8];
+    float amax = 0.f;
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      const int base = c * 256 + lane * 8;
+      const bool active = base < C;
+      float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      if (active) {
+        uint4 sc = make_uint4(0, 0, 0, 0), sh = make_uint4(0, 0, 0, 0);
+        if (MODULATE) {
+          sc = *reinterpret_cast<const uint4*>(scale + mb + base);
+          sh = *reinterpret_cast<const uint4*>(shift + mb + base);
+        }
+        const uint32_t* scw = reinterpret_cast<const uint32_t*>(&sc);
+        const uint32_t* shw = reinterpret_cast<const uint32_t*>(&sh);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          uint64_t yy = f2_mul(d[c][i], inv2);
+          if (AFFINE) {
+            const uint64_t w2 = f2_pack(weight[base + 2 * i], weight[base + 2 * i + 1]);
+            const uint64_t b2 = f2_pack(bias[base + 2 * i], bias[base + 2 * i + 1]);
+            yy = f2_add(f2_mul(yy, w2), b2);
+          }
+          uint32_t h = Cvt<T>::from_f2(yy);
+          if (MODULATE) h = Cvt<T>::add2(Cvt<T>::mul2(h, scw[i]), shw[i]);
+          const T* hp = reinterpret_cast<const T*>(&h);
+          v[2 * i] = Cvt<T>::to_f(hp[0]);
+          v[2 * i + 1] = Cvt<T>::to_f(hp[1]);
+        }
+        const float4 s0 = *reinterpret_cast<const float4*>(sign + base);
+        const float4 s1 = *reinterpret_cast<const float4*>(sign + base + 4);
+        v[0] = __fmul_rn(v[0], s0.x); v[1] = __fmul_rn(v[1], s0.y);
+        v[2] = __fmul_rn(v[2], s0.z); v[3] = __fmul_rn(v[3], s0.w);
+        v[4] = __fmul_rn(v[4], s1.x); v[5] = __fmul_rn(v[5], s1.y);
+        v[6] = __fmul_rn(v[6], s1.z); v[7] = __fmul_rn(v[7], s1.w);
+      }
+#pragma unroll
+      for (int dd = 1; dd < 8; dd <<= 1) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          if (i & dd) continue;
+          const float u = v[i], w = v[i | dd];
+          v[i] = __fadd_rn(u, w);
+          v[i | dd] = __fsub_rn(u, w);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = butterfly_lane(v[i], 1, g & 1);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = butterfly_lane(v[i], 2, g & 2);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(butterfly_lane(v[i], 4, g & 4), 0.125f);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        y[c][i] = v[i];
+        if (active) amax = fmaxf(amax, fabsf(v[i]));
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float sc = __fdiv_rn(fmaxf(amax, 1e-8f), 127.0f);
+    const float inv = __frcp_rn(sc);
+    if (lane == 0) qscale[row] = sc;
+    int8_t* qr = q + row * C;
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      const int base = c * 256 + lane * 8;
+      if (base >= C) continue;
+      uint32_t w[2] = {0u, 0u};
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        w[i >> 2] |= ((uint32_t)(uint8_t)(int8_t)quant_code(y[c][i], sc, inv)) << (8 * (i & 3));
+      *reinterpret_cast<uint2*>(qr + base) = make_uint2(w[0], w[1]);
+    }
+  }
+}
+
+template <typename T, int NCH>
+static void launch_lnq(const void* x, int64_t rows, int C, float eps, const float* w, const float* b, const void* sc,
+                       const void* sh, int64_t rpb, int64_t ms, const float* sign, int8_t* q, float* qs,
+                       cudaStream_t st) {
+  const int64_t blocks = (rows + kLnqRowsPerBlock - 1) / kLnqRowsPerBlock,
+                cap = (int64_t)sm_count() * (2048 / (kLnqRowsPerBlock * 32));
+  const unsigned grid = (unsigned)(blocks < cap ? blocks : cap);
+  const T* xt = (const T*)x;
+  const T* s = (const T*)sc;
+  const T* t = (const T*)sh;
+  if (w && sc)
+    ln_quant_kernel<T, NCH, true, true><<<grid, kLnqRowsPerBlock * 32, 0, st>>>(xt, rows, C, eps, w, b, s, t, rpb, ms,
+                                                                               sign, q, qs);
+  else if (w)
+    ln_quant_kernel<T, NCH, true, false><<<grid, kLnqRowsPerBlock * 32, 0, st>>>(xt, rows, C, eps, w, b, s, t, rpb,
+                                                                                ms, sign, q, qs);
+  else if (sc)
+    ln_quant_kernel<T, NCH, false, true><<<grid, kLnqRowsPerBlock * 32, 0, st>>>(xt, rows, C, eps, w, b, s, t, rpb,
+                                                                                ms, sign, q, qs);
+  else
+    ln_quant_kernel<T, NCH, false, false><<<grid, kLnqRowsPerBlock * 32, 0, st>>>(xt, rows, C, eps, w, b, s, t, rpb,
+                                                                                 ms, sign, q, qs);
+}
+
+template <typename T>
+static int dispatch_lnq(const void* x, int64_t rows, int C, float eps, const float* w, const float* b, const void* sc,
+                        const void* sh, int64_t rpb, int64_t ms, const float* sign, int8_t* q, float* qs,
+                        cudaStream_t st) {
+  switch ((C + 255) / 256) {
+#define HI3D_LNQ_CASE(n) \
+  case n:                \
+    launch_lnq<T, n>(x, rows, C, eps, w, b, sc, sh, rpb, ms, sign, q, qs, st); break;
+    HI3D_LNQ_CASE(1)
+    HI3D_LNQ_CASE(2)
+    HI3D_LNQ_CASE(3)
+    HI3D_LNQ_CASE(4)
+    HI3D_LNQ_CASE(5)
+    HI3D_LNQ_CASE(6)
+    HI3D_LNQ_CASE(7)
+    HI3D_LNQ_CASE(8)
+    HI3D_LNQ_CASE(9)
+    HI3D_LNQ_CASE(10)
+    HI3D_LNQ_CASE(11)
+    HI3D_LNQ_CASE(12)
+    HI3D_LNQ_CASE(13)
+    HI3D_LNQ_CASE(14)
+    HI3D_LNQ_CASE(15)
+    HI3D_LNQ_CASE(16)
+#undef HI3D_LNQ_CASE
+    default:
+      return set_error(HI3D_ERR_UNSUPPORTED, "layer_norm_quantize: channels %d not supported (<= 4096)", C);
+  }
+  return check_launch("layer_norm_quantize");
+}
+
 template <typename T, int IPW, int WPR, bool ROTATE>
 static void launch_q(const void* x, const float* sign, int8_t* q, float* scale, int64_t rows, int K, cudaStream_t st) {
   constexpr int RPB = 8 / WPR;
@@ -198,4 +397,33 @@ extern "C" int hi3d_quantize_act_i8(const void* x, const float* multiplier, int8
     return rotate ? launch_quant<__nv_bfloat16, true>(x, multiplier, q, scale, rows, K, st)
                   : launch_quant<__nv_bfloat16, false>(x, multiplier, q, scale, rows, K, st);
   return set_error(HI3D_ERR_INVALID_ARGUMENT, "quantize_act_i8: dtype must be f16 or bf16");
+}
+
+extern "C" int hi3d_layer_norm_quantize(const void* x, int8_t* q, float* qscale, int64_t rows, int64_t channels,
+                                        float eps, const float* weight, const float* bias, const void* scale,
+                                        const void* shift, int64_t rows_per_batch, int64_t mod_stride,
+                                        const float* sign, int dtype, void* stream) {
+  if (!x || !q || !qscale || !sign || rows < 0 || channels <= 0)
+    return set_error(HI3D_ERR_INVALID_ARGUMENT, "layer_norm_quantize: bad pointers or sizes");
+  if (channels % 64) return set_error(HI3D_ERR_INVALID_ARGUMENT, "signed H64 requires width divisible by 64");
+  if (channels > 4096)
+    return set_error(HI3D_ERR_UNSUPPORTED, "layer_norm_quantize: channels above 4096 not supported");
+  if ((weight == nullptr) != (bias == nullptr) || (scale == nullptr) != (shift == nullptr))
+    return set_error(HI3D_ERR_INVALID_ARGUMENT, "layer_norm_quantize: weight/bias and scale/shift come in pairs");
+  if (!aligned16(x) || !aligned16(sign) || (reinterpret_cast<uintptr_t>(q) & 7) ||
+      (scale && (!aligned16(scale) || !aligned16(shift))))
+    return set_error(HI3D_ERR_INVALID_ARGUMENT, "layer_norm_quantize: misaligned pointers");
+  if (scale && (rows_per_batch <= 0 || mod_stride % 8))
+    return set_error(HI3D_ERR_INVALID_ARGUMENT, "layer_norm_quantize: bad rows_per_batch / mod_stride");
+  if (rows == 0) return HI3D_OK;
+  if (rows_per_batch <= 0) rows_per_batch = rows;
+  cudaStream_t st = as_stream(stream);
+  const int C = (int)channels;
+  if (dtype == HI3D_F16)
+    return dispatch_lnq<__half>(x, rows, C, eps, weight, bias, scale, shift, rows_per_batch, mod_stride, sign, q,
+                                qscale, st);
+  if (dtype == HI3D_BF16)
+    return dispatch_lnq<__nv_bfloat16>(x, rows, C, eps, weight, bias, scale, shift, rows_per_batch, mod_stride, sign,
+                                       q, qscale, st);
+  return set_error(HI3D_ERR_INVALID_ARGUMENT, "layer_norm_quantize: dtype must be f16 or bf16");
 }

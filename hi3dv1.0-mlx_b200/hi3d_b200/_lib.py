@@ -99,6 +99,9 @@ SIGNATURES: dict[str, tuple] = {
     "hi3d_child_table_workspace_size": (_i32, [_i64, ctypes.POINTER(_i64)]),
     "hi3d_child_structure": (_i32, [_c_void_p, _i64, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _c_void_p]),
     "hi3d_child_table": (_i32, [_c_void_p, _i64, _c_void_p, _c_void_p, _i64, _c_void_p, _c_void_p, _c_void_p]),
+    "hi3d_layer_norm_quantize": (_i32, [_c_void_p] * 3 + [_i64, _i64, _f32] + [_c_void_p] * 4 + [_i64, _i64,
+                                                                                          _c_void_p, _i32,
+                                                                                          _c_void_p]),
     "hi3d_serialize_workspace_size": (_i32, [_i64, ctypes.POINTER(_i64)]),
     "hi3d_serialize": (_i32, [_c_void_p, _i64, _i32, _i32, _c_void_p, _c_void_p, _c_void_p, _i64, _c_void_p]),
     "hi3d_window_attention": (_i32, [_c_void_p, _c_void_p, _i64, _i64, _i32, _i32, _i32, _f32, _c_void_p, _i32,

@@ -139,6 +139,15 @@ def negative_cross(w: dict) -> torch.Tensor:
     return linear(v_bias, w, "cross_attn.to_out")
 
 
+def _norm_for(w: dict, name: str):
+    """The norm feeding projection ``name``: LayerNorm-modulate into 16-bit rows, or, when the
+    projection is W8A8, fused with the activation quantiser (the int8 rows and scales the
+    projection would compute itself; the 16-bit rows are never written)."""
+    if f"{name}.w8_scale" in w:
+        return _w8a8.layer_norm_quantize
+    return kernels.layer_norm_modulate
+
+
 def _modulation(w: dict, mod: torch.Tensor, c: int, dt: torch.dtype):
     """shift/gate in the torso dtype and ``(1 + scale)`` rounded to it (transformer.py:545-548)."""
     parts = (w["modulation"] + mod.float()).view(6, c)
@@ -182,7 +191,7 @@ def block_forward(w: dict, x: torch.Tensor, mod: torch.Tensor, cos: torch.Tensor
 
     # self-attention
     xs = x[:1] if shared_self and batch > 1 else x
-    h = kernels.layer_norm_modulate(xs, 1e-6, scale=scale_msa, shift=shift_msa)
+    h = _norm_for(w, "self_attn.to_qkv")(xs, 1e-6, scale=scale_msa, shift=shift_msa)
     q, k, v = qkv_rope(h.view(-1, c), w, cos, sin, xs.shape[0], heads, d)
     a = attention.flash_attention(q, k, v, scale)
     linear(a, w, "self_attn.to_out", epilogue="residual", residual=xs, gate=gate_msa)
@@ -190,7 +199,7 @@ def block_forward(w: dict, x: torch.Tensor, mod: torch.Tensor, cos: torch.Tensor
         x[1:].copy_(xs.expand(batch - 1, n, c))
 
     # cross-attention (positive branches), constant for the zero-condition branch
-    h = kernels.layer_norm_modulate(x, 1e-6, weight=w["norm2.weight"], bias=w["norm2.bias"])
+    h = _norm_for(w, "cross_attn.to_q")(x, 1e-6, weight=w["norm2.weight"], bias=w["norm2.bias"])
     for b in range(n_pos):
         qc = linear(h[b], w, "cross_attn.to_q").view(1, n, heads, d)
         o = attention.flash_attention(qc, ck, cv, scale, q_layout="bnhd")[0]
@@ -200,7 +209,7 @@ def block_forward(w: dict, x: torch.Tensor, mod: torch.Tensor, cos: torch.Tensor
             kernels.gate_residual(x[b], negative.to(dt).expand(n, c).contiguous(), None)
 
     # MLP
-    h = kernels.layer_norm_modulate(x, 1e-6, scale=scale_mlp, shift=shift_mlp)
+    h = _norm_for(w, "mlp.mlp.0")(x, 1e-6, scale=scale_mlp, shift=shift_mlp)
     h = linear(h, w, "mlp.mlp.0", epilogue="gelu")
     linear(h, w, "mlp.mlp.2", epilogue="residual", residual=x, gate=gate_mlp)
     return x
@@ -221,19 +230,19 @@ def block_forward_packed(w: dict, x: torch.Tensor, mod: torch.Tensor, cos: torch
         x = x.clone()
     shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp = _modulation(w, mod, c, dt)
 
-    h = kernels.layer_norm_modulate(x, 1e-6, scale=scale_msa, shift=shift_msa)
+    h = _norm_for(w, "self_attn.to_qkv")(x, 1e-6, scale=scale_msa, shift=shift_msa)
     q, k, v = qkv_rope(h, w, cos, sin, 1, heads, d)
     tr = lambda z: z[0].permute(1, 0, 2)  # [1, H, T, D] -> [T, H, D] view
     a = attention.flash_attn_varlen(tr(q), tr(k), tr(v), cu_seqlens, cu_seqlens, max_seqlen, scale)
     linear(a.view(t, c), w, "self_attn.to_out", epilogue="residual", residual=x, gate=gate_msa)
 
-    h = kernels.layer_norm_modulate(x, 1e-6, weight=w["norm2.weight"], bias=w["norm2.bias"])
+    h = _norm_for(w, "cross_attn.to_q")(x, 1e-6, weight=w["norm2.weight"], bias=w["norm2.bias"])
     qc = linear(h, w, "cross_attn.to_q").view(t, heads, d)
     o = attention.flash_attn_varlen(qc, ck[0].permute(1, 0, 2), cv[0].permute(1, 0, 2), cu_seqlens, None,
                                     max_seqlen, scale)
     linear(o.view(t, c), w, "cross_attn.to_out", epilogue="residual", residual=x)
 
-    h = kernels.layer_norm_modulate(x, 1e-6, scale=scale_mlp, shift=shift_mlp)
+    h = _norm_for(w, "mlp.mlp.0")(x, 1e-6, scale=scale_mlp, shift=shift_mlp)
     h = linear(h, w, "mlp.mlp.0", epilogue="gelu")
     linear(h, w, "mlp.mlp.2", epilogue="residual", residual=x, gate=gate_mlp)
     return x

@@ -83,6 +83,70 @@ def gemm_accumulators(a: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
     return out[:, :n]
 
 
+class Quantized:
+    """Activations already quantised per row (``q [R, K]`` int8, ``scale [R]`` fp32) standing in
+    for the 16-bit ``x [..., K]`` they came from (``shape``, ``dtype``): :func:`linear` and
+    :func:`linear_qkv_rope` take them in place of ``x`` and skip their own quantisation.
+    ``[b]`` selects batch element ``b`` of a ``[B, N, K]`` input."""
+
+    def __init__(self, q: torch.Tensor, scale: torch.Tensor, shape: tuple, dtype: torch.dtype):
+        self.q, self.scale, self.shape, self.dtype = q, scale, tuple(shape), dtype
+        self.device = q.device
+
+    def view(self, *shape) -> "Quantized":
+        return Quantized(self.q, self.scale, (self.q.shape[0], self.shape[-1]), self.dtype)
+
+    def __getitem__(self, b: int) -> "Quantized":
+        if len(self.shape) != 3:
+            raise ValueError("batch indexing needs a [B, N, K] input")
+        n = self.shape[1]
+        return Quantized(self.q[b * n:(b + 1) * n], self.scale[b * n:(b + 1) * n], self.shape[1:], self.dtype)
+
+
+def layer_norm_quantize(x: torch.Tensor, eps: float, weight: torch.Tensor | None = None,
+                        bias: torch.Tensor | None = None, scale: torch.Tensor | None = None,
+                        shift: torch.Tensor | None = None) -> Quantized:
+    """``quantize_activation(layer_norm_modulate(x, ...))`` in one pass (the 16-bit normalised
+    rows are never written); arguments as :func:`hi3d_b200.kernels.layer_norm_modulate`."""
+    _lib.require_cuda(x, weight, bias, scale, shift)
+    c = x.shape[-1]
+    if x.dtype not in (torch.float16, torch.bfloat16):
+        raise ValueError("layer_norm_quantize takes float16/bfloat16 rows")
+    if (weight is None) != (bias is None) or (scale is None) != (shift is None):
+        raise ValueError("weight/bias and scale/shift come in pairs")
+    xc = x.contiguous()
+    rows = xc.numel() // c
+    rows_per_batch, mod_stride = rows, 0
+    if scale is not None:
+        scale = scale.to(x.dtype).reshape(-1, c).contiguous()
+        shift = shift.to(x.dtype).reshape(-1, c).contiguous()
+        nb = scale.shape[0]
+        if nb > 1:
+            if x.dim() < 3 or x.shape[0] != nb:
+                raise ValueError(f"per-batch modulation [{nb}, C] needs x [{nb}, N, C]")
+            rows_per_batch, mod_stride = rows // nb, c
+    if weight is not None:
+        weight = weight.float().contiguous()
+        bias = bias.float().contiguous()
+    q = torch.empty((rows, c), dtype=torch.int8, device=x.device)
+    s = torch.empty(rows, dtype=torch.float32, device=x.device)
+    rc = _lib.load().hi3d_layer_norm_quantize(xc.data_ptr(), q.data_ptr(), s.data_ptr(), rows, c, float(eps),
+                                              _lib.ptr(weight), _lib.ptr(bias), _lib.ptr(scale), _lib.ptr(shift),
+                                              rows_per_batch, mod_stride, _signs_on(c, x.device).data_ptr(),
+                                              _lib.dtype_code(x), _lib.stream(x))
+    _lib.check(rc, "layer_norm_quantize")
+    return Quantized(q, s, x.shape, x.dtype)
+
+
+def _quantized(x, multiplier, rotate):
+    """``(q, scale, out_dtype)`` of ``x`` (or of an already quantised :class:`Quantized`)."""
+    if isinstance(x, Quantized):
+        return x.q, x.scale, x.dtype
+    out_dtype = x.dtype if x.dtype in (torch.float16, torch.bfloat16) else torch.float16
+    q, s = quantize_activation(x.to(out_dtype), multiplier, rotate)
+    return q, s, out_dtype
+
+
 def linear(x: torch.Tensor, w: torch.Tensor, sw: torch.Tensor, bias: torch.Tensor, tile=(64, 128),
            multiplier: torch.Tensor | None = None, epilogue: str = "store", residual: torch.Tensor | None = None,
            gate: torch.Tensor | None = None, rotate: bool = True) -> torch.Tensor:
@@ -90,13 +154,12 @@ def linear(x: torch.Tensor, w: torch.Tensor, sw: torch.Tensor, bias: torch.Tenso
     accumulation, dequantise ``half(float(acc) * sa * sw + bias)`` (w8a8.py:105-119).
     ``tile`` is accepted for signature compatibility (the B200 kernel uses 128 x 256 tiles).
     ``epilogue``/``residual``/``gate`` as in :func:`hi3d_b200.linear.linear`."""
-    _lib.require_cuda(x, w, sw, bias, residual, gate)
+    _lib.require_cuda(x if isinstance(x, torch.Tensor) else x.q, w, sw, bias, residual, gate)
     if w.dtype != torch.int8 or sw.dtype != torch.float32:
         raise ValueError("W8A8 requires int8 weights and float32 scales")
     if w.dim() != 2 or x.shape[-1] != w.shape[1] or sw.shape != (w.shape[0],) or bias.shape != (w.shape[0],):
         raise ValueError("incompatible W8A8 projection shapes")
-    out_dtype = x.dtype if x.dtype in (torch.float16, torch.bfloat16) else torch.float16
-    a, sa = quantize_activation(x.to(out_dtype), multiplier, rotate)
+    a, sa, out_dtype = _quantized(x, multiplier, rotate)
     m, k = a.shape
     n = w.shape[0]
     epi = _EPI[epilogue]
@@ -123,14 +186,13 @@ def linear_qkv_rope(x: torch.Tensor, w: torch.Tensor, sw: torch.Tensor, bias: to
     RoPE + QK RMS norm + head split in the GEMM epilogue (as ``hi3d_b200.linear.linear_qkv_rope``)."""
     from .linear import _qkv_rope_args
 
-    _lib.require_cuda(x, w, sw, bias, cos, sin, gamma_q, gamma_k)
+    _lib.require_cuda(x if isinstance(x, torch.Tensor) else x.q, w, sw, bias, cos, sin, gamma_q, gamma_k)
     if w.dtype != torch.int8 or sw.dtype != torch.float32:
         raise ValueError("W8A8 requires int8 weights and float32 scales")
     if w.shape != (3 * heads * head_dim, x.shape[-1]) or sw.shape != (w.shape[0],) or bias.shape != (w.shape[0],):
         raise ValueError("incompatible W8A8 projection shapes")
-    out_dtype = x.dtype if x.dtype in (torch.float16, torch.bfloat16) else torch.float16
-    aq, sa = quantize_activation(x.to(out_dtype), multiplier, rotate)
-    _, m, n, cos, sin, gq, gk, q, k, v = _qkv_rope_args(x, cos, sin, gamma_q, gamma_k, batch, heads, head_dim,
+    aq, sa, out_dtype = _quantized(x, multiplier, rotate)
+    _, m, n, cos, sin, gq, gk, q, k, v = _qkv_rope_args(aq, cos, sin, gamma_q, gamma_k, batch, heads, head_dim,
                                                         token_major, out_dtype)
     b = bias.to(out_dtype).contiguous()
     rc = _lib.load().hi3d_gemm_w8a8_qkv_rope(aq.data_ptr(), w.contiguous().data_ptr(), sa.data_ptr(),

@@ -337,6 +337,16 @@ HI3D_API int hi3d_sparse_conv_act(const void* x, const int32_t* table, const uin
                                   const void* bias, void* out, int64_t n_in, int64_t n_out, int cin, int cout, int act,
                                   int dtype, void* stream);
 
+/* hi3d_layer_norm_modulate followed by hi3d_quantize_act_i8 (signed H64, `sign` [channels]) in one
+ * pass: the input of a W8A8 projection that follows a norm (the block's QKV, cross-attention Q
+ * and MLP-in projections, src/hi3d_mac/mlx_backend/transformer.py:543-588 with the w8a8 hook
+ * :504-507).  q [rows, channels] int8 and qscale [rows] fp32 equal those of quantising the
+ * rounded layer_norm_modulate output, which is never written.  channels % 64 == 0, <= 4096. */
+HI3D_API int hi3d_layer_norm_quantize(const void* x, int8_t* q, float* qscale, int64_t rows, int64_t channels,
+                                      float eps, const float* weight, const float* bias, const void* scale,
+                                      const void* shift, int64_t rows_per_batch, int64_t mod_stride,
+                                      const float* sign, int dtype, void* stream);
+
 /* ---- sparse VAE decoder ---------------------------------------------------- */
 /* Bytes of workspace hi3d_group_norm_stats needs. */
 HI3D_API int hi3d_group_norm_stats_workspace_size(int64_t n, int64_t channels, int64_t* bytes);

@@ -191,3 +191,29 @@ def test_linear_qkv_rope_rejects_unsupported_layouts():
     g = torch.ones(2, 64, device=DEV)
     with pytest.raises(NotImplementedError):
         lin.linear_qkv_rope(x, w, None, cos, cos, g, g, 1, 2, 64)
+
+
+@pytest.mark.parametrize("c", [64, 1024, 2112, 4096])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_layer_norm_quantize_bit_exact(c, dtype):
+    """The fused LayerNorm(-modulate) + signed-H64 quantiser equals quantising the 16-bit
+    LayerNorm output, codes and scales bit for bit (modulation per batch element, fp32 affine)."""
+    from hi3d_b200 import kernels
+
+    rng = np.random.default_rng(c)
+    x = _t((rng.standard_normal((2, 150, c)) * 3 + 0.5).astype(np.float32), dtype)
+    sc = _t((1 + 0.2 * rng.standard_normal((2, c))).astype(np.float32), dtype)
+    sh = _t((0.1 * rng.standard_normal((2, c))).astype(np.float32), dtype)
+    w = _t(rng.uniform(0.5, 1.5, c).astype(np.float32))
+    b = _t(rng.normal(0, 0.1, c).astype(np.float32))
+    for kw in (dict(scale=sc, shift=sh), dict(weight=w, bias=b), {}):
+        fused = w8a8.layer_norm_quantize(x, 1e-6, **kw)
+        q, s = w8a8.quantize_activation(kernels.layer_norm_modulate(x, 1e-6, **kw))
+        assert torch.equal(fused.q, q) and torch.equal(fused.scale, s)
+    # the projections accept the quantised rows in place of x
+    wq, sw = w8a8.quantize_weight((torch.randn(256, c, device="cuda") * 0.02).half())
+    bias = torch.zeros(256, dtype=torch.float16, device="cuda")
+    h = kernels.layer_norm_modulate(x.half(), 1e-6, scale=sc.half(), shift=sh.half())
+    fused = w8a8.layer_norm_quantize(x.half(), 1e-6, scale=sc.half(), shift=sh.half())
+    assert torch.equal(w8a8.linear(fused, wq, sw, bias), w8a8.linear(h, wq, sw, bias))
+    assert torch.equal(w8a8.linear(fused[1], wq, sw, bias), w8a8.linear(h[1], wq, sw, bias))
