@@ -29,10 +29,47 @@ __device__ __forceinline__ void load8(const T* p, float (&f)[8]) {
   for (int i = 0; i < 8; ++i) f[i] = Cvt<T>::to_f(h[i]);
 }
 
-// (clear, set) -> (clear + set, clear - set) across lanes `dist` apart
-__device__ __forceinline__ float butterfly_lane(float v, int dist, bool set) {
-  const float other = __shfl_xor_sync(0xffffffffu, v, dist);
-  return set ? __fsub_rn(other, v) : __fadd_rn(v, other);
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// Signed H64 of one lane's 8 elements v (element index bits 0-2), the lane's partners 1, 2
+// and 4 lanes apart holding index bits 3-5 (g = lane % 8): the same operations in the same
+// order as above, with the first two in-register stages on packed pairs (v[k], v[k + 4]),
+// and each cross-lane stage as one exact fma(v, +-1, other) (x - v equals x + (-1) v).
+__device__ __forceinline__ void h64_rotate(float (&v)[8], const float* __restrict__ sign, int g) {
+  const float4 s0 = *reinterpret_cast<const float4*>(sign);
+  const float4 s1 = *reinterpret_cast<const float4*>(sign + 4);
+  uint64_t P[4];
+  P[0] = f2_mul(f2_pack(v[0], v[4]), f2_pack(s0.x, s1.x));
+  P[1] = f2_mul(f2_pack(v[1], v[5]), f2_pack(s0.y, s1.y));
+  P[2] = f2_mul(f2_pack(v[2], v[6]), f2_pack(s0.z, s1.z));
+  P[3] = f2_mul(f2_pack(v[3], v[7]), f2_pack(s0.w, s1.w));
+  // element bit 0: (0,1), (2,3), (4,5), (6,7)
+  uint64_t a = f2_add(P[0], P[1]), b = f2_sub(P[0], P[1]), c = f2_add(P[2], P[3]), d = f2_sub(P[2], P[3]);
+  // element bit 1: (0,2), (1,3), (4,6), (5,7)
+  P[0] = f2_add(a, c);
+  P[2] = f2_sub(a, c);
+  P[1] = f2_add(b, d);
+  P[3] = f2_sub(b, d);
+  // element bit 2: (k, k + 4) inside each pair
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    float lo, hi;
+    f2_unpack(P[k], lo, hi);
+    v[k] = __fadd_rn(lo, hi);
+    v[k + 4] = __fsub_rn(lo, hi);
+  }
+  // element bits 3, 4, 5 across lanes; the last stage scales by 1/8 (exact)
+  const float m1 = (g & 1) ? -1.0f : 1.0f, m2 = (g & 2) ? -1.0f : 1.0f, m4 = (g & 4) ? -1.0f : 1.0f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __fmaf_rn(v[i], m1, __shfl_xor_sync(0xffffffffu, v[i], 1));
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __fmaf_rn(v[i], m2, __shfl_xor_sync(0xffffffffu, v[i], 2));
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(__fmaf_rn(v[i], m4, __shfl_xor_sync(0xffffffffu, v[i], 4)), 0.125f);
 }
 
 // rint(y / s) with y / s the correctly rounded IEEE quotient, clamped to
@@ -41,11 +78,22 @@ __device__ __forceinline__ float butterfly_lane(float v, int dist, bool set) {
 // when z is farther than 3e-5 from a half-integer, the true quotient and its
 // rounded value lie on the same side of it and rint(z) is the answer.  The few
 // quotients closer to a rounding tie take the exact division.
-__device__ __forceinline__ int quant_code(float y, float s, float inv) {
-  const float z = __fmul_rn(y, inv);
-  float r = rintf(z);
-  if (fabsf(z - r) >= 0.5f - 3e-5f) r = rintf(__fdiv_rn(y, s));
-  return (int)fminf(fmaxf(r, -127.0f), 127.0f);
+// Codes of 8 values, packed little-endian into two words (a saturating conversion
+// after the clamp at -127).
+__device__ __forceinline__ uint2 quant_pack8(const float (&y)[8], float s, float inv) {
+  int c[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float z = __fmul_rn(y[i], inv);
+    float r = rintf(z);
+    if (fabsf(z - r) >= 0.5f - 3e-5f) r = rintf(__fdiv_rn(y[i], s));
+    int q;
+    asm("cvt.rni.sat.s8.f32 %0, %1;" : "=r"(q) : "f"(fmaxf(r, -127.0f)));
+    c[i] = q;
+  }
+  const uint32_t w0 = __byte_perm(__byte_perm(c[0], c[1], 0x0040), __byte_perm(c[2], c[3], 0x0040), 0x5410);
+  const uint32_t w1 = __byte_perm(__byte_perm(c[4], c[5], 0x0040), __byte_perm(c[6], c[7], 0x0040), 0x5410);
+  return make_uint2(w0, w1);
 }
 
 // One row per WPR warps of a 256-thread block; warp `part` of a row handles the
@@ -71,37 +119,9 @@ __global__ void __launch_bounds__(256) quant_h64_kernel(const T* __restrict__ x,
       const int base = (part + j * WPR) * 256 + lane * 8;
       const bool active = row_ok && base < K;
       float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      if (active) {
-        load8<T>(xr + base, v);
-        if (ROTATE) {
-          const float4 s0 = *reinterpret_cast<const float4*>(sign + base);
-          const float4 s1 = *reinterpret_cast<const float4*>(sign + base + 4);
-          v[0] = __fmul_rn(v[0], s0.x); v[1] = __fmul_rn(v[1], s0.y);
-          v[2] = __fmul_rn(v[2], s0.z); v[3] = __fmul_rn(v[3], s0.w);
-          v[4] = __fmul_rn(v[4], s1.x); v[5] = __fmul_rn(v[5], s1.y);
-          v[6] = __fmul_rn(v[6], s1.z); v[7] = __fmul_rn(v[7], s1.w);
-        }
-      }
+      if (active) load8<T>(xr + base, v);
       if (ROTATE) {
-        // element bits 0, 1, 2: in registers
-#pragma unroll
-        for (int d = 1; d < 8; d <<= 1) {
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            if (i & d) continue;
-            const float u = v[i], w = v[i | d];
-            v[i] = __fadd_rn(u, w);
-            v[i | d] = __fsub_rn(u, w);
-          }
-        }
-        // element bits 3, 4: lanes 1 and 2 apart; bit 5: lanes 4 apart, with the 1/8 scale
-        const int g = lane & 7;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) v[i] = butterfly_lane(v[i], 1, g & 1);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) v[i] = butterfly_lane(v[i], 2, g & 2);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(butterfly_lane(v[i], 4, g & 4), 0.125f);
+        h64_rotate(v, sign + (active ? base : 0), lane & 7);
       }
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
@@ -127,11 +147,7 @@ __global__ void __launch_bounds__(256) quant_h64_kernel(const T* __restrict__ x,
       for (int j = 0; j < IPW; ++j) {
         const int base = (part + j * WPR) * 256 + lane * 8;
         if (base >= K) continue;
-        uint32_t w[2] = {0u, 0u};
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-          w[i >> 2] |= ((uint32_t)(uint8_t)(int8_t)quant_code(y[j][i], s, inv)) << (8 * (i & 3));
-        *reinterpret_cast<uint2*>(qr + base) = make_uint2(w[0], w[1]);
+        *reinterpret_cast<uint2*>(qr + base) = quant_pack8(y[j], s, inv);
       }
     }
     if (WPR > 1) __syncthreads();  // red[] is rewritten by the next group
@@ -234,29 +250,8 @@ __global__ void __launch_bounds__(kLnqRowsPerBlock * 32)
           v[2 * i] = Cvt<T>::to_f(hp[0]);
           v[2 * i + 1] = Cvt<T>::to_f(hp[1]);
         }
-        const float4 s0 = *reinterpret_cast<const float4*>(sign + base);
-        const float4 s1 = *reinterpret_cast<const float4*>(sign + base + 4);
-        v[0] = __fmul_rn(v[0], s0.x); v[1] = __fmul_rn(v[1], s0.y);
-        v[2] = __fmul_rn(v[2], s0.z); v[3] = __fmul_rn(v[3], s0.w);
-        v[4] = __fmul_rn(v[4], s1.x); v[5] = __fmul_rn(v[5], s1.y);
-        v[6] = __fmul_rn(v[6], s1.z); v[7] = __fmul_rn(v[7], s1.w);
       }
-#pragma unroll
-      for (int dd = 1; dd < 8; dd <<= 1) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          if (i & dd) continue;
-          const float u = v[i], w = v[i | dd];
-          v[i] = __fadd_rn(u, w);
-          v[i | dd] = __fsub_rn(u, w);
-        }
-      }
-#pragma unroll
-      for (int i = 0; i < 8; ++i) v[i] = butterfly_lane(v[i], 1, g & 1);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) v[i] = butterfly_lane(v[i], 2, g & 2);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(butterfly_lane(v[i], 4, g & 4), 0.125f);
+      h64_rotate(v, sign + (active ? base : 0), g);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         y[c][i] = v[i];
@@ -273,11 +268,7 @@ __global__ void __launch_bounds__(kLnqRowsPerBlock * 32)
     for (int c = 0; c < NCH; ++c) {
       const int base = c * 256 + lane * 8;
       if (base >= C) continue;
-      uint32_t w[2] = {0u, 0u};
-#pragma unroll
-      for (int i = 0; i < 8; ++i)
-        w[i >> 2] |= ((uint32_t)(uint8_t)(int8_t)quant_code(y[c][i], sc, inv)) << (8 * (i & 3));
-      *reinterpret_cast<uint2*>(qr + base) = make_uint2(w[0], w[1]);
+      *reinterpret_cast<uint2*>(qr + base) = quant_pack8(y[c], sc, inv);
     }
   }
 }
