@@ -41,8 +41,8 @@ __device__ __forceinline__ __half store_t<__half>(float v) {
 
 // ---------------------------------------------------------------------------
 // GroupNorm statistics.  Stage 1: block b sums rows [b * chunk, (b + 1) * chunk) per
-// channel (fp32, rows in order) into partial[b][c] and partial_sq[b][c].  Stage 2: one
-// block sums the partials of each channel in block order, then per group
+// channel (fp32, rows in order) into partial[b][c] and partial_sq[b][c].  Stage 2 sums
+// the partials of each column in a fixed order (deterministic), then per group
 // mean = S1 / (count + eps), var = S2 / (count + eps) - mean^2, inv = 1 / sqrt(var + eps)
 // with count = n * width (vae.py:142-164), written back per channel.
 // ---------------------------------------------------------------------------
@@ -65,19 +65,33 @@ __global__ void __launch_bounds__(256) gn_partial_kernel(const X* __restrict__ x
   }
 }
 
-__global__ void __launch_bounds__(256) gn_finish_kernel(const float* __restrict__ partial, int blocks, int c,
-                                                        int groups, int64_t n, float eps, float* __restrict__ mean,
+// Stage 2a: column e of the [blocks][2 c] partials summed by a 32 x 32 thread block: segment y
+// sums partials y, y + 32, ... in order (a warp reads 32 consecutive columns of one partial),
+// then the 32 segment sums are added in segment order.
+__global__ void __launch_bounds__(1024) gn_columns_kernel(const float* __restrict__ partial, int blocks, int cols,
+                                                          float* __restrict__ colsum) {
+  __shared__ float seg[32][33];
+  const int e = blockIdx.x * 32 + threadIdx.x;
+  float a = 0.f;
+  if (e < cols) {
+#pragma unroll 4
+    for (int k = threadIdx.y; k < blocks; k += 32) a = __fadd_rn(a, partial[(int64_t)k * cols + e]);
+  }
+  seg[threadIdx.y][threadIdx.x] = a;
+  __syncthreads();
+  if (threadIdx.y == 0 && e < cols) {
+    float t = 0.f;
+    for (int y = 0; y < 32; ++y) t = __fadd_rn(t, seg[y][threadIdx.x]);
+    colsum[e] = t;
+  }
+}
+
+// Stage 2b: per group from the channel sums colsum[0, c) and sums of squares colsum[c, 2 c).
+__global__ void __launch_bounds__(256) gn_finish_kernel(const float* __restrict__ colsum, int c, int groups,
+                                                        int64_t n, float eps, float* __restrict__ mean,
                                                         float* __restrict__ inv) {
   extern __shared__ float sh[];  // [2 c]
-  for (int ch = threadIdx.x; ch < c; ch += blockDim.x) {
-    float a = 0.f, b = 0.f;
-    for (int k = 0; k < blocks; ++k) {
-      a = __fadd_rn(a, partial[(int64_t)k * 2 * c + ch]);
-      b = __fadd_rn(b, partial[(int64_t)k * 2 * c + c + ch]);
-    }
-    sh[ch] = a;
-    sh[c + ch] = b;
-  }
+  for (int e = threadIdx.x; e < 2 * c; e += blockDim.x) sh[e] = colsum[e];
   __syncthreads();
   const int width = c / groups;
   const float count = __fadd_rn((float)((double)n * width), eps);
@@ -97,6 +111,14 @@ __global__ void __launch_bounds__(256) gn_finish_kernel(const float* __restrict_
   }
 }
 
+// swish(u) = u * sigmoid(u) with the stable sigmoid e = 1 / (1 + exp(|u|))
+// (kernels.py:242-260): exp and the reciprocal on the MUFU unit (relative error ~1e-6 for
+// |u| <= 20); an overflowed exp gives e = 0.
+__device__ __forceinline__ float swish_stable(float u) {
+  const float e = __fdividef(1.0f, 1.0f + __expf(fabsf(u)));
+  return u < 0.0f ? u * e : u * (1.0f - e);
+}
+
 // u = (x - mean) * inv * w + b in fp32; swish(u) = u * sigmoid(u) with the stable
 // sigmoid e = 1 / (1 + exp(|u|)) (kernels.py:242-260); rounded once to T.
 template <typename X, typename T>
@@ -109,8 +131,7 @@ __global__ void __launch_bounds__(256) gn_swish_kernel(const X* __restrict__ x, 
     const int ch = (int)(i % c);
     const float u =
         __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(load_f<X>(x + i), mean[ch]), inv[ch]), w[ch]), b[ch]);
-    const float e = 1.0f / (1.0f + expf(fabsf(u)));
-    out[i] = store_t<T>(u < 0.0f ? u * e : u * (1.0f - e));
+    out[i] = store_t<T>(swish_stable(u));
   }
 }
 
@@ -162,7 +183,21 @@ __global__ void __launch_bounds__(256) gn_partial_v8_kernel(const X* __restrict_
   const int64_t r1 = min(n, r0 + chunk);
   if (rr < lanes) {
     float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, b[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int64_t r = r0 + rr; r < r1; r += lanes) {
+    int64_t r = r0 + rr;
+    // four rows' loads in flight, summed in the same row order as one row at a time
+    for (; r + 3 * lanes < r1; r += 4 * lanes) {
+      float xv[4][8];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) load8f<X>(x + (r + u * lanes) * c + v * 8, xv[u]);
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          a[i] = __fadd_rn(a[i], xv[u][i]);
+          b[i] = __fmaf_rn(xv[u][i], xv[u][i], b[i]);
+        }
+    }
+    for (; r < r1; r += lanes) {
       float xv[8];
       load8f<X>(x + r * c + v * 8, xv);
 #pragma unroll
@@ -201,10 +236,57 @@ __global__ void __launch_bounds__(256) gn_swish_v8_kernel(const X* __restrict__ 
     for (int i = 0; i < 8; ++i) {
       const float u = __fadd_rn(
           __fmul_rn(__fmul_rn(__fsub_rn(xv[i], mean[ch + i]), inv[ch + i]), w[ch + i]), b[ch + i]);
-      const float e = 1.0f / (1.0f + expf(fabsf(u)));
-      o[i] = u < 0.0f ? u * e : u * (1.0f - e);
+      o[i] = swish_stable(u);
     }
     store8<T>(out + t * 8, o);
+  }
+}
+
+// Row-blocked form (256 % (channels / 8) == 0): thread (rr, v) keeps the statistics and
+// affine parameters of channels 8v .. 8v + 7 in registers and walks rows rr, rr + R, ... of
+// its block's row stride with four rows' loads in flight; same arithmetic per element as
+// gn_swish_v8_kernel.
+template <typename X, typename T>
+__global__ void __launch_bounds__(256, 2) gn_swish_rows_kernel(const X* __restrict__ x, int64_t n, int c,
+                                                            const float* __restrict__ mean,
+                                                            const float* __restrict__ inv,
+                                                            const float* __restrict__ w,
+                                                            const float* __restrict__ b, T* __restrict__ out) {
+  const int vecs = c / 8, lanes = blockDim.x / vecs;
+  const int v = threadIdx.x % vecs, rr = threadIdx.x / vecs;
+  float mu[8], iv[8], ww[8], bb[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    mu[i] = mean[v * 8 + i];
+    iv[i] = inv[v * 8 + i];
+    ww[i] = w[v * 8 + i];
+    bb[i] = b[v * 8 + i];
+  }
+  auto act8 = [&](const float (&xv)[8], float (&o)[8]) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float u = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(xv[i], mu[i]), iv[i]), ww[i]), bb[i]);
+      o[i] = swish_stable(u);
+    }
+  };
+  const int64_t step = (int64_t)gridDim.x * lanes;
+  int64_t r = (int64_t)blockIdx.x * lanes + rr;
+  for (; r + 3 * step < n; r += 4 * step) {
+    float xv[4][8];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) load8f<X>(x + (r + u * step) * c + v * 8, xv[u]);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      float o[8];
+      act8(xv[u], o);
+      store8<T>(out + (r + u * step) * c + v * 8, o);
+    }
+  }
+  for (; r < n; r += step) {
+    float xv[8], o[8];
+    load8f<X>(x + r * c + v * 8, xv);
+    act8(xv, o);
+    store8<T>(out + r * c + v * 8, o);
   }
 }
 
@@ -320,6 +402,101 @@ __global__ void __launch_bounds__(256) window_attn_kernel(const T* __restrict__ 
   for (int d = 0; d < D; ++d) orow[d] = store_t<T>(o[d] * il);
 }
 
+// Vectorised form (qkv and out 16-byte aligned): K/V of the block's heads staged with
+// 16-byte loads, each thread's query row read the same way, keys taken eight at a time (one
+// running-maximum correction per eight keys instead of one per key), the output row written
+// as 16-byte vectors.
+template <typename T, int D>
+__global__ void __launch_bounds__(256, D <= 32 ? 2 : 1) window_attn_v8_kernel(const T* __restrict__ qkv,
+                                                             const int32_t* __restrict__ gather, int64_t n,
+                                                             int64_t n_pad, int L, int heads, int heads_per_block,
+                                                             float scale, T* __restrict__ out) {
+  extern __shared__ float kv[];  // [heads_per_block][L][2][D]
+  constexpr int V = D / 8;       // 8-element vectors per head row
+  const int64_t w = blockIdx.x;
+  const int h0 = blockIdx.y * heads_per_block;
+  const int64_t row_stride = (int64_t)3 * heads * D;
+  const int64_t base = w * L;
+  for (int e = threadIdx.x; e < heads_per_block * L * 2 * V; e += blockDim.x) {
+    const int ch = e % V;
+    int t = e / V;
+    const int kvsel = t & 1;
+    t >>= 1;
+    const int i = t % L, hh = t / L;
+    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (h0 + hh < heads && base + i < n_pad) {
+      const int64_t r = gather[base + i];
+      load8f<T>(qkv + r * row_stride + (int64_t)(1 + kvsel) * heads * D + (int64_t)(h0 + hh) * D + ch * 8, v);
+    }
+    float* dst = kv + ((int64_t)(hh * L + i) * 2 + kvsel) * D + ch * 8;
+    *reinterpret_cast<float4*>(dst) = make_float4(v[0], v[1], v[2], v[3]);
+    *reinterpret_cast<float4*>(dst + 4) = make_float4(v[4], v[5], v[6], v[7]);
+  }
+  __syncthreads();
+  const int hh = threadIdx.x / L, i = threadIdx.x % L;
+  const int h = h0 + hh;
+  if (hh >= heads_per_block || h >= heads) return;
+  const int64_t p = base + i;
+  if (p >= n) return;
+  const int64_t r = gather[p];
+  float q[D], o[D];
+#pragma unroll
+  for (int c = 0; c < V; ++c) {
+    float v[8];
+    load8f<T>(qkv + r * row_stride + (int64_t)h * D + c * 8, v);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      q[c * 8 + u] = v[u] * scale;
+      o[c * 8 + u] = 0.f;
+    }
+  }
+  const float* kh = kv + (int64_t)hh * L * 2 * D;
+  float mx = -INFINITY, l = 0.f;
+  const int64_t left = n_pad - base;
+  const int len = left < L ? (int)left : L;
+  for (int j = 0; j < len; j += 8) {
+    float s[8];
+    float cm = -INFINITY;
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      s[u] = -INFINITY;
+      if (j + u < len) {
+        const float* kj = kh + (j + u) * 2 * D;
+        float a = 0.f;
+#pragma unroll
+        for (int d = 0; d < D; ++d) a = fmaf(q[d], kj[d], a);
+        s[u] = a;
+      }
+      cm = fmaxf(cm, s[u]);
+    }
+    const float mnew = fmaxf(mx, cm);
+    const float corr = expf(mx - mnew);
+    l *= corr;
+#pragma unroll
+    for (int d = 0; d < D; ++d) o[d] *= corr;
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      if (j + u < len) {
+        const float pj = expf(s[u] - mnew);
+        const float* vj = kh + (j + u) * 2 * D + D;
+        l += pj;
+#pragma unroll
+        for (int d = 0; d < D; ++d) o[d] = fmaf(pj, vj[d], o[d]);
+      }
+    }
+    mx = mnew;
+  }
+  const float il = 1.0f / l;
+  T* orow = out + r * (int64_t)heads * D + (int64_t)h * D;
+#pragma unroll
+  for (int c = 0; c < V; ++c) {
+    float v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) v[u] = o[c * 8 + u] * il;
+    store8<T>(orow + c * 8, v);
+  }
+}
+
 // Space-filling-curve keys (vae.py:49-56): bit i of x, y, z goes to key bits 3i + 2,
 // 3i + 1, 3i; `swap_xy` serializes (y, x, z) (the "z-trans" order).
 __global__ void morton_kernel(const int32_t* __restrict__ coords, int64_t n, int depth, int swap_xy,
@@ -359,7 +536,7 @@ static int gn_blocks(int64_t n) {
 extern "C" int hi3d_group_norm_stats_workspace_size(int64_t n, int64_t channels, int64_t* bytes) {
   if (n < 0 || channels <= 0 || !bytes)
     return set_error(HI3D_ERR_INVALID_ARGUMENT, "group_norm_stats: bad sizes");
-  *bytes = (int64_t)gn_blocks(n) * 2 * channels * 4 + 256;
+  *bytes = ((int64_t)gn_blocks(n) + 1) * 2 * channels * 4 + 256;  // partials + column sums
   return HI3D_OK;
 }
 
@@ -397,7 +574,9 @@ extern "C" int hi3d_group_norm_stats(const void* x, int64_t n, int64_t channels,
     cudaError_t e = cudaFuncSetAttribute(gn_finish_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return set_error(HI3D_ERR_CUDA, "group_norm_stats: %s", cudaGetErrorString(e));
   }
-  gn_finish_kernel<<<1, 256, smem, st>>>(partial, blocks, c, groups, n, eps, mean, inv);
+  float* colsum = partial + (int64_t)blocks * 2 * c;
+  gn_columns_kernel<<<(2 * c + 31) / 32, dim3(32, 32), 0, st>>>(partial, blocks, 2 * c, colsum);
+  gn_finish_kernel<<<1, 256, smem, st>>>(colsum, c, groups, n, eps, mean, inv);
   return check_launch("group_norm_stats");
 }
 
@@ -411,6 +590,24 @@ extern "C" int hi3d_group_norm_swish(const void* x, int64_t n, int64_t channels,
   if (n == 0) return HI3D_OK;
   cudaStream_t st = as_stream(stream);
   const int c = (int)channels;
+  if (c % 8 == 0 && c <= 2048 && 256 % (c / 8) == 0 && aligned16(x) && aligned16(out)) {
+    const int lanes = 256 / (c / 8);
+    const int64_t blocks = (n + lanes - 1) / lanes, cap = (int64_t)sm_count() * 2;  // two resident per SM
+    const unsigned grid = (unsigned)(blocks < cap ? blocks : cap);
+    if (in_dtype == HI3D_F16 && out_dtype == HI3D_F16)
+      gn_swish_rows_kernel<__half, __half>
+          <<<grid, 256, 0, st>>>((const __half*)x, n, c, mean, inv, weight, bias, (__half*)out);
+    else if (in_dtype == HI3D_F16)
+      gn_swish_rows_kernel<__half, float>
+          <<<grid, 256, 0, st>>>((const __half*)x, n, c, mean, inv, weight, bias, (float*)out);
+    else if (out_dtype == HI3D_F16)
+      gn_swish_rows_kernel<float, __half>
+          <<<grid, 256, 0, st>>>((const float*)x, n, c, mean, inv, weight, bias, (__half*)out);
+    else
+      gn_swish_rows_kernel<float, float>
+          <<<grid, 256, 0, st>>>((const float*)x, n, c, mean, inv, weight, bias, (float*)out);
+    return check_launch("group_norm_swish");
+  }
   if (c % 8 == 0 && aligned16(x) && aligned16(out)) {
     const int64_t total = n * (c / 8), blocks = (total + 255) / 256, cap = (int64_t)sm_count() * 8;
     const unsigned grid = (unsigned)(blocks < cap ? blocks : cap);
@@ -497,7 +694,8 @@ static int launch_window(const void* qkv, const int32_t* gather, int64_t n, int6
                          float scale, void* out, cudaStream_t st) {
   const int hpb = max(1, min(heads, 256 / L));
   const size_t smem = (size_t)hpb * L * 2 * D * sizeof(float);
-  auto kern = window_attn_kernel<T, D>;
+  const bool vec = aligned16(qkv) && aligned16(out);
+  auto kern = vec ? window_attn_v8_kernel<T, D> : window_attn_kernel<T, D>;
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return set_error(HI3D_ERR_CUDA, "window_attention: %s", cudaGetErrorString(e));

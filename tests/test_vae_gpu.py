@@ -20,7 +20,10 @@ def _t(a):
     return torch.from_numpy(np.ascontiguousarray(a)).to(DEV)
 
 
-@pytest.mark.parametrize("c,dtype", [(512, np.float16), (128, np.float32), (64, np.float16), (256, np.float32)])
+# 512/128/64/256: row-blocked swish kernel (256 % (c / 8) == 0); 24: 8-channel vector kernel;
+# 12: scalar kernels
+@pytest.mark.parametrize("c,dtype", [(512, np.float16), (128, np.float32), (64, np.float16), (256, np.float32),
+                                     (24, np.float16), (12, np.float32)])
 def test_group_stats_and_swish(c, dtype):
     rng = np.random.default_rng(c)
     x = (rng.standard_normal((20000, c)) * rng.uniform(0.5, 3, c) + rng.normal(0, 1, c)).astype(dtype)
@@ -85,15 +88,25 @@ def test_serialization_bit_exact():
             assert np.array_equal(vae.window_index(perm).cpu().numpy(), ops.window_index(rp))
 
 
-@pytest.mark.parametrize("n,heads,d,dtype", [(1000, 32, 16, torch.float32), (1000, 32, 16, torch.float16),
-                                             (960, 8, 32, torch.float16), (30, 4, 64, torch.float32),
-                                             (5000, 32, 16, torch.float16)])
-def test_window_attention_matches_oracle(n, heads, d, dtype):
+# misaligned: qkv starts one element past a 16-byte boundary (the scalar kernel); otherwise
+# the vectorised kernel
+@pytest.mark.parametrize("n,heads,d,dtype,misaligned",
+                         [(1000, 32, 16, torch.float32, False), (1000, 32, 16, torch.float16, False),
+                          (960, 8, 32, torch.float16, False), (30, 4, 64, torch.float32, False),
+                          (5000, 32, 16, torch.float16, False), (1000, 32, 16, torch.float16, True),
+                          (700, 4, 64, torch.float32, True), (700, 4, 64, torch.float16, False)])
+def test_window_attention_matches_oracle(n, heads, d, dtype, misaligned):
     rng = np.random.default_rng(n + d)
     coords = synthetic.shell_coords(n, 48, 14, 3, seed=n)
     perm, inverse = vae.serialization(coords)[n % 2]
     gather = vae.window_index(perm)
     qkv = rng.standard_normal((n, 3 * heads * d)).astype(np.float32)
-    got = vae.window_attention(_t(qkv).to(dtype), gather, heads).float().cpu().numpy()
+    q_dev = _t(qkv).to(dtype)
+    if misaligned:
+        buf = torch.empty(q_dev.numel() + 1, dtype=dtype, device=DEV)
+        buf[1:].copy_(q_dev.reshape(-1))
+        q_dev = buf[1:].view(q_dev.shape)
+        assert q_dev.is_contiguous() and q_dev.data_ptr() % 16 != 0
+    got = vae.window_attention(q_dev, gather, heads).float().cpu().numpy()
     want = ops.window_attention_f64(qkv, gather.cpu().numpy(), inverse.cpu().numpy(), heads)
     assert rel_l2(got, want) < (2e-6 if dtype == torch.float32 else 2e-3)
