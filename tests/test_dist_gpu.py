@@ -4,8 +4,8 @@ Every row-wise kernel computes a row independently of the others; the sharded at
 combines the rank's own keys (attended while the other rank's are gathered) and the gathered
 keys by their log-sum-exp weights, which agrees with the single pass to within 16-bit output
 rounding.  So the stack output must match the unsharded one to the block tolerance (relative
-L2 1e-3 over two blocks) with most elements bit-identical.  Needs two GPUs
-(``gpurun --gpus 2``); skipped otherwise.
+L2 1e-3 over two blocks) with most elements bit-identical.  Needs two GPUs on one node;
+skipped otherwise.
 """
 
 from __future__ import annotations
