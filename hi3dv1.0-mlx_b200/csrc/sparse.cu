@@ -350,11 +350,26 @@ __global__ void __launch_bounds__(CV_THREADS, 1)
     bool ok = true;
     int pending[CV_LAG + 1];
     int npend = 0;
+    // Neighbour rows of this thread's eight tile rows for one tap, read from the table once
+    // per tap (not per channel chunk); the next present tap's rows are requested while the
+    // current tap's chunks are gathered, so the table latency is off the gather path.
+    auto tap_rows = [&](int mt, int k, int (&dst)[8]) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int o = mt * CV_BM + i * 16 + rsub;
+        dst[i] = o < p.n_out ? p.table[(int64_t)o * 27 + k] : p.n_in;
+      }
+    };
     for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
       const int mt = tile / p.tiles_n, nt = tile % p.tiles_n;
-      const uint32_t taps = p.tap_mask[mt];
-      for (int k = 0; ok && k < 27; ++k) {
-        if (!(taps >> k & 1u)) continue;
+      const uint32_t taps = p.tap_mask[mt] & ((1u << 27) - 1);
+      int cur[8], nxt[8];
+      int k = taps ? __ffs(taps) - 1 : 27;
+      if (k < 27) tap_rows(mt, k, cur);
+      while (ok && k < 27) {
+        const uint32_t later = taps & ~((2u << k) - 1);  // present taps after k
+        const int kn = later ? __ffs(later) - 1 : 27;
+        if (kn < 27) tap_rows(mt, kn, nxt);
         for (int c = 0; c < p.kchunks; ++c, ++it) {
           const int s = it % CV_NST, n = it / CV_NST;
           if (!(ok = mbar_wait(&bar->empty[s], (n & 1) ^ 1, abort, 201))) break;
@@ -367,9 +382,7 @@ __global__ void __launch_bounds__(CV_THREADS, 1)
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             const int row = i * 16 + rsub;
-            const int o = mt * CV_BM + row;
-            int src_row = p.n_in;
-            if (o < p.n_out) src_row = p.table[(int64_t)o * 27 + k];
+            const int src_row = cur[i];
             const bool present = src_row < p.n_in && ch < p.cin;
             const T* src = present ? x + (int64_t)src_row * p.cin + ch : x;
             const uint32_t dst = dst0 + row * 128 + ((chunk ^ (row & 7)) << 4);
@@ -385,6 +398,11 @@ __global__ void __launch_bounds__(CV_THREADS, 1)
             --npend;
           }
         }
+        if (kn < 27) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) cur[i] = nxt[i];
+        }
+        k = kn;
       }
     }
     cp_async_wait<0>();
