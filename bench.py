@@ -1,6 +1,6 @@
 """Benchmark of the sparse-DiT refinement torso on B200 (BASELINE configs[1] by default).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--no-extras]
                     [--workload stack|stack_w8a8|block|attention|attention262k|conv|forward|vae]
 
 One step = one forward of the 24-block stack (C=1024, 16 heads x 64, GELU MLP 4x,
@@ -9,20 +9,24 @@ resident in HBM.  ``value`` is block tokens/s = blocks * T / step time (whole jo
 max over ranks).  With N>1 GPUs (torchrun) the T tokens are split into N query
 slices and every block all-gathers K/V over NCCL (strong scaling).
 
+Beside the headline (outside its timed region) the default line carries the other BASELINE
+configurations: ``cfg4_attention`` (262,144 bf16 tokens as 4 objects of 65,536, query-sharded
+over the N GPUs), and at N=1 ``cfg2_w8a8`` (the W8A8 stack and its int8 GEMMs) and
+``cfg5_conv`` (neighbour map, submanifold and stride-2 conv), each with its roofline fraction
+and CPU baseline.  At N>1 it adds the per-phase breakdown of a step (maximum over ranks) and
+``sharded_rel_l2``, the sharded stack's first two blocks against the same blocks on one GPU.
+
 ``--workload attention`` times the self-attention kernel alone at the same size
 (T=32,768, 16x64 heads, fp16); ``--workload attention262k`` the high-resolution
-config (262,144 tokens packed as 4 objects of 65,536, bf16, varlen), query-sharded
-over the GPUs.  Both report attention TFLOP/s (4 * Nq * Nk * H * D per object).
+config (cfg4), query-sharded over the GPUs.  Both report attention TFLOP/s
+(4 * Nq * Nk * H * D per object).  ``--workload conv`` times the cfg5 submanifold
+convolution; ``--workload forward`` the whole refinement transformer around the same stack;
+``--workload vae`` the VAE decoder's kernels.
 
-``--workload conv`` times the cfg5 submanifold convolution; ``--workload forward`` the whole
-refinement transformer around the same stack (input layer, two fine/low res blocks, the
-24 blocks, the upsampling and output res blocks, LayerNorm + output layer) on a fine shell
-whose downsampled level holds ~34k tokens, reporting transformer tokens/s.
-
-Rank 0 prints one JSON line.  ``--impl reference`` times the CPU path instead: the
-oracle port of the reference block (the reference itself is Python that cannot travel
-to the GPU box), on the host's cores, on a row-sampled bounded sample of the same
-workload.
+Rank 0 prints one JSON line.  ``--impl reference`` times the reference's CPU path instead, on
+every host thread: the upstream PyTorch block with the reference's flash_attn shim, restated in
+torch (oracle/torch_block.py, pinned to the upstream module) because the reference itself cannot
+travel to the GPU box; one whole block of the stack per step.
 """
 
 from __future__ import annotations
@@ -163,42 +167,105 @@ def device_weights(device, seed: int = 100, blocks: int = BLOCKS) -> list[dict]:
     return out
 
 
-# ----------------------------------------------------------------------------- CPU baseline
+# ----------------------------------------------------------------------------- configs
+#
+# One config dict per workload, used verbatim by both arms so that their lines describe the
+# same workload.
 
+
+def stack_config(workload: str, nblocks: int, world: int) -> dict:
+    if workload == "stack_w8a8":
+        name = (f"cfg2: W8A8 {BLOCKS}-block stack fwd (int8 signed-H64 activations, int8 rotated weights, int32 "
+                f"accumulate, fp16 dequant), T={T_TOKENS}, C={CHANNELS}, {HEADS}x{CHANNELS // HEADS} heads, "
+                f"{COND} cond tokens")
+    else:
+        name = (f"cfg1: {nblocks}-block sparse-DiT stack fwd, T={T_TOKENS} shell tokens in {GRID}^3, C={CHANNELS}, "
+                f"{HEADS}x{CHANNELS // HEADS} heads, {COND} cond tokens, fp16")
+    return {"workload": name, "blocks": nblocks, "tokens": T_TOKENS,
+            "parallelism": f"query-sharded x{world}" if world > 1 else "none",
+            "l2": "inputs larger than L2 (705 MB of weights + activations per step)"}
+
+
+def attention_config(big: bool, world: int) -> dict:
+    d = CHANNELS // HEADS
+    if big:
+        return {"workload": f"cfg4: self-attention, 4 objects x 65536 tokens varlen, {HEADS}x{d} heads, bf16, K/V "
+                            f"shards exchanged between the ranks of each object",
+                "tokens": 4 * 65536, "parallelism": f"query-sharded x{world}" if world > 1 else "none",
+                "l2": "inputs larger than L2"}
+    return {"workload": f"cfg1: self-attention, T={T_TOKENS}, {HEADS}x{d} heads, fp16", "tokens": T_TOKENS,
+            "parallelism": f"query-sharded x{world}" if world > 1 else "none", "l2": "inputs larger than L2"}
+
+
+CONV_N, CONV_C = 200_000, 256
+
+
+def conv_config() -> dict:
+    return {"workload": f"cfg5: submanifold 3x3x3 conv, {CONV_N} shell voxels in 128^3, {CONV_C}->{CONV_C} channels, "
+                        f"fp16", "l2": "inputs larger than L2 (102 MB features + 102 MB output)"}
+
+
+# ----------------------------------------------------------------------------- CPU baseline
+#
+# The reference's CPU path for this hot path is its upstream PyTorch block with the reference's
+# torch shims (fp32; attention by SDPA over bounded query blocks).  The reference itself cannot
+# travel to the GPU box; oracle/torch_block.py restates that path in torch and is pinned to the
+# upstream module's output (tests/test_oracle_golden.py), so the CPU arm times the restatement,
+# on every host thread the process may use.
 
 _CPU_CACHE: dict = {}
 
 
-def cpu_block_seconds(sample: int, seed: int = 0) -> tuple[float, dict]:
-    """One fp32 CPU block at the full workload size, estimated from a row sample (oracle port)."""
+def cpu_threads() -> int:
+    """Use every host thread this process may run on (torchrun sets OMP_NUM_THREADS=1)."""
+    import torch
+
+    n = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    torch.set_num_threads(n)
+    return n
+
+
+def _cpu_block_inputs(seed: int = 0):
     from hi3d_b200 import synthetic
-    from oracle import ops
+    from oracle import torch_block
 
     if "block" not in _CPU_CACHE:
         coords, cos, sin, x, mod, cond = make_inputs(seed)
-        w = synthetic.block_weights(CHANNELS, CHANNELS, HEADS, seed=seed + 5)
+        w = torch_block.weights_f32(synthetic.block_weights(CHANNELS, CHANNELS, HEADS, seed=seed + 5))
         _CPU_CACHE["block"] = (w, x, mod, cos, sin, cond)
-    w, x, mod, cos, sin, cond = _CPU_CACHE["block"]
-    return ops.block_seconds_sampled(w, x, mod, cos, sin, cond, HEADS, sample=sample, seed=seed)
+    return _CPU_CACHE["block"]
 
 
-def cpu_attention_tflops(big: bool, sample: int = 256) -> tuple[float, str]:
-    """fp32 numpy attention of ``sample`` query rows against one whole object (all heads),
-    scaled to TFLOP/s with the same 4 * Nq * Nk * H * D count as the GPU arm."""
+def cpu_block_seconds(rows: int | None = None) -> float:
+    """Wall seconds of one whole fp32 block of the reference's CPU path over the first ``rows``
+    tokens (all T by default)."""
+    from oracle import torch_block
+
+    w, x, mod, cos, sin, cond = _cpu_block_inputs()
+    r = slice(0, rows or x.shape[0])
+    t0 = time.perf_counter()
+    torch_block.block_forward(w, x[r], mod, cos[r], sin[r], cond, HEADS)
+    return time.perf_counter() - t0
+
+
+def cpu_attention_tflops(big: bool, sample: int = 512) -> tuple[float, str]:
+    """The reference's shim attention (fp32 SDPA, torch_backend/attention.py:20-38) of ``sample``
+    query rows against one whole object, scaled to TFLOP/s with the GPU arm's 4 Nq Nk H D count."""
+    import torch
+
+    from oracle import torch_block
+
     per = 65536 if big else T_TOKENS
     d = CHANNELS // HEADS
     if ("attn", big) not in _CPU_CACHE:
-        rng = np.random.default_rng(7)
-        _CPU_CACHE[("attn", big)] = tuple(rng.standard_normal((HEADS, n, d)).astype(np.float32)
-                                          for n in (sample, per, per))
+        g = torch.Generator().manual_seed(7)
+        _CPU_CACHE[("attn", big)] = tuple(torch.randn((n, HEADS, d), generator=g) for n in (sample, per, per))
     q, k, v = _CPU_CACHE[("attn", big)]
     t0 = time.perf_counter()
-    for h in range(HEADS):
-        s = q[h] @ k[h].T * np.float32(d ** -0.5)
-        p = np.exp(s - s.max(-1, keepdims=True))
-        _ = (p / p.sum(-1, keepdims=True)) @ v[h]
+    torch_block.attend(q, k, v, d ** -0.5)
     secs = time.perf_counter() - t0
-    return 4.0 * sample * per * HEADS * d / secs / 1e12, f"{sample} query rows x {per} keys x {HEADS} heads, fp32"
+    return 4.0 * sample * per * HEADS * d / secs / 1e12, (f"{sample} query rows x {per} keys x {HEADS} heads, fp32 "
+                                                          f"SDPA (the reference's flash_attn shim)")
 
 
 def forward_inputs():
@@ -212,13 +279,15 @@ def forward_inputs():
     return _CPU_CACHE["fwd"]
 
 
-def cpu_forward_seconds(sample: int = 512) -> tuple[float, str]:
-    """One fp32 CPU forward of the whole transformer (oracle port): the embedding and I/O stages
-    run in full at the workload size; the 24 blocks are the row-sampled block estimate on the
-    low level, times 24."""
+def cpu_forward_seconds() -> tuple[float, float, str]:
+    """One fp32 CPU forward of the whole transformer: the embedding and I/O stages in full at the
+    workload size (numpy oracle port), plus one whole block of the reference's CPU path on the
+    low-level tokens whose time counts 24 times (the 24 blocks have one shape).  Returns
+    ``(estimated forward seconds, wall seconds spent, description)``."""
     from hi3d_b200 import synthetic
-    from oracle import ops
+    from oracle import ops, torch_block
 
+    t_wall = time.perf_counter()
     coords, feats, cond = forward_inputs()
     w = synthetic.model_weights(CHANNELS, CHANNELS, HEADS, 1, io_channels=FWD_IO, seed=3)
     io_only = {k: v for k, v in w.items() if not k.startswith("blocks.")}
@@ -229,12 +298,14 @@ def cpu_forward_seconds(sample: int = 512) -> tuple[float, str]:
     cos, sin = ops.rope_tables(low, CHANNELS // HEADS)
     x = synthetic.features(low.shape[0], CHANNELS, seed=6, dtype=np.float32)
     mod = synthetic.modulation(CHANNELS, FWD_T, seed=7)
-    bw = {k[len("blocks.0."):]: v for k, v in w.items() if k.startswith("blocks.0.")}
-    blk_s, _ = ops.block_seconds_sampled(bw, x, mod, cos, sin, cond, HEADS, sample=sample, seed=0)
-    desc = (f"whole transformer fp32 (numpy oracle port): embedding + I/O stages in full on {coords.shape[0]} fine "
-            f"voxels ({io_s:.1f} s), plus {BLOCKS} x one block on {low.shape[0]} low tokens estimated from "
-            f"{sample} sampled query rows ({blk_s:.1f} s each)")
-    return io_s + BLOCKS * blk_s, desc
+    bw = torch_block.weights_f32({k[len("blocks.0."):]: v for k, v in w.items() if k.startswith("blocks.0.")})
+    t0 = time.perf_counter()
+    torch_block.block_forward(bw, x, mod, cos, sin, cond, HEADS)
+    blk_s = time.perf_counter() - t0
+    desc = (f"whole transformer fp32: embedding + I/O stages in full on {coords.shape[0]} fine voxels (numpy oracle "
+            f"port, {io_s:.1f} s) plus one whole block of the reference's CPU path (torch restatement) on "
+            f"{low.shape[0]} low tokens ({blk_s:.1f} s), counted {BLOCKS} times")
+    return io_s + BLOCKS * blk_s, time.perf_counter() - t_wall, desc
 
 
 def cpu_conv_tflops(sample: int = 20000) -> tuple[float, str]:
@@ -244,7 +315,7 @@ def cpu_conv_tflops(sample: int = 20000) -> tuple[float, str]:
     from oracle import ops
 
     if "conv" not in _CPU_CACHE:
-        n, c = 200_000, 256
+        n, c = CONV_N, CONV_C
         coords = synthetic.shell_coords(n, 128, 48, 4, seed=5)
         rng = np.random.default_rng(3)
         table = ops.neighbour_table(coords)[:sample]
@@ -261,67 +332,265 @@ def cpu_conv_tflops(sample: int = 20000) -> tuple[float, str]:
     return 2.0 * wt.shape[1] * wt.shape[2] * pairs / secs / 1e12, f"{sample} output rows of cfg5, fp32 gather-GEMM"
 
 
+W8A8_GEMMS = (("self_attn.to_qkv", 1024, 3072), ("self_attn.to_out", 1024, 1024), ("cross_attn.to_q", 1024, 1024),
+              ("cross_attn.to_out", 1024, 1024), ("mlp.mlp.0", 1024, 4096), ("mlp.mlp.2", 4096, 1024))
+
+
+def cpu_w8a8_tops(rows: int = 64) -> tuple[float, str]:
+    """The reference's CPU statement of the W8A8 GEMM (its contract test, int64 numpy,
+    tests/test_w8a8_inference.py:15) over ``rows`` rows of each of a block's six projections."""
+    rng = np.random.default_rng(9)
+    ops_total, secs = 0.0, 0.0
+    for _, k, n in W8A8_GEMMS:
+        a = rng.integers(-127, 128, (rows, k), dtype=np.int8)
+        w = rng.integers(-127, 128, (n, k), dtype=np.int8)
+        t0 = time.perf_counter()
+        _ = a.astype(np.int64) @ w.astype(np.int64).T
+        secs += time.perf_counter() - t0
+        ops_total += 2.0 * rows * k * n
+    return ops_total / secs / 1e12, f"{rows} rows of each of a block's six projections, int64 numpy GEMM"
+
+
+# ----------------------------------------------------------------------------- reference arm
+
+
 def run_reference(args) -> None:
+    """The CPU path of the reference, timed on the host's cores (rank 0 only under torchrun)."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    cores = os.cpu_count()
+    cores = cpu_threads()
+    world = args.gpus
+    secs = []
+
+    def steps(fn):
+        for i in range(args.warmup + args.steps):
+            t0 = time.perf_counter()
+            r = fn()
+            if i >= args.warmup:
+                secs.append(time.perf_counter() - t0)
+        return r
+
     if args.workload in ("stack", "stack_w8a8", "block"):
-        sample = 512
-        secs = []
-        for i in range(args.warmup + args.steps):
-            s, _ = cpu_block_seconds(sample, seed=0)
-            if i >= args.warmup:
-                secs.append(s)
-        per_block = statistics.median(secs)
-        value, unit, metric = T_TOKENS / per_block, "tokens/s", "block_tokens_per_s"
-        ms_step = per_block * BLOCKS * 1e3
-        desc = (f"one fp32 block at T={T_TOKENS} per step (numpy oracle port of the reference block): K/V side on "
-                f"all rows, {sample} sampled query rows for the rest, scaled by T/{sample}")
-        workload = f"cfg1 block on CPU: T={T_TOKENS}, C={CHANNELS}, H={HEADS}x64, L={COND}"
+        nblocks = 1 if args.workload == "block" else BLOCKS
+        _cpu_block_inputs()
+        steps(cpu_block_seconds)
+        metric, unit = "block_tokens_per_s", "tokens/s"
+        value = T_TOKENS * len(secs) / sum(secs)
+        config = stack_config(args.workload, nblocks, world)
+        desc = (f"one whole fp32 block at T={T_TOKENS} per step (each of the stack's {nblocks} blocks has this "
+                f"shape): the reference's CPU path, upstream block + flash_attn shim (SDPA over query blocks), "
+                f"restated in torch and pinned to the upstream module")
+        if args.workload == "stack_w8a8":
+            desc += "; the reference's W8A8 GEMM exists only as a Metal kernel, so its CPU path is this fp32 block"
     elif args.workload == "forward":
-        secs = []
-        for i in range(args.warmup + args.steps):
-            sec, desc = cpu_forward_seconds()
-            if i >= args.warmup:
-                secs.append(sec)
         from oracle import ops
 
+        est = []
+        steps(lambda: est.append(cpu_forward_seconds()))
         n_low = ops.downsample_structure(forward_inputs()[0])[0].shape[0]
-        per = statistics.median(secs)
-        value, unit, metric, ms_step = n_low / per, "tokens/s", "forward_tokens_per_s", per * 1e3
-        workload = f"whole transformer on CPU: {FWD_FINE} fine voxels, {n_low} low tokens, {BLOCKS} blocks"
+        fwd_s = statistics.median(e[0] for e in est[args.warmup:])
+        desc = est[-1][2]
+        metric, unit, value = "forward_tokens_per_s", "tokens/s", n_low / fwd_s
+        config = {"workload": f"whole refinement transformer fwd: {FWD_FINE} fine shell voxels, {n_low} low tokens, "
+                              f"{BLOCKS} blocks", "low_tokens": n_low}
     elif args.workload in ("conv", "vae"):
         vals = []
-        for i in range(args.warmup + args.steps):
-            v, desc = cpu_conv_tflops()
-            if i >= args.warmup:
-                vals.append(v)
-        value, unit, ms_step = statistics.median(vals), "TFLOP/s", None
+        steps(lambda: vals.append(cpu_conv_tflops()))
+        value, unit = statistics.median(v[0] for v in vals[args.warmup:]), "TFLOP/s"
+        desc = vals[-1][1]
         metric = "sparse_conv_tflops" if args.workload == "conv" else "vae_conv_gn_swish_tflops"
-        workload = "cfg5 submanifold conv on CPU (the convolution that dominates both workloads)"
+        config = conv_config()
     else:
         big = args.workload == "attention262k"
         vals = []
-        for i in range(args.warmup + args.steps):
-            v, desc = cpu_attention_tflops(big)
-            if i >= args.warmup:
-                vals.append(v)
-        value, unit, metric = statistics.median(vals), "TFLOP/s", "attention_tflops"
-        ms_step = None
-        workload = "cfg4 self-attention on CPU" if big else "cfg1 self-attention on CPU"
+        steps(lambda: vals.append(cpu_attention_tflops(big)))
+        value, unit, metric = statistics.median(v[0] for v in vals[args.warmup:]), "TFLOP/s", "attention_tflops"
+        desc = vals[-1][1]
+        config = attention_config(big, world)
     line = {
         "impl": "reference", "metric": metric, "value": value, "unit": unit,
-        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": sum(secs) / len(secs) * 1e3,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": workload, "blocks": BLOCKS},
+        "config": config,
         "cpu_baseline": {"value": value, "unit": unit, "cores": cores, "kind": "port", "sample": desc},
         "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
-# ----------------------------------------------------------------------------- GPU arm
+# ----------------------------------------------------------------------------- GPU arm: helpers
+
+
+def _timed(fn, steps: int, warmup: int) -> float:
+    """Milliseconds per call of ``fn`` (CUDA events on the current stream, after ``warmup`` calls)."""
+    import torch
+
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def _max_over_ranks(ms: float, world: int, dev) -> float:
+    import torch
+    import torch.distributed as dist
+
+    if world == 1:
+        return ms
+    t = torch.tensor([ms], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def measure_w8a8(weights, inputs, steps: int, warmup: int, fp16_ms: float) -> dict:
+    """cfg2 beside the headline: the W8A8 24-block stack (weights quantised on the GPU from the
+    same fp16 weights) and each int8 projection GEMM of a block at M = T."""
+    import torch
+
+    from hi3d_b200 import transformer, w8a8
+
+    x_dev, mod_d, cos_d, sin_d, cond_d = inputs
+    w8 = [transformer.to_w8a8(w) for w in weights]
+    stack = transformer.BlockStack(w8, HEADS)
+    kvs = [transformer.context_kv(w, cond_d, HEADS) for w in w8]
+    ms = _timed(lambda: stack(x_dev[None], mod_d, cos_d, sin_d, kvs), steps, warmup)
+    g = torch.Generator(device=x_dev.device).manual_seed(11)
+    per, ops_all, t_all = {}, 0.0, 0.0
+    for name, k, n in W8A8_GEMMS:
+        a = torch.randint(-127, 128, (T_TOKENS, k), generator=g, device=x_dev.device, dtype=torch.int8)
+        sa = torch.rand(T_TOKENS, generator=g, device=x_dev.device) * 0.01 + 1e-3
+        qa = w8a8.Quantized(a, sa, (T_TOKENS, k), torch.float16)
+        wq, sw, b = w8[0][f"{name}.weight"], w8[0][f"{name}.w8_scale"], w8[0][f"{name}.bias"]
+        t = _timed(lambda: w8a8.linear(qa, wq, sw, b), steps, warmup)
+        per[name] = 2.0 * T_TOKENS * k * n / (t / 1e3) / 1e12
+        ops_all += 2.0 * T_TOKENS * k * n
+        t_all += t
+    del w8, stack, kvs
+    tops = ops_all / (t_all / 1e3) / 1e12
+    peaks = _peaks()
+    peak = 2 * peaks["bf16_tflops"]
+    cv, cdesc = cpu_w8a8_tops()
+    return {"ms_per_step": ms, "tokens_per_s": BLOCKS * T_TOKENS / (ms / 1e3), "fp16_over_w8a8_time": fp16_ms / ms,
+            "int8_gemm_tops": tops, "int8_gemm_tops_per_projection": per,
+            "roofline": {"bound": "tensor", "achieved": tops, "peak": peak, "unit": "TOP/s", "frac": tops / peak,
+                         "peak_source": f"2 x {peaks['source']} bf16_tflops burst (the dense int8 rate is twice "
+                                        f"the bf16 rate); GEMMs timed alone"},
+            "cpu_baseline": {"value": cv, "unit": "TOP/s", "cores": torch.get_num_threads(), "kind": "port",
+                             "sample": cdesc}}
+
+
+def measure_conv(dev, steps: int, warmup: int) -> dict:
+    """cfg5: neighbour map, submanifold conv and the stride-2 conv at 200,000 voxels, 256 -> 256."""
+    import torch
+
+    from hi3d_b200 import sparse, synthetic
+
+    n, c = CONV_N, CONV_C
+    coords = synthetic.shell_coords(n, 128, 48, 4, seed=5)
+    g = torch.Generator(device=dev).manual_seed(3)
+    x = torch.randn((n, c), generator=g, device=dev).half()
+    w = (torch.randn((c, 3, 3, 3, c), generator=g, device=dev) * 0.02).half()
+    b = (torch.randn(c, generator=g, device=dev) * 0.02).half()
+    cdev = torch.from_numpy(coords).to(dev)
+    level = sparse.Level(cdev, sparse.neighbour_table(cdev))
+    map_ms = _timed(lambda: sparse.neighbour_table(cdev), steps, warmup)
+    mask = level.tap_mask
+    pairs = int((level.table < n).sum().item())
+    conv_ms = _timed(lambda: sparse.conv(x, level.table, w, b, tap_mask=mask), steps, warmup)
+    low, _, _ = sparse.downsample_structure(cdev)
+    table2 = sparse.neighbour_table(cdev, query=low, stride=2)
+    mask2 = sparse.conv_tap_mask(table2, n)
+    pairs2 = int((table2 < n).sum().item())
+    down_ms = _timed(lambda: sparse.conv(x, table2, w, b, n_in=n, tap_mask=mask2), steps, warmup)
+    struct_ms = _timed(lambda: sparse.downsample_structure(cdev), steps, warmup)
+    tflops = 2.0 * c * c * pairs / (conv_ms / 1e3) / 1e12
+    peaks = _peaks()
+    cv, cdesc = cpu_conv_tflops()
+    return {"value": tflops, "unit": "TFLOP/s", "ms": conv_ms, "pairs": pairs,
+            "dense_equivalent_tflops": 2.0 * 27 * n * c * c / (conv_ms / 1e3) / 1e12,
+            "neighbour_map_ms": map_ms, "lookups_per_s": 27 * n / (map_ms / 1e3),
+            "stride2_conv_ms": down_ms, "stride2_low_voxels": int(low.shape[0]), "stride2_pairs": pairs2,
+            "stride2_tflops": 2.0 * c * c * pairs2 / (down_ms / 1e3) / 1e12,
+            "downsample_structure_ms": struct_ms,
+            "roofline": {"bound": "tensor", "achieved": tflops, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                         "frac": tflops / peaks["bf16_tflops"], "traffic": _profile_traffic("sparse_conv_cfg5"),
+                         "peak_source": f"{peaks['source']} bf16_tflops (burst; kernel timed alone)"},
+            "cpu_baseline": {"value": cv, "unit": "TFLOP/s", "cores": torch.get_num_threads(), "kind": "port",
+                             "sample": cdesc}}
+
+
+def measure_cfg4(dev, world: int, rank: int, steps: int, warmup: int, sub) -> dict:
+    """cfg4: bf16 self-attention over 4 objects x 65,536 tokens, the packed tokens split into
+    contiguous slices over the ranks.  With at most 4 ranks each rank holds whole objects and
+    attends them alone; with more, the ranks of one object exchange its K/V shards (``sub``, from
+    ``dist.object_group``) while attending their own keys.  Every rank times its own slice; the
+    step time is the maximum over ranks."""
+    import torch
+
+    from hi3d_b200 import attention, dist as hdist
+
+    objects, per, d = 4, 65536, CHANNELS // HEADS
+    tl = objects * per // world
+    g = torch.Generator(device=dev).manual_seed(7 + rank)
+    # RoPE'd, RMS-normalised queries/keys have per-head norm sqrt(D): unit-variance entries
+    q, k, v = (torch.randn((tl, HEADS, d), generator=g, device=dev).bfloat16() for _ in range(3))
+    scale = d ** -0.5
+    if sub is None:
+        n_obj = objects // world
+        cu = torch.arange(n_obj + 1, device=dev, dtype=torch.int32) * per
+        out = torch.empty_like(q)
+        step = lambda: attention.flash_attn_varlen(q, k, v, cu, cu, per, scale, out=out)
+        exchange = 0
+    else:
+        kvb = tuple(torch.empty((per, HEADS, d), dtype=q.dtype, device=dev) for _ in range(2))
+        step = lambda: hdist.sharded_self_attention(q[None], k, v, scale, sub, kvb)
+        exchange = 2 * (per - tl) * HEADS * d * 2
+    ms = _timed(step, steps, warmup)
+    ms = _max_over_ranks(ms, world, dev)
+    flops = 4.0 * objects * per * per * HEADS * d
+    tflops = flops / (ms / 1e3) / 1e12
+    peaks = _peaks()
+    peak = peaks["bf16_tflops_sustained"]
+    line = {"value": tflops, "unit": "TFLOP/s", "ms_per_layer": ms, "tflops_per_gpu": tflops / world,
+            "kv_bytes_received_per_rank": exchange,
+            "roofline": {"bound": "tensor", "achieved": tflops / world, "peak": peak, "unit": "TFLOP/s",
+                         "frac": tflops / world / peak,
+                         "peak_source": f"{peaks['source']} bf16_tflops_sustained (burst {peaks['bf16_tflops']})"}}
+    if rank == 0 and world == 1:
+        cv, cdesc = cpu_attention_tflops(True)
+        line["cpu_baseline"] = {"value": cv, "unit": "TFLOP/s", "cores": torch.get_num_threads(), "kind": "port",
+                                "sample": cdesc}
+    return line
+
+
+def sharded_parity(weights, inputs_local, inputs_full, world: int, rank: int, dev) -> float | None:
+    """Relative L2 between the first two blocks run query-sharded over the ranks and the same two
+    blocks on one GPU (rank 0), on the bench inputs; None on ranks other than 0."""
+    import torch
+
+    from hi3d_b200 import dist as hdist, transformer
+
+    x_l, mod_d, cos_l, sin_l, cond_d = inputs_local
+    two = weights[:2]
+    kvs = [transformer.context_kv(w, cond_d, HEADS) for w in two]
+    y_local = hdist.ShardedBlockStack(two, HEADS)(x_l, mod_d, cos_l, sin_l, kvs)
+    y_all = hdist.gather_rows(y_local)
+    if rank != 0:
+        return None
+    x_f, cos_f, sin_f = inputs_full
+    ref = transformer.BlockStack(two, HEADS)(x_f[None], mod_d, cos_f, sin_f, kvs)[0]
+    return float((y_all.float() - ref.float()).norm() / ref.float().norm())
+
+
+# ----------------------------------------------------------------------------- GPU arm: stack
 
 
 def run_ours(args) -> None:
@@ -340,6 +609,7 @@ def run_ours(args) -> None:
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
     _lib.load()
+    cpu_threads()
 
     coords, cos, sin, x, mod, cond = make_inputs(0)
     if T_TOKENS % world:
@@ -388,11 +658,7 @@ def run_ours(args) -> None:
         barrier()
     launches = _lib.LAUNCHES[0]
     attn = attention.TIMER.stop()
-    ms = start.elapsed_time(end)
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    ms = _max_over_ranks(start.elapsed_time(end), world, dev)
     ms_per_step = ms / args.steps
     value = nblocks * T_TOKENS / (ms_per_step / 1e3)
 
@@ -408,11 +674,7 @@ def run_ours(args) -> None:
     e1.record(stream)
     torch.cuda.synchronize()
     barrier()
-    e2e_ms = e0.elapsed_time(e1)
-    if world > 1:
-        t = torch.tensor([e2e_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
+    e2e_ms = _max_over_ranks(e0.elapsed_time(e1), world, dev)
     e2e_value = nblocks * T_TOKENS / (e2e_ms / args.steps / 1e3)
 
     # ---- roofline of the dominant kernel (self-attention)
@@ -435,14 +697,7 @@ def run_ours(args) -> None:
         "metric": "block_tokens_per_s", "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-        "config": {"workload": (f"cfg2: W8A8 {BLOCKS}-block stack fwd (int8 signed-H64 activations, int8 rotated "
-                                f"weights, int32 accumulate, fp16 dequant), T={T_TOKENS}, C={CHANNELS}, "
-                                f"{HEADS}x{CHANNELS // HEADS} heads, {COND} cond tokens"
-                                if args.workload == "stack_w8a8" else
-                                f"cfg1: {nblocks}-block sparse-DiT stack fwd, T={T_TOKENS} shell tokens in {GRID}^3, "
-                                f"C={CHANNELS}, {HEADS}x{CHANNELS // HEADS} heads, {COND} cond tokens, fp16"),
-                   "blocks": nblocks, "tokens": T_TOKENS, "parallelism": f"query-sharded x{world}" if world > 1 else "none",
-                   "l2": "inputs larger than L2 (705 MB of weights + activations per step)"},
+        "config": stack_config(args.workload, nblocks, world),
         "roofline": roofline,
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": x_host.numel() * 2,
                 "d2h_bytes_per_step": out_host.numel() * 2},
@@ -450,12 +705,52 @@ def run_ours(args) -> None:
         "clocks": clocks.summary(),
         "attention_tflops": achieved,
     }
+    extra = args.workload == "stack" and not args.no_extras
+    if world > 1:
+        # per-phase breakdown of one step on every rank (outside the timed region), the maximum
+        # over ranks per phase, then the sharded stack's parity against one GPU
+        timer = hdist.PhaseTimer()
+        torch.cuda.synchronize()
+        barrier()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for _ in range(2):
+            stack(x_dev, mod_d, cos_d, sin_d, kvs, timer=timer)
+        t1.record()
+        phases = timer.totals()
+        names = sorted(phases)
+        vals = torch.tensor([phases[n] / 2 for n in names] + [t0.elapsed_time(t1) / 2], device=dev)
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+        bd = {n: float(v) for n, v in zip(names + ["step_with_marks"], vals.tolist())}
+        line["breakdown_ms_per_step"] = bd
+        if args.workload in ("stack", "block"):
+            x_full = torch.from_numpy(x).to(dev) if rank == 0 else None
+            cos_f = torch.from_numpy(cos).to(dev) if rank == 0 else None
+            sin_f = torch.from_numpy(sin).to(dev) if rank == 0 else None
+            err = sharded_parity(weights, (x_dev, mod_d, cos_d, sin_d, cond_d), (x_full, cos_f, sin_f), world, rank,
+                                 dev)
+            if rank == 0:
+                line["sharded_rel_l2"] = err
+                line["sharded_rel_l2_case"] = "first 2 blocks query-sharded vs one GPU on the bench inputs"
+        barrier()
+    if extra:
+        # the north-star's multi-GPU configuration beside the headline (outside its timed region)
+        sub = hdist.object_group(4) if world > 1 else None
+        line["cfg4_attention"] = measure_cfg4(dev, world, rank, max(3, args.steps // 4), 2, sub)
+        line["extra_keys"] = ["cfg4_attention"]
+    if extra and world == 1:
+        line["cfg2_w8a8"] = measure_w8a8(weights, (x_dev, mod_d, cos_d, sin_d, cond_d), max(3, args.steps // 2),
+                                         args.warmup, ms_per_step)
+        line["cfg5_conv"] = measure_conv(dev, args.steps, args.warmup)
+        line["extra_keys"] += ["cfg2_w8a8", "cfg5_conv"]
     if rank == 0 and world == 1:
-        secs, phases = cpu_block_seconds(1024, seed=0)
-        cpu_value = T_TOKENS / secs
-        line["cpu_baseline"] = {"value": cpu_value, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
-                                "sample": f"one fp32 block at T={T_TOKENS} (numpy oracle port): K/V side on all "
-                                          f"rows, 1024 sampled query rows for the rest, scaled by T/1024",
+        cpu_block_seconds(rows=4096)  # warm the thread pool and allocator
+        secs = cpu_block_seconds()
+        line["cpu_baseline"] = {"value": T_TOKENS / secs, "unit": "tokens/s", "cores": torch.get_num_threads(),
+                                "kind": "port",
+                                "sample": f"one whole fp32 block at T={T_TOKENS} (one of the stack's {nblocks}): the "
+                                          f"reference's CPU path (upstream block + flash_attn shim), restated in torch",
                                 "seconds_per_block": secs}
     if rank == 0:
         print(json.dumps(line), flush=True)
@@ -465,11 +760,12 @@ def run_ours(args) -> None:
 
 
 def run_attention(args, big: bool) -> None:
-    """Self-attention kernel alone: cfg1 (T=32768 fp16, one object) or cfg4 (4 x 65536 bf16 varlen)."""
+    """Self-attention kernel alone: cfg1 (T=32768 fp16, one object) or cfg4 (4 x 65536 bf16 varlen,
+    query-sharded over the GPUs with per-object K/V exchange)."""
     import torch
     import torch.distributed as dist
 
-    from hi3d_b200 import _lib, attention
+    from hi3d_b200 import _lib, attention, dist as hdist
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -481,89 +777,83 @@ def run_attention(args, big: bool) -> None:
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
     _lib.load()
+    cpu_threads()
     d = CHANNELS // HEADS
-    if big:
-        objects, per, dtype = 4, 65536, torch.bfloat16
-    else:
-        objects, per, dtype = 1, T_TOKENS, torch.float16
-    total = objects * per
-    g = torch.Generator(device=dev).manual_seed(7)
-    # RoPE'd, RMS-normalised queries/keys have per-head norm sqrt(D): unit-variance entries
-    k = torch.randn((total, HEADS, d), generator=g, device=dev).to(dtype)
-    v = torch.randn((total, HEADS, d), generator=g, device=dev).to(dtype)
-    # query rows of this rank: a contiguous slice of every object (keys stay per object)
-    if per % world:
-        raise ValueError("tokens per object must divide by the number of GPUs")
-    ql = per // world
-    q = torch.randn((objects * ql, HEADS, d), generator=g, device=dev).to(dtype)
-    cu_q = torch.arange(0, objects + 1, device=dev, dtype=torch.int32) * ql
-    cu_k = torch.arange(0, objects + 1, device=dev, dtype=torch.int32) * per
-    out = torch.empty_like(q)
-    flops = 4.0 * objects * ql * per * HEADS * d  # per rank per launch
-
-    def step():
-        attention.flash_attn_varlen(q, k, v, cu_q, cu_k, ql, d ** -0.5, out=out)
-
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
-    stream = torch.cuda.current_stream()
-    _lib.LAUNCHES[0] = 0
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-        e0.record(stream)
-        for _ in range(args.steps):
-            step()
-        e1.record(stream)
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
-    launches = _lib.LAUNCHES[0]
-    ms = e0.elapsed_time(e1)
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    ms_step = ms / args.steps
-    tflops = flops * world / (ms_step / 1e3) / 1e12
-    per_gpu = flops / (ms_step / 1e3) / 1e12
     peaks = _peaks()
-    # end to end: q/k/v from pinned host memory, output back to the host
-    hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
-    hout = torch.empty_like(hq).pin_memory()
-    torch.cuda.synchronize()
-    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    f0.record(stream)
-    for _ in range(args.steps):
-        dq, dk, dv = (t.to(dev, non_blocking=True) for t in (hq, hk, hv))
-        hout.copy_(attention.flash_attn_varlen(dq, dk, dv, cu_q, cu_k, ql, d ** -0.5), non_blocking=True)
-    f1.record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = f0.elapsed_time(f1) / args.steps
-    name = "flash_attn_fwd_cfg4" if big else "flash_attn_fwd_cfg1"
-    cpu = None
-    if rank == 0 and world == 1:
-        cv, cdesc = cpu_attention_tflops(big)
-        cpu = {"value": cv, "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": "port", "sample": cdesc}
+    _lib.LAUNCHES[0] = 0
+    if big:
+        sub = hdist.object_group(4) if world > 1 else None
+        with ClockSampler(local) as clocks:
+            r = measure_cfg4(dev, world, rank, args.steps, args.warmup, sub)
+        launches = _lib.LAUNCHES[0]
+        ms_step, tflops = r["ms_per_layer"], r["value"]
+        roof = dict(r["roofline"], traffic=_profile_traffic("flash_attn_fwd_cfg4"))
+        # end to end: this rank's q/k/v slice from pinned host memory, the output back to the host
+        tl = 4 * 65536 // world
+        g = torch.Generator().manual_seed(8 + rank)
+        hq, hk, hv = (torch.randn((tl, HEADS, d), generator=g).bfloat16().pin_memory() for _ in range(3))
+        hout = torch.empty((tl, HEADS, d), dtype=torch.bfloat16).pin_memory()
+        kvb = tuple(torch.empty((65536, HEADS, d), dtype=torch.bfloat16, device=dev) for _ in range(2))
+
+        def e2e_step():
+            dq, dk, dv = (t.to(dev, non_blocking=True) for t in (hq, hk, hv))
+            if sub is None:
+                n_obj = 4 // world
+                cu = torch.arange(n_obj + 1, device=dev, dtype=torch.int32) * 65536
+                o = attention.flash_attn_varlen(dq, dk, dv, cu, cu, 65536, d ** -0.5)
+            else:
+                o = hdist.sharded_self_attention(dq[None], dk, dv, d ** -0.5, sub, kvb)[0].view(tl, HEADS, d)
+            hout.copy_(o, non_blocking=True)
+
+        e2e_ms = _max_over_ranks(_timed(e2e_step, args.steps, 1), world, dev)
+        flops_all = 4.0 * 4 * 65536 * 65536 * HEADS * d
+        e2e = {"value": flops_all / (e2e_ms / 1e3) / 1e12, "unit": "TFLOP/s",
+               "h2d_bytes_per_step": 3 * tl * HEADS * d * 2, "d2h_bytes_per_step": tl * HEADS * d * 2}
+        cpu = r.get("cpu_baseline")
+        extra = {"kv_bytes_received_per_rank": r["kv_bytes_received_per_rank"]}
+    else:
+        g = torch.Generator(device=dev).manual_seed(7)
+        per = T_TOKENS
+        k = torch.randn((per, HEADS, d), generator=g, device=dev).half()
+        v = torch.randn((per, HEADS, d), generator=g, device=dev).half()
+        if per % world:
+            raise ValueError("tokens must divide by the number of GPUs")
+        ql = per // world
+        q = torch.randn((ql, HEADS, d), generator=g, device=dev).half()
+        cu_q = torch.tensor([0, ql], device=dev, dtype=torch.int32)
+        cu_k = torch.tensor([0, per], device=dev, dtype=torch.int32)
+        out = torch.empty_like(q)
+        with ClockSampler(local) as clocks:
+            ms_step = _timed(lambda: attention.flash_attn_varlen(q, k, v, cu_q, cu_k, ql, d ** -0.5, out=out),
+                             args.steps, args.warmup)
+        launches = _lib.LAUNCHES[0]
+        ms_step = _max_over_ranks(ms_step, world, dev)
+        flops = 4.0 * ql * per * HEADS * d
+        tflops = flops * world / (ms_step / 1e3) / 1e12
+        roof = {"bound": "tensor", "achieved": tflops / world, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                "frac": tflops / world / peaks["bf16_tflops"], "traffic": _profile_traffic("flash_attn_fwd_cfg1"),
+                "peak_source": f"{peaks['source']} bf16_tflops (burst; kernel timed alone)"}
+        hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
+        hout = torch.empty_like(hq).pin_memory()
+
+        def e2e_step():
+            dq, dk, dv = (t.to(dev, non_blocking=True) for t in (hq, hk, hv))
+            hout.copy_(attention.flash_attn_varlen(dq, dk, dv, cu_q, cu_k, ql, d ** -0.5), non_blocking=True)
+
+        e2e_ms = _max_over_ranks(_timed(e2e_step, args.steps, 1), world, dev)
+        e2e = {"value": flops * world / (e2e_ms / 1e3) / 1e12, "unit": "TFLOP/s",
+               "h2d_bytes_per_step": (q.numel() + k.numel() + v.numel()) * 2, "d2h_bytes_per_step": out.numel() * 2}
+        cpu = None
+        if rank == 0 and world == 1:
+            cv, cdesc = cpu_attention_tflops(False)
+            cpu = {"value": cv, "unit": "TFLOP/s", "cores": torch.get_num_threads(), "kind": "port", "sample": cdesc}
+        extra = {}
     line = {
         "metric": "attention_tflops", "value": tflops, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": "bf16" if big else "f16", "data": "synthetic",
-        "config": {"workload": (f"cfg4: self-attention, {objects} objects x {per} tokens varlen, {HEADS}x{d} heads, bf16"
-                                if big else f"cfg1: self-attention, T={per}, {HEADS}x{d} heads, fp16"),
-                   "tokens": total, "parallelism": f"query-sharded x{world}" if world > 1 else "none",
-                   "l2": "inputs larger than L2" if total * HEADS * d * 2 * 3 > 126e6 else "inputs fit in L2"},
-        "roofline": {"bound": "tensor", "achieved": per_gpu, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
-                     "frac": per_gpu / peaks["bf16_tflops"], "traffic": _profile_traffic(name),
-                     "peak_source": f"{peaks['source']} bf16_tflops (burst; kernel timed alone)"},
-        "e2e": {"value": flops * world / (e2e_ms / 1e3) / 1e12, "unit": "TFLOP/s",
-                "h2d_bytes_per_step": (q.numel() + k.numel() + v.numel()) * 2,
-                "d2h_bytes_per_step": out.numel() * 2},
-        "gpu_launches": launches,
-        "clocks": clocks.summary(),
+        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16" if big else "f16", "data": "synthetic",
+        "config": attention_config(big, world), "roofline": roof, "e2e": e2e, "gpu_launches": launches,
+        "clocks": clocks.summary(), **extra,
     }
     if cpu is not None:
         line["cpu_baseline"] = cpu
@@ -586,65 +876,35 @@ def run_conv(args) -> None:
     torch.cuda.set_device(0)
     dev = torch.device("cuda", 0)
     _lib.load()
-    n, c = 200_000, 256
-    coords = synthetic.shell_coords(n, 128, 48, 4, seed=5)
-    g = torch.Generator(device=dev).manual_seed(3)
-    x = torch.randn((n, c), generator=g, device=dev).half()
-    w = (torch.randn((c, 3, 3, 3, c), generator=g, device=dev) * 0.02).half()
-    b = (torch.randn(c, generator=g, device=dev) * 0.02).half()
-    cdev = torch.from_numpy(coords).to(dev)
-    for _ in range(3):
-        level = sparse.Level(cdev, sparse.neighbour_table(cdev))
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(args.steps):
-        table = sparse.neighbour_table(cdev)
-    e1.record()
-    torch.cuda.synchronize()
-    map_ms = e0.elapsed_time(e1) / args.steps
-    mask = level.tap_mask
-    pairs = int((level.table < n).sum().item())
-    step = lambda: sparse.conv(x, level.table, w, b, tap_mask=mask)
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
+    cpu_threads()
     _lib.LAUNCHES[0] = 0
     with ClockSampler(0) as clocks:
-        e0.record()
-        for _ in range(args.steps):
-            step()
-        e1.record()
-        torch.cuda.synchronize()
+        r = measure_conv(dev, args.steps, args.warmup)
     launches = _lib.LAUNCHES[0]
-    ms = e0.elapsed_time(e1) / args.steps
-    flops = 2.0 * c * c * pairs
-    dense_flops = 2.0 * 27 * n * c * c
-    peaks = _peaks()
-    hx = x.cpu().pin_memory()
+    n, c = CONV_N, CONV_C
+    coords = synthetic.shell_coords(n, 128, 48, 4, seed=5)
+    cdev = torch.from_numpy(coords).to(dev)
+    level = sparse.Level(cdev, sparse.neighbour_table(cdev))
+    g = torch.Generator(device=dev).manual_seed(3)
+    w = (torch.randn((c, 3, 3, 3, c), generator=g, device=dev) * 0.02).half()
+    b = (torch.randn(c, generator=g, device=dev) * 0.02).half()
+    hx = torch.randn((n, c), generator=g).half().pin_memory()
     hout = torch.empty((n, c), dtype=torch.float16).pin_memory()
-    torch.cuda.synchronize()
-    e0.record()
-    for _ in range(args.steps):
-        hout.copy_(sparse.conv(hx.to(dev, non_blocking=True), level.table, w, b, tap_mask=mask), non_blocking=True)
-    e1.record()
-    torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1) / args.steps
+    mask = level.tap_mask
+    e2e_ms = _timed(lambda: hout.copy_(sparse.conv(hx.to(dev, non_blocking=True), level.table, w, b, tap_mask=mask),
+                                       non_blocking=True), args.steps, 1)
+    flops = 2.0 * c * c * r["pairs"]
+    cfg = dict(conv_config(), **{k: r[k] for k in ("pairs", "dense_equivalent_tflops", "neighbour_map_ms",
+                                                    "lookups_per_s", "stride2_conv_ms", "stride2_tflops",
+                                                    "downsample_structure_ms")})
     line = {
-        "metric": "sparse_conv_tflops", "value": flops / (ms / 1e3) / 1e12, "unit": "TFLOP/s", "n_gpus": 1,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "none",
-        "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-        "config": {"workload": f"cfg5: submanifold 3x3x3 conv, {n} shell voxels in 128^3, {c}->{c} channels, fp16",
-                   "pairs": pairs, "dense_equivalent_tflops": dense_flops / (ms / 1e3) / 1e12,
-                   "neighbour_map_ms": map_ms, "lookups_per_s": 27 * n / (map_ms / 1e3),
-                   "l2": "inputs larger than L2 (102 MB features + 102 MB output)"},
-        "roofline": {"bound": "tensor", "achieved": flops / (ms / 1e3) / 1e12, "peak": peaks["bf16_tflops"],
-                     "unit": "TFLOP/s", "frac": flops / (ms / 1e3) / 1e12 / peaks["bf16_tflops"],
-                     "traffic": _profile_traffic("sparse_conv_cfg5"),
-                     "peak_source": f"{peaks['source']} bf16_tflops (burst)"},
+        "metric": "sparse_conv_tflops", "value": r["value"], "unit": "TFLOP/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["ms"], "higher_is_better": True,
+        "scaling": "none", "vs_baseline": None, "dtype": "f16", "data": "synthetic", "config": cfg,
+        "roofline": r["roofline"],
         "e2e": {"value": flops / (e2e_ms / 1e3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": n * c * 2,
                 "d2h_bytes_per_step": n * c * 2},
-        "gpu_launches": launches, "clocks": clocks.summary(),
+        "gpu_launches": launches, "clocks": clocks.summary(), "cpu_baseline": r["cpu_baseline"],
     }
     print(json.dumps(line), flush=True)
 
@@ -659,6 +919,7 @@ def run_forward(args) -> None:
     torch.cuda.set_device(0)
     dev = torch.device("cuda", 0)
     _lib.load()
+    cpu_threads()
     coords, feats, cond = forward_inputs()
     cfg = model.ModelConfig(model_channels=CHANNELS, cond_channels=CHANNELS, num_heads=HEADS, num_blocks=BLOCKS,
                             io_channels=FWD_IO)
@@ -720,11 +981,12 @@ def run_forward(args) -> None:
         "metric": "forward_tokens_per_s", "value": n_low / (ms / 1e3), "unit": "tokens/s", "n_gpus": 1,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "none",
         "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-        "config": {"workload": (f"whole refinement transformer fwd: {coords.shape[0]} fine shell voxels in "
-                                f"{FWD_GRID}^3 -> {n_low} low tokens, I/O stage {FWD_IO} channels, {BLOCKS} blocks "
-                                f"C={CHANNELS} {HEADS}x{CHANNELS // HEADS} heads, {COND} cond tokens, fp16 torso"),
-                   "fine_voxels": int(coords.shape[0]), "low_tokens": n_low, "io_stages_ms": io_ms,
-                   "stack_ms": ms - io_ms, "guided_batch2_ms": guided_ms,
+        "config": {"workload": f"whole refinement transformer fwd: {FWD_FINE} fine shell voxels, {n_low} low tokens, "
+                               f"{BLOCKS} blocks", "low_tokens": n_low,
+                   "detail": (f"{coords.shape[0]} fine shell voxels in {FWD_GRID}^3 -> {n_low} low tokens, I/O stage "
+                              f"{FWD_IO} channels, {BLOCKS} blocks C={CHANNELS} {HEADS}x{CHANNELS // HEADS} heads, "
+                              f"{COND} cond tokens, fp16 torso"),
+                   "io_stages_ms": io_ms, "stack_ms": ms - io_ms, "guided_batch2_ms": guided_ms,
                    "l2": "inputs larger than L2 (705 MB of weights per step)"},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak, "traffic": None,
@@ -735,9 +997,9 @@ def run_forward(args) -> None:
                 "d2h_bytes_per_step": out_host.numel() * 4},
         "gpu_launches": launches, "clocks": clocks.summary(),
     }
-    secs, desc = cpu_forward_seconds()
-    line["cpu_baseline"] = {"value": n_low / secs, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
-                            "sample": desc}
+    secs, _, desc = cpu_forward_seconds()
+    line["cpu_baseline"] = {"value": n_low / secs, "unit": "tokens/s", "cores": torch.get_num_threads(),
+                            "kind": "port", "sample": desc}
     print(json.dumps(line), flush=True)
 
 
@@ -820,6 +1082,7 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-extras", action="store_true", help="headline only (no cfg2/cfg4/cfg5 extras)")
     ap.add_argument("--workload", choices=["stack", "stack_w8a8", "block", "attention", "attention262k", "conv",
                                            "forward", "vae"], default="stack")
     args = ap.parse_args()

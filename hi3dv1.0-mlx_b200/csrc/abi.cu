@@ -77,9 +77,35 @@ int encode_tmap(CUtensorMap* map, CUtensorMapDataType type, int rank, const void
   return HI3D_OK;
 }
 
+// One thread waits on an mbarrier that nothing arrives at; the bounded wait
+// gives up after `limit_ns`, records HI3D_ERR_DEVICE_TIMEOUT at site
+// kSiteWaitSelftest and the kernel returns normally.
+constexpr int kSiteWaitSelftest = 900;
+
+__global__ void wait_timeout_selftest_kernel(uint64_t limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) mbar_wait_slow(&bar, 0, &abort, kSiteWaitSelftest, limit_ns);
+  __syncthreads();
+}
+
 }  // namespace hi3d
 
 using namespace hi3d;
+
+extern "C" int hi3d_wait_timeout_selftest(int64_t limit_ns, void* stream) {
+  if (limit_ns < 1000 || limit_ns > 1000000000)
+    return set_error(HI3D_ERR_INVALID_ARGUMENT, "wait_timeout_selftest: limit %lld ns outside [1e3, 1e9]",
+                     (long long)limit_ns);
+  wait_timeout_selftest_kernel<<<1, 32, 0, as_stream(stream)>>>((uint64_t)limit_ns);
+  return check_launch("wait_timeout_selftest");
+}
 
 extern "C" int hi3d_version(void) { return 100; }
 

@@ -134,7 +134,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // On time-out the first failing site is recorded in the device status word.
 // The spin loop is out of line so that the common case (phase already
 // complete, or completing within one suspended try_wait) costs one try_wait.
-static __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, volatile int* abort, int where) {
+// `limit_ns` is kWaitNs in every kernel of the library; hi3d_wait_timeout_selftest
+// passes a short one to show that a wait which runs out reports and returns.
+static __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, volatile int* abort, int where,
+                                                   uint64_t limit_ns = kWaitNs) {
   uint64_t t0 = 0;
   for (uint32_t i = 0; i < kSpinLimit; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
@@ -143,7 +146,7 @@ static __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parit
       const uint64_t now = global_ns();
       if (t0 == 0)
         t0 = now;
-      else if (now - t0 > kWaitNs)
+      else if (now - t0 > limit_ns)
         break;
     }
   }

@@ -170,6 +170,9 @@ extern "C" int hi3d_sharded_attn_workspace_size(void* comm, int64_t s_rows, int 
                                                 int64_t* bytes) {
   if (!comm || !bytes || s_rows < 0 || heads <= 0)
     return set_error(HI3D_ERR_INVALID_ARGUMENT, "sharded_attn_workspace_size: bad arguments");
+  if (head_dim != 64 && head_dim != 96 && head_dim != 128)
+    return set_error(HI3D_ERR_UNSUPPORTED, "sharded_attn_workspace_size: head_dim %d (supported: 64, 96, 128)",
+                     head_dim);
   const Comm* c = static_cast<const Comm*>(comm);
   const Plan p = make_plan(c->rank, c->world, s_rows, heads, head_dim);
   const int64_t po = part_bytes(p.slots, s_rows, heads, head_dim);
@@ -182,6 +185,8 @@ extern "C" int hi3d_sharded_attn(void* comm, const void* q, const void* k, const
                                  void* workspace, int64_t workspace_bytes, void* stream) {
   if (!comm || !q || !k || !v || !k_all || !v_all || !out || s_rows < 0 || heads <= 0)
     return set_error(HI3D_ERR_INVALID_ARGUMENT, "sharded_attn: bad arguments");
+  if (head_dim != 64 && head_dim != 96 && head_dim != 128)
+    return set_error(HI3D_ERR_UNSUPPORTED, "sharded_attn: head_dim %d (supported: 64, 96, 128)", head_dim);
   if (dtype != HI3D_F16 && dtype != HI3D_BF16)
     return set_error(HI3D_ERR_INVALID_ARGUMENT, "sharded_attn: dtype must be f16 or bf16");
   Comm* c = static_cast<Comm*>(comm);

@@ -26,6 +26,9 @@ namespace hi3d {
 namespace sparse {
 
 constexpr uint64_t kEmpty = ~0ull;
+// device status sites of the hash build (`where` of hi3d_device_status; `detail` = row)
+constexpr int kSiteCoordRange = 210;  // a coordinate outside [0, 2^21)
+constexpr int kSiteTableFull = 211;   // no free slot (cannot happen at load <= 0.5)
 constexpr int kCoordBits = 21;
 constexpr int kCoordMax = (1 << kCoordBits) - 1;
 
@@ -48,7 +51,10 @@ __global__ void hash_insert_kernel(const int32_t* __restrict__ coords, int64_t n
   if (i >= n) return;
   const int x = coords[3 * i], y = coords[3 * i + 1], z = coords[3 * i + 2];
   if (x < 0 || y < 0 || z < 0 || x > kCoordMax || y > kCoordMax || z > kCoordMax) {
+    // the row is left out of the table (its neighbours see it as absent) and the
+    // first such row is reported through hi3d_device_status
     atomicExch(overflow, 2);
+    report_error(HI3D_ERR_INVALID_ARGUMENT, kSiteCoordRange, (int)i);
     return;
   }
   const uint64_t key = pack_key(x, y, z);
@@ -64,6 +70,7 @@ __global__ void hash_insert_kernel(const int32_t* __restrict__ coords, int64_t n
     slot = (slot + 1) & mask;
   }
   atomicExch(overflow, 1);
+  report_error(HI3D_ERR_CAPACITY, kSiteTableFull, (int)i);
 }
 
 __global__ void hash_query_kernel(const int32_t* __restrict__ q, int64_t nq, int stride, const uint64_t* __restrict__ keys,
@@ -593,26 +600,40 @@ static_assert(2 * (uint64_t)HI3D_NEIGHBOUR_MAP_NOALLOC_MAX_VOXELS <= kNoAllocCap
 // keys [cap] u64 at 0, vals [cap] i32 at kNoAllocValsOff, overflow flag at kNoAllocFlagOff
 static __device__ __align__(256) uint8_t g_nmap_scratch[kNoAllocBytes];
 
-// In host code `g_nmap_scratch` names a host-side stand-in, not device memory;
-// its device address is looked up once per device and cached here.
+// In host code `g_nmap_scratch` names a host-side stand-in, not device memory.
+// The device address belongs to the context current at the lookup (it changes
+// after cudaDeviceReset, and differs under a driver-API context other than the
+// primary one), so every call outside stream capture looks it up again in the
+// current context; that is a host-side table lookup once the module is loaded.
+// The last address per device is kept only for calls made while `st` is
+// capturing, where the lookup is not attempted.
 constexpr int kMaxDevices = 64;
 static std::mutex g_nmap_mu;
 static uint8_t* g_nmap_ptr[kMaxDevices] = {};
 
-static int nmap_scratch(uint8_t** out) {
+static int nmap_scratch(cudaStream_t st, uint8_t** out) {
   int dev = -1;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return set_error(HI3D_ERR_CUDA, "neighbour_map_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
   if (dev < 0 || dev >= kMaxDevices)
     return set_error(HI3D_ERR_UNSUPPORTED, "neighbour_map_noalloc: device ordinal %d above %d", dev, kMaxDevices - 1);
+  cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
+  e = cudaStreamIsCapturing(st, &capture);
+  if (e != cudaSuccess)
+    return set_error(HI3D_ERR_CUDA, "neighbour_map_noalloc: cudaStreamIsCapturing: %s", cudaGetErrorString(e));
   std::lock_guard<std::mutex> lock(g_nmap_mu);
-  if (!g_nmap_ptr[dev]) {
+  if (capture == cudaStreamCaptureStatusNone) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_nmap_scratch);
     if (e != cudaSuccess)
       return set_error(HI3D_ERR_CUDA, "neighbour_map_noalloc: cudaGetSymbolAddress on device %d: %s", dev,
                        cudaGetErrorString(e));
     g_nmap_ptr[dev] = static_cast<uint8_t*>(p);
+  } else if (!g_nmap_ptr[dev]) {
+    return set_error(HI3D_ERR_INVALID_ARGUMENT,
+                     "neighbour_map_noalloc: first call on device %d made during stream capture; "
+                     "make one call on this device before capturing",
+                     dev);
   }
   *out = g_nmap_ptr[dev];
   return HI3D_OK;
@@ -636,10 +657,10 @@ extern "C" int hi3d_neighbour_map_build_noalloc(const int32_t* coords, int64_t n
     query = coords;
     nq = n;
   }
-  uint8_t* ws = nullptr;
-  int rc = nmap_scratch(&ws);
-  if (rc) return rc;
   cudaStream_t st = as_stream(stream);
+  uint8_t* ws = nullptr;
+  int rc = nmap_scratch(st, &ws);
+  if (rc) return rc;
   const uint32_t cap = hash_capacity(n);  // <= kNoAllocCap by the limit above
   uint64_t* keys = reinterpret_cast<uint64_t*>(ws);
   int32_t* vals = reinterpret_cast<int32_t*>(ws + kNoAllocValsOff);

@@ -55,6 +55,7 @@ SIGNATURES: dict[str, tuple] = {
     "hi3d_version": (_i32, []),
     "hi3d_last_error_string": (ctypes.c_char_p, []),
     "hi3d_device_status": (_i32, [ctypes.POINTER(_i32)] * 4 + [_i32]),
+    "hi3d_wait_timeout_selftest": (_i32, [_i64, _c_void_p]),
     "hi3d_layer_norm_modulate": (_i32, [_c_void_p, _c_void_p, _i64, _i64, _f32, _c_void_p, _c_void_p, _c_void_p,
                                         _c_void_p, _i64, _i64, _i32, _c_void_p]),
     "hi3d_qkv_rope_rms": (_i32, [_c_void_p] * 8 + [_i64, _i64, _i32, _i32, _i32, _i32, _c_void_p]),

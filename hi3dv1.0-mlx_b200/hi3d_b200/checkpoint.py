@@ -75,7 +75,17 @@ def save_weights(path: str | Path, weights: dict, metadata: dict[str, str] | Non
 
 def check_precision(tensors: dict, metadata: dict, precision: Precision) -> None:
     """The reference's checks (transformer.py:291-300): a ``hi3d-w8a8-h64`` file needs the W8A8
-    GEMM mode and an fp16 torso; the W8A8 mode needs such a file."""
+    GEMM mode and an fp16 torso; the W8A8 mode needs such a file.
+
+    Any other pre-quantized file is the reference's affine group-quantized weight-only format
+    (a ``layout`` metadata entry and ``*.scales``/``*.biases`` tensors, transformer.py:296-298,
+    consumed by MLX ``quantized_matmul``); it is not supported here and is rejected by name
+    instead of being read as dense weights."""
+    if metadata.get("format") != W8A8_FORMAT and (
+            "layout" in metadata or any(k.endswith((".scales", ".biases")) for k in tensors)):
+        raise NotImplementedError(
+            "affine group-quantized (weight-only INT8/INT4 'layout') checkpoints are not supported; "
+            "use the original fp16/fp32 safetensors or a hi3d-w8a8-h64 file")
     if metadata.get("format") == W8A8_FORMAT:
         if precision.gemm != "w8a8" or precision.dtype != torch.float16:
             raise ValueError("W8A8 weights require the w8a8 GEMM mode and fp16 torso")

@@ -36,12 +36,102 @@ def gather_rows(local: torch.Tensor, group=None, out: torch.Tensor | None = None
     return (out, work) if async_op else out
 
 
+class PhaseTimer:
+    """CUDA events at the phase boundaries of the sharded block, on the compute stream: the
+    time between consecutive marks is charged to the phase named by the later mark.  Used by
+    the benchmark's per-phase breakdown; None (the default) records nothing."""
+
+    def __init__(self):
+        self.marks: list[tuple[str, torch.cuda.Event]] = []
+
+    def mark(self, name: str) -> None:
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        self.marks.append((name, e))
+
+    def totals(self) -> dict[str, float]:
+        """Milliseconds per phase, summed over everything recorded (synchronises)."""
+        torch.cuda.synchronize()
+        out: dict[str, float] = {}
+        for (_, e0), (name, e1) in zip(self.marks, self.marks[1:]):
+            if name != "start":
+                out[name] = out.get(name, 0.0) + e0.elapsed_time(e1)
+        return out
+
+
+def sharded_self_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float, group=None,
+                           kv_buffers: tuple[torch.Tensor, torch.Tensor] | None = None,
+                           mark=None) -> torch.Tensor:
+    """Self-attention of this rank's query rows over the keys of every rank of ``group``, which
+    hold consecutive slices of one sequence in rank order.  ``q [1, S, H, D]`` (token-major),
+    ``k, v [S, H, D]``; returns ``[1, S, H * D]``.
+
+    K and V are all-gathered (NCCL over NVLink) while this rank attends its own keys; the keys
+    before and after the own slice are attended once the gather is complete, and the partial
+    results are merged by their log-sum-exp weights (exact: softmax rows never cross ranks).
+    ``mark`` (a :class:`PhaseTimer` method) receives the phase boundaries."""
+    mark = mark or (lambda name: None)
+    t_local, heads, d = k.shape
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    if kv_buffers is None:
+        kv_buffers = tuple(torch.empty((world * t_local, heads, d), dtype=k.dtype, device=k.device) for _ in range(2))
+    k_all, v_all = kv_buffers
+    _, hk = gather_rows(k, group, out=k_all, async_op=True)
+    _, hv = gather_rows(v, group, out=v_all, async_op=True)
+    bhnd = lambda t: t.permute(1, 0, 2)[None]  # [rows, H, D] token-major -> [1, H, rows, D] view
+    key_sets = [(0, rank * t_local), ((rank + 1) * t_local, world * t_local)]
+    splits = [attention.auto_key_splits(t_local, t_local, heads, d, device=k.device)]
+    splits += [attention.auto_key_splits(t_local, hi - lo, heads, d, device=k.device) for lo, hi in key_sets if hi > lo]
+    parts = attention.AttentionParts(q, scale, sum(splits), q_layout="bnhd")
+    parts.add(bhnd(k), bhnd(v), splits[0])
+    mark("attention")
+    hk.wait()
+    hv.wait()
+    mark("kv_gather_wait")
+    i = 1
+    for lo, hi in key_sets:
+        if hi > lo:
+            parts.add(bhnd(k_all[lo:hi]), bhnd(v_all[lo:hi]), splits[i])
+            i += 1
+    mark("attention")
+    return parts.merge()
+
+
+def object_group(objects: int, group=None):
+    """For ``objects`` equal packed sequences split into contiguous slices over the ranks of
+    ``group``: the subgroup of the ranks that share this rank's object when there are more ranks
+    than objects (each object over ``world / objects`` ranks), or None when every rank holds
+    whole objects and self-attention needs no exchange.  Every rank of ``group`` must call this
+    (subgroup creation is collective)."""
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    if world <= objects:
+        if objects % world:
+            raise ValueError(f"{objects} objects do not split evenly over {world} ranks")
+        return None
+    if world % objects:
+        raise ValueError(f"{world} ranks do not split evenly over {objects} objects")
+    per = world // objects
+    ranks = dist.get_process_group_ranks(group) if group is not None else list(range(world))
+    mine = None
+    for o in range(objects):
+        sub = dist.new_group(ranks[o * per:(o + 1) * per])
+        if o == rank // per:
+            mine = sub
+    return mine
+
+
 def block_forward_sharded(w: dict, x: torch.Tensor, mod: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
                           ck: torch.Tensor, cv: torch.Tensor, heads: int, group=None,
-                          kv_buffers: tuple[torch.Tensor, torch.Tensor] | None = None) -> torch.Tensor:
-    """One block on this rank's rows ``x [T/P, C]`` (updated in place) of a single object."""
+                          kv_buffers: tuple[torch.Tensor, torch.Tensor] | None = None,
+                          timer: PhaseTimer | None = None) -> torch.Tensor:
+    """One block on this rank's rows ``x [T/P, C]`` (updated in place) of a single object.
+    ``timer`` marks the phases (projections, own-key attention, exposed K/V gather wait, the
+    other keys' attention, merge, cross-attention, MLP)."""
+    mark = timer.mark if timer is not None else (lambda name: None)
+    mark("start")
     t_local, c = x.shape
-    world = dist.get_world_size(group)
     d = c // heads
     scale = d ** -0.5
     dt = x.dtype
@@ -49,38 +139,23 @@ def block_forward_sharded(w: dict, x: torch.Tensor, mod: torch.Tensor, cos: torc
 
     h = kernels.layer_norm_modulate(x, 1e-6, scale=scale_msa, shift=shift_msa)
     q, k, v = qkv_rope(h, w, cos, sin, 1, heads, d, token_major=True)
-    if kv_buffers is None:
-        kv_buffers = tuple(torch.empty((world * t_local, heads, d), dtype=dt, device=x.device) for _ in range(2))
-    k_all, v_all = kv_buffers
-    _, hk = gather_rows(k[0], group, out=k_all, async_op=True)
-    _, hv = gather_rows(v[0], group, out=v_all, async_op=True)
-    # Attend to this rank's own keys while the others are being gathered, then to the keys
-    # before and after the local shard; the partials are merged by their log-sum-exp weights.
-    rank = dist.get_rank(group)
-    bhnd = lambda t: t.permute(1, 0, 2)[None]  # [rows, H, D] token-major -> [1, H, rows, D] view
-    key_sets = [(0, rank * t_local), ((rank + 1) * t_local, world * t_local)]
-    splits = [attention.auto_key_splits(t_local, t_local, heads, d, device=x.device)]
-    splits += [attention.auto_key_splits(t_local, hi - lo, heads, d, device=x.device) for lo, hi in key_sets if hi > lo]
-    parts = attention.AttentionParts(q, scale, sum(splits), q_layout="bnhd")
-    parts.add(bhnd(k[0]), bhnd(v[0]), splits[0])
-    hk.wait()
-    hv.wait()
-    i = 1
-    for lo, hi in key_sets:
-        if hi > lo:
-            parts.add(bhnd(k_all[lo:hi]), bhnd(v_all[lo:hi]), splits[i])
-            i += 1
-    a = parts.merge()
+    mark("projections")
+    a = sharded_self_attention(q, k[0], v[0], scale, group, kv_buffers, mark)
+    mark("merge")
     linear(a[0], w, "self_attn.to_out", epilogue="residual", residual=x, gate=gate_msa)
+    mark("projections")
 
     h = kernels.layer_norm_modulate(x, 1e-6, weight=w["norm2.weight"], bias=w["norm2.bias"])
     qc = linear(h, w, "cross_attn.to_q").view(1, t_local, heads, d)
+    mark("projections")
     o = attention.flash_attention(qc, ck, cv, scale, q_layout="bnhd")[0]
+    mark("cross_attention")
     linear(o, w, "cross_attn.to_out", epilogue="residual", residual=x)
 
     h = kernels.layer_norm_modulate(x, 1e-6, scale=scale_mlp, shift=shift_mlp)
     h = linear(h, w, "mlp.mlp.0", epilogue="gelu")
     linear(h, w, "mlp.mlp.2", epilogue="residual", residual=x, gate=gate_mlp)
+    mark("projections")
     return x
 
 
@@ -94,7 +169,7 @@ class ShardedBlockStack:
         self._kv = None
 
     def __call__(self, x_local: torch.Tensor, mod: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
-                 kvs: list[tuple[torch.Tensor, torch.Tensor]]) -> torch.Tensor:
+                 kvs: list[tuple[torch.Tensor, torch.Tensor]], timer: PhaseTimer | None = None) -> torch.Tensor:
         x = x_local.clone()
         t_local, c = x.shape
         world = dist.get_world_size(self.group)
@@ -102,7 +177,8 @@ class ShardedBlockStack:
         if self._kv is None or self._kv[0].shape != shape or self._kv[0].device != x.device:
             self._kv = tuple(torch.empty(shape, dtype=x.dtype, device=x.device) for _ in range(2))
         for i, w in enumerate(self.weights):
-            block_forward_sharded(w, x, mod, cos, sin, kvs[i][0], kvs[i][1], self.heads, self.group, self._kv)
+            block_forward_sharded(w, x, mod, cos, sin, kvs[i][0], kvs[i][1], self.heads, self.group, self._kv,
+                                  timer=timer)
         return x
 
 

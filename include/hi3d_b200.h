@@ -54,6 +54,14 @@ HI3D_API const char* hi3d_last_error_string(void);
  * reset != 0 clears it afterwards.  Synchronises the current device. */
 HI3D_API int hi3d_device_status(int* code, int* where, int* block, int* detail, int reset);
 
+/* No counterpart in the reference (it has no device-side waits): a check of the library's
+ * time-out path.  Launches one CTA whose thread waits on an mbarrier that nothing arrives at,
+ * through the same bounded wait every kernel of the library uses, but with a limit of
+ * limit_ns (1e3 .. 1e9 ns) instead of the library's 2 s.  The kernel returns normally; the
+ * status word then holds HI3D_ERR_DEVICE_TIMEOUT with where = 900, and the context stays
+ * usable. */
+HI3D_API int hi3d_wait_timeout_selftest(int64_t limit_ns, void* stream);
+
 /* ---- LayerNorm32 + adaLN modulation ------------------------------------- */
 /* Replaces kernels.layer_norm_modulate (src/hi3d_mac/mlx_backend/kernels.py:206-237,
  * kernel :162-201) and upstream LayerNorm32 (src/sparc3d/nn/norm.py:12-17).
@@ -247,7 +255,10 @@ HI3D_API int hi3d_neighbour_map_workspace_size(int64_t n, int64_t* bytes);
  * coords [n, 3] int32 (x, y, z) in [0, 2^21); query [nq, 3] (NULL = coords, nq ignored);
  * table [nq, 27] int32: table[o, k] = row of coords equal to query[o] * stride + d_k, or n
  * when absent, d_k = (k / 9 - 1, k / 3 % 3 - 1, k % 3 - 1).  stride 1 (submanifold) or 2
- * (query = downsampled coordinates).  Duplicate coordinates resolve to the last row. */
+ * (query = downsampled coordinates).  Duplicate coordinates resolve to the last row.
+ * A coords row outside [0, 2^21) is left out of the table (its neighbours see it as absent)
+ * and reported without a host synchronisation: hi3d_device_status then gives
+ * HI3D_ERR_INVALID_ARGUMENT, where = 210, detail = the first such row seen. */
 HI3D_API int hi3d_neighbour_map_build(const int32_t* coords, int64_t n, const int32_t* query, int64_t nq,
                                       int stride, int32_t* table, void* workspace, int64_t workspace_bytes,
                                       void* stream);

@@ -613,73 +613,3 @@ def sample_f32(w: dict, noise: np.ndarray, coords: np.ndarray, cond: np.ndarray,
         else:
             x = (x - dt * v1).astype(F32)
     return x
-
-
-# ----------------------------------------------------------------------------- CPU baseline timing
-
-
-def block_seconds_sampled(w: dict, x: np.ndarray, mod: np.ndarray, cos: np.ndarray, sin: np.ndarray,
-                          ctx: np.ndarray, heads: int, sample: int, seed: int = 0) -> tuple[float, dict]:
-    """Estimated CPU seconds of one fp32 block over all ``T`` tokens of one object, from a row sample.
-
-    Keys and values of self-attention need every token, so the K/V side (LN-modulate, the K/V
-    columns of the QKV GEMM, RoPE + norm of K) runs on all ``T`` rows and is timed in full.
-    Every per-query-row step (the Q projection, attention of the query rows against all keys,
-    output projection, cross-attention, both LayerNorms, the MLP) runs on ``sample`` random rows
-    and its time is scaled by ``T / sample``.  Same arithmetic as :func:`block_forward_f32`.
-    Returns ``(seconds, phase_seconds)``.
-    """
-    import time
-
-    f = np.float32
-    t, c = x.shape
-    d = c // heads
-    rows = np.sort(np.random.default_rng(seed).choice(t, sample, replace=False))
-    parts = (w["modulation"].astype(f) + mod.astype(f)).reshape(6, c)
-    shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp = parts
-    W = {k: v.astype(f) for k, v in w.items()}
-    xf = x.astype(f)
-
-    def rope_norm(z, g):
-        z = z.reshape(z.shape[0], heads, d // 2, 2)
-        cc, ss = cos_r[:, None, :], sin_r[:, None, :]
-        re = z[..., 0] * cc - z[..., 1] * ss
-        im = z[..., 0] * ss + z[..., 1] * cc
-        y = np.stack([re, im], -1).reshape(z.shape[0], heads, d)
-        return y / np.maximum(np.linalg.norm(y, axis=-1, keepdims=True), 1e-12) * W[g] * f(math.sqrt(d))
-
-    t0 = time.perf_counter()
-    h = layer_norm32_f32(xf) * (1 + scale_msa) + shift_msa
-    wk, wv = W["self_attn.to_qkv.weight"][c:2 * c], W["self_attn.to_qkv.weight"][2 * c:]
-    bk, bv = W["self_attn.to_qkv.bias"][c:2 * c], W["self_attn.to_qkv.bias"][2 * c:]
-    cos_r, sin_r = cos, sin
-    k = rope_norm(h @ wk.T + bk, "self_attn.k_rms_norm.gamma")
-    v = (h @ wv.T + bv).reshape(t, heads, d)
-    kv_seconds = time.perf_counter() - t0
-
-    t1 = time.perf_counter()
-    cos_r, sin_r = cos[rows], sin[rows]
-    hq = h[rows]
-    q = rope_norm(hq @ W["self_attn.to_qkv.weight"][:c].T + W["self_attn.to_qkv.bias"][:c], "self_attn.q_rms_norm.gamma")
-    a = np.empty((sample, heads, d), f)
-    for hh in range(heads):
-        s = q[:, hh] @ k[:, hh].T * f(d ** -0.5)
-        p = np.exp(s - s.max(-1, keepdims=True))
-        a[:, hh] = (p / p.sum(-1, keepdims=True)) @ v[:, hh]
-    xs = xf[rows] + (a.reshape(sample, c) @ W["self_attn.to_out.weight"].T + W["self_attn.to_out.bias"]) * gate_msa
-    h2 = layer_norm32_f32(xs, W["norm2.weight"], W["norm2.bias"])
-    qc = (h2 @ W["cross_attn.to_q.weight"].T + W["cross_attn.to_q.bias"]).reshape(sample, heads, d)
-    kv = (ctx.astype(f) @ W["cross_attn.to_kv.weight"].T + W["cross_attn.to_kv.bias"]).reshape(-1, 2, heads, d)
-    o = np.empty((sample, heads, d), f)
-    for hh in range(heads):
-        s = qc[:, hh] @ kv[:, 0, hh].T * f(d ** -0.5)
-        p = np.exp(s - s.max(-1, keepdims=True))
-        o[:, hh] = (p / p.sum(-1, keepdims=True)) @ kv[:, 1, hh]
-    xs = xs + o.reshape(sample, c) @ W["cross_attn.to_out.weight"].T + W["cross_attn.to_out.bias"]
-    h3 = layer_norm32_f32(xs) * (1 + scale_mlp) + shift_mlp
-    m = h3 @ W["mlp.mlp.0.weight"].T + W["mlp.mlp.0.bias"]
-    m = 0.5 * m * (1.0 + np.tanh(f(math.sqrt(2.0 / math.pi)) * (m + f(0.044715) * m * m * m)))
-    xs = xs + (m @ W["mlp.mlp.2.weight"].T + W["mlp.mlp.2.bias"]) * gate_mlp
-    row_seconds = time.perf_counter() - t1
-    total = kv_seconds + row_seconds * t / sample
-    return total, {"kv_all_rows": kv_seconds, "query_rows_sampled": row_seconds, "sample_rows": sample, "rows": t}

@@ -1,9 +1,9 @@
 """Generate the golden fixtures in this directory from the reference's own code.
 
-Run once in a container that has the reference source tree (read-only) at
-``$HI3D_REFERENCE`` (default ``/root/reference``):
+Run once in a container that has the reference source tree (read-only); name its
+root in ``HI3D_REFERENCE`` (required):
 
-    python tests/golden/make_golden.py
+    HI3D_REFERENCE=<reference checkout> python tests/golden/make_golden.py
 
 It imports the reference's runnable CPU code only:
 
@@ -27,7 +27,9 @@ from pathlib import Path
 import numpy as np
 
 HERE = Path(__file__).resolve().parent
-REF = Path(os.environ.get("HI3D_REFERENCE", "/root/reference")) / "src"
+if not os.environ.get("HI3D_REFERENCE"):
+    raise SystemExit("set HI3D_REFERENCE to the root of the reference source tree")
+REF = Path(os.environ["HI3D_REFERENCE"]) / "src"
 sys.path.insert(0, str(HERE.parents[1] / "hi3dv1.0-mlx_b200"))
 
 

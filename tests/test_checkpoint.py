@@ -54,6 +54,15 @@ def test_precision_checks_follow_the_reference():
     checkpoint.check_precision({}, {}, Precision())
 
 
+def test_group_quantized_weight_only_files_are_rejected_by_name():
+    # the reference's affine group-quantized format: 'layout' metadata + .scales/.biases
+    layout = {"layout": json.dumps({"blocks.0.mlp.mlp.0": [64, 8]})}
+    with pytest.raises(NotImplementedError, match="group-quantized"):
+        checkpoint.check_precision({"blocks.0.mlp.mlp.0.weight": np.zeros(2, np.uint32)}, layout, Precision())
+    with pytest.raises(NotImplementedError, match="group-quantized"):
+        checkpoint.check_precision({"blocks.0.mlp.mlp.0.scales": np.ones(2, np.float16)}, {}, Precision())
+
+
 @pytest.mark.gpu
 def test_checkpoints_drive_the_model(tmp_path):
     from test_oracle_golden import forward_case

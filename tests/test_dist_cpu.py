@@ -68,6 +68,28 @@ def _dying_rank(rank, world, port):
     os._exit(0)
 
 
+def _object_groups(rank, world, port):
+    """cfg4's object-aware sharding: 4 ranks over 2 objects pair up; over 4 objects, each rank
+    owns one object and needs no exchange."""
+    _init(rank, world, port)
+    from hi3d_b200.dist import gather_rows, object_group
+
+    assert object_group(4) is None
+    sub = object_group(2)
+    assert dist.get_world_size(sub) == 2
+    got = gather_rows(torch.tensor([[float(rank)]]), group=sub)
+    mate = rank ^ 1
+    assert got.flatten().tolist() == [float(min(rank, mate)), float(max(rank, mate))]
+    with pytest.raises(ValueError):
+        object_group(3)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_object_groups_pair_the_ranks_of_one_object():
+    mp.spawn(_object_groups, args=(4, _free_port()), nprocs=4, join=True)
+
+
 def test_query_sharded_attention_matches_unsharded():
     mp.spawn(_sharded_attention, args=(2, _free_port()), nprocs=2, join=True)
 

@@ -82,6 +82,23 @@ def test_block_forward_matches_upstream_module():
     assert rel_l2(y, g["y"]) < 1e-5
 
 
+def test_torch_block_port_matches_upstream_module():
+    """The torch restatement of the reference's CPU path (timed as the CPU baseline, and the
+    checker of the full-size parity tests) against the upstream module, in full and on a row
+    subset (keys and values still from every token)."""
+    from oracle import torch_block
+
+    g = _load("block")
+    w = {k[2:]: g[k] for k in g.files if k.startswith("w:")}
+    lens = [int(n) for n in g["lens"]]
+    cos, sin = ops.rope_tables(g["coords"][:, 1:], 64)
+    y = torch_block.block_forward(w, g["x"], g["mod"], cos, sin, g["ctx"], 2, seqlens=lens).numpy()
+    assert rel_l2(y, g["y"]) < 1e-5
+    rows = np.array([0, 3, 59, 60, 61, 119])
+    yr = torch_block.block_forward(w, g["x"], g["mod"], cos, sin, g["ctx"], 2, seqlens=lens, rows=rows).numpy()
+    assert rel_l2(yr, g["y"][rows]) < 1e-5
+
+
 def forward_case():
     """Inputs, weights and the upstream velocity of the whole-transformer fixture."""
     from hi3d_b200 import synthetic
