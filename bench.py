@@ -658,6 +658,13 @@ def run_ours(args) -> None:
         barrier()
     launches = _lib.LAUNCHES[0]
     attn = attention.TIMER.stop()
+    # host time to enqueue one step onto an idle stream: below the device step time, the
+    # step is device-bound
+    h0 = time.perf_counter()
+    run(x_dev)
+    host_ms = (time.perf_counter() - h0) * 1e3
+    torch.cuda.synchronize()
+    barrier()
     ms = _max_over_ranks(start.elapsed_time(end), world, dev)
     ms_per_step = ms / args.steps
     value = nblocks * T_TOKENS / (ms_per_step / 1e3)
@@ -704,6 +711,7 @@ def run_ours(args) -> None:
         "gpu_launches": launches,
         "clocks": clocks.summary(),
         "attention_tflops": achieved,
+        "host_enqueue_ms_per_step": host_ms,
     }
     extra = args.workload == "stack" and not args.no_extras
     if world > 1:

@@ -39,36 +39,11 @@ constexpr int kRowsPerTile = 128;
 #define HI3D_ATTN_EMU_PAIRS 4
 #endif
 constexpr int kEmuPairs = HI3D_ATTN_EMU_PAIRS;
-// fp16 kernels: exponentials per 16-pair chunk evaluated two at a time by
-// ex2.approx.f16x2 on an fp16-rounded argument (the last pairs of the chunk;
-// an even count); their P is produced packed, and their row-sum terms are
-// added pairwise in fp16 before the fp32 accumulation.
-#ifndef HI3D_ATTN_H2_PAIRS
-#define HI3D_ATTN_H2_PAIRS 0
-#endif
-#ifndef HI3D_ATTN_H2_EMU_PAIRS
-#define HI3D_ATTN_H2_EMU_PAIRS 0
-#endif
-static_assert(HI3D_ATTN_H2_PAIRS % 2 == 0 && HI3D_ATTN_H2_PAIRS + HI3D_ATTN_H2_EMU_PAIRS <= 16, "pair split");
 // Row maximum growth (log2 units) tolerated before O and l are rescaled.
 #ifndef HI3D_ATTN_RESCALE_LOG2
 #define HI3D_ATTN_RESCALE_LOG2 8.0f
 #endif
 constexpr float kRescaleLog2 = HI3D_ATTN_RESCALE_LOG2;
-
-__device__ __forceinline__ uint32_t ex2_h2(uint32_t x) {
-  uint32_t y;
-  asm("ex2.approx.f16x2 %0, %1;" : "=r"(y) : "r"(x));
-  return y;
-}
-__device__ __forceinline__ uint32_t hadd2_u(uint32_t a, uint32_t b) {
-  __half2 r = __hadd2(*reinterpret_cast<const __half2*>(&a), *reinterpret_cast<const __half2*>(&b));
-  return *reinterpret_cast<uint32_t*>(&r);
-}
-__device__ __forceinline__ uint64_t h2_to_f2(uint32_t a) {
-  const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&a));
-  return f2_pack(f.x, f.y);
-}
 
 template <int D>
 struct Cfg {
@@ -356,8 +331,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (warp_grow) alpha = grow ? ex2_approx(m_run - m_new) : 1.0f;
       const uint64_t negm = f2_pack(-m_new, -m_new);
       uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};  // four independent packed row-sum chains
-      constexpr int kH2 = std::is_same<T, __half>::value ? HI3D_ATTN_H2_PAIRS : 0;
-      constexpr int kEmu = kH2 > 0 ? HI3D_ATTN_H2_EMU_PAIRS : kEmuPairs;
 #pragma unroll
       for (int c = 0; c < C::BK / 32; ++c) {
         uint32_t pk[16];
@@ -365,14 +338,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int e = 0; e < 16; ++e) {
           const uint64_t sx = f2_pack(__uint_as_float(sv[c * 32 + 2 * e]), __uint_as_float(sv[c * 32 + 2 * e + 1]));
           const uint64_t xx = f2_fma(sx, scale2x2, negm);
-          if (e >= 16 - kH2) {
-            float x0, x1;
-            f2_unpack(xx, x0, x1);
-            pk[e] = ex2_h2(Cvt<T>::pack2(x0, x1));
-            continue;
-          }
           uint64_t pp;
-          if (e < kEmu) {
+          if (e < kEmuPairs) {
             pp = f2_exp2_poly(xx);
           } else {
             float x0, x1;
@@ -383,11 +350,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           float p0, p1;
           f2_unpack(pp, p0, p1);
           pk[e] = Cvt<T>::pack2(p0, p1);
-        }
-#pragma unroll
-        for (int e = 16 - kH2; e < 16; e += 2) {
-          const int a = (e >> 1) & 3;
-          acc[a] = f2_add(acc[a], h2_to_f2(hadd2_u(pk[e], pk[e + 1])));
         }
         // P of block j overwrites P of block j-1: wait until P V of block
         // j-1 has completed (which also makes O final for the correction).

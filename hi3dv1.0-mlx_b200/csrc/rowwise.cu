@@ -57,6 +57,17 @@ __global__ void __launch_bounds__(kLnRowsPerBlock * 32)
                   const float* __restrict__ weight, const float* __restrict__ bias, const T* __restrict__ scale,
                   const T* __restrict__ shift, int64_t rows_per_batch, int64_t mod_stride) {
   const int lane = threadIdx.x & 31;
+  // The fp32 affine parameters are the same for every row: staged once per block in
+  // shared memory ([weight | bias], NCH * 256 each, zero past C), so the per-row
+  // reads are short shared-memory loads instead of L1/L2 round trips.
+  extern __shared__ float ln_wb[];
+  if constexpr (AFFINE) {
+    for (int i = threadIdx.x; i < NCH * 256; i += blockDim.x) {
+      ln_wb[i] = i < C ? weight[i] : 0.f;
+      ln_wb[NCH * 256 + i] = i < C ? bias[i] : 0.f;
+    }
+    __syncthreads();
+  }
   // grid-stride over rows (the grid is sized to whole waves), one warp per row
   for (int64_t row = (int64_t)blockIdx.x * kLnRowsPerBlock + (threadIdx.x >> 5); row < rows;
        row += (int64_t)gridDim.x * kLnRowsPerBlock) {
@@ -118,10 +129,10 @@ __global__ void __launch_bounds__(kLnRowsPerBlock * 32)
       }
       uint64_t wv[4], bv[4];
       if (AFFINE) {
-        const float4 w0 = *reinterpret_cast<const float4*>(weight + base);
-        const float4 w1 = *reinterpret_cast<const float4*>(weight + base + 4);
-        const float4 b0 = *reinterpret_cast<const float4*>(bias + base);
-        const float4 b1 = *reinterpret_cast<const float4*>(bias + base + 4);
+        const float4 w0 = *reinterpret_cast<const float4*>(ln_wb + base);
+        const float4 w1 = *reinterpret_cast<const float4*>(ln_wb + base + 4);
+        const float4 b0 = *reinterpret_cast<const float4*>(ln_wb + NCH * 256 + base);
+        const float4 b1 = *reinterpret_cast<const float4*>(ln_wb + NCH * 256 + base + 4);
         wv[0] = f2_pack(w0.x, w0.y), wv[1] = f2_pack(w0.z, w0.w), wv[2] = f2_pack(w1.x, w1.y),
         wv[3] = f2_pack(w1.z, w1.w);
         bv[0] = f2_pack(b0.x, b0.y), bv[1] = f2_pack(b0.z, b0.w), bv[2] = f2_pack(b1.x, b1.y),
@@ -155,14 +166,15 @@ static void launch_ln(const void* x, void* out, int64_t rows, int C, float eps, 
   T* ot = (T*)out;
   const T* s = (const T*)sc;
   const T* t = (const T*)sh;
+  const size_t wb = (size_t)2 * NCH * 256 * sizeof(float);  // affine parameters in shared memory
   if (act && w)  // the res-block norm1: affine, then SiLU
-    ln_mod_kernel<T, NCH, true, false, true><<<grid, block, 0, st>>>(xt, ot, rows, C, eps, w, b, s, t, rpb, ms);
+    ln_mod_kernel<T, NCH, true, false, true><<<grid, block, wb, st>>>(xt, ot, rows, C, eps, w, b, s, t, rpb, ms);
   else if (act)  // the res-block norm2: modulation, then SiLU
     ln_mod_kernel<T, NCH, false, true, true><<<grid, block, 0, st>>>(xt, ot, rows, C, eps, w, b, s, t, rpb, ms);
   else if (w && sc)
-    ln_mod_kernel<T, NCH, true, true, false><<<grid, block, 0, st>>>(xt, ot, rows, C, eps, w, b, s, t, rpb, ms);
+    ln_mod_kernel<T, NCH, true, true, false><<<grid, block, wb, st>>>(xt, ot, rows, C, eps, w, b, s, t, rpb, ms);
   else if (w)
-    ln_mod_kernel<T, NCH, true, false, false><<<grid, block, 0, st>>>(xt, ot, rows, C, eps, w, b, s, t, rpb, ms);
+    ln_mod_kernel<T, NCH, true, false, false><<<grid, block, wb, st>>>(xt, ot, rows, C, eps, w, b, s, t, rpb, ms);
   else if (sc)
     ln_mod_kernel<T, NCH, false, true, false><<<grid, block, 0, st>>>(xt, ot, rows, C, eps, w, b, s, t, rpb, ms);
   else

@@ -13,9 +13,11 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <chrono>
 #include <cmath>
 #include <cstring>
 #include <mutex>
+#include <thread>
 
 #include "abi.h"
 
@@ -29,6 +31,8 @@ struct NcclApi {
   ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
   ncclResult_t (*group_start)() = nullptr;
   ncclResult_t (*group_end)() = nullptr;
+  ncclResult_t (*comm_get_async_error)(ncclComm_t, ncclResult_t*) = nullptr;
+  ncclResult_t (*comm_abort)(ncclComm_t) = nullptr;
   const char* (*error_string)(ncclResult_t) = nullptr;
   bool ok = false;
 };
@@ -47,8 +51,11 @@ const NcclApi& nccl() {
     api.group_start = reinterpret_cast<decltype(api.group_start)>(dlsym(h, "ncclGroupStart"));
     api.group_end = reinterpret_cast<decltype(api.group_end)>(dlsym(h, "ncclGroupEnd"));
     api.error_string = reinterpret_cast<decltype(api.error_string)>(dlsym(h, "ncclGetErrorString"));
+    api.comm_get_async_error =
+        reinterpret_cast<decltype(api.comm_get_async_error)>(dlsym(h, "ncclCommGetAsyncError"));
+    api.comm_abort = reinterpret_cast<decltype(api.comm_abort)>(dlsym(h, "ncclCommAbort"));
     api.ok = api.get_unique_id && api.comm_init_rank && api.comm_destroy && api.all_gather && api.group_start &&
-             api.group_end && api.error_string;
+             api.group_end && api.error_string && api.comm_get_async_error && api.comm_abort;
   });
   return api;
 }
@@ -57,13 +64,25 @@ int nccl_error(const char* what, ncclResult_t r) {
   return set_error(HI3D_ERR_NCCL, "%s: %s", what, nccl().error_string ? nccl().error_string(r) : "NCCL error");
 }
 
-// A communicator with the side stream and events of the K/V gather.
+// A communicator with the side stream and events of the K/V gather.  `aborted`
+// is set once ncclCommAbort has run (by hi3d_nccl_comm_abort, or by
+// hi3d_nccl_comm_wait on an asynchronous error or at its limit); the
+// communicator then refuses new work and is only destroyed.
 struct Comm {
   ncclComm_t comm = nullptr;
   int rank = 0, world = 1, device = 0;
   cudaStream_t side = nullptr;
   cudaEvent_t inputs_ready = nullptr, gathered = nullptr;
+  bool aborted = false;
 };
+
+int abort_comm(Comm* c) {
+  if (c->aborted) return HI3D_OK;
+  c->aborted = true;
+  ncclResult_t r = nccl().comm_abort(c->comm);
+  c->comm = nullptr;
+  return r == ncclSuccess ? HI3D_OK : nccl_error("ncclCommAbort", r);
+}
 
 // Key splits per query block that fill whole waves of `sms` one-CTA-per-SM blocks:
 // the s minimising ceil(ctas * s / sms) / s, taken only when it beats no split by
@@ -154,10 +173,59 @@ extern "C" int hi3d_nccl_comm_init(const void* id, int world, int rank, void** c
   return HI3D_OK;
 }
 
+extern "C" int hi3d_nccl_comm_check(void* comm) {
+  if (!comm) return set_error(HI3D_ERR_INVALID_ARGUMENT, "nccl_comm_check: null communicator");
+  Comm* c = static_cast<Comm*>(comm);
+  if (c->aborted) return set_error(HI3D_ERR_NCCL, "nccl_comm_check: communicator aborted");
+  ncclResult_t async = ncclSuccess;
+  ncclResult_t r = nccl().comm_get_async_error(c->comm, &async);
+  if (r != ncclSuccess) return nccl_error("ncclCommGetAsyncError", r);
+  if (async != ncclSuccess && async != ncclInProgress) return nccl_error("asynchronous NCCL error", async);
+  return HI3D_OK;
+}
+
+extern "C" int hi3d_nccl_comm_abort(void* comm) {
+  if (!comm) return set_error(HI3D_ERR_INVALID_ARGUMENT, "nccl_comm_abort: null communicator");
+  return abort_comm(static_cast<Comm*>(comm));
+}
+
+extern "C" int hi3d_nccl_comm_wait(void* comm, void* stream, int64_t timeout_ms) {
+  if (!comm || timeout_ms < 0) return set_error(HI3D_ERR_INVALID_ARGUMENT, "nccl_comm_wait: bad arguments");
+  Comm* c = static_cast<Comm*>(comm);
+  if (c->aborted) return set_error(HI3D_ERR_NCCL, "nccl_comm_wait: communicator aborted");
+  cudaStream_t st = as_stream(stream);
+  const auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    // the caller's stream waits on the gather, so its completion covers the side stream's
+    // work of every hi3d_sharded_attn enqueued on it; the side stream is checked as well
+    cudaError_t e1 = cudaStreamQuery(st), e2 = cudaStreamQuery(c->side);
+    if (e1 != cudaSuccess && e1 != cudaErrorNotReady)
+      return set_error(HI3D_ERR_CUDA, "nccl_comm_wait: %s", cudaGetErrorString(e1));
+    if (e2 != cudaSuccess && e2 != cudaErrorNotReady)
+      return set_error(HI3D_ERR_CUDA, "nccl_comm_wait: %s", cudaGetErrorString(e2));
+    if (e1 == cudaSuccess && e2 == cudaSuccess) return HI3D_OK;
+    ncclResult_t async = ncclSuccess;
+    ncclResult_t r = nccl().comm_get_async_error(c->comm, &async);
+    if (r != ncclSuccess || (async != ncclSuccess && async != ncclInProgress)) {
+      const ncclResult_t why = r != ncclSuccess ? r : async;
+      abort_comm(c);
+      return nccl_error("nccl_comm_wait: asynchronous NCCL error, communicator aborted", why);
+    }
+    const auto ms =
+        std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0).count();
+    if (ms >= timeout_ms) {
+      abort_comm(c);
+      return set_error(HI3D_ERR_NCCL, "nccl_comm_wait: work not finished after %lld ms, communicator aborted",
+                       (long long)timeout_ms);
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(100));
+  }
+}
+
 extern "C" int hi3d_nccl_comm_destroy(void* comm) {
   if (!comm) return HI3D_OK;
   Comm* c = static_cast<Comm*>(comm);
-  cudaStreamSynchronize(c->side);
+  if (!c->aborted) cudaStreamSynchronize(c->side);
   if (c->inputs_ready) cudaEventDestroy(c->inputs_ready);
   if (c->gathered) cudaEventDestroy(c->gathered);
   if (c->side) cudaStreamDestroy(c->side);
@@ -187,6 +255,7 @@ extern "C" int hi3d_sharded_attn(void* comm, const void* q, const void* k, const
     return set_error(HI3D_ERR_INVALID_ARGUMENT, "sharded_attn: bad arguments");
   if (head_dim != 64 && head_dim != 96 && head_dim != 128)
     return set_error(HI3D_ERR_UNSUPPORTED, "sharded_attn: head_dim %d (supported: 64, 96, 128)", head_dim);
+  if (static_cast<Comm*>(comm)->aborted) return set_error(HI3D_ERR_NCCL, "sharded_attn: communicator aborted");
   if (dtype != HI3D_F16 && dtype != HI3D_BF16)
     return set_error(HI3D_ERR_INVALID_ARGUMENT, "sharded_attn: dtype must be f16 or bf16");
   Comm* c = static_cast<Comm*>(comm);

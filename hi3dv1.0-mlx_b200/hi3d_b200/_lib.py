@@ -73,6 +73,9 @@ SIGNATURES: dict[str, tuple] = {
     "hi3d_nccl_unique_id": (_i32, [_c_void_p]),
     "hi3d_nccl_comm_init": (_i32, [_c_void_p, _i32, _i32, ctypes.POINTER(_c_void_p)]),
     "hi3d_nccl_comm_destroy": (_i32, [_c_void_p]),
+    "hi3d_nccl_comm_check": (_i32, [_c_void_p]),
+    "hi3d_nccl_comm_wait": (_i32, [_c_void_p, _c_void_p, _i64]),
+    "hi3d_nccl_comm_abort": (_i32, [_c_void_p]),
     "hi3d_sharded_attn_workspace_size": (_i32, [_c_void_p, _i64, _i32, _i32, ctypes.POINTER(_i64)]),
     "hi3d_sharded_attn": (_i32, [_c_void_p] * 7 + [_i64, _i32, _i32, ctypes.c_float, _i32, _c_void_p, _i64,
                                                    _c_void_p]),

@@ -204,6 +204,31 @@ class NcclComm:
                    launched=False)
         self.handle = handle
 
+    def check(self) -> None:
+        """Raise ``RuntimeError`` if NCCL reports an asynchronous error on this communicator."""
+        from . import _lib
+
+        _lib.check(_lib.load().hi3d_nccl_comm_check(self.handle), "nccl_comm_check", launched=False)
+
+    def wait(self, stream=None, timeout_s: float = 30.0) -> None:
+        """Wait on the host for the work enqueued on ``stream`` (default: the current stream) and
+        on the gather's side stream; on an asynchronous NCCL error or after ``timeout_s`` the
+        communicator is aborted (which ends collectives still waiting for a peer) and
+        ``RuntimeError`` is raised."""
+        import torch
+
+        from . import _lib
+
+        st = (stream or torch.cuda.current_stream()).cuda_stream
+        _lib.check(_lib.load().hi3d_nccl_comm_wait(self.handle, st, int(timeout_s * 1000)), "nccl_comm_wait",
+                   launched=False)
+
+    def abort(self) -> None:
+        """Abort the communicator (a peer is known to be gone); it then refuses new work."""
+        from . import _lib
+
+        _lib.check(_lib.load().hi3d_nccl_comm_abort(self.handle), "nccl_comm_abort", launched=False)
+
     def close(self) -> None:
         from . import _lib
 

@@ -185,6 +185,19 @@ HI3D_API int hi3d_flash_attn_merge(const hi3d_attn_args* args, int num_slots, co
 HI3D_API int hi3d_nccl_unique_id(void* id);
 HI3D_API int hi3d_nccl_comm_init(const void* id, int world, int rank, void** comm);
 HI3D_API int hi3d_nccl_comm_destroy(void* comm);
+
+/* Failure handling of the communicator (no counterpart in the reference, which has no
+ * distributed code).  hi3d_nccl_comm_check: HI3D_ERR_NCCL when NCCL reports an asynchronous
+ * error (a peer failed, a network error), without waiting.  hi3d_nccl_comm_wait: waits on the
+ * host, up to timeout_ms, for the work enqueued on `stream` and on the gather's side stream,
+ * polling ncclCommGetAsyncError meanwhile; on an asynchronous error or at the limit it calls
+ * ncclCommAbort (which ends NCCL kernels still waiting for a peer) and returns HI3D_ERR_NCCL.
+ * hi3d_nccl_comm_abort: the same abort, for a caller that learnt on the host (a store, a
+ * heartbeat) that a peer is gone.  An aborted communicator refuses hi3d_sharded_attn and is
+ * only destroyed. */
+HI3D_API int hi3d_nccl_comm_check(void* comm);
+HI3D_API int hi3d_nccl_comm_wait(void* comm, void* stream, int64_t timeout_ms);
+HI3D_API int hi3d_nccl_comm_abort(void* comm);
 HI3D_API int hi3d_sharded_attn_workspace_size(void* comm, int64_t s_rows, int heads, int head_dim, int64_t* bytes);
 HI3D_API int hi3d_sharded_attn(void* comm, const void* q, const void* k, const void* v, void* k_all, void* v_all,
                                void* out, int64_t s_rows, int heads, int head_dim, float scale, int dtype,
@@ -275,9 +288,10 @@ HI3D_API int hi3d_neighbour_map_build(const int32_t* coords, int64_t n, const in
  * GPU that loads the library until the process exits.  A larger n returns HI3D_ERR_CAPACITY;
  * nq is not limited.  Nothing is allocated, at set-up or per call.
  *
- * The first call on a device (the one current when it is made) looks up that device's address
- * of the array; make that first call before any stream capture.  `stream` must belong to the
- * current device.  Every call on a device shares the one array, and each call clears the part
+ * Every call outside stream capture looks up the array's address in the context current at the
+ * call (so a cudaDeviceReset or a driver-API context of its own is followed); a call made while
+ * `stream` is capturing reuses the address of the last call on that device, so make one call
+ * on a device before capturing.  `stream` must belong to the current device.  Every call on a device shares the one array, and each call clears the part
  * it uses before building, so calls in sequence are independent, but calls that overlap on the
  * GPU (on two streams, or from two host threads) race and give wrong tables. */
 #define HI3D_NEIGHBOUR_MAP_NOALLOC_MAX_VOXELS 262144

@@ -92,8 +92,12 @@ def test_24_block_stack_at_4096_tokens():
     for w in blocks:
         ref = torch_block.block_forward(torch_block.weights_f32(w), ref, mod, cos, sin, ctx, 16).numpy()
     assert rel_l2(got, ref) < TOL
+    # The update after 24 blocks is 17 % of |x|.  Storing the residual stream in fp16 after
+    # every block, with the oracle otherwise in fp32, already gives a 5.9e-3 relative error on
+    # it (1.0e-3 on the output) for this case; the kernels' own 16-bit roundings (normalised
+    # rows, projections, P, GELU) come on top.  The bound is 2.5x the storage part.
     xf = x.astype(np.float32)
-    assert rel_l2(got - xf, ref - xf) < 1e-2
+    assert rel_l2(got - xf, ref - xf) < 1.5e-2
 
 
 def test_cfg4_bf16_varlen_attention_on_four_65536_token_objects():
