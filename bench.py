@@ -53,6 +53,9 @@ HEADS = 16
 COND = 1370
 BLOCKS = 24
 GRID, RADIUS, THICK = 64, 24.0, 3.0
+# the released model's block: C = 2112, 22 heads x 96, condition 2917 x 2048
+# (src/sparc3d/models/transformers/config.py:101-111)
+REL_C, REL_HEADS, REL_CC, REL_L = 2112, 22, 2048, 2917
 # whole-transformer workload: fine voxels on a shell in 128^3 (R=48 +-4) -> 34,316 low tokens
 FWD_FINE, FWD_GRID, FWD_RADIUS, FWD_THICK, FWD_IO, FWD_T = 120000, 128, 48.0, 4.0, 256, 0.37
 
@@ -142,27 +145,29 @@ def make_inputs(seed: int = 0):
     return coords, cos, sin, x, mod, cond
 
 
-def device_weights(device, seed: int = 100, blocks: int = BLOCKS) -> list[dict]:
-    """``blocks`` blocks of N(0, 0.02) fp16 weights generated on the device (seeded)."""
+def device_weights(device, seed: int = 100, blocks: int = BLOCKS, c: int = CHANNELS, cc: int = CHANNELS,
+                   heads: int = HEADS) -> list[dict]:
+    """``blocks`` blocks of N(0, 0.02) fp16 weights generated on the device (seeded): hidden
+    width ``c``, condition width ``cc``, ``heads`` heads."""
     import torch
 
     from hi3d_b200.synthetic import BLOCK_LINEARS
 
     g = torch.Generator(device=device).manual_seed(seed)
-    c, d = CHANNELS, CHANNELS // HEADS
+    d = c // heads
     out = []
     for _ in range(blocks):
         w = {}
         for name, i_mult, o_mult in BLOCK_LINEARS:
             w[f"{name}.weight"] = (torch.randn((o_mult * c, i_mult * c), generator=g, device=device) * 0.02).half()
             w[f"{name}.bias"] = (torch.randn(o_mult * c, generator=g, device=device) * 0.02).half()
-        w["cross_attn.to_kv.weight"] = (torch.randn((2 * c, c), generator=g, device=device) * 0.02).half()
+        w["cross_attn.to_kv.weight"] = (torch.randn((2 * c, cc), generator=g, device=device) * 0.02).half()
         w["cross_attn.to_kv.bias"] = (torch.randn(2 * c, generator=g, device=device) * 0.02).half()
         w["modulation"] = torch.randn((1, 6 * c), generator=g, device=device) / c ** 0.5
         w["norm2.weight"] = torch.ones(c, device=device)
         w["norm2.bias"] = torch.zeros(c, device=device)
-        w["self_attn.q_rms_norm.gamma"] = torch.ones((HEADS, d), device=device)
-        w["self_attn.k_rms_norm.gamma"] = torch.ones((HEADS, d), device=device)
+        w["self_attn.q_rms_norm.gamma"] = torch.ones((heads, d), device=device)
+        w["self_attn.k_rms_norm.gamma"] = torch.ones((heads, d), device=device)
         out.append(w)
     return out
 
@@ -225,26 +230,35 @@ def cpu_threads() -> int:
     return n
 
 
-def _cpu_block_inputs(seed: int = 0):
-    from hi3d_b200 import synthetic
+def _cpu_block_inputs(seed: int = 0, released: bool = False):
+    from hi3d_b200 import synthetic, transformer
     from oracle import torch_block
 
-    if "block" not in _CPU_CACHE:
-        coords, cos, sin, x, mod, cond = make_inputs(seed)
-        w = torch_block.weights_f32(synthetic.block_weights(CHANNELS, CHANNELS, HEADS, seed=seed + 5))
-        _CPU_CACHE["block"] = (w, x, mod, cos, sin, cond)
-    return _CPU_CACHE["block"]
+    key = ("block", released)
+    if key not in _CPU_CACHE:
+        if released:
+            coords = synthetic.shell_coords(T_TOKENS, GRID, RADIUS, THICK, seed=seed)
+            cos, sin = transformer.rope_tables(coords, REL_C // REL_HEADS)
+            x = synthetic.features(T_TOKENS, REL_C, seed=seed + 1)
+            mod = synthetic.modulation(REL_C, 0.5, seed=seed + 2).astype(np.float16)
+            cond = synthetic.features(REL_L, REL_CC, seed=seed + 3)
+            w = synthetic.block_weights(REL_C, REL_CC, REL_HEADS, seed=seed + 5)
+        else:
+            coords, cos, sin, x, mod, cond = make_inputs(seed)
+            w = synthetic.block_weights(CHANNELS, CHANNELS, HEADS, seed=seed + 5)
+        _CPU_CACHE[key] = (torch_block.weights_f32(w), x, mod, cos, sin, cond)
+    return _CPU_CACHE[key]
 
 
-def cpu_block_seconds(rows: int | None = None) -> float:
+def cpu_block_seconds(rows: int | None = None, released: bool = False) -> float:
     """Wall seconds of one whole fp32 block of the reference's CPU path over the first ``rows``
-    tokens (all T by default)."""
+    tokens (all T by default); ``released``: at the released model's shape."""
     from oracle import torch_block
 
-    w, x, mod, cos, sin, cond = _cpu_block_inputs()
+    w, x, mod, cos, sin, cond = _cpu_block_inputs(released=released)
     r = slice(0, rows or x.shape[0])
     t0 = time.perf_counter()
-    torch_block.block_forward(w, x[r], mod, cos[r], sin[r], cond, HEADS)
+    torch_block.block_forward(w, x[r], mod, cos[r], sin[r], cond, REL_HEADS if released else HEADS)
     return time.perf_counter() - t0
 
 
@@ -371,7 +385,17 @@ def run_reference(args) -> None:
                 secs.append(time.perf_counter() - t0)
         return r
 
-    if args.workload in ("stack", "stack_w8a8", "block"):
+    if args.workload == "released":
+        _cpu_block_inputs(released=True)
+        steps(lambda: cpu_block_seconds(released=True))
+        metric, unit = "block_tokens_per_s", "tokens/s"
+        value = T_TOKENS * len(secs) / sum(secs)
+        d = REL_C // REL_HEADS
+        config = {"workload": f"released shape: {BLOCKS}-block stack fwd, T={T_TOKENS}, C={REL_C}, "
+                              f"{REL_HEADS}x{d} heads, {REL_L} cond tokens of width {REL_CC}, fp16"}
+        desc = (f"one whole fp32 block at the released shape, T={T_TOKENS}, per step: the reference's CPU "
+                f"path (upstream block + flash_attn shim) restated in torch")
+    elif args.workload in ("stack", "stack_w8a8", "block"):
         nblocks = 1 if args.workload == "block" else BLOCKS
         _cpu_block_inputs()
         steps(cpu_block_seconds)
@@ -605,9 +629,7 @@ def run_ours(args) -> None:
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
-        import datetime
-
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+        hdist.init_nccl(dev)
     _lib.load()
     cpu_threads()
 
@@ -781,9 +803,7 @@ def run_attention(args, big: bool) -> None:
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
-        import datetime
-
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+        hdist.init_nccl(dev)
     _lib.load()
     cpu_threads()
     d = CHANNELS // HEADS
@@ -1011,6 +1031,68 @@ def run_forward(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_released(args) -> None:
+    """The 24-block stack at the released model's shape, T = 32,768 tokens (fp16, one GPU).
+    At head dim 96 the QKV projection runs as a plain GEMM followed by the RoPE + QK-norm row
+    kernel (the fused epilogue needs head dim 64); the line reports block tokens/s, the
+    self-attention TFLOP/s and the per-block split of projections, norms and attention."""
+    import torch
+
+    from hi3d_b200 import _lib, attention, synthetic, transformer
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    _lib.load()
+    cpu_threads()
+    d = REL_C // REL_HEADS
+    coords = synthetic.shell_coords(T_TOKENS, GRID, RADIUS, THICK, seed=0)
+    cos, sin = transformer.rope_tables(coords, d)
+    x = synthetic.features(T_TOKENS, REL_C, seed=1)
+    mod = synthetic.modulation(REL_C, 0.5, seed=2).astype(np.float16)
+    cond = synthetic.features(REL_L, REL_CC, seed=3)
+    weights = device_weights(dev, blocks=BLOCKS, c=REL_C, cc=REL_CC, heads=REL_HEADS)
+    stack = transformer.BlockStack(weights, REL_HEADS)
+    x_dev = torch.from_numpy(x).to(dev)
+    cos_d, sin_d = torch.from_numpy(cos).to(dev), torch.from_numpy(sin).to(dev)
+    mod_d = torch.from_numpy(mod).to(dev)
+    kvs = stack.prepare(torch.from_numpy(cond).to(dev))
+    run = lambda xin: stack(xin[None], mod_d, cos_d, sin_d, kvs)[0]
+    attention.TIMER.start()
+    _lib.LAUNCHES[0] = 0
+    with ClockSampler(0) as clocks:
+        ms = _timed(lambda: run(x_dev), args.steps, args.warmup)
+    launches = _lib.LAUNCHES[0]
+    attn = attention.TIMER.stop()
+    self_l = [r for r in attn if r["nk"] == T_TOKENS and r["flops"]]
+    cross_l = [r for r in attn if r["nk"] == REL_L and r["flops"]]
+    a_ms = sum(r["ms"] for r in self_l) / max(1, len(self_l))
+    a_tflops = sum(r["flops"] for r in self_l) / max(1, len(self_l)) / (a_ms / 1e3) / 1e12 if a_ms else 0.0
+    c_ms = sum(r["ms"] for r in cross_l) / max(1, len(cross_l))
+    peaks = _peaks()
+    value = BLOCKS * T_TOKENS / (ms / 1e3)
+    x_host = torch.from_numpy(x).pin_memory()
+    out_host = torch.empty_like(x_host).pin_memory()
+    e2e_ms = _timed(lambda: out_host.copy_(run(x_host.to(dev, non_blocking=True)), non_blocking=True), args.steps, 1)
+    line = {
+        "metric": "block_tokens_per_s", "value": value, "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "none", "vs_baseline": None,
+        "dtype": "f16", "data": "synthetic",
+        "config": {"workload": f"released shape: {BLOCKS}-block stack fwd, T={T_TOKENS}, C={REL_C}, "
+                               f"{REL_HEADS}x{d} heads, {REL_L} cond tokens of width {REL_CC}, fp16",
+                   "self_attention_ms_per_block": a_ms, "cross_attention_ms_per_block": c_ms,
+                   "other_ms_per_block": ms / BLOCKS - a_ms - c_ms,
+                   "l2": "inputs larger than L2 (weights 2.4 GB per step)"},
+        "roofline": {"bound": "tensor", "achieved": a_tflops, "peak": peaks["bf16_tflops_sustained"],
+                     "unit": "TFLOP/s", "frac": a_tflops / peaks["bf16_tflops_sustained"],
+                     "kernel": "hi3d::attn::flash_fwd_kernel<half,96,false>",
+                     "peak_source": f"{peaks['source']} bf16_tflops_sustained"},
+        "e2e": {"value": BLOCKS * T_TOKENS / (e2e_ms / 1e3), "unit": "tokens/s",
+                "h2d_bytes_per_step": x_host.numel() * 2, "d2h_bytes_per_step": out_host.numel() * 2},
+        "gpu_launches": launches, "clocks": clocks.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_vae(args) -> None:
     """The VAE decoder's kernels at decoder sizes (one line; value = conv(swish(GN(x))) TFLOP/s):
     a 256-channel level of 200,000 voxels (cfg5's shell) through GroupNorm statistics + swish +
@@ -1092,7 +1174,7 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-extras", action="store_true", help="headline only (no cfg2/cfg4/cfg5 extras)")
     ap.add_argument("--workload", choices=["stack", "stack_w8a8", "block", "attention", "attention262k", "conv",
-                                           "forward", "vae"], default="stack")
+                                           "forward", "vae", "released"], default="stack")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -1106,6 +1188,8 @@ def main() -> None:
         run_forward(args)
     elif args.workload == "vae":
         run_vae(args)
+    elif args.workload == "released":
+        run_released(args)
     else:
         run_attention(args, big=args.workload == "attention262k")
 

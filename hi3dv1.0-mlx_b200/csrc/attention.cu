@@ -81,7 +81,22 @@ struct Params {
   float* part_o;
   float* part_lse;
   int64_t part_rows;
+  // Partial mode with k_splits == 1 only: instead of writing its partial, this launch
+  // folds the partials of slots [0, slot0) into its own result (merge_kernel's
+  // arithmetic, slots in order with this range last) and writes the final rows to `out`.
+  int merge_final;
 };
+
+// out row (b, qrow, h) of the final result
+template <typename T>
+__device__ __forceinline__ T* out_row(const Params& p, int b, int64_t q_start, int64_t qrow, int h) {
+  return reinterpret_cast<T*>(p.out) + (int64_t)(p.cu_q ? 0 : b) * p.o_batch + (q_start + qrow) * p.o_row +
+         (int64_t)h * p.o_head;
+}
+
+__device__ __forceinline__ float slot_lse(const Params& p, int s, int64_t prow, int h) {
+  return p.part_lse[((int64_t)s * p.part_rows + prow) * p.heads + h];
+}
 
 struct Barriers {
   uint64_t q_full;
@@ -138,12 +153,43 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int kb0 = (int)((int64_t)split * nblk_all / p.k_splits);
     nblk = (int)((int64_t)(split + 1) * nblk_all / p.k_splits) - kb0;
     if (nblk <= 0) {
-      // no keys for this CTA: its rows are marked empty (log2-sum-exp -inf)
+      // no keys for this CTA: its rows are marked empty (log2-sum-exp -inf), or, when
+      // merging, the final rows come from the earlier slots alone
       for (int e = threadIdx.x; e < 2 * kRowsPerTile; e += blockDim.x) {
         const int64_t qr = q_row0 + e;
         if (qr >= q_len) continue;
         const int64_t prow = p.cu_q ? q_start + qr : (int64_t)b * p.nq + qr;
-        p.part_lse[((int64_t)(p.slot0 + split) * p.part_rows + prow) * p.heads + h] = -INFINITY;
+        if (!p.merge_final) {
+          p.part_lse[((int64_t)(p.slot0 + split) * p.part_rows + prow) * p.heads + h] = -INFINITY;
+          continue;
+        }
+        float mx = -INFINITY;
+        for (int s = 0; s < p.slot0; ++s) mx = fmaxf(mx, slot_lse(p, s, prow, h));
+        if (mx == -INFINITY) continue;  // no keys at all: the row is left untouched
+        float wsum = 0.f;
+        for (int s = 0; s < p.slot0; ++s) {
+          const float ls = slot_lse(p, s, prow, h);
+          if (ls != -INFINITY) wsum += exp2f(ls - mx);
+        }
+        const float iw = 1.0f / wsum;
+        T* dst = out_row<T>(p, b, q_start, qr, h);
+        for (int d0 = 0; d0 < D; d0 += 8) {
+          float acc[8] = {};
+          for (int s = 0; s < p.slot0; ++s) {
+            const float ls = slot_lse(p, s, prow, h);
+            if (ls == -INFINITY) continue;
+            const float w = exp2f(ls - mx);
+            const float* po = p.part_o + (((int64_t)s * p.part_rows + prow) * p.heads + h) * D + d0;
+#pragma unroll
+            for (int u = 0; u < 8; ++u) acc[u] += w * po[u];
+          }
+          uint4 o;
+          o.x = Cvt<T>::pack2(acc[0] * iw, acc[1] * iw);
+          o.y = Cvt<T>::pack2(acc[2] * iw, acc[3] * iw);
+          o.z = Cvt<T>::pack2(acc[4] * iw, acc[5] * iw);
+          o.w = Cvt<T>::pack2(acc[6] * iw, acc[7] * iw);
+          *reinterpret_cast<uint4*>(dst + d0) = o;
+        }
       }
       return;
     }
@@ -388,8 +434,62 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int64_t qrow = q_row0 + i * kRowsPerTile + row;
       const float inv = 1.0f / l_run;
       if constexpr (PARTIAL) {
-        // partial result of this key range: O / l in fp32 and the log2-sum-exp
         const int64_t prow = p.cu_q ? q_start + qrow : (int64_t)b * p.nq + qrow;
+        if (p.merge_final) {
+          // this range's O / l and log2-sum-exp folded with the earlier slots' partials
+          const float lse_own = m_run + log2f(l_run);
+          float mx = lse_own, wsum = 0.f;
+          if (qrow < q_len) {
+            for (int s = 0; s < p.slot0; ++s) mx = fmaxf(mx, slot_lse(p, s, prow, h));
+            for (int s = 0; s < p.slot0; ++s) {
+              const float ls = slot_lse(p, s, prow, h);
+              if (ls != -INFINITY) wsum += exp2f(ls - mx);
+            }
+          }
+          const float w_own = exp2f(lse_own - mx);
+          wsum += w_own;
+          const float iw = 1.0f / wsum;
+          T* dst = out_row<T>(p, b, q_start, qrow, h);
+#pragma unroll
+          for (int oc = 0; oc < (D + 31) / 32; ++oc) {
+            uint32_t r[32];
+            __syncwarp();
+            tmem_ld32(tO + oc * 32, r);
+            tmem_wait_ld();
+            if (qrow < q_len) {
+              float acc[32];
+#pragma unroll
+              for (int e = 0; e < 32; ++e) acc[e] = 0.f;
+              for (int s = 0; s < p.slot0; ++s) {
+                const float ls = slot_lse(p, s, prow, h);
+                if (ls == -INFINITY) continue;
+                const float w = exp2f(ls - mx);
+                const float* po = p.part_o + (((int64_t)s * p.part_rows + prow) * p.heads + h) * D + oc * 32;
+#pragma unroll
+                for (int e = 0; e < 32 && oc * 32 + e < D; e += 4) {
+                  const float4 v4 = *reinterpret_cast<const float4*>(po + e);
+                  acc[e] += w * v4.x;
+                  acc[e + 1] += w * v4.y;
+                  acc[e + 2] += w * v4.z;
+                  acc[e + 3] += w * v4.w;
+                }
+              }
+#pragma unroll
+              for (int e = 0; e < 32 && oc * 32 + e < D; e += 8) {
+                float o[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) o[u] = (acc[e + u] + w_own * (__uint_as_float(r[e + u]) * inv)) * iw;
+                uint4 w4;
+                w4.x = Cvt<T>::pack2(o[0], o[1]);
+                w4.y = Cvt<T>::pack2(o[2], o[3]);
+                w4.z = Cvt<T>::pack2(o[4], o[5]);
+                w4.w = Cvt<T>::pack2(o[6], o[7]);
+                *reinterpret_cast<uint4*>(dst + oc * 32 + e) = w4;
+              }
+            }
+          }
+        } else {
+        // partial result of this key range: O / l in fp32 and the log2-sum-exp
         float* po = p.part_o + (((int64_t)(p.slot0 + split) * p.part_rows + prow) * p.heads + h) * D;
         if (qrow < q_len) p.part_lse[((int64_t)(p.slot0 + split) * p.part_rows + prow) * p.heads + h] = m_run + log2f(l_run);
 #pragma unroll
@@ -405,6 +505,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                   make_float4(__uint_as_float(r[e]) * inv, __uint_as_float(r[e + 1]) * inv,
                               __uint_as_float(r[e + 2]) * inv, __uint_as_float(r[e + 3]) * inv);
           }
+        }
         }
       } else {
         T* dst = reinterpret_cast<T*>(p.out) + (int64_t)(p.cu_q ? 0 : b) * p.o_batch + (q_start + qrow) * p.o_row +
@@ -491,7 +592,7 @@ static int make_attn_map(CUtensorMap* map, const void* base, int dtype, int D, i
 // slots [slot0, slot0 + k_splits) of part_o / part_lse (no merge).
 template <typename T, int D>
 static int launch_attn(const hi3d_attn_args* a, cudaStream_t st, int k_splits = 1, float* part_o = nullptr,
-                       float* part_lse = nullptr, int slot0 = 0) {
+                       float* part_lse = nullptr, int slot0 = 0, bool merge_final = false) {
   using C = attn::Cfg<D>;
   const bool varlen_q = a->cu_seqlens_q != nullptr, varlen_k = a->cu_seqlens_k != nullptr;
   const int64_t qb = varlen_q ? 1 : a->num_seqs;
@@ -525,6 +626,7 @@ static int launch_attn(const hi3d_attn_args* a, cudaStream_t st, int k_splits = 
   p.part_o = part_o;
   p.part_lse = part_lse;
   p.part_rows = varlen_q ? a->nq : (int64_t)a->num_seqs * a->nq;
+  p.merge_final = merge_final ? 1 : 0;
   const int64_t grid = (int64_t)p.tiles_per_seq * a->num_seqs * a->heads * k_splits;
   if (grid == 0) return HI3D_OK;
   if (grid > 0x7fffffff) return set_error(HI3D_ERR_INVALID_ARGUMENT, "flash_attn: too many tiles");
@@ -577,11 +679,11 @@ static int check_attn_args(const hi3d_attn_args* a) {
 
 template <typename T>
 static int dispatch_attn(const hi3d_attn_args* a, cudaStream_t st, int k_splits, float* part_o, float* part_lse,
-                         int slot0) {
+                         int slot0, bool merge_final = false) {
   switch (a->head_dim) {
-    case 64: return launch_attn<T, 64>(a, st, k_splits, part_o, part_lse, slot0);
-    case 96: return launch_attn<T, 96>(a, st, k_splits, part_o, part_lse, slot0);
-    default: return launch_attn<T, 128>(a, st, k_splits, part_o, part_lse, slot0);
+    case 64: return launch_attn<T, 64>(a, st, k_splits, part_o, part_lse, slot0, merge_final);
+    case 96: return launch_attn<T, 96>(a, st, k_splits, part_o, part_lse, slot0, merge_final);
+    default: return launch_attn<T, 128>(a, st, k_splits, part_o, part_lse, slot0, merge_final);
   }
 }
 
@@ -657,6 +759,26 @@ extern "C" int hi3d_flash_attn_fwd_partial(const hi3d_attn_args* a, int k_splits
   cudaStream_t st = as_stream(stream);
   return a->dtype == HI3D_BF16 ? dispatch_attn<__nv_bfloat16>(a, st, k_splits, part_o, part_lse, slot0)
                                : dispatch_attn<__half>(a, st, k_splits, part_o, part_lse, slot0);
+}
+
+extern "C" int hi3d_flash_attn_fwd_partial_merge(const hi3d_attn_args* a, int slot0, const float* part_o,
+                                                 const float* part_lse, int64_t part_rows, void* stream) {
+  int rc = check_attn_args(a);
+  if (rc) return rc;
+  if (slot0 < 0 || slot0 > 64 || (slot0 > 0 && (!part_o || !part_lse || !aligned16(part_o))))
+    return set_error(HI3D_ERR_INVALID_ARGUMENT,
+                     "flash_attn_partial_merge: slot0 in [0, 64] and the partial buffers (part_o 16-byte aligned)");
+  const int64_t rows = a->cu_seqlens_q ? a->nq : (int64_t)a->num_seqs * a->nq;
+  if (slot0 > 0 && part_rows != rows)
+    return set_error(HI3D_ERR_INVALID_ARGUMENT, "flash_attn_partial_merge: part_rows %lld, the query rows are %lld",
+                     (long long)part_rows, (long long)rows);
+  if (a->nq == 0 || a->num_seqs == 0) return HI3D_OK;
+  cudaStream_t st = as_stream(stream);
+  // the partial instantiation with merge_final reads part_o / part_lse only below slot0
+  float* po = const_cast<float*>(part_o);
+  float* pl = const_cast<float*>(part_lse);
+  return a->dtype == HI3D_BF16 ? dispatch_attn<__nv_bfloat16>(a, st, 1, po, pl, slot0, true)
+                               : dispatch_attn<__half>(a, st, 1, po, pl, slot0, true);
 }
 
 extern "C" int hi3d_flash_attn_merge(const hi3d_attn_args* a, int num_slots, const float* part_o,

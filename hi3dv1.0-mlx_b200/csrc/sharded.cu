@@ -161,7 +161,11 @@ extern "C" int hi3d_nccl_comm_init(const void* id, int world, int rank, void** c
     delete c;
     return nccl_error("ncclCommInitRank", r);
   }
-  cudaError_t e = cudaStreamCreateWithFlags(&c->side, cudaStreamNonBlocking);
+  // the gather's side stream at the highest priority: its NCCL kernel takes the next SMs that
+  // free up while the attention grid occupies the GPU
+  int lo_prio = 0, hi_prio = 0;
+  cudaError_t e = cudaDeviceGetStreamPriorityRange(&lo_prio, &hi_prio);
+  if (e == cudaSuccess) e = cudaStreamCreateWithPriority(&c->side, cudaStreamNonBlocking, hi_prio);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->inputs_ready, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->gathered, cudaEventDisableTiming);
   if (e != cudaSuccess) {
@@ -316,12 +320,15 @@ extern "C" int hi3d_sharded_attn(void* comm, const void* q, const void* k, const
   slot += p.splits[0];
   e = cudaStreamWaitEvent(st, c->gathered, 0);
   if (e != cudaSuccess) return set_error(HI3D_ERR_CUDA, "sharded_attn: %s", cudaGetErrorString(e));
+  const int last = p.ranges[2][1] > p.ranges[2][0] ? 2 : (p.ranges[1][1] > p.ranges[1][0] ? 1 : 0);
   for (int i = 1; i < 3; ++i) {
     const int64_t lo = p.ranges[i][0], n = p.ranges[i][1] - lo;
     if (n <= 0) continue;
     const uint8_t* kb = static_cast<const uint8_t*>(k_all) + lo * row * esz;
     const uint8_t* vb = static_cast<const uint8_t*>(v_all) + lo * row * esz;
     hi3d_attn_args a = args_for(kb, vb, n);
+    if (i == last && p.splits[i] == 1)  // the last range in one pass, merged in its epilogue
+      return hi3d_flash_attn_fwd_partial_merge(&a, slot, part_o, part_lse, s_rows, st);
     if ((rc = hi3d_flash_attn_fwd_partial(&a, p.splits[i], slot, part_o, part_lse, s_rows, st))) return rc;
     slot += p.splits[i];
   }

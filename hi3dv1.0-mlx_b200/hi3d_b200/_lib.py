@@ -69,6 +69,8 @@ SIGNATURES: dict[str, tuple] = {
     "hi3d_flash_attn_fwd_split": (_i32, [ctypes.POINTER(AttnArgs), _i32, _c_void_p, _i64, _c_void_p]),
     "hi3d_flash_attn_fwd_partial": (_i32, [ctypes.POINTER(AttnArgs), _i32, _i32, _c_void_p, _c_void_p, _i64,
                                            _c_void_p]),
+    "hi3d_flash_attn_fwd_partial_merge": (_i32, [ctypes.POINTER(AttnArgs), _i32, _c_void_p, _c_void_p, _i64,
+                                                 _c_void_p]),
     "hi3d_flash_attn_merge": (_i32, [ctypes.POINTER(AttnArgs), _i32, _c_void_p, _c_void_p, _c_void_p]),
     "hi3d_nccl_unique_id": (_i32, [_c_void_p]),
     "hi3d_nccl_comm_init": (_i32, [_c_void_p, _i32, _i32, ctypes.POINTER(_c_void_p)]),

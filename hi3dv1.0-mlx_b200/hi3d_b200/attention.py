@@ -218,6 +218,35 @@ class AttentionParts:
             TIMER.records.append({"nq": args.nq, "nk": args.nk, "flops": flops, "e0": e0, "e1": e1, "part": True})
         self.used += splits
 
+    def add_final(self, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
+        """The last key set in one pass, merged with the partials added so far inside the
+        attention kernel's epilogue (``hi3d_flash_attn_fwd_partial_merge``); returns the
+        ``[B, Nq, H * D]`` output that :meth:`merge` would return after ``add(k, v, 1)``."""
+        _lib.require_cuda(k, v)
+        if k.shape[1] != self.heads or k.shape[3] != self.dim or v.shape != k.shape or k.dtype != self.q.dtype:
+            raise ValueError(f"keys {tuple(k.shape)} do not match the queries")
+        for t, n in ((k, "k"), (v, "v")):
+            _check_inner(t, n)
+        if k.shape[2] == 0:
+            return self.merge()
+        out = torch.empty((self.batch, self.nq, self.heads * self.dim), dtype=self.q.dtype, device=self.q.device)
+        if self.nq == 0 or self.batch == 0:
+            return out
+        args = _dense_args(self.q, k, v, out, self.scale, self.layout)
+        rec = TIMER.records is not None
+        if rec:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+        rc = _lib.load().hi3d_flash_attn_fwd_partial_merge(ctypes.byref(args), self.used, self.part_o.data_ptr(),
+                                                           self.part_lse.data_ptr(), self.batch * self.nq,
+                                                           _lib.stream(self.q))
+        _lib.check(rc, "flash_attention partial merge")
+        if rec:
+            e1.record()
+            flops = 4.0 * args.nq * args.nk * args.heads * args.head_dim * args.num_seqs
+            TIMER.records.append({"nq": args.nq, "nk": args.nk, "flops": flops, "e0": e0, "e1": e1, "part": True})
+        return out
+
     def merge(self) -> torch.Tensor:
         """``[B, Nq, H * D]`` from all key sets added so far."""
         out = torch.empty((self.batch, self.nq, self.heads * self.dim), dtype=self.q.dtype, device=self.q.device)

@@ -18,6 +18,19 @@ from . import attention, kernels
 from .transformer import _modulation, linear, qkv_rope
 
 
+def init_nccl(device, timeout_s: float = 300.0) -> None:
+    """``torch.distributed`` over NCCL for one process per GPU (env:// rendezvous), with the
+    NCCL streams at high priority: the K/V gather's copy kernels then take the next SMs that
+    free up while the attention grid (one CTA per SM) occupies the GPU, instead of waiting
+    behind the whole grid."""
+    import datetime
+
+    opts = dist.ProcessGroupNCCL.Options()
+    opts.is_high_priority_stream = True
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=timeout_s), device_id=device,
+                            pg_options=opts)
+
+
 def shard_slice(total: int, rank: int, world: int) -> slice:
     """Contiguous query-row slice of ``rank``: the rows ``[rank * total / world, ...)``."""
     if total % world:
@@ -89,11 +102,14 @@ def sharded_self_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, sc
     hk.wait()
     hv.wait()
     mark("kv_gather_wait")
-    i = 1
-    for lo, hi in key_sets:
-        if hi > lo:
-            parts.add(bhnd(k_all[lo:hi]), bhnd(v_all[lo:hi]), splits[i])
-            i += 1
+    ranges = [(lo, hi) for lo, hi in key_sets if hi > lo]
+    for i, (lo, hi) in enumerate(ranges, start=1):
+        if i == len(ranges) and splits[i] == 1:
+            # the last key range in one pass: merged inside its epilogue, no separate merge
+            out = parts.add_final(bhnd(k_all[lo:hi]), bhnd(v_all[lo:hi]))
+            mark("attention")
+            return out
+        parts.add(bhnd(k_all[lo:hi]), bhnd(v_all[lo:hi]), splits[i])
     mark("attention")
     return parts.merge()
 

@@ -167,6 +167,14 @@ HI3D_API int hi3d_flash_attn_fwd_partial(const hi3d_attn_args* args, int k_split
                                          float* part_lse, int64_t part_rows, void* stream);
 HI3D_API int hi3d_flash_attn_merge(const hi3d_attn_args* args, int num_slots, const float* part_o,
                                    const float* part_lse, void* stream);
+/* The last key range of a split attention in one pass, merged on the fly: attends the keys of
+ * `args` (one split) and, instead of writing a partial, combines its O / l and log2-sum-exp with
+ * the partials already in slots [0, slot0) (the arithmetic of hi3d_flash_attn_merge, slots in
+ * order with this range last) and writes the final rows to args->out.  Replaces a
+ * hi3d_flash_attn_fwd_partial(k_splits = 1) + hi3d_flash_attn_merge pair; part_o / part_lse are
+ * only read (may be NULL when slot0 == 0). */
+HI3D_API int hi3d_flash_attn_fwd_partial_merge(const hi3d_attn_args* args, int slot0, const float* part_o,
+                                               const float* part_lse, int64_t part_rows, void* stream);
 
 /* ---- query-sharded self-attention over NCCL ------------------------------ */
 /* One process per GPU.  hi3d_nccl_unique_id fills a 128-byte id on one rank, which the caller

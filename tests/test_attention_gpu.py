@@ -167,3 +167,77 @@ def test_attention_parts_over_disjoint_key_sets_match_single_pass():
     assert (got.float() - one.float()).abs().max().item() <= 2 * 2 ** -10 * one.float().abs().max().item()
     exact = ops.attention_f64(q.transpose(0, 2, 1, 3), k, v, d ** -0.5)
     assert rel_rms(got.float().cpu().numpy(), exact) < 3e-4  # both [1, Nq, H * D]
+
+
+@pytest.mark.parametrize("h,d,dtype", [(8, 64, torch.float16), (4, 128, torch.bfloat16), (6, 96, torch.float16)])
+def test_last_key_set_merged_in_its_epilogue_equals_partial_plus_merge(h, d, dtype):
+    """hi3d_flash_attn_fwd_partial_merge (the last key set attended in one pass and folded with
+    the earlier partials in its epilogue) is bit-identical to adding it as a partial and running
+    the merge kernel, and within the float64 bound."""
+    rng = np.random.default_rng(12 + d)
+    q = (rng.standard_normal((1, 500, h, d)) * 2).astype(np.float32)
+    k = (rng.standard_normal((1, h, 3000, d)) * 2).astype(np.float32)
+    v = rng.standard_normal((1, h, 3000, d)).astype(np.float32)
+    qt, kt, vt = _t(q, dtype), _t(k, dtype), _t(v, dtype)
+    sets = ((1000, 2000, 1), (0, 1000, 2), (2000, 3000, 1))
+    ref_parts = attention.AttentionParts(qt, d ** -0.5, slots=8, q_layout="bnhd")
+    for lo, hi, s in sets:
+        ref_parts.add(kt[:, :, lo:hi], vt[:, :, lo:hi], k_splits=s)
+    want = ref_parts.merge()
+    parts = attention.AttentionParts(qt, d ** -0.5, slots=8, q_layout="bnhd")
+    for lo, hi, s in sets[:-1]:
+        parts.add(kt[:, :, lo:hi], vt[:, :, lo:hi], k_splits=s)
+    got = parts.add_final(kt[:, :, 2000:3000], vt[:, :, 2000:3000])
+    assert torch.equal(got, want)
+    exact = ops.attention_f64(*(t.float().cpu().numpy() for t in (qt.transpose(1, 2), kt, vt)), d ** -0.5)
+    assert rel_rms(got.float().cpu().numpy(), exact) < (3e-4 if dtype == torch.float16 else 4e-3)
+    # no earlier partials: the merged launch is a plain single pass
+    solo = attention.AttentionParts(qt, d ** -0.5, slots=1, q_layout="bnhd").add_final(kt, vt)
+    assert torch.equal(solo, attention.flash_attention(qt, kt, vt, d ** -0.5, q_layout="bnhd", k_splits=1))
+
+
+def test_partial_merge_varlen_with_empty_key_ranges():
+    """Varlen sequences whose last key range is empty take their rows from the earlier
+    partials alone; an empty sequence stays untouched, as with the merge kernel."""
+    import ctypes
+
+    from hi3d_b200 import _lib
+
+    rng = np.random.default_rng(13)
+    h, d = 4, 64
+    cu_q = np.array([0, 200, 200, 450], np.int32)
+    cu_k1 = np.array([0, 300, 300, 700], np.int32)      # first key set: keys of every sequence
+    cu_k2 = np.array([0, 0, 0, 250], np.int32)          # last key set: sequence 0 has none
+    q = (rng.standard_normal((450, h, d)) * 2).astype(np.float16)
+    k1, v1 = (rng.standard_normal((700, h, d)) * 2).astype(np.float16), rng.standard_normal((700, h, d)).astype(np.float16)
+    k2, v2 = (rng.standard_normal((250, h, d)) * 2).astype(np.float16), rng.standard_normal((250, h, d)).astype(np.float16)
+    tq, tk1, tv1, tk2, tv2 = (_t(a, torch.float16) for a in (q, k1, v1, k2, v2))
+    cq, c1, c2 = (_t(a, torch.int32) for a in (cu_q, cu_k1, cu_k2))
+    part_o = torch.empty((1, 450, h, d), dtype=torch.float32, device=DEV)
+    part_lse = torch.empty((1, 450, h), dtype=torch.float32, device=DEV)
+    lib = _lib.load()
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def args(k, v, ck, out):
+        return _lib.AttnArgs(q=tq.data_ptr(), k=k.data_ptr(), v=v.data_ptr(), out=out.data_ptr(),
+                             q_row=h * d, q_head=d, k_row=h * d, k_head=d, v_row=h * d, v_head=d, o_row=h * d,
+                             o_head=d, cu_seqlens_q=cq.data_ptr(), cu_seqlens_k=ck.data_ptr(), nq=450,
+                             nk=k.shape[0], max_seqlen_q=250, num_seqs=3, heads=h, head_dim=d, dtype=_lib.F16,
+                             scale=d ** -0.5)
+
+    out = torch.full((450, h, d), 7.0, dtype=torch.float16, device=DEV)
+    a1 = args(tk1, tv1, c1, out)
+    assert lib.hi3d_flash_attn_fwd_partial(ctypes.byref(a1), 1, 0, part_o.data_ptr(), part_lse.data_ptr(), 450,
+                                           stream) == _lib.OK
+    a2 = args(tk2, tv2, c2, out)
+    assert lib.hi3d_flash_attn_fwd_partial_merge(ctypes.byref(a2), 1, part_o.data_ptr(), part_lse.data_ptr(), 450,
+                                                 stream) == _lib.OK
+    got = out.float().cpu().numpy()
+    kk = [np.concatenate([k1[0:300], k2[0:0]]), None, np.concatenate([k1[300:700], k2[0:250]])]
+    vv = [np.concatenate([v1[0:300], v2[0:0]]), None, np.concatenate([v1[300:700], v2[0:250]])]
+    for i, (lo, hi) in enumerate(((0, 200), (200, 200), (200, 450))):
+        if hi == lo:
+            continue
+        exact = ops.attention_varlen(q[lo:hi], kk[i], vv[i], [0, hi - lo], [0, kk[i].shape[0]], d ** -0.5)
+        assert rel_rms(got[lo:hi], exact) < 3e-4
+    assert _lib.device_status()["code"] == 0
