@@ -84,15 +84,18 @@ int abort_comm(Comm* c) {
   return r == ncclSuccess ? HI3D_OK : nccl_error("ncclCommAbort", r);
 }
 
-// Key splits per query block that fill whole waves of `sms` one-CTA-per-SM blocks:
-// the s minimising ceil(ctas * s / sms) / s, taken only when it beats no split by
-// more than 3 % and leaves at least two key blocks per split (as the Python side).
+// Key splits per query block (as the Python side, attention.auto_splits): the s minimising
+// the modelled launch time ceil(ctas * s / sms) * (overhead + key_blocks / s), with the fixed
+// cost of a CTA (set-up, first scores, epilogue) ≈ 2.25 key blocks, taken only when it beats
+// no split by more than 3 % and leaves at least two key blocks per split.
 int auto_splits(int64_t ctas, int64_t key_blocks, int sms) {
+  constexpr double kOverhead = 2.25;
+  auto cost = [&](int s) { return std::ceil((double)ctas * s / sms) * (kOverhead + (double)key_blocks / s); };
   int best = 1;
-  double best_t = std::ceil((double)ctas / sms);
+  double best_t = cost(1);
   for (int s = 2; s <= 8; ++s) {
     if (key_blocks < 2 * s) break;
-    const double t = std::ceil((double)ctas * s / sms) / s;
+    const double t = cost(s);
     if (t < best_t * 0.97) {
       best = s;
       best_t = t;

@@ -64,15 +64,24 @@ def _sm_count(device_index: int) -> int:
     return torch.cuda.get_device_properties(device_index).multi_processor_count
 
 
+# Fixed time of one attention CTA (set-up, Q load and first scores, epilogue) in key blocks:
+# ≈ 5670 cycles against ≈ 2525 per 128-key block (cfg1 clock traces).
+CTA_OVERHEAD_BLOCKS = 2.25
+
+
 def auto_splits(ctas: int, key_blocks: int, sms: int, max_splits: int = 8) -> int:
-    """Key splits per query block that fill the waves of ``sms`` CTAs (one per SM): the s
-    minimising ceil(ctas * s / sms) / s, taken only when it beats no split by more than 3 %
-    (the merge costs a little) and leaves at least two key blocks per split."""
-    best, best_t = 1, float(math.ceil(ctas / sms))
+    """Key splits per query block for ``ctas`` query-block CTAs over ``key_blocks`` key blocks on
+    ``sms`` SMs (one CTA per SM): the s minimising the modelled launch time
+    ceil(ctas * s / sms) * (overhead + key_blocks / s), taken only when it beats no split by more
+    than 3 % (the partials and their merge cost a little).  Short key ranges (cross-attention,
+    one rank's own shard) stay unsplit: splitting them fills waves with CTAs dominated by their
+    fixed cost."""
+    cost = lambda s: math.ceil(ctas * s / sms) * (CTA_OVERHEAD_BLOCKS + key_blocks / s)
+    best, best_t = 1, cost(1)
     for s in range(2, max_splits + 1):
         if key_blocks < 2 * s:
             break
-        t = math.ceil(ctas * s / sms) / s
+        t = cost(s)
         if t < best_t * 0.97:
             best, best_t = s, t
     return best

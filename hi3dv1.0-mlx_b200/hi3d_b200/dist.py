@@ -72,46 +72,72 @@ class PhaseTimer:
         return out
 
 
+def exchange_rotated(k: torch.Tensor, v: torch.Tensor, k_rot: torch.Tensor, v_rot: torch.Tensor, steps,
+                     group=None) -> list:
+    """Point-to-point part of the K/V exchange: for every j in ``steps`` this rank receives the
+    slices of rank ``r + j`` into rows ``(j - 1) * S`` of ``k_rot`` / ``v_rot`` and sends its own
+    to rank ``r - j`` (ranks of ``group``, modulo its size), all in one NCCL group.  Returns the
+    works (``wait()`` orders the current stream after them).  In this rank-rotated layout the
+    other ranks' keys are contiguous, and attention does not depend on the order of its keys."""
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    t = k.shape[0]
+    ops = []
+    for j in steps:
+        src, dst = (rank + j) % world, (rank - j) % world
+        rows = slice((j - 1) * t, j * t)
+        ops += [dist.P2POp(dist.isend, k, group=group, group_peer=dst),
+                dist.P2POp(dist.irecv, k_rot[rows], group=group, group_peer=src),
+                dist.P2POp(dist.isend, v, group=group, group_peer=dst),
+                dist.P2POp(dist.irecv, v_rot[rows], group=group, group_peer=src)]
+    return dist.batch_isend_irecv(ops) if ops else []
+
+
 def sharded_self_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float, group=None,
                            kv_buffers: tuple[torch.Tensor, torch.Tensor] | None = None,
                            mark=None) -> torch.Tensor:
     """Self-attention of this rank's query rows over the keys of every rank of ``group``, which
-    hold consecutive slices of one sequence in rank order.  ``q [1, S, H, D]`` (token-major),
-    ``k, v [S, H, D]``; returns ``[1, S, H * D]``.
+    hold consecutive slices of one sequence.  ``q [1, S, H, D]`` (token-major), ``k, v [S, H, D]``;
+    returns ``[1, S, H * D]``.
 
-    K and V are all-gathered (NCCL over NVLink) while this rank attends its own keys; the keys
-    before and after the own slice are attended once the gather is complete, and the partial
-    results are merged by their log-sum-exp weights (exact: softmax rows never cross ranks).
-    ``mark`` (a :class:`PhaseTimer` method) receives the phase boundaries."""
+    The other ranks' K/V slices arrive over NCCL point-to-point in two groups (the ranks r + 1
+    .. r + g first, then the rest; :func:`exchange_rotated`) while this rank attends its own keys;
+    the first group's keys are attended while the second group is still in flight, then the
+    second group's, and the partial results are merged by their log-sum-exp weights (exact:
+    softmax rows never cross ranks; the last merge runs in the last launch's epilogue when that
+    launch is not split).  ``kv_buffers``: ``[(world - 1) * S, H, D]`` receive buffers (or
+    larger).  ``mark`` (a :class:`PhaseTimer` method) receives the phase boundaries."""
     mark = mark or (lambda name: None)
     t_local, heads, d = k.shape
     world = dist.get_world_size(group)
-    rank = dist.get_rank(group)
     if kv_buffers is None:
-        kv_buffers = tuple(torch.empty((world * t_local, heads, d), dtype=k.dtype, device=k.device) for _ in range(2))
-    k_all, v_all = kv_buffers
-    _, hk = gather_rows(k, group, out=k_all, async_op=True)
-    _, hv = gather_rows(v, group, out=v_all, async_op=True)
+        kv_buffers = tuple(torch.empty(((world - 1) * t_local, heads, d), dtype=k.dtype, device=k.device)
+                           for _ in range(2))
+    k_rot, v_rot = kv_buffers
+    g = (world - 1 + 1) // 2  # first group: ranks r + 1 .. r + g
+    first = exchange_rotated(k.contiguous(), v.contiguous(), k_rot, v_rot, range(1, g + 1), group)
+    second = exchange_rotated(k.contiguous(), v.contiguous(), k_rot, v_rot, range(g + 1, world), group)
     bhnd = lambda t: t.permute(1, 0, 2)[None]  # [rows, H, D] token-major -> [1, H, rows, D] view
-    key_sets = [(0, rank * t_local), ((rank + 1) * t_local, world * t_local)]
+    ranges = [(0, g * t_local), (g * t_local, (world - 1) * t_local)]
+    ranges = [(lo, hi) for lo, hi in ranges if hi > lo]
     splits = [attention.auto_key_splits(t_local, t_local, heads, d, device=k.device)]
-    splits += [attention.auto_key_splits(t_local, hi - lo, heads, d, device=k.device) for lo, hi in key_sets if hi > lo]
+    splits += [attention.auto_key_splits(t_local, hi - lo, heads, d, device=k.device) for lo, hi in ranges]
     parts = attention.AttentionParts(q, scale, sum(splits), q_layout="bnhd")
     parts.add(bhnd(k), bhnd(v), splits[0])
     mark("attention")
-    hk.wait()
-    hv.wait()
-    mark("kv_gather_wait")
-    ranges = [(lo, hi) for lo, hi in key_sets if hi > lo]
-    for i, (lo, hi) in enumerate(ranges, start=1):
+    for i, ((lo, hi), works) in enumerate(zip(ranges, (first, second)), start=1):
+        for w in works:
+            w.wait()
+        mark("kv_gather_wait")
         if i == len(ranges) and splits[i] == 1:
-            # the last key range in one pass: merged inside its epilogue, no separate merge
-            out = parts.add_final(bhnd(k_all[lo:hi]), bhnd(v_all[lo:hi]))
+            out = parts.add_final(bhnd(k_rot[lo:hi]), bhnd(v_rot[lo:hi]))
             mark("attention")
             return out
-        parts.add(bhnd(k_all[lo:hi]), bhnd(v_all[lo:hi]), splits[i])
-    mark("attention")
-    return parts.merge()
+        parts.add(bhnd(k_rot[lo:hi]), bhnd(v_rot[lo:hi]), splits[i])
+        mark("attention")
+    out = parts.merge()
+    mark("merge")
+    return out
 
 
 def object_group(objects: int, group=None):
@@ -143,8 +169,9 @@ def block_forward_sharded(w: dict, x: torch.Tensor, mod: torch.Tensor, cos: torc
                           kv_buffers: tuple[torch.Tensor, torch.Tensor] | None = None,
                           timer: PhaseTimer | None = None) -> torch.Tensor:
     """One block on this rank's rows ``x [T/P, C]`` (updated in place) of a single object.
-    ``timer`` marks the phases (projections, own-key attention, exposed K/V gather wait, the
-    other keys' attention, merge, cross-attention, MLP)."""
+    ``timer`` marks the phases: LN + QKV projection, attention (own keys, then the other ranks'),
+    exposed K/V exchange wait, merge, self-attention output projection, LN + cross-attention Q,
+    cross-attention, its output projection, LN + MLP."""
     mark = timer.mark if timer is not None else (lambda name: None)
     mark("start")
     t_local, c = x.shape
@@ -155,23 +182,23 @@ def block_forward_sharded(w: dict, x: torch.Tensor, mod: torch.Tensor, cos: torc
 
     h = kernels.layer_norm_modulate(x, 1e-6, scale=scale_msa, shift=shift_msa)
     q, k, v = qkv_rope(h, w, cos, sin, 1, heads, d, token_major=True)
-    mark("projections")
+    mark("qkv")
     a = sharded_self_attention(q, k[0], v[0], scale, group, kv_buffers, mark)
-    mark("merge")
     linear(a[0], w, "self_attn.to_out", epilogue="residual", residual=x, gate=gate_msa)
-    mark("projections")
+    mark("to_out")
 
     h = kernels.layer_norm_modulate(x, 1e-6, weight=w["norm2.weight"], bias=w["norm2.bias"])
     qc = linear(h, w, "cross_attn.to_q").view(1, t_local, heads, d)
-    mark("projections")
+    mark("cross_q")
     o = attention.flash_attention(qc, ck, cv, scale, q_layout="bnhd")[0]
     mark("cross_attention")
     linear(o, w, "cross_attn.to_out", epilogue="residual", residual=x)
+    mark("cross_out")
 
     h = kernels.layer_norm_modulate(x, 1e-6, scale=scale_mlp, shift=shift_mlp)
     h = linear(h, w, "mlp.mlp.0", epilogue="gelu")
     linear(h, w, "mlp.mlp.2", epilogue="residual", residual=x, gate=gate_mlp)
-    mark("projections")
+    mark("mlp")
     return x
 
 
@@ -189,7 +216,7 @@ class ShardedBlockStack:
         x = x_local.clone()
         t_local, c = x.shape
         world = dist.get_world_size(self.group)
-        shape = (world * t_local, self.heads, c // self.heads)
+        shape = ((world - 1) * t_local, self.heads, c // self.heads)
         if self._kv is None or self._kv[0].shape != shape or self._kv[0].device != x.device:
             self._kv = tuple(torch.empty(shape, dtype=x.dtype, device=x.device) for _ in range(2))
         for i, w in enumerate(self.weights):

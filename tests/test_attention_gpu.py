@@ -148,6 +148,8 @@ def test_auto_splits_fill_waves():
     assert attention.auto_splits(256, 256, 148) == 4    # one eighth of the queries per GPU
     assert attention.auto_splits(512, 256, 148) == 2
     assert attention.auto_splits(256, 3, 148) == 1      # too few key blocks to split
+    assert attention.auto_splits(256, 11, 148) == 1     # cross-attention at 8 GPUs: CTA set-up dominates
+    assert attention.auto_splits(256, 32, 148) == 1     # one rank's own key shard at 8 GPUs
 
 
 def test_attention_parts_over_disjoint_key_sets_match_single_pass():
