@@ -418,6 +418,21 @@ def run_reference(args) -> None:
         metric, unit, value = "forward_tokens_per_s", "tokens/s", n_low / fwd_s
         config = {"workload": f"whole refinement transformer fwd: {FWD_FINE} fine shell voxels, {n_low} low tokens, "
                               f"{BLOCKS} blocks", "low_tokens": n_low}
+    elif args.workload == "kernels":
+        import torch
+
+        x = torch.randn((T_TOKENS, CHANNELS))
+        sc, sh = torch.randn(CHANNELS), torch.randn(CHANNELS)
+
+        def ln():
+            # the reference's CPU LayerNorm32 + modulation (norm.py:12-17, modulated.py:55-56), fp32
+            torch.nn.functional.layer_norm(x, (CHANNELS,), eps=1e-6) * (1 + sc) + sh
+
+        steps(ln)
+        value, unit, metric = 2.0 * T_TOKENS * CHANNELS * 4 * len(secs) / sum(secs) / 1e9, "GB/s", "layer_norm_modulate_gbs"
+        desc = f"fp32 LayerNorm32 + modulation of {T_TOKENS} x {CHANNELS} rows on the host (the reference's CPU path)"
+        config = {"workload": f"row kernels and projection epilogues at T={T_TOKENS}, C={CHANNELS} (quantiser also "
+                              f"at width 4096), fp16, each timed alone"}
     elif args.workload in ("conv", "vae"):
         vals = []
         steps(lambda: vals.append(cpu_conv_tflops()))
@@ -1093,6 +1108,70 @@ def run_released(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_kernels(args) -> None:
+    """The block's row kernels and projection epilogues alone at cfg1/cfg2 sizes (one GPU): the
+    two LayerNorm forms (T x 1024, inputs rotated over 8 copies so every launch reads HBM), the
+    W8A8 activation quantiser at widths 1024 and 4096, and the K = 1024 projection with each
+    epilogue (store, residual, gated residual).  ``value`` is the modulated LayerNorm's fraction of
+    the measured HBM bandwidth; every kernel's time and fraction is in ``config``."""
+    import torch
+
+    from hi3d_b200 import _lib, kernels, linear, w8a8
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    _lib.load()
+    peaks = _peaks()
+    g = torch.Generator(device=dev).manual_seed(5)
+    R, C = T_TOKENS, CHANNELS
+    xs = [torch.randn((R, C), generator=g, device=dev).half() for _ in range(8)]
+    sc, sh = torch.randn(C, generator=g, device=dev).half(), torch.randn(C, generator=g, device=dev).half()
+    wln, bln = torch.rand(C, generator=g, device=dev) + 0.5, torch.randn(C, generator=g, device=dev) * 0.1
+    res = {}
+    _lib.LAUNCHES[0] = 0
+    it = [0]
+
+    def rot():
+        it[0] += 1
+        return xs[it[0] % 8]
+
+    with ClockSampler(0) as clocks:
+        for name, kw in (("layer_norm_modulate", dict(scale=sc, shift=sh)), ("layer_norm_affine", dict(weight=wln, bias=bln))):
+            ms = _timed(lambda: kernels.layer_norm_modulate(rot(), 1e-6, **kw), args.steps, args.warmup)
+            gbs = 4.0 * R * C / (ms / 1e3) / 1e9
+            res[name] = {"us": ms * 1e3, "gbs": gbs, "hbm_frac": gbs / peaks["hbm_gbs"]}
+        for k in (1024, 4096):
+            xq = torch.randn((R, k), generator=g, device=dev).half()
+            ms = _timed(lambda: w8a8.quantize_activation(xq), args.steps, args.warmup)
+            gbs = (3.0 * R * k + 4 * R) / (ms / 1e3) / 1e9
+            res[f"quantize_act_i8_k{k}"] = {"us": ms * 1e3, "gbs": gbs, "hbm_frac": gbs / peaks["hbm_gbs"]}
+        a = xs[0]
+        wt = (torch.randn((C, C), generator=g, device=dev) * 0.02).half()
+        bt = (torch.randn(C, generator=g, device=dev) * 0.02).half()
+        resid = torch.randn((R, C), generator=g, device=dev).half()
+        gate = torch.randn(C, generator=g, device=dev).half()
+        for name, kw in (("gemm_store", dict(epilogue="store")), ("gemm_residual", dict(epilogue="residual", residual=resid)),
+                         ("gemm_gated_residual", dict(epilogue="residual", residual=resid, gate=gate))):
+            ms = _timed(lambda: linear.linear(a, wt, bt, **kw), args.steps, args.warmup)
+            tf = 2.0 * R * C * C / (ms / 1e3) / 1e12
+            res[name] = {"us": ms * 1e3, "tflops": tf, "tensor_frac": tf / peaks["bf16_tflops"]}
+    launches = _lib.LAUNCHES[0]
+    v = res["layer_norm_modulate"]["gbs"]
+    line = {
+        "metric": "layer_norm_modulate_gbs", "value": v, "unit": "GB/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": res["layer_norm_modulate"]["us"] / 1e3,
+        "higher_is_better": True, "scaling": "none", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": {"workload": f"row kernels and projection epilogues at T={R}, C={C} (quantiser also at width "
+                               f"4096), fp16, each timed alone", "kernels": res,
+                   "l2": "LayerNorm inputs rotated over 8 copies (> L2); quantiser / GEMM inputs > L2",
+                   "peak_source": f"{peaks['source']} hbm_gbs {peaks['hbm_gbs']}, bf16_tflops {peaks['bf16_tflops']}"},
+        "roofline": {"bound": "hbm", "achieved": v, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": v / peaks["hbm_gbs"], "traffic": None},
+        "gpu_launches": launches, "clocks": clocks.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_vae(args) -> None:
     """The VAE decoder's kernels at decoder sizes (one line; value = conv(swish(GN(x))) TFLOP/s):
     a 256-channel level of 200,000 voxels (cfg5's shell) through GroupNorm statistics + swish +
@@ -1174,7 +1253,7 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-extras", action="store_true", help="headline only (no cfg2/cfg4/cfg5 extras)")
     ap.add_argument("--workload", choices=["stack", "stack_w8a8", "block", "attention", "attention262k", "conv",
-                                           "forward", "vae", "released"], default="stack")
+                                           "forward", "vae", "released", "kernels"], default="stack")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -1190,6 +1269,8 @@ def main() -> None:
         run_vae(args)
     elif args.workload == "released":
         run_released(args)
+    elif args.workload == "kernels":
+        run_kernels(args)
     else:
         run_attention(args, big=args.workload == "attention262k")
 
