@@ -569,8 +569,8 @@ def measure_conv(dev, steps: int, warmup: int) -> dict:
 def measure_cfg4(dev, world: int, rank: int, steps: int, warmup: int, sub) -> dict:
     """cfg4: bf16 self-attention over 4 objects x 65,536 tokens, the packed tokens split into
     contiguous slices over the ranks.  With at most 4 ranks each rank holds whole objects and
-    attends them alone; with more, the ranks of one object exchange its K/V shards (``sub``, from
-    ``dist.object_group``) while attending their own keys.  Every rank times its own slice; the
+    attends them alone; with more, the ranks of one object all-gather its K/V shards (``sub``, from
+    ``dist.object_group``), then attend all its keys.  Every rank times its own slice; the
     step time is the maximum over ranks."""
     import torch
 
@@ -589,8 +589,11 @@ def measure_cfg4(dev, world: int, rank: int, steps: int, warmup: int, sub) -> di
         step = lambda: attention.flash_attn_varlen(q, k, v, cu, cu, per, scale, out=out)
         exchange = 0
     else:
-        kvb = tuple(torch.empty((per, HEADS, d), dtype=q.dtype, device=dev) for _ in range(2))
-        step = lambda: hdist.sharded_self_attention(q[None], k, v, scale, sub, kvb)
+        # this rank's keys/values in its slot of the gather buffers (where the projection writes them)
+        kvb = hdist.kv_gather_buffers(tl, HEADS, d, q.dtype, dev, sub)
+        hdist.own_rows(kvb[0], sub)[0].copy_(k)
+        hdist.own_rows(kvb[1], sub)[0].copy_(v)
+        step = lambda: hdist.sharded_self_attention(q[None], kvb[0], kvb[1], scale, sub)
         exchange = 2 * (per - tl) * HEADS * d * 2
     ms = _timed(step, steps, warmup)
     ms = _max_over_ranks(ms, world, dev)
@@ -836,16 +839,19 @@ def run_attention(args, big: bool) -> None:
         g = torch.Generator().manual_seed(8 + rank)
         hq, hk, hv = (torch.randn((tl, HEADS, d), generator=g).bfloat16().pin_memory() for _ in range(3))
         hout = torch.empty((tl, HEADS, d), dtype=torch.bfloat16).pin_memory()
-        kvb = tuple(torch.empty((65536, HEADS, d), dtype=torch.bfloat16, device=dev) for _ in range(2))
+        kvb = hdist.kv_gather_buffers(tl, HEADS, d, torch.bfloat16, dev, sub) if sub is not None else None
 
         def e2e_step():
-            dq, dk, dv = (t.to(dev, non_blocking=True) for t in (hq, hk, hv))
+            dq = hq.to(dev, non_blocking=True)
             if sub is None:
+                dk, dv = (t.to(dev, non_blocking=True) for t in (hk, hv))
                 n_obj = 4 // world
                 cu = torch.arange(n_obj + 1, device=dev, dtype=torch.int32) * 65536
                 o = attention.flash_attn_varlen(dq, dk, dv, cu, cu, 65536, d ** -0.5)
-            else:
-                o = hdist.sharded_self_attention(dq[None], dk, dv, d ** -0.5, sub, kvb)[0].view(tl, HEADS, d)
+            else:  # keys/values straight into this rank's slot of the gather buffers
+                hdist.own_rows(kvb[0], sub)[0].copy_(hk, non_blocking=True)
+                hdist.own_rows(kvb[1], sub)[0].copy_(hv, non_blocking=True)
+                o = hdist.sharded_self_attention(dq[None], kvb[0], kvb[1], d ** -0.5, sub)[0].view(tl, HEADS, d)
             hout.copy_(o, non_blocking=True)
 
         e2e_ms = _max_over_ranks(_timed(e2e_step, args.steps, 1), world, dev)

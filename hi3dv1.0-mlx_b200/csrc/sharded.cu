@@ -86,11 +86,14 @@ int abort_comm(Comm* c) {
 
 // Key splits per query block (as the Python side, attention.auto_splits): the s minimising
 // the modelled launch time ceil(ctas * s / sms) * (overhead + key_blocks / s), with the fixed
-// cost of a CTA (set-up, first scores, epilogue) ≈ 2.25 key blocks, taken only when it beats
-// no split by more than 3 % and leaves at least two key blocks per split.
+// cost of a CTA (set-up, first scores, epilogue) ≈ 2.25 key blocks and a split launch (the
+// partial kernel, whose fp32 partials and merge follow) charged 1.2x the single pass, taken only
+// when it beats no split by more than 3 % and leaves at least two key blocks per split.
 int auto_splits(int64_t ctas, int64_t key_blocks, int sms) {
-  constexpr double kOverhead = 2.25;
-  auto cost = [&](int s) { return std::ceil((double)ctas * s / sms) * (kOverhead + (double)key_blocks / s); };
+  constexpr double kOverhead = 2.25, kPartial = 1.2;
+  auto cost = [&](int s) {
+    return std::ceil((double)ctas * s / sms) * (kOverhead + (double)key_blocks / s) * (s > 1 ? kPartial : 1.0);
+  };
   int best = 1;
   double best_t = cost(1);
   for (int s = 2; s <= 8; ++s) {
@@ -104,34 +107,35 @@ int auto_splits(int64_t ctas, int64_t key_blocks, int sms) {
   return best;
 }
 
-struct Plan {
-  int64_t ranges[3][2];  // key row ranges: own slice, before it, after it
-  int splits[3];
-  int slots;
-};
-
-Plan make_plan(int rank, int world, int64_t s_rows, int heads, int head_dim) {
-  Plan p{};
-  const int64_t total = s_rows * world;
-  p.ranges[0][0] = rank * s_rows;
-  p.ranges[0][1] = (rank + 1) * s_rows;
-  p.ranges[1][0] = 0;
-  p.ranges[1][1] = rank * s_rows;
-  p.ranges[2][0] = (rank + 1) * s_rows;
-  p.ranges[2][1] = total;
-  const int bk = head_dim == 64 ? 128 : 64;
-  const int64_t ctas = (s_rows + 255) / 256 * heads;
-  p.slots = 0;
-  for (int r = 0; r < 3; ++r) {
-    const int64_t n = p.ranges[r][1] - p.ranges[r][0];
-    p.splits[r] = n > 0 ? auto_splits(ctas, (n + bk - 1) / bk, sm_count()) : 0;
-    p.slots += p.splits[r];
-  }
-  return p;
+// The one attention launch of the sharded block: this rank's s_rows queries over all
+// world * s_rows keys, as one dense sequence ([rows, heads, head_dim] token-major operands).
+hi3d_attn_args gathered_args(const void* q, const void* k_all, const void* v_all, void* out, int64_t s_rows,
+                             int64_t total, int heads, int head_dim, int dtype, float scale) {
+  const int64_t row = (int64_t)heads * head_dim;
+  hi3d_attn_args a{};
+  a.q = q;
+  a.k = k_all;
+  a.v = v_all;
+  a.out = out;
+  a.q_row = a.k_row = a.v_row = a.o_row = row;
+  a.q_head = a.k_head = a.v_head = a.o_head = head_dim;
+  a.q_batch = a.o_batch = s_rows * row;
+  a.k_batch = a.v_batch = 0;
+  a.nq = s_rows;
+  a.nk = total;
+  a.max_seqlen_q = s_rows;
+  a.num_seqs = 1;
+  a.heads = heads;
+  a.head_dim = head_dim;
+  a.dtype = dtype;
+  a.scale = scale;
+  return a;
 }
 
-int64_t part_bytes(int slots, int64_t s_rows, int heads, int head_dim) {
-  return (int64_t)slots * s_rows * heads * head_dim * 4;
+int plan_splits(int world, int64_t s_rows, int heads, int head_dim) {
+  const int bk = head_dim == 64 ? 128 : 64;
+  const int64_t keys = s_rows * world;
+  return keys > 0 ? auto_splits((s_rows + 255) / 256 * heads, (keys + bk - 1) / bk, sm_count()) : 1;
 }
 
 }  // namespace
@@ -249,8 +253,13 @@ extern "C" int hi3d_sharded_attn_workspace_size(void* comm, int64_t s_rows, int 
     return set_error(HI3D_ERR_UNSUPPORTED, "sharded_attn_workspace_size: head_dim %d (supported: 64, 96, 128)",
                      head_dim);
   const Comm* c = static_cast<const Comm*>(comm);
-  const Plan p = make_plan(c->rank, c->world, s_rows, heads, head_dim);
-  const int64_t po = part_bytes(p.slots, s_rows, heads, head_dim);
+  const int splits = plan_splits(c->world, s_rows, heads, head_dim);
+  if (splits == 1) {
+    *bytes = 256;  // the single pass needs none; a non-empty buffer keeps the contract simple
+    return HI3D_OK;
+  }
+  // the layout of hi3d_flash_attn_split_workspace_size: fp32 O partials, then the log-sum-exps
+  const int64_t po = (int64_t)splits * s_rows * heads * head_dim * 4;
   *bytes = ((po + 255) & ~int64_t(255)) + po / head_dim + 256;
   return HI3D_OK;
 }
@@ -273,15 +282,13 @@ extern "C" int hi3d_sharded_attn(void* comm, const void* q, const void* k, const
   if (!workspace || workspace_bytes < need || !aligned16(workspace))
     return set_error(HI3D_ERR_CAPACITY, "sharded_attn: workspace %lld bytes, need %lld (16-byte aligned)",
                      (long long)workspace_bytes, (long long)need);
-  const Plan p = make_plan(c->rank, c->world, s_rows, heads, head_dim);
-  float* part_o = static_cast<float*>(workspace);
-  float* part_lse = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) +
-                                             ((part_bytes(p.slots, s_rows, heads, head_dim) + 255) & ~int64_t(255)));
   cudaStream_t st = as_stream(stream);
   const int64_t row = (int64_t)heads * head_dim;  // elements per token row
-  const size_t esz = 2;
 
-  // K/V gather on the side stream, after the caller's stream has produced k and v
+  // K/V gather on the high-priority side stream, after the caller's stream has produced k and v;
+  // the caller's stream then waits for it.  A single pass over all keys is faster than attending
+  // the own slice while the gather runs: the partial kernel and the merge cost more than the
+  // exposed gather.
   cudaError_t e = cudaEventRecord(c->inputs_ready, st);
   if (e == cudaSuccess) e = cudaStreamWaitEvent(c->side, c->inputs_ready, 0);
   if (e != cudaSuccess) return set_error(HI3D_ERR_CUDA, "sharded_attn: %s", cudaGetErrorString(e));
@@ -293,48 +300,11 @@ extern "C" int hi3d_sharded_attn(void* comm, const void* q, const void* k, const
   if (r != ncclSuccess) return nccl_error("ncclAllGather", r);
   if (r2 != ncclSuccess) return nccl_error("ncclGroupEnd", r2);
   e = cudaEventRecord(c->gathered, c->side);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(st, c->gathered, 0);
   if (e != cudaSuccess) return set_error(HI3D_ERR_CUDA, "sharded_attn: %s", cudaGetErrorString(e));
 
-  // one dense sequence: queries [S, H, D] token-major against a key range
-  auto args_for = [&](const void* kp, const void* vp, int64_t nk) {
-    hi3d_attn_args a{};
-    a.q = q;
-    a.k = kp;
-    a.v = vp;
-    a.out = out;
-    a.q_row = a.k_row = a.v_row = a.o_row = row;
-    a.q_head = a.k_head = a.v_head = a.o_head = head_dim;
-    a.q_batch = a.o_batch = s_rows * row;
-    a.k_batch = a.v_batch = 0;
-    a.nq = s_rows;
-    a.nk = nk;
-    a.max_seqlen_q = s_rows;
-    a.num_seqs = 1;
-    a.heads = heads;
-    a.head_dim = head_dim;
-    a.dtype = dtype;
-    a.scale = scale;
-    return a;
-  };
-  int slot = 0;
-  // own keys while the gather runs
-  hi3d_attn_args own = args_for(k, v, s_rows);
-  if ((rc = hi3d_flash_attn_fwd_partial(&own, p.splits[0], slot, part_o, part_lse, s_rows, st))) return rc;
-  slot += p.splits[0];
-  e = cudaStreamWaitEvent(st, c->gathered, 0);
-  if (e != cudaSuccess) return set_error(HI3D_ERR_CUDA, "sharded_attn: %s", cudaGetErrorString(e));
-  const int last = p.ranges[2][1] > p.ranges[2][0] ? 2 : (p.ranges[1][1] > p.ranges[1][0] ? 1 : 0);
-  for (int i = 1; i < 3; ++i) {
-    const int64_t lo = p.ranges[i][0], n = p.ranges[i][1] - lo;
-    if (n <= 0) continue;
-    const uint8_t* kb = static_cast<const uint8_t*>(k_all) + lo * row * esz;
-    const uint8_t* vb = static_cast<const uint8_t*>(v_all) + lo * row * esz;
-    hi3d_attn_args a = args_for(kb, vb, n);
-    if (i == last && p.splits[i] == 1)  // the last range in one pass, merged in its epilogue
-      return hi3d_flash_attn_fwd_partial_merge(&a, slot, part_o, part_lse, s_rows, st);
-    if ((rc = hi3d_flash_attn_fwd_partial(&a, p.splits[i], slot, part_o, part_lse, s_rows, st))) return rc;
-    slot += p.splits[i];
-  }
-  hi3d_attn_args m = args_for(k, v, s_rows);
-  return hi3d_flash_attn_merge(&m, slot, part_o, part_lse, st);
+  const hi3d_attn_args a = gathered_args(q, k_all, v_all, out, s_rows, s_rows * c->world, heads, head_dim, dtype,
+                                         scale);
+  return hi3d_flash_attn_fwd_split(&a, plan_splits(c->world, s_rows, heads, head_dim), workspace, workspace_bytes,
+                                   st);
 }

@@ -67,16 +67,18 @@ def _sm_count(device_index: int) -> int:
 # Fixed time of one attention CTA (set-up, Q load and first scores, epilogue) in key blocks:
 # ≈ 5670 cycles against ≈ 2525 per 128-key block (cfg1 clock traces).
 CTA_OVERHEAD_BLOCKS = 2.25
+PARTIAL_FACTOR = 1.2  # measured: the partial kernel + merge against the single pass, same keys
 
 
 def auto_splits(ctas: int, key_blocks: int, sms: int, max_splits: int = 8) -> int:
     """Key splits per query block for ``ctas`` query-block CTAs over ``key_blocks`` key blocks on
     ``sms`` SMs (one CTA per SM): the s minimising the modelled launch time
-    ceil(ctas * s / sms) * (overhead + key_blocks / s), taken only when it beats no split by more
-    than 3 % (the partials and their merge cost a little).  Short key ranges (cross-attention,
-    one rank's own shard) stay unsplit: splitting them fills waves with CTAs dominated by their
-    fixed cost."""
-    cost = lambda s: math.ceil(ctas * s / sms) * (CTA_OVERHEAD_BLOCKS + key_blocks / s)
+    ceil(ctas * s / sms) * (overhead + key_blocks / s), a split launch (the partial kernel, its
+    fp32 partials and the merge) charged :data:`PARTIAL_FACTOR` times the single pass, taken only
+    when it beats no split by more than 3 %.  Short key ranges (cross-attention) and grids of
+    about two waves or more stay unsplit."""
+    cost = lambda s: (math.ceil(ctas * s / sms) * (CTA_OVERHEAD_BLOCKS + key_blocks / s)
+                      * (PARTIAL_FACTOR if s > 1 else 1.0))
     best, best_t = 1, cost(1)
     for s in range(2, max_splits + 1):
         if key_blocks < 2 * s:

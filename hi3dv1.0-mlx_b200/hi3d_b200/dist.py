@@ -15,7 +15,7 @@ import torch
 import torch.distributed as dist
 
 from . import attention, kernels
-from .transformer import _modulation, linear, qkv_rope
+from .transformer import _modulation, linear, modulation_all, qkv_rope
 
 
 def init_nccl(device, timeout_s: float = 300.0) -> None:
@@ -72,72 +72,48 @@ class PhaseTimer:
         return out
 
 
-def exchange_rotated(k: torch.Tensor, v: torch.Tensor, k_rot: torch.Tensor, v_rot: torch.Tensor, steps,
-                     group=None) -> list:
-    """Point-to-point part of the K/V exchange: for every j in ``steps`` this rank receives the
-    slices of rank ``r + j`` into rows ``(j - 1) * S`` of ``k_rot`` / ``v_rot`` and sends its own
-    to rank ``r - j`` (ranks of ``group``, modulo its size), all in one NCCL group.  Returns the
-    works (``wait()`` orders the current stream after them).  In this rank-rotated layout the
-    other ranks' keys are contiguous, and attention does not depend on the order of its keys."""
-    world = dist.get_world_size(group)
-    rank = dist.get_rank(group)
-    t = k.shape[0]
-    ops = []
-    for j in steps:
-        src, dst = (rank + j) % world, (rank - j) % world
-        rows = slice((j - 1) * t, j * t)
-        ops += [dist.P2POp(dist.isend, k, group=group, group_peer=dst),
-                dist.P2POp(dist.irecv, k_rot[rows], group=group, group_peer=src),
-                dist.P2POp(dist.isend, v, group=group, group_peer=dst),
-                dist.P2POp(dist.irecv, v_rot[rows], group=group, group_peer=src)]
-    return dist.batch_isend_irecv(ops) if ops else []
-
-
-def sharded_self_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float, group=None,
-                           kv_buffers: tuple[torch.Tensor, torch.Tensor] | None = None,
+def sharded_self_attention(q: torch.Tensor, k_all: torch.Tensor, v_all: torch.Tensor, scale: float, group=None,
                            mark=None) -> torch.Tensor:
     """Self-attention of this rank's query rows over the keys of every rank of ``group``, which
-    hold consecutive slices of one sequence.  ``q [1, S, H, D]`` (token-major), ``k, v [S, H, D]``;
-    returns ``[1, S, H * D]``.
-
-    The other ranks' K/V slices arrive over NCCL point-to-point in two groups (the ranks r + 1
-    .. r + g first, then the rest; :func:`exchange_rotated`) while this rank attends its own keys;
-    the first group's keys are attended while the second group is still in flight, then the
-    second group's, and the partial results are merged by their log-sum-exp weights (exact:
-    softmax rows never cross ranks; the last merge runs in the last launch's epilogue when that
-    launch is not split).  ``kv_buffers``: ``[(world - 1) * S, H, D]`` receive buffers (or
-    larger).  ``mark`` (a :class:`PhaseTimer` method) receives the phase boundaries."""
+    hold consecutive slices of one sequence.  ``q [1, S, H, D]`` (token-major); ``k_all, v_all
+    [P * S, H, D]`` whose rows ``[r * S, (r + 1) * S)`` already hold this rank's keys / values
+    (the QKV projection writes them there, ``qkv_rope(out=...)``).  The other ranks' rows are
+    filled by one in-place all-gather each (NCCL over NVLink, on the high-priority NCCL stream,
+    which the current stream then waits for), and the queries attend all keys in one pass;
+    returns ``[1, S, H * D]``.  Softmax rows never cross ranks, so the result is the single-GPU
+    attention of these rows.  Attending the own keys while the gather runs and merging partials
+    was measured slower: the partial kernel and the merge cost more than the exposed gather.
+    ``mark`` (a :class:`PhaseTimer` method) receives the phase boundaries."""
     mark = mark or (lambda name: None)
-    t_local, heads, d = k.shape
-    world = dist.get_world_size(group)
-    if kv_buffers is None:
-        kv_buffers = tuple(torch.empty(((world - 1) * t_local, heads, d), dtype=k.dtype, device=k.device)
-                           for _ in range(2))
-    k_rot, v_rot = kv_buffers
-    g = (world - 1 + 1) // 2  # first group: ranks r + 1 .. r + g
-    first = exchange_rotated(k.contiguous(), v.contiguous(), k_rot, v_rot, range(1, g + 1), group)
-    second = exchange_rotated(k.contiguous(), v.contiguous(), k_rot, v_rot, range(g + 1, world), group)
-    bhnd = lambda t: t.permute(1, 0, 2)[None]  # [rows, H, D] token-major -> [1, H, rows, D] view
-    ranges = [(0, g * t_local), (g * t_local, (world - 1) * t_local)]
-    ranges = [(lo, hi) for lo, hi in ranges if hi > lo]
-    splits = [attention.auto_key_splits(t_local, t_local, heads, d, device=k.device)]
-    splits += [attention.auto_key_splits(t_local, hi - lo, heads, d, device=k.device) for lo, hi in ranges]
-    parts = attention.AttentionParts(q, scale, sum(splits), q_layout="bnhd")
-    parts.add(bhnd(k), bhnd(v), splits[0])
+    gather_kv(k_all, v_all, group)
+    mark("kv_gather_wait")
+    bhnd = lambda x: x.permute(1, 0, 2)[None]  # [rows, H, D] token-major -> [1, H, rows, D] view
+    out = attention.flash_attention(q, bhnd(k_all), bhnd(v_all), scale, q_layout="bnhd")
     mark("attention")
-    for i, ((lo, hi), works) in enumerate(zip(ranges, (first, second)), start=1):
-        for w in works:
-            w.wait()
-        mark("kv_gather_wait")
-        if i == len(ranges) and splits[i] == 1:
-            out = parts.add_final(bhnd(k_rot[lo:hi]), bhnd(v_rot[lo:hi]))
-            mark("attention")
-            return out
-        parts.add(bhnd(k_rot[lo:hi]), bhnd(v_rot[lo:hi]), splits[i])
-        mark("attention")
-    out = parts.merge()
-    mark("merge")
     return out
+
+
+def gather_kv(k_all: torch.Tensor, v_all: torch.Tensor, group=None) -> None:
+    """Fill the other ranks' rows of ``k_all, v_all [P * S, ...]`` from this rank's rows
+    (:func:`own_rows`) in place, one all-gather each (NCCL for CUDA tensors, gloo for CPU ones)."""
+    if dist.get_world_size(group) == 1:
+        return
+    for buf in (k_all, v_all):
+        dist.all_gather_into_tensor(buf, own_rows(buf, group)[0], group=group)
+
+
+def kv_gather_buffers(t_local: int, heads: int, d: int, dtype, device, group=None):
+    """``k_all, v_all [P * t_local, H, D]``: the gather buffers of :func:`sharded_self_attention`."""
+    shape = (dist.get_world_size(group) * t_local, heads, d)
+    return tuple(torch.empty(shape, dtype=dtype, device=device) for _ in range(2))
+
+
+def own_rows(buf: torch.Tensor, group=None) -> torch.Tensor:
+    """This rank's slice ``[1, S, H, D]`` of a gather buffer ``[P * S, H, D]`` (contiguous)."""
+    world = dist.get_world_size(group)
+    t = buf.shape[0] // world
+    r = dist.get_rank(group)
+    return buf[r * t:(r + 1) * t].view(1, t, *buf.shape[1:])
 
 
 def object_group(objects: int, group=None):
@@ -167,23 +143,30 @@ def object_group(objects: int, group=None):
 def block_forward_sharded(w: dict, x: torch.Tensor, mod: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
                           ck: torch.Tensor, cv: torch.Tensor, heads: int, group=None,
                           kv_buffers: tuple[torch.Tensor, torch.Tensor] | None = None,
-                          timer: PhaseTimer | None = None) -> torch.Tensor:
+                          timer: PhaseTimer | None = None, mods: tuple | None = None) -> torch.Tensor:
     """One block on this rank's rows ``x [T/P, C]`` (updated in place) of a single object.
-    ``timer`` marks the phases: LN + QKV projection, attention (own keys, then the other ranks'),
-    exposed K/V exchange wait, merge, self-attention output projection, LN + cross-attention Q,
-    cross-attention, its output projection, LN + MLP."""
+    ``kv_buffers``: the K/V gather buffers (:func:`kv_gather_buffers`; allocated when None).
+    ``timer`` marks the phases: LN + QKV projection, K/V gather, self-attention, its output
+    projection, LN + cross-attention Q, cross-attention, its output projection, LN + MLP.
+    ``mods``: this block's modulation vectors precomputed by
+    :func:`hi3d_b200.transformer.modulation_all`."""
     mark = timer.mark if timer is not None else (lambda name: None)
     mark("start")
     t_local, c = x.shape
     d = c // heads
     scale = d ** -0.5
     dt = x.dtype
-    shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp = _modulation(w, mod, c, dt)
+    shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp = mods if mods is not None else \
+        _modulation(w, mod, c, dt)
 
+    if kv_buffers is None:
+        kv_buffers = kv_gather_buffers(t_local, heads, d, dt, x.device, group)
+    k_all, v_all = kv_buffers
     h = kernels.layer_norm_modulate(x, 1e-6, scale=scale_msa, shift=shift_msa)
-    q, k, v = qkv_rope(h, w, cos, sin, 1, heads, d, token_major=True)
+    q, _, _ = qkv_rope(h, w, cos, sin, 1, heads, d, token_major=True,
+                       out=(None, own_rows(k_all, group), own_rows(v_all, group)))
     mark("qkv")
-    a = sharded_self_attention(q, k[0], v[0], scale, group, kv_buffers, mark)
+    a = sharded_self_attention(q, k_all, v_all, scale, group, mark)
     linear(a[0], w, "self_attn.to_out", epilogue="residual", residual=x, gate=gate_msa)
     mark("to_out")
 
@@ -210,18 +193,23 @@ class ShardedBlockStack:
         self.heads = heads
         self.group = group
         self._kv = None
+        self._mod_w = None  # [blocks, 6C] stacked modulation parameters (built on first use)
 
     def __call__(self, x_local: torch.Tensor, mod: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
                  kvs: list[tuple[torch.Tensor, torch.Tensor]], timer: PhaseTimer | None = None) -> torch.Tensor:
         x = x_local.clone()
         t_local, c = x.shape
         world = dist.get_world_size(self.group)
-        shape = ((world - 1) * t_local, self.heads, c // self.heads)
-        if self._kv is None or self._kv[0].shape != shape or self._kv[0].device != x.device:
-            self._kv = tuple(torch.empty(shape, dtype=x.dtype, device=x.device) for _ in range(2))
+        shape = (world * t_local, self.heads, c // self.heads)
+        if (self._kv is None or self._kv[0].shape != shape or self._kv[0].device != x.device
+                or self._kv[0].dtype != x.dtype):
+            self._kv = kv_gather_buffers(t_local, self.heads, c // self.heads, x.dtype, x.device, self.group)
+        if self._mod_w is None:
+            self._mod_w = torch.stack([w["modulation"].reshape(-1).float() for w in self.weights])
+        mods = modulation_all(self._mod_w, mod, c, x.dtype)  # every block's vectors in a few launches
         for i, w in enumerate(self.weights):
             block_forward_sharded(w, x, mod, cos, sin, kvs[i][0], kvs[i][1], self.heads, self.group, self._kv,
-                                  timer=timer)
+                                  timer=timer, mods=mods[i])
         return x
 
 
@@ -284,7 +272,7 @@ def sharded_attention(comm: NcclComm, q: torch.Tensor, k: torch.Tensor, v: torch
                       kv_buffers: tuple[torch.Tensor, torch.Tensor] | None = None) -> torch.Tensor:
     """Self-attention of this rank's rows through the native ``hi3d_sharded_attn``: ``q, k, v
     [S, H, D]`` (token-major slices of one sequence, rank order); K/V gathered over the library's
-    NCCL communicator while the own keys are attended.  Returns ``[S, H * D]``."""
+    NCCL communicator, then all keys attended in one launch.  Returns ``[S, H * D]``."""
     import ctypes
 
     from . import _lib

@@ -65,13 +65,15 @@ def layer_norm_modulate(x: torch.Tensor, eps: float, weight: torch.Tensor | None
 
 
 def qkv_rope_rms(qkv: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, gamma_q: torch.Tensor,
-                 gamma_k: torch.Tensor, batch: int, heads: int, head_dim: int, token_major: bool = False):
+                 gamma_k: torch.Tensor, batch: int, heads: int, head_dim: int, token_major: bool = False,
+                 out: tuple | None = None):
     """Split a fused ``[B * N, 3 * H * D]`` projection into ``q, k, v [B, H, N, D]``.
 
     RoPE on adjacent channel pairs (``cos``/``sin`` ``[N, D/2]`` fp32), then
     ``x / max(|x|, 1e-12) * gamma * sqrt(D)`` on queries and keys in fp32; values are
     copied bit-exactly.  Reference: kernels.py:22-90.  ``token_major=True`` returns
-    ``[B, N, H, D]`` instead (rows contiguous per token, for a cross-rank gather).
+    ``[B, N, H, D]`` instead (rows contiguous per token, for a cross-rank gather).  ``out``:
+    optional ``(q, k, v)`` tensors to write (None entries are allocated).
     """
     _lib.require_cuda(qkv, cos, sin, gamma_q, gamma_k)
     rows = qkv.shape[0]
@@ -88,9 +90,9 @@ def qkv_rope_rms(qkv: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, gamma_
     gq = gamma_q.float().reshape(heads, head_dim).contiguous()
     gk = gamma_k.float().reshape(heads, head_dim).contiguous()
     shape = (batch, n, heads, head_dim) if token_major else (batch, heads, n, head_dim)
-    q = torch.empty(shape, dtype=qkv.dtype, device=qkv.device)
-    k = torch.empty_like(q)
-    v = torch.empty_like(q)
+    from .linear import qkv_outputs
+
+    q, k, v = qkv_outputs(shape, qkv.dtype, qkv.device, out)
     rc = _lib.load().hi3d_qkv_rope_rms(qkv.data_ptr(), cos.data_ptr(), sin.data_ptr(), gq.data_ptr(), gk.data_ptr(),
                                        q.data_ptr(), k.data_ptr(), v.data_ptr(), batch, n, heads, head_dim,
                                        int(token_major), _lib.dtype_code(qkv), _lib.stream(qkv))

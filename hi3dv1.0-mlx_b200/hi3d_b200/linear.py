@@ -65,7 +65,21 @@ def qkv_rope_supported(heads: int, head_dim: int) -> bool:
     return head_dim == 64 and (heads * 64) % 256 == 0
 
 
-def _qkv_rope_args(x, cos, sin, gamma_q, gamma_k, batch, heads, head_dim, token_major, dtype):
+def qkv_outputs(shape: tuple, dtype: torch.dtype, device, out: tuple | None):
+    """``q, k, v`` output tensors of ``shape``: new ones, or the caller's (``out``), which must be
+    contiguous tensors of that shape and dtype on the device (e.g. this rank's slot of a K/V
+    gather buffer, so the projection writes there directly)."""
+    if out is None:
+        q = torch.empty(shape, dtype=dtype, device=device)
+        return q, torch.empty_like(q), torch.empty_like(q)
+    for t in out:
+        if t is not None and (tuple(t.shape) != tuple(shape) or t.dtype != dtype or not t.is_contiguous()
+                              or t.device != torch.device(device)):
+            raise ValueError(f"q/k/v outputs must be contiguous {tuple(shape)} {dtype} tensors on {device}")
+    return tuple(torch.empty(shape, dtype=dtype, device=device) if t is None else t for t in out)
+
+
+def _qkv_rope_args(x, cos, sin, gamma_q, gamma_k, batch, heads, head_dim, token_major, dtype, out=None):
     k = x.shape[-1]
     a = x.reshape(-1, k)
     if not a.is_contiguous():
@@ -81,26 +95,26 @@ def _qkv_rope_args(x, cos, sin, gamma_q, gamma_k, batch, heads, head_dim, token_
     gq = gamma_q.float().reshape(heads, head_dim).contiguous()
     gk = gamma_k.float().reshape(heads, head_dim).contiguous()
     shape = (batch, n, heads, head_dim) if token_major else (batch, heads, n, head_dim)
-    q = torch.empty(shape, dtype=dtype, device=x.device)
-    return a, m, n, cos, sin, gq, gk, q, torch.empty_like(q), torch.empty_like(q)
+    q, k, v = qkv_outputs(shape, dtype, x.device, out)
+    return a, m, n, cos, sin, gq, gk, q, k, v
 
 
 def linear_qkv_rope(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None, cos: torch.Tensor,
                     sin: torch.Tensor, gamma_q: torch.Tensor, gamma_k: torch.Tensor, batch: int, heads: int,
-                    head_dim: int, token_major: bool = False):
+                    head_dim: int, token_major: bool = False, out: tuple | None = None):
     """The attention input projection ``x @ W^T + bias`` (``W [3 H D, K]``) split into
     ``q, k, v [B, H, N, D]`` with RoPE + QK RMS norm applied in the GEMM epilogue: the same
     result as :func:`linear` followed by :func:`hi3d_b200.kernels.qkv_rope_rms`
     (transformer.py:501-516, kernels.py:22-90) without writing the projection to memory.
-    ``token_major=True`` returns ``[B, N, H, D]``.  Raises ``NotImplementedError`` unless
-    :func:`qkv_rope_supported`."""
+    ``token_major=True`` returns ``[B, N, H, D]``.  ``out``: optional ``(q, k, v)`` tensors to write
+    (None entries are allocated).  Raises ``NotImplementedError`` unless :func:`qkv_rope_supported`."""
     _lib.require_cuda(x, weight, bias, cos, sin, gamma_q, gamma_k)
     if x.dtype not in (torch.float16, torch.bfloat16) or weight.dtype != x.dtype:
         raise ValueError("linear_qkv_rope takes float16/bfloat16 activations and weights of one dtype")
     if weight.shape != (3 * heads * head_dim, x.shape[-1]):
         raise ValueError(f"weight must be [3*H*D, K], got {tuple(weight.shape)}")
     a, m, n, cos, sin, gq, gk, q, k, v = _qkv_rope_args(x, cos, sin, gamma_q, gamma_k, batch, heads, head_dim,
-                                                        token_major, x.dtype)
+                                                        token_major, x.dtype, out)
     b = None if bias is None else bias.to(x.dtype).contiguous()
     rc = _lib.load().hi3d_gemm_qkv_rope(a.data_ptr(), weight.contiguous().data_ptr(), _lib.ptr(b), cos.data_ptr(),
                                         sin.data_ptr(), gq.data_ptr(), gk.data_ptr(), q.data_ptr(), k.data_ptr(),

@@ -90,20 +90,21 @@ def linear(x: torch.Tensor, w: dict, name: str, epilogue: str = "store", residua
 
 
 def qkv_rope(h: torch.Tensor, w: dict, cos: torch.Tensor, sin: torch.Tensor, batch: int, heads: int, d: int,
-             token_major: bool = False):
+             token_major: bool = False, out: tuple | None = None):
     """``q, k, v`` of the self-attention: the ``self_attn.to_qkv`` projection with RoPE + QK RMS
     norm (transformer.py:501-516 then kernels.py:22-90).  Fused into the GEMM epilogue when the
-    head layout allows it (head dim 64), else the projection followed by the row kernel."""
+    head layout allows it (head dim 64), else the projection followed by the row kernel.
+    ``out``: optional ``(q, k, v)`` tensors written in place of new ones."""
     name = "self_attn.to_qkv"
     gq, gk = w["self_attn.q_rms_norm.gamma"], w["self_attn.k_rms_norm.gamma"]
     if _linear.qkv_rope_supported(heads, d):
         if f"{name}.w8_scale" in w:
             return _w8a8.linear_qkv_rope(h, w[f"{name}.weight"], w[f"{name}.w8_scale"], w[f"{name}.bias"], cos, sin,
-                                         gq, gk, batch, heads, d, token_major)
+                                         gq, gk, batch, heads, d, token_major, out=out)
         return _linear.linear_qkv_rope(h, w[f"{name}.weight"], w[f"{name}.bias"], cos, sin, gq, gk, batch, heads, d,
-                                       token_major)
+                                       token_major, out=out)
     qkv = linear(h, w, name)
-    return kernels.qkv_rope_rms(qkv, cos, sin, gq, gk, batch, heads, d, token_major=token_major)
+    return kernels.qkv_rope_rms(qkv, cos, sin, gq, gk, batch, heads, d, token_major=token_major, out=out)
 
 
 BLOCK_PROJECTIONS = ("self_attn.to_qkv", "self_attn.to_out", "cross_attn.to_q", "cross_attn.to_out", "mlp.mlp.0",

@@ -181,7 +181,7 @@ def linear(x: torch.Tensor, w: torch.Tensor, sw: torch.Tensor, bias: torch.Tenso
 def linear_qkv_rope(x: torch.Tensor, w: torch.Tensor, sw: torch.Tensor, bias: torch.Tensor, cos: torch.Tensor,
                     sin: torch.Tensor, gamma_q: torch.Tensor, gamma_k: torch.Tensor, batch: int, heads: int,
                     head_dim: int, token_major: bool = False, multiplier: torch.Tensor | None = None,
-                    rotate: bool = True):
+                    rotate: bool = True, out: tuple | None = None):
     """The attention input projection through int8 (as :func:`linear`, w8a8.py:105-119) with
     RoPE + QK RMS norm + head split in the GEMM epilogue (as ``hi3d_b200.linear.linear_qkv_rope``)."""
     from .linear import _qkv_rope_args
@@ -193,7 +193,7 @@ def linear_qkv_rope(x: torch.Tensor, w: torch.Tensor, sw: torch.Tensor, bias: to
         raise ValueError("incompatible W8A8 projection shapes")
     aq, sa, out_dtype = _quantized(x, multiplier, rotate)
     _, m, n, cos, sin, gq, gk, q, k, v = _qkv_rope_args(aq, cos, sin, gamma_q, gamma_k, batch, heads, head_dim,
-                                                        token_major, out_dtype)
+                                                        token_major, out_dtype, out)
     b = bias.to(out_dtype).contiguous()
     rc = _lib.load().hi3d_gemm_w8a8_qkv_rope(aq.data_ptr(), w.contiguous().data_ptr(), sa.data_ptr(),
                                              sw.contiguous().data_ptr(), b.data_ptr(), cos.data_ptr(), sin.data_ptr(),

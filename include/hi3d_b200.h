@@ -187,9 +187,10 @@ HI3D_API int hi3d_flash_attn_fwd_partial_merge(const hi3d_attn_args* args, int s
  * one GPU and has no counterpart; it replaces attention.flash_attention, attention.py:238-277,
  * over all T rows).  This rank holds rows [rank * s_rows, (rank + 1) * s_rows) of one sequence:
  * q, k, v [s_rows, heads, head_dim] token-major.  The K/V slices of all ranks are all-gathered
- * into k_all, v_all [world * s_rows, heads, head_dim] on a side stream while the stream attends
- * the rank's own keys; then the keys before and after its slice; the partials are merged into
- * out [s_rows, heads * head_dim].  Same numerics as hi3d_flash_attn_fwd_split. */
+ * into k_all, v_all [world * s_rows, heads, head_dim] on a high-priority side stream, which
+ * `stream` then waits for; the queries attend all keys in one launch (key-split when the grid
+ * is short of waves) into out [s_rows, heads * head_dim].  Same numerics as
+ * hi3d_flash_attn_fwd_split over the gathered keys. */
 HI3D_API int hi3d_nccl_unique_id(void* id);
 HI3D_API int hi3d_nccl_comm_init(const void* id, int world, int rank, void** comm);
 HI3D_API int hi3d_nccl_comm_destroy(void* comm);

@@ -145,11 +145,12 @@ def test_key_split_varlen_with_short_and_empty_sequences():
 
 def test_auto_splits_fill_waves():
     assert attention.auto_splits(2048, 256, 148) == 1   # cfg1 on one GPU: 13.8 waves already
-    assert attention.auto_splits(256, 256, 148) == 4    # one eighth of the queries per GPU
-    assert attention.auto_splits(512, 256, 148) == 2
+    assert attention.auto_splits(256, 256, 148) == 1    # one eighth of the queries per GPU: the partial
+    assert attention.auto_splits(512, 256, 148) == 1    # kernel's cost outweighs the wave tail
+    assert attention.auto_splits(16, 256, 148) == 8     # a short grid over long keys
+    assert attention.auto_splits(64, 512, 148) == 2
     assert attention.auto_splits(256, 3, 148) == 1      # too few key blocks to split
     assert attention.auto_splits(256, 11, 148) == 1     # cross-attention at 8 GPUs: CTA set-up dominates
-    assert attention.auto_splits(256, 32, 148) == 1     # one rank's own key shard at 8 GPUs
 
 
 def test_attention_parts_over_disjoint_key_sets_match_single_pass():

@@ -86,31 +86,26 @@ def _object_groups(rank, world, port):
     dist.destroy_process_group()
 
 
-def _rotated_exchange(rank, world, port):
-    """Two point-to-point groups (ranks r+1, r+2 then r+3) fill the rank-rotated buffer: row
-    block j - 1 holds rank r + j's slice, so the other ranks' rows are contiguous."""
+def _kv_gather_in_place(rank, world, port):
+    """Each rank writes its slice into its own rows of the gather buffers; the in-place gather
+    fills the other ranks' rows in rank order and leaves the own rows as they were."""
     _init(rank, world, port)
-    from hi3d_b200.dist import exchange_rotated
+    from hi3d_b200.dist import gather_kv, kv_gather_buffers, own_rows
 
     t = 3
-    k = torch.full((t, 2, 4), float(rank))
-    v = torch.full((t, 2, 4), float(100 + rank))
-    k_rot, v_rot = torch.empty(((world - 1) * t, 2, 4)), torch.empty(((world - 1) * t, 2, 4))
-    for works in (exchange_rotated(k, v, k_rot, v_rot, range(1, 3)),
-                  exchange_rotated(k, v, k_rot, v_rot, range(3, world))):
-        for w in works:
-            w.wait()
-    for j in range(1, world):
-        src = (rank + j) % world
-        assert torch.equal(k_rot[(j - 1) * t:j * t], torch.full((t, 2, 4), float(src)))
-        assert torch.equal(v_rot[(j - 1) * t:j * t], torch.full((t, 2, 4), float(100 + src)))
-    assert exchange_rotated(k, v, k_rot, v_rot, range(4, world)) == []
+    k_all, v_all = kv_gather_buffers(t, 2, 4, torch.float32, "cpu")
+    own_rows(k_all)[0].copy_(torch.full((t, 2, 4), float(rank)))
+    own_rows(v_all)[0].copy_(torch.full((t, 2, 4), float(100 + rank)))
+    gather_kv(k_all, v_all)
+    for r in range(world):
+        assert torch.equal(k_all[r * t:(r + 1) * t], torch.full((t, 2, 4), float(r)))
+        assert torch.equal(v_all[r * t:(r + 1) * t], torch.full((t, 2, 4), float(100 + r)))
     dist.barrier()
     dist.destroy_process_group()
 
 
-def test_rotated_exchange_places_each_rank_after_the_own():
-    mp.spawn(_rotated_exchange, args=(4, _free_port()), nprocs=4, join=True)
+def test_kv_gather_in_place_fills_every_rank_slot():
+    mp.spawn(_kv_gather_in_place, args=(4, _free_port()), nprocs=4, join=True)
 
 
 def test_object_groups_pair_the_ranks_of_one_object():

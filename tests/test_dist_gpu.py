@@ -1,11 +1,10 @@
 """Query-sharded block stack on 2 GPUs (NCCL) vs the single-GPU stack.
 
 Every row-wise kernel computes a row independently of the others; the sharded attention
-combines the rank's own keys (attended while the other rank's are gathered) and the gathered
-keys by their log-sum-exp weights, which agrees with the single pass to within 16-bit output
-rounding.  So the stack output must match the unsharded one to the block tolerance (relative
-L2 1e-3 over two blocks) with most elements bit-identical.  Needs two GPUs on one node;
-skipped otherwise.
+gathers every rank's keys and attends them in one pass (key-split only when the grid is short
+of waves, which agrees with the single pass to within 16-bit output rounding).  So the stack
+output must match the unsharded one to the block tolerance (relative L2 1e-3 over two blocks)
+with most elements bit-identical.  Needs two GPUs on one node; skipped otherwise.
 """
 
 from __future__ import annotations
@@ -106,8 +105,8 @@ def _worker_native(rank, world, port, result_path):
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 def test_native_sharded_attention_matches_single_gpu(tmp_path):
-    """hi3d_sharded_attn over the library's own NCCL communicator (gather on a side stream,
-    own keys first, merge) vs one pass over all keys on one GPU: within 16-bit output rounding."""
+    """hi3d_sharded_attn over the library's own NCCL communicator (gather on a side stream, then
+    all keys in one launch) vs one pass over all keys on one GPU: within 16-bit output rounding."""
     out = tmp_path / "r.npy"
     mp.spawn(_worker_native, args=(2, _free_port(), str(out)), nprocs=2, join=True)
     (rel,) = np.load(out)
