@@ -178,7 +178,7 @@ def device_weights(device, seed: int = 100, blocks: int = BLOCKS, c: int = CHANN
 # same workload.
 
 
-def stack_config(workload: str, nblocks: int, world: int) -> dict:
+def stack_config(workload: str, nblocks: int, world: int, transport: str = "nccl") -> dict:
     if workload == "stack_w8a8":
         name = (f"cfg2: W8A8 {BLOCKS}-block stack fwd (int8 signed-H64 activations, int8 rotated weights, int32 "
                 f"accumulate, fp16 dequant), T={T_TOKENS}, C={CHANNELS}, {HEADS}x{CHANNELS // HEADS} heads, "
@@ -186,8 +186,9 @@ def stack_config(workload: str, nblocks: int, world: int) -> dict:
     else:
         name = (f"cfg1: {nblocks}-block sparse-DiT stack fwd, T={T_TOKENS} shell tokens in {GRID}^3, C={CHANNELS}, "
                 f"{HEADS}x{CHANNELS // HEADS} heads, {COND} cond tokens, fp16")
+    kv = {"nccl": "NCCL all-gather", "peer": "QKV epilogue stores into peers' symmetric buffers"}[transport]
     return {"workload": name, "blocks": nblocks, "tokens": T_TOKENS,
-            "parallelism": f"query-sharded x{world}" if world > 1 else "none",
+            "parallelism": f"query-sharded x{world}, K/V by {kv}" if world > 1 else "none",
             "l2": "inputs larger than L2 (705 MB of weights + activations per step)"}
 
 
@@ -401,7 +402,7 @@ def run_reference(args) -> None:
         steps(cpu_block_seconds)
         metric, unit = "block_tokens_per_s", "tokens/s"
         value = T_TOKENS * len(secs) / sum(secs)
-        config = stack_config(args.workload, nblocks, world)
+        config = stack_config(args.workload, nblocks, world, args.kv_transport)
         desc = (f"one whole fp32 block at T={T_TOKENS} per step (each of the stack's {nblocks} blocks has this "
                 f"shape): the reference's CPU path, upstream block + flash_attn shim (SDPA over query blocks), "
                 f"restated in torch and pinned to the upstream module")
@@ -476,6 +477,37 @@ def _timed(fn, steps: int, warmup: int) -> float:
     e1.record()
     torch.cuda.synchronize()
     return e0.elapsed_time(e1) / steps
+
+
+def _timed_graph(fn, steps: int, warmup: int, per_graph: int = 16) -> float:
+    """Milliseconds per call of ``fn`` on the device alone: ``per_graph`` calls captured in one
+    CUDA graph, replayed ``steps`` times between CUDA events (after ``warmup`` eager calls and one
+    replay).  For kernels of a few tens of microseconds, whose eager launches through Python
+    would leave the GPU waiting on the host."""
+    import torch
+
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(side):
+        with torch.cuda.graph(graph, stream=side):
+            for _ in range(per_graph):
+                fn()
+    torch.cuda.current_stream().wait_stream(side)
+    graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / (steps * per_graph)
+    del graph
+    return ms
 
 
 def _max_over_ranks(ms: float, world: int, dev) -> float:
@@ -613,7 +645,8 @@ def measure_cfg4(dev, world: int, rank: int, steps: int, warmup: int, sub) -> di
     return line
 
 
-def sharded_parity(weights, inputs_local, inputs_full, world: int, rank: int, dev) -> float | None:
+def sharded_parity(weights, inputs_local, inputs_full, world: int, rank: int, dev,
+                   transport: str = "nccl") -> float | None:
     """Relative L2 between the first two blocks run query-sharded over the ranks and the same two
     blocks on one GPU (rank 0), on the bench inputs; None on ranks other than 0."""
     import torch
@@ -623,7 +656,7 @@ def sharded_parity(weights, inputs_local, inputs_full, world: int, rank: int, de
     x_l, mod_d, cos_l, sin_l, cond_d = inputs_local
     two = weights[:2]
     kvs = [transformer.context_kv(w, cond_d, HEADS) for w in two]
-    y_local = hdist.ShardedBlockStack(two, HEADS)(x_l, mod_d, cos_l, sin_l, kvs)
+    y_local = hdist.ShardedBlockStack(two, HEADS, transport=transport)(x_l, mod_d, cos_l, sin_l, kvs)
     y_all = hdist.gather_rows(y_local)
     if rank != 0:
         return None
@@ -669,7 +702,7 @@ def run_ours(args) -> None:
         stack = transformer.BlockStack(weights, HEADS)
         run = lambda xin: stack(xin[None], mod_d, cos_d, sin_d, kvs)[0]
     else:
-        stack = hdist.ShardedBlockStack(weights, HEADS)
+        stack = hdist.ShardedBlockStack(weights, HEADS, transport=args.kv_transport)
         run = lambda xin: stack(xin, mod_d, cos_d, sin_d, kvs)
     kvs = [transformer.context_kv(w, cond_d, HEADS) for w in weights]
 
@@ -744,7 +777,7 @@ def run_ours(args) -> None:
         "metric": "block_tokens_per_s", "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-        "config": stack_config(args.workload, nblocks, world),
+        "config": stack_config(args.workload, nblocks, world, args.kv_transport),
         "roofline": roofline,
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": x_host.numel() * 2,
                 "d2h_bytes_per_step": out_host.numel() * 2},
@@ -777,7 +810,7 @@ def run_ours(args) -> None:
             cos_f = torch.from_numpy(cos).to(dev) if rank == 0 else None
             sin_f = torch.from_numpy(sin).to(dev) if rank == 0 else None
             err = sharded_parity(weights, (x_dev, mod_d, cos_d, sin_d, cond_d), (x_full, cos_f, sin_f), world, rank,
-                                 dev)
+                                 dev, args.kv_transport)
             if rank == 0:
                 line["sharded_rel_l2"] = err
                 line["sharded_rel_l2_case"] = "first 2 blocks query-sharded vs one GPU on the bench inputs"
@@ -1141,38 +1174,67 @@ def run_kernels(args) -> None:
         it[0] += 1
         return xs[it[0] % 8]
 
+    xqs = {k: [torch.randn((R, k), generator=g, device=dev).half() for _ in range(8 if k == 1024 else 2)]
+           for k in (1024, 4096)}
+    wt = (torch.randn((C, C), generator=g, device=dev) * 0.02).half()
+    bt = (torch.randn(C, generator=g, device=dev) * 0.02).half()
+    resids = [torch.randn((R, C), generator=g, device=dev).half() for _ in range(8)]
+    gate = (torch.randn(C, generator=g, device=dev) * 0.1).half()
+
+    def ln(**kw):
+        return lambda: kernels.layer_norm_modulate(rot(), 1e-6, **kw)
+
+    def quant(k):
+        def call():
+            it[0] += 1
+            return w8a8.quantize_activation(xqs[k][it[0] % len(xqs[k])])
+        return call
+
+    def gemm(**kw):
+        def call():
+            a = rot()  # activations and residuals rotated over 8 copies each (> L2)
+            extra = dict(residual=resids[it[0] % 8]) if kw["epilogue"] == "residual" else {}
+            return linear.linear(a, wt, bt, **kw, **extra)
+        return call
+
+    hbm = lambda nbytes: lambda ms: {"gbs": nbytes / (ms / 1e3) / 1e9,
+                                     "hbm_frac": nbytes / (ms / 1e3) / 1e9 / peaks["hbm_gbs"]}
+    tensor = lambda flop: lambda ms: {"tflops": flop / (ms / 1e3) / 1e12,
+                                      "tensor_frac": flop / (ms / 1e3) / 1e12 / peaks["bf16_tflops"]}
+    table = [  # name, call, algorithmic rate from the per-launch time
+        ("layer_norm_modulate", ln(scale=sc, shift=sh), hbm(4.0 * R * C)),
+        ("layer_norm_affine", ln(weight=wln, bias=bln), hbm(4.0 * R * C)),
+        ("quantize_act_i8_k1024", quant(1024), hbm(3.0 * R * 1024 + 4 * R)),
+        ("quantize_act_i8_k4096", quant(4096), hbm(3.0 * R * 4096 + 4 * R)),
+        ("gemm_store", gemm(epilogue="store"), tensor(2.0 * R * C * C)),
+        ("gemm_residual", gemm(epilogue="residual"), tensor(2.0 * R * C * C)),
+        ("gemm_gated_residual", gemm(epilogue="residual", gate=gate), tensor(2.0 * R * C * C)),
+    ]
+    if args.only:
+        table = [t for t in table if t[0] == args.only]
+        if not table:
+            raise SystemExit(f"--only {args.only}: not a kernel of this workload")
+    # every kernel's launches captured in a CUDA graph (_timed_graph): eager launches through
+    # Python take longer on the host than these kernels take on the device
     with ClockSampler(0) as clocks:
-        for name, kw in (("layer_norm_modulate", dict(scale=sc, shift=sh)), ("layer_norm_affine", dict(weight=wln, bias=bln))):
-            ms = _timed(lambda: kernels.layer_norm_modulate(rot(), 1e-6, **kw), args.steps, args.warmup)
-            gbs = 4.0 * R * C / (ms / 1e3) / 1e9
-            res[name] = {"us": ms * 1e3, "gbs": gbs, "hbm_frac": gbs / peaks["hbm_gbs"]}
-        for k in (1024, 4096):
-            xq = torch.randn((R, k), generator=g, device=dev).half()
-            ms = _timed(lambda: w8a8.quantize_activation(xq), args.steps, args.warmup)
-            gbs = (3.0 * R * k + 4 * R) / (ms / 1e3) / 1e9
-            res[f"quantize_act_i8_k{k}"] = {"us": ms * 1e3, "gbs": gbs, "hbm_frac": gbs / peaks["hbm_gbs"]}
-        a = xs[0]
-        wt = (torch.randn((C, C), generator=g, device=dev) * 0.02).half()
-        bt = (torch.randn(C, generator=g, device=dev) * 0.02).half()
-        resid = torch.randn((R, C), generator=g, device=dev).half()
-        gate = torch.randn(C, generator=g, device=dev).half()
-        for name, kw in (("gemm_store", dict(epilogue="store")), ("gemm_residual", dict(epilogue="residual", residual=resid)),
-                         ("gemm_gated_residual", dict(epilogue="residual", residual=resid, gate=gate))):
-            ms = _timed(lambda: linear.linear(a, wt, bt, **kw), args.steps, args.warmup)
-            tf = 2.0 * R * C * C / (ms / 1e3) / 1e12
-            res[name] = {"us": ms * 1e3, "tflops": tf, "tensor_frac": tf / peaks["bf16_tflops"]}
+        for name, call, rate in table:
+            ms = _timed_graph(call, args.steps, args.warmup)
+            res[name] = {"us": ms * 1e3, **rate(ms)}
     launches = _lib.LAUNCHES[0]
-    v = res["layer_norm_modulate"]["gbs"]
+    head = table[0][0]
+    v = res[head].get("gbs", res[head].get("tflops"))
+    unit = "GB/s" if "gbs" in res[head] else "TFLOP/s"
     line = {
-        "metric": "layer_norm_modulate_gbs", "value": v, "unit": "GB/s", "n_gpus": 1,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": res["layer_norm_modulate"]["us"] / 1e3,
+        "metric": f"{head}_{'gbs' if unit == 'GB/s' else 'tflops'}", "value": v, "unit": unit, "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": res[head]["us"] / 1e3,
         "higher_is_better": True, "scaling": "none", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
         "config": {"workload": f"row kernels and projection epilogues at T={R}, C={C} (quantiser also at width "
-                               f"4096), fp16, each timed alone", "kernels": res,
-                   "l2": "LayerNorm inputs rotated over 8 copies (> L2); quantiser / GEMM inputs > L2",
+                               f"4096), fp16, each timed alone (16 launches per CUDA graph replay)", "kernels": res,
+                   "l2": "every kernel's inputs rotated over copies totalling more than L2",
                    "peak_source": f"{peaks['source']} hbm_gbs {peaks['hbm_gbs']}, bf16_tflops {peaks['bf16_tflops']}"},
-        "roofline": {"bound": "hbm", "achieved": v, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                     "frac": v / peaks["hbm_gbs"], "traffic": None},
+        "roofline": {"bound": "hbm" if unit == "GB/s" else "tensor", "achieved": v,
+                     "peak": peaks["hbm_gbs"] if unit == "GB/s" else peaks["bf16_tflops"], "unit": unit,
+                     "frac": res[head].get("hbm_frac", res[head].get("tensor_frac")), "traffic": None},
         "gpu_launches": launches, "clocks": clocks.summary(),
     }
     print(json.dumps(line), flush=True)
@@ -1258,6 +1320,10 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-extras", action="store_true", help="headline only (no cfg2/cfg4/cfg5 extras)")
+    ap.add_argument("--kv-transport", choices=["nccl", "peer"], default="nccl",
+                    help="N > 1: K/V of each block by NCCL all-gather, or by the QKV projection's own stores into "
+                         "the peers' symmetric buffers")
+    ap.add_argument("--only", default=None, help="--workload kernels: time this one kernel (e.g. layer_norm_affine)")
     ap.add_argument("--workload", choices=["stack", "stack_w8a8", "block", "attention", "attention262k", "conv",
                                            "forward", "vae", "released", "kernels"], default="stack")
     args = ap.parse_args()

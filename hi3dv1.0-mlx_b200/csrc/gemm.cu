@@ -48,6 +48,7 @@ constexpr int SMEM_PAIR =
 enum Kind { KIND_F16 = 0, KIND_BF16 = 1, KIND_I8 = 2 };
 
 enum Epi { EPI_STORE = 0, EPI_GELU = 1, EPI_RESIDUAL = 2, EPI_QKV_ROPE = 3 };
+constexpr int kMaxPeers = 7;  // peer GPUs of one node
 
 struct Params {
   void* out;          // [M, ldo] output (or the residual stream for EPI_RESIDUAL)
@@ -70,6 +71,11 @@ struct Params {
   void* k;
   void* v;
   int seq_n, heads, token_major;
+  // EPI_QKV_ROPE: every k / v store is repeated at address + peer_off[i] (the same rows of
+  // the peers' gather buffers, mapped into this process), so the projection itself
+  // all-gathers K and V over NVLink
+  int npeers;
+  int64_t peer_off[kMaxPeers];
 };
 
 struct Barriers {
@@ -385,7 +391,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int b2 = m / p.seq_n, n2 = m - b2 * p.seq_n;
                 const int64_t row = p.token_major ? ((int64_t)b2 * p.seq_n + n2) * p.heads + head
                                                   : ((int64_t)b2 * p.heads + head) * p.seq_n + n2;
-                *reinterpret_cast<uint4*>(dst_base + row * 64 + half * 32 + j * 8) = yq;
+                OutT* dst = dst_base + row * 64 + half * 32 + j * 8;
+                *reinterpret_cast<uint4*>(dst) = yq;
+                if (part > 0) {  // K and V rows also into every peer's gather buffer (NVLink stores)
+#pragma unroll 1
+                  for (int pp = 0; pp < p.npeers; ++pp)
+                    *reinterpret_cast<uint4*>(reinterpret_cast<char*>(dst) + p.peer_off[pp]) = yq;
+                }
               }
             }
             __syncwarp();
@@ -520,6 +532,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive(&bar->acc_empty[acc]);
       }
     }
+    // stores into the peers' gather buffers are performed at system scope before this grid
+    // completes, hence before the cross-GPU barrier that follows it on the stream signals them
+    if (EPI == EPI_QKV_ROPE && p.npeers > 0) __threadfence_system();
   }
 
   tc_fence_before();
@@ -744,14 +759,38 @@ static int qkv_rope_params(const char* what, const void* a, const void* w, const
   return HI3D_OK;
 }
 
+static int set_peers(const char* what, const int64_t* peer_offsets, int num_peers, gemm::Params* p) {
+  if (num_peers < 0 || num_peers > gemm::kMaxPeers || (num_peers > 0 && !peer_offsets))
+    return set_error(HI3D_ERR_INVALID_ARGUMENT, "%s: num_peers must be in [0, %d] with the offsets given", what,
+                     gemm::kMaxPeers);
+  p->npeers = num_peers;
+  for (int i = 0; i < num_peers; ++i) {
+    if (peer_offsets[i] % 16 || peer_offsets[i] == 0)
+      return set_error(HI3D_ERR_INVALID_ARGUMENT, "%s: peer offset %d must be a non-zero multiple of 16 bytes", what,
+                       i);
+    p->peer_off[i] = peer_offsets[i];
+  }
+  return HI3D_OK;
+}
+
 extern "C" int hi3d_gemm_qkv_rope(const void* a, const void* w, const void* bias, const float* cosv,
                                   const float* sinv, const float* gamma_q, const float* gamma_k, void* q, void* k,
                                   void* v, int64_t m, int64_t n_seq, int heads, int head_dim, int64_t kdim,
                                   int token_major, int dtype, void* stream) {
+  return hi3d_gemm_qkv_rope_peers(a, w, bias, cosv, sinv, gamma_q, gamma_k, q, k, v, m, n_seq, heads, head_dim, kdim,
+                                  token_major, dtype, nullptr, 0, stream);
+}
+
+extern "C" int hi3d_gemm_qkv_rope_peers(const void* a, const void* w, const void* bias, const float* cosv,
+                                        const float* sinv, const float* gamma_q, const float* gamma_k, void* q,
+                                        void* k, void* v, int64_t m, int64_t n_seq, int heads, int head_dim,
+                                        int64_t kdim, int token_major, int dtype, const int64_t* peer_offsets,
+                                        int num_peers, void* stream) {
   gemm::Params p;
   int rc = qkv_rope_params("gemm_qkv_rope", a, w, cosv, sinv, gamma_q, gamma_k, q, k, v, m, n_seq, heads, head_dim,
                            kdim, token_major, &p);
   if (rc) return rc;
+  if ((rc = set_peers("gemm_qkv_rope", peer_offsets, num_peers, &p))) return rc;
   if (kdim % 8) return set_error(HI3D_ERR_INVALID_ARGUMENT, "gemm_qkv_rope: K must be a multiple of 8");
   if (m == 0) return HI3D_OK;
   p.bias = bias;
@@ -769,10 +808,21 @@ extern "C" int hi3d_gemm_w8a8_qkv_rope(const int8_t* a, const int8_t* w, const f
                                        const float* gamma_k, void* q, void* k, void* v, int64_t m, int64_t n_seq,
                                        int heads, int head_dim, int64_t kdim, int token_major, int out_dtype,
                                        void* stream) {
+  return hi3d_gemm_w8a8_qkv_rope_peers(a, w, sa, sw, bias, cosv, sinv, gamma_q, gamma_k, q, k, v, m, n_seq, heads,
+                                       head_dim, kdim, token_major, out_dtype, nullptr, 0, stream);
+}
+
+extern "C" int hi3d_gemm_w8a8_qkv_rope_peers(const int8_t* a, const int8_t* w, const float* sa, const float* sw,
+                                             const void* bias, const float* cosv, const float* sinv,
+                                             const float* gamma_q, const float* gamma_k, void* q, void* k, void* v,
+                                             int64_t m, int64_t n_seq, int heads, int head_dim, int64_t kdim,
+                                             int token_major, int out_dtype, const int64_t* peer_offsets,
+                                             int num_peers, void* stream) {
   gemm::Params p;
   int rc = qkv_rope_params("gemm_w8a8_qkv_rope", a, w, cosv, sinv, gamma_q, gamma_k, q, k, v, m, n_seq, heads,
                            head_dim, kdim, token_major, &p);
   if (rc) return rc;
+  if ((rc = set_peers("gemm_w8a8_qkv_rope", peer_offsets, num_peers, &p))) return rc;
   if (!sa || !sw) return set_error(HI3D_ERR_INVALID_ARGUMENT, "gemm_w8a8_qkv_rope: scales are required");
   if (kdim % 16) return set_error(HI3D_ERR_INVALID_ARGUMENT, "gemm_w8a8_qkv_rope: K must be a multiple of 16");
   if (m == 0) return HI3D_OK;

@@ -15,6 +15,7 @@ import torch
 import torch.distributed as dist
 
 from . import attention, kernels
+from .peer import PeerKV
 from .transformer import _modulation, linear, modulation_all, qkv_rope
 
 
@@ -87,16 +88,30 @@ def sharded_self_attention(q: torch.Tensor, k_all: torch.Tensor, v_all: torch.Te
     mark = mark or (lambda name: None)
     gather_kv(k_all, v_all, group)
     mark("kv_gather_wait")
-    bhnd = lambda x: x.permute(1, 0, 2)[None]  # [rows, H, D] token-major -> [1, H, rows, D] view
-    out = attention.flash_attention(q, bhnd(k_all), bhnd(v_all), scale, q_layout="bnhd")
+    out = attend_gathered(q, k_all, v_all, scale)
     mark("attention")
     return out
 
 
+def attend_gathered(q: torch.Tensor, k_all: torch.Tensor, v_all: torch.Tensor, scale: float) -> torch.Tensor:
+    """This rank's queries ``[1, S, H, D]`` over all gathered keys ``[P * S, H, D]`` in one pass
+    (key-split only when the grid is short of waves); returns ``[1, S, H * D]``."""
+    bhnd = lambda x: x.permute(1, 0, 2)[None]  # [rows, H, D] token-major -> [1, H, rows, D] view
+    return attention.flash_attention(q, bhnd(k_all), bhnd(v_all), scale, q_layout="bnhd")
+
+
 def gather_kv(k_all: torch.Tensor, v_all: torch.Tensor, group=None) -> None:
     """Fill the other ranks' rows of ``k_all, v_all [P * S, ...]`` from this rank's rows
-    (:func:`own_rows`) in place, one all-gather each (NCCL for CUDA tensors, gloo for CPU ones)."""
+    (:func:`own_rows`) in place: one all-gather each, both in one NCCL group for CUDA tensors
+    (gloo for CPU ones)."""
     if dist.get_world_size(group) == 1:
+        return
+    if k_all.is_cuda:  # both gathers in one NCCL group (one launch)
+        from torch.distributed.distributed_c10d import _coalescing_manager
+
+        with _coalescing_manager(group):
+            for buf in (k_all, v_all):
+                dist.all_gather_into_tensor(buf, own_rows(buf, group)[0], group=group)
         return
     for buf in (k_all, v_all):
         dist.all_gather_into_tensor(buf, own_rows(buf, group)[0], group=group)
@@ -142,12 +157,15 @@ def object_group(objects: int, group=None):
 
 def block_forward_sharded(w: dict, x: torch.Tensor, mod: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
                           ck: torch.Tensor, cv: torch.Tensor, heads: int, group=None,
-                          kv_buffers: tuple[torch.Tensor, torch.Tensor] | None = None,
-                          timer: PhaseTimer | None = None, mods: tuple | None = None) -> torch.Tensor:
+                          kv_buffers=None, timer: PhaseTimer | None = None,
+                          mods: tuple | None = None) -> torch.Tensor:
     """One block on this rank's rows ``x [T/P, C]`` (updated in place) of a single object.
-    ``kv_buffers``: the K/V gather buffers (:func:`kv_gather_buffers`; allocated when None).
-    ``timer`` marks the phases: LN + QKV projection, K/V gather, self-attention, its output
-    projection, LN + cross-attention Q, cross-attention, its output projection, LN + MLP.
+    ``kv_buffers``: the K/V gather buffers, either a pair from :func:`kv_gather_buffers` (filled
+    by an NCCL all-gather after the projection; allocated when None) or a
+    :class:`hi3d_b200.peer.PeerKV` (the projection stores the rows into every peer's buffer
+    itself, then a cross-GPU barrier).  ``timer`` marks the phases: LN + QKV projection, K/V
+    gather (or barrier), self-attention, its output projection, LN + cross-attention Q,
+    cross-attention, its output projection, LN + MLP.
     ``mods``: this block's modulation vectors precomputed by
     :func:`hi3d_b200.transformer.modulation_all`."""
     mark = timer.mark if timer is not None else (lambda name: None)
@@ -161,12 +179,22 @@ def block_forward_sharded(w: dict, x: torch.Tensor, mod: torch.Tensor, cos: torc
 
     if kv_buffers is None:
         kv_buffers = kv_gather_buffers(t_local, heads, d, dt, x.device, group)
-    k_all, v_all = kv_buffers
     h = kernels.layer_norm_modulate(x, 1e-6, scale=scale_msa, shift=shift_msa)
-    q, _, _ = qkv_rope(h, w, cos, sin, 1, heads, d, token_major=True,
-                       out=(None, own_rows(k_all, group), own_rows(v_all, group)))
-    mark("qkv")
-    a = sharded_self_attention(q, k_all, v_all, scale, group, mark)
+    if isinstance(kv_buffers, PeerKV):
+        k_all, v_all, offs = kv_buffers.next()
+        q, _, _ = qkv_rope(h, w, cos, sin, 1, heads, d, token_major=True,
+                           out=(None, own_rows(k_all, group), own_rows(v_all, group)), peer_offsets=offs)
+        mark("qkv")
+        kv_buffers.barrier(q)
+        mark("kv_gather_wait")
+        a = attend_gathered(q, k_all, v_all, scale)
+        mark("attention")
+    else:
+        k_all, v_all = kv_buffers
+        q, _, _ = qkv_rope(h, w, cos, sin, 1, heads, d, token_major=True,
+                           out=(None, own_rows(k_all, group), own_rows(v_all, group)))
+        mark("qkv")
+        a = sharded_self_attention(q, k_all, v_all, scale, group, mark)
     linear(a[0], w, "self_attn.to_out", epilogue="residual", residual=x, gate=gate_msa)
     mark("to_out")
 
@@ -186,13 +214,20 @@ def block_forward_sharded(w: dict, x: torch.Tensor, mod: torch.Tensor, cos: torc
 
 
 class ShardedBlockStack:
-    """The block stack over ``P`` ranks, token-sharded; weights replicated on every rank."""
+    """The block stack over ``P`` ranks, token-sharded; weights replicated on every rank.
+    ``transport``: how each block's K/V reach the other ranks, ``"nccl"`` (in-place NCCL
+    all-gather after the projection) or ``"peer"`` (the projection's epilogue stores them into
+    the peers' symmetric buffers over NVLink, then a cross-GPU barrier; :class:`PeerKV`)."""
 
-    def __init__(self, weights: list[dict], heads: int, group=None):
+    def __init__(self, weights: list[dict], heads: int, group=None, transport: str = "nccl"):
+        if transport not in ("nccl", "peer"):
+            raise ValueError(f"unknown K/V transport {transport!r}")
         self.weights = weights
         self.heads = heads
         self.group = group
+        self.transport = transport
         self._kv = None
+        self._kv_key = None
         self._mod_w = None  # [blocks, 6C] stacked modulation parameters (built on first use)
 
     def __call__(self, x_local: torch.Tensor, mod: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
@@ -200,10 +235,14 @@ class ShardedBlockStack:
         x = x_local.clone()
         t_local, c = x.shape
         world = dist.get_world_size(self.group)
-        shape = (world * t_local, self.heads, c // self.heads)
-        if (self._kv is None or self._kv[0].shape != shape or self._kv[0].device != x.device
-                or self._kv[0].dtype != x.dtype):
-            self._kv = kv_gather_buffers(t_local, self.heads, c // self.heads, x.dtype, x.device, self.group)
+        key = (t_local, c, x.dtype, x.device)
+        if self._kv is None or self._kv_key != key:  # (re)built on every rank alike: PeerKV is collective
+            d = c // self.heads
+            if self.transport == "peer" and world > 1:
+                self._kv = PeerKV(t_local, self.heads, d, x.dtype, x.device, self.group)
+            else:
+                self._kv = kv_gather_buffers(t_local, self.heads, d, x.dtype, x.device, self.group)
+            self._kv_key = key
         if self._mod_w is None:
             self._mod_w = torch.stack([w["modulation"].reshape(-1).float() for w in self.weights])
         mods = modulation_all(self._mod_w, mod, c, x.dtype)  # every block's vectors in a few launches

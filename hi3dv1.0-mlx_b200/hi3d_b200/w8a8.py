@@ -181,10 +181,10 @@ def linear(x: torch.Tensor, w: torch.Tensor, sw: torch.Tensor, bias: torch.Tenso
 def linear_qkv_rope(x: torch.Tensor, w: torch.Tensor, sw: torch.Tensor, bias: torch.Tensor, cos: torch.Tensor,
                     sin: torch.Tensor, gamma_q: torch.Tensor, gamma_k: torch.Tensor, batch: int, heads: int,
                     head_dim: int, token_major: bool = False, multiplier: torch.Tensor | None = None,
-                    rotate: bool = True, out: tuple | None = None):
+                    rotate: bool = True, out: tuple | None = None, peer_offsets: tuple[int, ...] = ()):
     """The attention input projection through int8 (as :func:`linear`, w8a8.py:105-119) with
     RoPE + QK RMS norm + head split in the GEMM epilogue (as ``hi3d_b200.linear.linear_qkv_rope``)."""
-    from .linear import _qkv_rope_args
+    from .linear import _qkv_rope_args, peer_offset_array
 
     _lib.require_cuda(x if isinstance(x, torch.Tensor) else x.q, w, sw, bias, cos, sin, gamma_q, gamma_k)
     if w.dtype != torch.int8 or sw.dtype != torch.float32:
@@ -195,10 +195,12 @@ def linear_qkv_rope(x: torch.Tensor, w: torch.Tensor, sw: torch.Tensor, bias: to
     _, m, n, cos, sin, gq, gk, q, k, v = _qkv_rope_args(aq, cos, sin, gamma_q, gamma_k, batch, heads, head_dim,
                                                         token_major, out_dtype, out)
     b = bias.to(out_dtype).contiguous()
-    rc = _lib.load().hi3d_gemm_w8a8_qkv_rope(aq.data_ptr(), w.contiguous().data_ptr(), sa.data_ptr(),
-                                             sw.contiguous().data_ptr(), b.data_ptr(), cos.data_ptr(), sin.data_ptr(),
-                                             gq.data_ptr(), gk.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(), m,
-                                             n, heads, head_dim, aq.shape[1], int(token_major),
-                                             _lib.dtype_code(q), _lib.stream(x))
+    rc = _lib.load().hi3d_gemm_w8a8_qkv_rope_peers(aq.data_ptr(), w.contiguous().data_ptr(), sa.data_ptr(),
+                                                   sw.contiguous().data_ptr(), b.data_ptr(), cos.data_ptr(),
+                                                   sin.data_ptr(), gq.data_ptr(), gk.data_ptr(), q.data_ptr(),
+                                                   k.data_ptr(), v.data_ptr(), m, n, heads, head_dim, aq.shape[1],
+                                                   int(token_major), _lib.dtype_code(q),
+                                                   peer_offset_array(peer_offsets), len(peer_offsets),
+                                                   _lib.stream(x))
     _lib.check(rc, "w8a8.linear_qkv_rope")
     return q, k, v

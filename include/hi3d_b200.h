@@ -260,6 +260,34 @@ HI3D_API int hi3d_gemm_w8a8_qkv_rope(const int8_t* a, const int8_t* w, const flo
                                      int heads, int head_dim, int64_t k_dim, int token_major, int out_dtype,
                                      void* stream);
 
+/* The two projections above fused with the K/V all-gather of the query-sharded block (no
+ * counterpart in the reference, which runs one GPU): every k and v store is repeated at
+ * address + peer_offsets[i] for i < num_peers (<= 7; non-zero multiples of 16 bytes), i.e. into
+ * the same rows of each peer GPU's gather buffer, mapped into this process (symmetric memory over
+ * NVLink).  The stores are plain: the caller orders them before the peers' reads with
+ * hi3d_peer_barrier on the same stream.  num_peers = 0 is the plain projection. */
+HI3D_API int hi3d_gemm_qkv_rope_peers(const void* a, const void* w, const void* bias, const float* cos,
+                                      const float* sin, const float* gamma_q, const float* gamma_k, void* q, void* k,
+                                      void* v, int64_t m, int64_t n_seq, int heads, int head_dim, int64_t k_dim,
+                                      int token_major, int dtype, const int64_t* peer_offsets, int num_peers,
+                                      void* stream);
+HI3D_API int hi3d_gemm_w8a8_qkv_rope_peers(const int8_t* a, const int8_t* w, const float* sa, const float* sw,
+                                           const void* bias, const float* cos, const float* sin,
+                                           const float* gamma_q, const float* gamma_k, void* q, void* k, void* v,
+                                           int64_t m, int64_t n_seq, int heads, int head_dim, int64_t k_dim,
+                                           int token_major, int out_dtype, const int64_t* peer_offsets,
+                                           int num_peers, void* stream);
+
+/* Cross-GPU barrier of the peer-store gather: flags_dev is a device array of `world` pointers
+ * to each rank's int32 flag words [world] (symmetric memory, zeroed before the first use); this
+ * rank writes `epoch` into word `rank` of every peer's flags (release, system scope; ordered
+ * after all earlier work on `stream`), then waits until every peer's word in its own flags has
+ * reached `epoch` (acquire).  epoch increases by one per barrier (wrap-around safe).  The wait is
+ * bounded by limit_ns (1e3 .. 6e10): when it runs out the device status word holds
+ * HI3D_ERR_DEVICE_TIMEOUT with where = 950, detail = the peer, and the kernel returns. */
+HI3D_API int hi3d_peer_barrier(void* const* flags_dev, int rank, int world, uint32_t epoch, int64_t limit_ns,
+                               void* stream);
+
 /* Replaces w8a8.quantize_activation (src/hi3d_mac/mlx_backend/w8a8.py:25-58, :95-102):
  * per row of x [rows, k] (k % 64 == 0), y = H64(x * multiplier) / 8 per 64-block (signed
  * natural-order Walsh-Hadamard, rotate != 0) or y = x (rotate == 0); s = max(max|y|, 1e-8) / 127;

@@ -30,7 +30,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, result_path):
+def _worker(rank, world, port, result_path, transport="nccl"):
     sys.path.insert(0, os.path.join(REPO, "hi3dv1.0-mlx_b200"))
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -53,9 +53,13 @@ def _worker(rank, world, port, result_path):
     kvs = [transformer.context_kv(w, ctx, heads) for w in ws]
     rows = hdist.shard_slice(t, rank, world)
     tt = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
-    stack = hdist.ShardedBlockStack(ws, heads)
-    y_local = stack(tt(x[rows]), tt(mod), tt(cos[rows]), tt(sin[rows]), kvs)
+    stack = hdist.ShardedBlockStack(ws, heads, transport=transport)
+    for _ in range(2):  # twice: the second call reuses the buffer sets (and the barrier epochs go on)
+        y_local = stack(tt(x[rows]), tt(mod), tt(cos[rows]), tt(sin[rows]), kvs)
     y = hdist.gather_rows(y_local)
+    from hi3d_b200 import _lib
+
+    assert _lib.device_status()["code"] == 0
     if rank == 0:
         ref = transformer.BlockStack(ws, heads)(tt(x)[None], tt(mod), tt(cos), tt(sin), kvs)[0]
         yf, rf = y.float(), ref.float()
@@ -66,9 +70,12 @@ def _worker(rank, world, port, result_path):
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_sharded_stack_matches_single_gpu(tmp_path):
+@pytest.mark.parametrize("transport", ["nccl", "peer"])
+def test_sharded_stack_matches_single_gpu(tmp_path, transport):
+    """Both K/V transports: the NCCL all-gather after the projection, and the projection's own
+    stores into the peers' symmetric buffers followed by the cross-GPU barrier."""
     out = tmp_path / "r.npy"
-    mp.spawn(_worker, args=(2, _free_port(), str(out)), nprocs=2, join=True)
+    mp.spawn(_worker, args=(2, _free_port(), str(out), transport), nprocs=2, join=True)
     rel, same = np.load(out)
     assert rel < 1e-3, rel
     assert same > 0.9, same
