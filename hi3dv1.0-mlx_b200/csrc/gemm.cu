@@ -454,8 +454,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 else
                   t = __uint_as_float(v[e + qq]);
                 if (p.bias) t = __fadd_rn(t, vec[col]);
-                y[qq] = Cvt<OutT>::to_f(Cvt<OutT>::from_f(t));  // round to the output type
-                if (EPI == EPI_GELU) y[qq] = gelu_tanh_f<OutT>(y[qq]);
+                if (EPI == EPI_GELU)  // GELU of the value rounded to the output type
+                  y[qq] = gelu_tanh_f<OutT>(Cvt<OutT>::to_f(Cvt<OutT>::from_f(t)));
+                else
+                  y[qq] = t;  // pack2 below rounds to the output type
               }
               uint4 w;
               w.x = Cvt<OutT>::pack2(y[0], y[1]);
@@ -480,22 +482,25 @@ __global__ void __launch_bounds__(kThreads, 1)
                 grow = reinterpret_cast<const OutT*>(p.gate) + (m / p.rows_per_batch) * p.gate_stride;
               if (p.vec && n + 8 <= p.N) {
                 if constexpr (EPI == EPI_RESIDUAL) {
+                  // x + round(y * gate), rounded, on 16-bit pairs: the product of two 16-bit values
+                  // is exact in fp32, and the fp32 sum of two 16-bit values rounds to the same
+                  // 16-bit value as the exact sum, so the correctly rounded pair instructions give
+                  // the scalar fp32 path's bits with an eighth of the instructions
                   const uint4 gv = gate_hoist ? gate_pre[c]
                                    : grow ? __ldg(reinterpret_cast<const uint4*>(grow + n)) : make_uint4(0, 0, 0, 0);
-                  const OutT* xa = reinterpret_cast<const OutT*>(&res[c][i]);
-                  const OutT* ga = reinterpret_cast<const OutT*>(&gv);
-                  float o[8];
-#pragma unroll
-                  for (int qq = 0; qq < 8; ++qq) {
-                    float g = Cvt<OutT>::to_f(ya[qq]);
-                    if (grow) g = Cvt<OutT>::to_f(Cvt<OutT>::from_f(__fmul_rn(g, Cvt<OutT>::to_f(ga[qq]))));
-                    o[qq] = __fadd_rn(Cvt<OutT>::to_f(xa[qq]), g);
-                  }
+                  const uint4 xv = res[c][i];
                   uint4 w;
-                  w.x = Cvt<OutT>::pack2(o[0], o[1]);
-                  w.y = Cvt<OutT>::pack2(o[2], o[3]);
-                  w.z = Cvt<OutT>::pack2(o[4], o[5]);
-                  w.w = Cvt<OutT>::pack2(o[6], o[7]);
+                  if (grow) {
+                    w.x = Cvt<OutT>::add2(xv.x, Cvt<OutT>::mul2(yv.x, gv.x));
+                    w.y = Cvt<OutT>::add2(xv.y, Cvt<OutT>::mul2(yv.y, gv.y));
+                    w.z = Cvt<OutT>::add2(xv.z, Cvt<OutT>::mul2(yv.z, gv.z));
+                    w.w = Cvt<OutT>::add2(xv.w, Cvt<OutT>::mul2(yv.w, gv.w));
+                  } else {
+                    w.x = Cvt<OutT>::add2(xv.x, yv.x);
+                    w.y = Cvt<OutT>::add2(xv.y, yv.y);
+                    w.z = Cvt<OutT>::add2(xv.z, yv.z);
+                    w.w = Cvt<OutT>::add2(xv.w, yv.w);
+                  }
                   *reinterpret_cast<uint4*>(orow + n) = w;
                 } else {
                   *reinterpret_cast<uint4*>(orow + n) = yv;
