@@ -186,7 +186,8 @@ def stack_config(workload: str, nblocks: int, world: int, transport: str = "nccl
     else:
         name = (f"cfg1: {nblocks}-block sparse-DiT stack fwd, T={T_TOKENS} shell tokens in {GRID}^3, C={CHANNELS}, "
                 f"{HEADS}x{CHANNELS // HEADS} heads, {COND} cond tokens, fp16")
-    kv = {"nccl": "NCCL all-gather", "peer": "QKV epilogue stores into peers' symmetric buffers"}[transport]
+    kv = {"nccl": "NCCL all-gather", "peer": "QKV epilogue stores into peers' symmetric buffers",
+          "multicast": "QKV epilogue multimem stores into every GPU's symmetric buffer"}[transport]
     return {"workload": name, "blocks": nblocks, "tokens": T_TOKENS,
             "parallelism": f"query-sharded x{world}, K/V by {kv}" if world > 1 else "none",
             "l2": "inputs larger than L2 (705 MB of weights + activations per step)"}
@@ -1320,9 +1321,9 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-extras", action="store_true", help="headline only (no cfg2/cfg4/cfg5 extras)")
-    ap.add_argument("--kv-transport", choices=["nccl", "peer"], default="nccl",
+    ap.add_argument("--kv-transport", choices=["nccl", "peer", "multicast"], default="nccl",
                     help="N > 1: K/V of each block by NCCL all-gather, or by the QKV projection's own stores into "
-                         "the peers' symmetric buffers")
+                         "the peers' symmetric buffers (one per peer, or one multimem store through NVSwitch)")
     ap.add_argument("--only", default=None, help="--workload kernels: time this one kernel (e.g. layer_norm_affine)")
     ap.add_argument("--workload", choices=["stack", "stack_w8a8", "block", "attention", "attention262k", "conv",
                                            "forward", "vae", "released", "kernels"], default="stack")

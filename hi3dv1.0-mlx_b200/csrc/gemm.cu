@@ -76,6 +76,10 @@ struct Params {
   // all-gathers K and V over NVLink
   int npeers;
   int64_t peer_off[kMaxPeers];
+  // or, when non-zero, every k / v store goes to address + mcast_off instead: an NVLink
+  // multicast mapping of the gather buffers, so one multimem store reaches every GPU bound to
+  // it (this one included) and NVSwitch does the fan-out
+  int64_t mcast_off;
 };
 
 struct Barriers {
@@ -86,6 +90,13 @@ struct Barriers {
   uint32_t tmem_base;
   int abort;
 };
+
+// 16 bytes to every GPU bound to the multicast address `mc` (relaxed, system scope)
+__device__ __forceinline__ void multimem_st16(void* mc, uint4 v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
+}
 
 template <typename OutT>
 __device__ __forceinline__ float gelu_tanh_f(float a) {
@@ -392,11 +403,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int64_t row = p.token_major ? ((int64_t)b2 * p.seq_n + n2) * p.heads + head
                                                   : ((int64_t)b2 * p.heads + head) * p.seq_n + n2;
                 OutT* dst = dst_base + row * 64 + half * 32 + j * 8;
-                *reinterpret_cast<uint4*>(dst) = yq;
-                if (part > 0) {  // K and V rows also into every peer's gather buffer (NVLink stores)
+                if (part > 0 && p.mcast_off) {  // K and V rows into every GPU's gather buffer at once
+                  multimem_st16(reinterpret_cast<char*>(dst) + p.mcast_off, yq);
+                } else {
+                  *reinterpret_cast<uint4*>(dst) = yq;
+                  if (part > 0) {  // K and V rows also into every peer's gather buffer (NVLink stores)
 #pragma unroll 1
-                  for (int pp = 0; pp < p.npeers; ++pp)
-                    *reinterpret_cast<uint4*>(reinterpret_cast<char*>(dst) + p.peer_off[pp]) = yq;
+                    for (int pp = 0; pp < p.npeers; ++pp)
+                      *reinterpret_cast<uint4*>(reinterpret_cast<char*>(dst) + p.peer_off[pp]) = yq;
+                  }
                 }
               }
             }
@@ -539,7 +554,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     // stores into the peers' gather buffers are performed at system scope before this grid
     // completes, hence before the cross-GPU barrier that follows it on the stream signals them
-    if (EPI == EPI_QKV_ROPE && p.npeers > 0) __threadfence_system();
+    if (EPI == EPI_QKV_ROPE && (p.npeers > 0 || p.mcast_off)) __threadfence_system();
   }
 
   tc_fence_before();
@@ -764,10 +779,15 @@ static int qkv_rope_params(const char* what, const void* a, const void* w, const
   return HI3D_OK;
 }
 
-static int set_peers(const char* what, const int64_t* peer_offsets, int num_peers, gemm::Params* p) {
+static int set_peers(const char* what, const int64_t* peer_offsets, int num_peers, int64_t multicast_offset,
+                     gemm::Params* p) {
   if (num_peers < 0 || num_peers > gemm::kMaxPeers || (num_peers > 0 && !peer_offsets))
     return set_error(HI3D_ERR_INVALID_ARGUMENT, "%s: num_peers must be in [0, %d] with the offsets given", what,
                      gemm::kMaxPeers);
+  if (multicast_offset % 16 || (multicast_offset && num_peers))
+    return set_error(HI3D_ERR_INVALID_ARGUMENT,
+                     "%s: multicast_offset must be a multiple of 16 bytes, and excludes peer offsets", what);
+  p->mcast_off = multicast_offset;
   p->npeers = num_peers;
   for (int i = 0; i < num_peers; ++i) {
     if (peer_offsets[i] % 16 || peer_offsets[i] == 0)
@@ -783,19 +803,19 @@ extern "C" int hi3d_gemm_qkv_rope(const void* a, const void* w, const void* bias
                                   void* v, int64_t m, int64_t n_seq, int heads, int head_dim, int64_t kdim,
                                   int token_major, int dtype, void* stream) {
   return hi3d_gemm_qkv_rope_peers(a, w, bias, cosv, sinv, gamma_q, gamma_k, q, k, v, m, n_seq, heads, head_dim, kdim,
-                                  token_major, dtype, nullptr, 0, stream);
+                                  token_major, dtype, nullptr, 0, 0, stream);
 }
 
 extern "C" int hi3d_gemm_qkv_rope_peers(const void* a, const void* w, const void* bias, const float* cosv,
                                         const float* sinv, const float* gamma_q, const float* gamma_k, void* q,
                                         void* k, void* v, int64_t m, int64_t n_seq, int heads, int head_dim,
                                         int64_t kdim, int token_major, int dtype, const int64_t* peer_offsets,
-                                        int num_peers, void* stream) {
+                                        int num_peers, int64_t multicast_offset, void* stream) {
   gemm::Params p;
   int rc = qkv_rope_params("gemm_qkv_rope", a, w, cosv, sinv, gamma_q, gamma_k, q, k, v, m, n_seq, heads, head_dim,
                            kdim, token_major, &p);
   if (rc) return rc;
-  if ((rc = set_peers("gemm_qkv_rope", peer_offsets, num_peers, &p))) return rc;
+  if ((rc = set_peers("gemm_qkv_rope", peer_offsets, num_peers, multicast_offset, &p))) return rc;
   if (kdim % 8) return set_error(HI3D_ERR_INVALID_ARGUMENT, "gemm_qkv_rope: K must be a multiple of 8");
   if (m == 0) return HI3D_OK;
   p.bias = bias;
@@ -814,7 +834,7 @@ extern "C" int hi3d_gemm_w8a8_qkv_rope(const int8_t* a, const int8_t* w, const f
                                        int heads, int head_dim, int64_t kdim, int token_major, int out_dtype,
                                        void* stream) {
   return hi3d_gemm_w8a8_qkv_rope_peers(a, w, sa, sw, bias, cosv, sinv, gamma_q, gamma_k, q, k, v, m, n_seq, heads,
-                                       head_dim, kdim, token_major, out_dtype, nullptr, 0, stream);
+                                       head_dim, kdim, token_major, out_dtype, nullptr, 0, 0, stream);
 }
 
 extern "C" int hi3d_gemm_w8a8_qkv_rope_peers(const int8_t* a, const int8_t* w, const float* sa, const float* sw,
@@ -822,12 +842,12 @@ extern "C" int hi3d_gemm_w8a8_qkv_rope_peers(const int8_t* a, const int8_t* w, c
                                              const float* gamma_q, const float* gamma_k, void* q, void* k, void* v,
                                              int64_t m, int64_t n_seq, int heads, int head_dim, int64_t kdim,
                                              int token_major, int out_dtype, const int64_t* peer_offsets,
-                                             int num_peers, void* stream) {
+                                             int num_peers, int64_t multicast_offset, void* stream) {
   gemm::Params p;
   int rc = qkv_rope_params("gemm_w8a8_qkv_rope", a, w, cosv, sinv, gamma_q, gamma_k, q, k, v, m, n_seq, heads,
                            head_dim, kdim, token_major, &p);
   if (rc) return rc;
-  if ((rc = set_peers("gemm_w8a8_qkv_rope", peer_offsets, num_peers, &p))) return rc;
+  if ((rc = set_peers("gemm_w8a8_qkv_rope", peer_offsets, num_peers, multicast_offset, &p))) return rc;
   if (!sa || !sw) return set_error(HI3D_ERR_INVALID_ARGUMENT, "gemm_w8a8_qkv_rope: scales are required");
   if (kdim % 16) return set_error(HI3D_ERR_INVALID_ARGUMENT, "gemm_w8a8_qkv_rope: K must be a multiple of 16");
   if (m == 0) return HI3D_OK;

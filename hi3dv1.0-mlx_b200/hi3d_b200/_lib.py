@@ -84,9 +84,9 @@ SIGNATURES: dict[str, tuple] = {
     "hi3d_gemm_qkv_rope": (_i32, [_c_void_p] * 10 + [_i64, _i64, _i32, _i32, _i64, _i32, _i32, _c_void_p]),
     "hi3d_gemm_w8a8_qkv_rope": (_i32, [_c_void_p] * 12 + [_i64, _i64, _i32, _i32, _i64, _i32, _i32, _c_void_p]),
     "hi3d_gemm_qkv_rope_peers": (_i32, [_c_void_p] * 10 + [_i64, _i64, _i32, _i32, _i64, _i32, _i32, _c_void_p,
-                                                           _i32, _c_void_p]),
+                                                           _i32, _i64, _c_void_p]),
     "hi3d_gemm_w8a8_qkv_rope_peers": (_i32, [_c_void_p] * 12 + [_i64, _i64, _i32, _i32, _i64, _i32, _i32,
-                                                                _c_void_p, _i32, _c_void_p]),
+                                                                _c_void_p, _i32, _i64, _c_void_p]),
     "hi3d_peer_barrier": (_i32, [_c_void_p, _i32, _i32, ctypes.c_uint32, _i64, _c_void_p]),
     "hi3d_neighbour_map_workspace_size": (_i32, [_i64, ctypes.POINTER(_i64)]),
     "hi3d_neighbour_map_build": (_i32, [_c_void_p, _i64, _c_void_p, _i64, _i32, _c_void_p, _c_void_p, _i64, _c_void_p]),

@@ -181,9 +181,9 @@ def block_forward_sharded(w: dict, x: torch.Tensor, mod: torch.Tensor, cos: torc
         kv_buffers = kv_gather_buffers(t_local, heads, d, dt, x.device, group)
     h = kernels.layer_norm_modulate(x, 1e-6, scale=scale_msa, shift=shift_msa)
     if isinstance(kv_buffers, PeerKV):
-        k_all, v_all, offs = kv_buffers.next()
+        k_all, v_all, store = kv_buffers.next()
         q, _, _ = qkv_rope(h, w, cos, sin, 1, heads, d, token_major=True,
-                           out=(None, own_rows(k_all, group), own_rows(v_all, group)), peer_offsets=offs)
+                           out=(None, own_rows(k_all, group), own_rows(v_all, group)), **store)
         mark("qkv")
         kv_buffers.barrier(q)
         mark("kv_gather_wait")
@@ -216,11 +216,12 @@ def block_forward_sharded(w: dict, x: torch.Tensor, mod: torch.Tensor, cos: torc
 class ShardedBlockStack:
     """The block stack over ``P`` ranks, token-sharded; weights replicated on every rank.
     ``transport``: how each block's K/V reach the other ranks, ``"nccl"`` (in-place NCCL
-    all-gather after the projection) or ``"peer"`` (the projection's epilogue stores them into
-    the peers' symmetric buffers over NVLink, then a cross-GPU barrier; :class:`PeerKV`)."""
+    all-gather after the projection), ``"peer"`` (the projection's epilogue stores them into
+    the peers' symmetric buffers over NVLink, then a cross-GPU barrier; :class:`PeerKV`) or
+    ``"multicast"`` (the same with one multimem store per row through NVSwitch)."""
 
     def __init__(self, weights: list[dict], heads: int, group=None, transport: str = "nccl"):
-        if transport not in ("nccl", "peer"):
+        if transport not in ("nccl", "peer", "multicast"):
             raise ValueError(f"unknown K/V transport {transport!r}")
         self.weights = weights
         self.heads = heads
@@ -238,8 +239,9 @@ class ShardedBlockStack:
         key = (t_local, c, x.dtype, x.device)
         if self._kv is None or self._kv_key != key:  # (re)built on every rank alike: PeerKV is collective
             d = c // self.heads
-            if self.transport == "peer" and world > 1:
-                self._kv = PeerKV(t_local, self.heads, d, x.dtype, x.device, self.group)
+            if self.transport in ("peer", "multicast") and world > 1:
+                self._kv = PeerKV(t_local, self.heads, d, x.dtype, x.device, self.group,
+                                  multicast=self.transport == "multicast")
             else:
                 self._kv = kv_gather_buffers(t_local, self.heads, d, x.dtype, x.device, self.group)
             self._kv_key = key

@@ -102,7 +102,7 @@ def _qkv_rope_args(x, cos, sin, gamma_q, gamma_k, batch, heads, head_dim, token_
 def linear_qkv_rope(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None, cos: torch.Tensor,
                     sin: torch.Tensor, gamma_q: torch.Tensor, gamma_k: torch.Tensor, batch: int, heads: int,
                     head_dim: int, token_major: bool = False, out: tuple | None = None,
-                    peer_offsets: tuple[int, ...] = ()):
+                    peer_offsets: tuple[int, ...] = (), multicast_offset: int = 0):
     """The attention input projection ``x @ W^T + bias`` (``W [3 H D, K]``) split into
     ``q, k, v [B, H, N, D]`` with RoPE + QK RMS norm applied in the GEMM epilogue: the same
     result as :func:`linear` followed by :func:`hi3d_b200.kernels.qkv_rope_rms`
@@ -110,7 +110,9 @@ def linear_qkv_rope(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | 
     ``token_major=True`` returns ``[B, N, H, D]``.  ``out``: optional ``(q, k, v)`` tensors to write
     (None entries are allocated).  ``peer_offsets``: byte offsets from ``k``/``v`` to the same rows of
     the peers' gather buffers, which the epilogue also stores (``hi3d_gemm_qkv_rope_peers``; see
-    :class:`hi3d_b200.peer.PeerKV`).  Raises ``NotImplementedError`` unless :func:`qkv_rope_supported`."""
+    :class:`hi3d_b200.peer.PeerKV`); or ``multicast_offset``: byte offset from ``k``/``v`` to their
+    NVLink multicast mapping, stored once for every GPU.  Raises ``NotImplementedError`` unless
+    :func:`qkv_rope_supported`."""
     _lib.require_cuda(x, weight, bias, cos, sin, gamma_q, gamma_k)
     if x.dtype not in (torch.float16, torch.bfloat16) or weight.dtype != x.dtype:
         raise ValueError("linear_qkv_rope takes float16/bfloat16 activations and weights of one dtype")
@@ -124,7 +126,7 @@ def linear_qkv_rope(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | 
                                               cos.data_ptr(), sin.data_ptr(), gq.data_ptr(), gk.data_ptr(),
                                               q.data_ptr(), k.data_ptr(), v.data_ptr(), m, n, heads, head_dim,
                                               a.shape[1], int(token_major), _lib.dtype_code(x), offs,
-                                              len(peer_offsets), _lib.stream(x))
+                                              len(peer_offsets), int(multicast_offset), _lib.stream(x))
     _lib.check(rc, "linear_qkv_rope")
     return q, k, v
 

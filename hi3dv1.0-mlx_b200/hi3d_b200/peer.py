@@ -10,8 +10,11 @@ orders the peers' stores before this rank's attention reads.  Two buffer sets
 alternate from block to block, which keeps a rank's stores for block i + 1 off
 rows that a peer may still read in block i - 1 (see ``csrc/peer.cu``).
 
-No multicast: every store names one peer's address, and every load (the
-attention's TMA loads of K/V) reads this GPU's own memory.
+With ``multicast=True`` the projection instead stores each K/V row once to an
+NVLink multicast mapping of the buffers (``multimem.st``): NVSwitch writes it
+into every GPU's buffer, this one included, so the epilogue issues one store per
+row instead of one per GPU.  Either way every load (the attention's TMA loads of
+K/V) reads this GPU's own memory; there is no TMA or bulk load with multicast.
 """
 
 from __future__ import annotations
@@ -26,14 +29,17 @@ class PeerKV:
     """Two sets of symmetric K/V gather buffers for ``S = t_local`` rows per rank, plus the
     barrier flags.  Construction is collective over ``group`` (every rank, same sizes).
 
-    ``next()`` returns the next set's ``(k_all, v_all, peer_offsets)``: ``k_all, v_all
-    [P * S, H, D]`` and the byte offsets from this rank's buffer to each peer's, for
-    ``qkv_rope(..., peer_offsets=...)``.  ``barrier()`` (after the projection, on the same
-    stream) returns once every peer's rows of that set have arrived; a peer that does not
-    arrive within ``limit_s`` leaves ``HI3D_ERR_DEVICE_TIMEOUT`` (where 950) in the device
-    status word instead of hanging the GPU."""
+    ``next()`` returns the next set's ``(k_all, v_all, store)``: ``k_all, v_all [P * S, H, D]``
+    and the keyword arguments for ``qkv_rope(..., **store)``: the byte offsets from this rank's
+    buffer to each peer's (``peer_offsets``), or to the buffer's multicast mapping
+    (``multicast_offset``, with ``multicast=True``; ``RuntimeError`` at construction when the
+    GPUs offer no multicast).  ``barrier()`` (after the projection, on the same stream) returns
+    once every peer's rows of that set have arrived; a peer that does not arrive within
+    ``limit_s`` leaves ``HI3D_ERR_DEVICE_TIMEOUT`` (where 950) in the device status word instead
+    of hanging the GPU."""
 
-    def __init__(self, t_local: int, heads: int, d: int, dtype, device, group=None, limit_s: float = 5.0):
+    def __init__(self, t_local: int, heads: int, d: int, dtype, device, group=None, limit_s: float = 5.0,
+                 multicast: bool = False):
         import torch.distributed._symmetric_memory as symm
 
         pg = group if group is not None else dist.group.WORLD
@@ -52,8 +58,15 @@ class PeerKV:
             dist.all_gather_object(place, buf.data_ptr() - ptrs[self.rank], group=group)
             if len(set(place)) != 1:
                 raise RuntimeError(f"symmetric buffers at different offsets on the ranks: {place}")
-            offs = tuple(int(ptrs[p] - ptrs[self.rank]) for p in range(self.world) if p != self.rank)
-            self._sets.append((buf, handle, offs))
+            if multicast:
+                mc = int(handle.multicast_ptr)
+                if not mc:
+                    raise RuntimeError("symmetric memory has no multicast mapping on these GPUs")
+                store = {"multicast_offset": mc - ptrs[self.rank]}
+            else:
+                store = {"peer_offsets": tuple(int(ptrs[p] - ptrs[self.rank])
+                                               for p in range(self.world) if p != self.rank)}
+            self._sets.append((buf, handle, store))
         flags = symm.empty((self.world,), dtype=torch.int32, device=self.device)
         flags.zero_()
         fh = symm.rendezvous(flags, pg)
@@ -71,10 +84,10 @@ class PeerKV:
         self.limit_ns = int(limit_s * 1e9)
         self._next = 0
 
-    def next(self) -> tuple[torch.Tensor, torch.Tensor, tuple[int, ...]]:
-        buf, _, offs = self._sets[self._next % 2]
+    def next(self) -> tuple[torch.Tensor, torch.Tensor, dict]:
+        buf, _, store = self._sets[self._next % 2]
         self._next += 1
-        return buf[0], buf[1], offs
+        return buf[0], buf[1], store
 
     def barrier(self, like: torch.Tensor) -> None:
         """The cross-rank barrier on the current stream of ``like``'s device."""

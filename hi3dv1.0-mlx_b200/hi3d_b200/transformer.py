@@ -90,22 +90,25 @@ def linear(x: torch.Tensor, w: dict, name: str, epilogue: str = "store", residua
 
 
 def qkv_rope(h: torch.Tensor, w: dict, cos: torch.Tensor, sin: torch.Tensor, batch: int, heads: int, d: int,
-             token_major: bool = False, out: tuple | None = None, peer_offsets: tuple[int, ...] = ()):
+             token_major: bool = False, out: tuple | None = None, peer_offsets: tuple[int, ...] = (),
+             multicast_offset: int = 0):
     """``q, k, v`` of the self-attention: the ``self_attn.to_qkv`` projection with RoPE + QK RMS
     norm (transformer.py:501-516 then kernels.py:22-90).  Fused into the GEMM epilogue when the
     head layout allows it (head dim 64), else the projection followed by the row kernel.
-    ``out``: optional ``(q, k, v)`` tensors written in place of new ones.  ``peer_offsets``: the
-    fused projection also stores K/V into the peers' gather buffers (only the fused form can;
-    ``NotImplementedError`` otherwise)."""
+    ``out``: optional ``(q, k, v)`` tensors written in place of new ones.  ``peer_offsets`` /
+    ``multicast_offset``: the fused projection also stores K/V into the peers' gather buffers
+    (only the fused form can; ``NotImplementedError`` otherwise)."""
     name = "self_attn.to_qkv"
     gq, gk = w["self_attn.q_rms_norm.gamma"], w["self_attn.k_rms_norm.gamma"]
     if _linear.qkv_rope_supported(heads, d):
         if f"{name}.w8_scale" in w:
             return _w8a8.linear_qkv_rope(h, w[f"{name}.weight"], w[f"{name}.w8_scale"], w[f"{name}.bias"], cos, sin,
-                                         gq, gk, batch, heads, d, token_major, out=out, peer_offsets=peer_offsets)
+                                         gq, gk, batch, heads, d, token_major, out=out, peer_offsets=peer_offsets,
+                                         multicast_offset=multicast_offset)
         return _linear.linear_qkv_rope(h, w[f"{name}.weight"], w[f"{name}.bias"], cos, sin, gq, gk, batch, heads, d,
-                                       token_major, out=out, peer_offsets=peer_offsets)
-    if peer_offsets:
+                                       token_major, out=out, peer_offsets=peer_offsets,
+                                       multicast_offset=multicast_offset)
+    if peer_offsets or multicast_offset:
         raise NotImplementedError("peer stores need the fused QKV projection (head_dim 64, heads * 64 % 256 == 0)")
     qkv = linear(h, w, name)
     return kernels.qkv_rope_rms(qkv, cos, sin, gq, gk, batch, heads, d, token_major=token_major, out=out)

@@ -181,7 +181,8 @@ def linear(x: torch.Tensor, w: torch.Tensor, sw: torch.Tensor, bias: torch.Tenso
 def linear_qkv_rope(x: torch.Tensor, w: torch.Tensor, sw: torch.Tensor, bias: torch.Tensor, cos: torch.Tensor,
                     sin: torch.Tensor, gamma_q: torch.Tensor, gamma_k: torch.Tensor, batch: int, heads: int,
                     head_dim: int, token_major: bool = False, multiplier: torch.Tensor | None = None,
-                    rotate: bool = True, out: tuple | None = None, peer_offsets: tuple[int, ...] = ()):
+                    rotate: bool = True, out: tuple | None = None, peer_offsets: tuple[int, ...] = (),
+                    multicast_offset: int = 0):
     """The attention input projection through int8 (as :func:`linear`, w8a8.py:105-119) with
     RoPE + QK RMS norm + head split in the GEMM epilogue (as ``hi3d_b200.linear.linear_qkv_rope``)."""
     from .linear import _qkv_rope_args, peer_offset_array
@@ -201,6 +202,6 @@ def linear_qkv_rope(x: torch.Tensor, w: torch.Tensor, sw: torch.Tensor, bias: to
                                                    k.data_ptr(), v.data_ptr(), m, n, heads, head_dim, aq.shape[1],
                                                    int(token_major), _lib.dtype_code(q),
                                                    peer_offset_array(peer_offsets), len(peer_offsets),
-                                                   _lib.stream(x))
+                                                   int(multicast_offset), _lib.stream(x))
     _lib.check(rc, "w8a8.linear_qkv_rope")
     return q, k, v

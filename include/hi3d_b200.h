@@ -264,19 +264,23 @@ HI3D_API int hi3d_gemm_w8a8_qkv_rope(const int8_t* a, const int8_t* w, const flo
  * counterpart in the reference, which runs one GPU): every k and v store is repeated at
  * address + peer_offsets[i] for i < num_peers (<= 7; non-zero multiples of 16 bytes), i.e. into
  * the same rows of each peer GPU's gather buffer, mapped into this process (symmetric memory over
- * NVLink).  The stores are plain: the caller orders them before the peers' reads with
- * hi3d_peer_barrier on the same stream.  num_peers = 0 is the plain projection. */
+ * NVLink).  Or, with multicast_offset != 0 (a multiple of 16; no peer offsets then), every k
+ * and v store goes once to address + multicast_offset, an NVLink multicast mapping of the
+ * gather buffers (multimem.st: NVSwitch writes it into every bound GPU's buffer, this one
+ * included).  The stores are relaxed: the caller orders them before the peers' reads with
+ * hi3d_peer_barrier on the same stream.  num_peers = 0 and multicast_offset = 0 is the plain
+ * projection. */
 HI3D_API int hi3d_gemm_qkv_rope_peers(const void* a, const void* w, const void* bias, const float* cos,
                                       const float* sin, const float* gamma_q, const float* gamma_k, void* q, void* k,
                                       void* v, int64_t m, int64_t n_seq, int heads, int head_dim, int64_t k_dim,
                                       int token_major, int dtype, const int64_t* peer_offsets, int num_peers,
-                                      void* stream);
+                                      int64_t multicast_offset, void* stream);
 HI3D_API int hi3d_gemm_w8a8_qkv_rope_peers(const int8_t* a, const int8_t* w, const float* sa, const float* sw,
                                            const void* bias, const float* cos, const float* sin,
                                            const float* gamma_q, const float* gamma_k, void* q, void* k, void* v,
                                            int64_t m, int64_t n_seq, int heads, int head_dim, int64_t k_dim,
                                            int token_major, int out_dtype, const int64_t* peer_offsets,
-                                           int num_peers, void* stream);
+                                           int num_peers, int64_t multicast_offset, void* stream);
 
 /* Cross-GPU barrier of the peer-store gather: flags_dev is a device array of `world` pointers
  * to each rank's int32 flag words [world] (symmetric memory, zeroed before the first use); this

@@ -70,10 +70,17 @@ def _worker(rank, world, port, result_path, transport="nccl"):
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("transport", ["nccl", "peer"])
+@pytest.mark.parametrize("transport", ["nccl", "peer", "multicast"])
 def test_sharded_stack_matches_single_gpu(tmp_path, transport):
-    """Both K/V transports: the NCCL all-gather after the projection, and the projection's own
-    stores into the peers' symmetric buffers followed by the cross-GPU barrier."""
+    """Every K/V transport: the NCCL all-gather after the projection, and the projection's own
+    stores into the peers' symmetric buffers (one per peer, or one multimem store through
+    NVSwitch) followed by the cross-GPU barrier.  The multicast case is skipped where the
+    GPUs offer no multicast mapping."""
+    if transport == "multicast":
+        import torch.distributed._symmetric_memory as symm
+
+        if not symm._SymmetricMemory.has_multicast_support(torch._C._autograd.DeviceType.CUDA, 0):
+            pytest.skip("no NVLink multicast on these GPUs")
     out = tmp_path / "r.npy"
     mp.spawn(_worker, args=(2, _free_port(), str(out), transport), nprocs=2, join=True)
     rel, same = np.load(out)
