@@ -89,15 +89,25 @@ class ClockSampler:
         self.index = index
         self.proc = None
         self.file = None
+        self.skip = 0
 
     def __enter__(self):
         try:
             self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.file,
+                                          "--format=csv,noheader,nounits", "-lms", "50"], stdout=self.file,
                                          stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
+            return self
+        # nvidia-smi takes a moment to start: wait (at most 5 s) for its first sample, so that a
+        # short timed region (a few hundred ms at 8 GPUs) is sampled too
+        t0 = time.time()
+        while time.time() - t0 < 5.0 and self.proc.poll() is None:
+            if Path(self.file.name).stat().st_size > 0:
+                break
+            time.sleep(0.02)
+        self.skip = len(Path(self.file.name).read_text().splitlines())  # samples taken before the region
         return self
 
     def __exit__(self, *exc):
@@ -111,8 +121,12 @@ class ClockSampler:
     def summary(self) -> dict:
         if self.proc is None or self.file is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        rows = [r.split(",") for r in Path(self.file.name).read_text().splitlines() if r.strip()]
+        lines = Path(self.file.name).read_text().splitlines()
         os.unlink(self.file.name)
+        # the samples taken during the region; the one just before it when the region was shorter
+        # than the sampling interval
+        lines = lines[self.skip:] or lines[-1:]
+        rows = [r.split(",") for r in lines if r.strip()]
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for r in rows:
@@ -186,6 +200,10 @@ def stack_config(workload: str, nblocks: int, world: int, transport: str = "nccl
     else:
         name = (f"cfg1: {nblocks}-block sparse-DiT stack fwd, T={T_TOKENS} shell tokens in {GRID}^3, C={CHANNELS}, "
                 f"{HEADS}x{CHANNELS // HEADS} heads, {COND} cond tokens, fp16")
+    if transport == "auto":
+        from hi3d_b200.dist import auto_transport
+
+        transport = auto_transport(world)
     kv = {"nccl": "NCCL all-gather", "peer": "QKV epilogue stores into peers' symmetric buffers",
           "multicast": "QKV epilogue multimem stores into every GPU's symmetric buffer"}[transport]
     return {"workload": name, "blocks": nblocks, "tokens": T_TOKENS,
@@ -1321,7 +1339,7 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-extras", action="store_true", help="headline only (no cfg2/cfg4/cfg5 extras)")
-    ap.add_argument("--kv-transport", choices=["nccl", "peer", "multicast"], default="nccl",
+    ap.add_argument("--kv-transport", choices=["auto", "nccl", "peer", "multicast"], default="auto",
                     help="N > 1: K/V of each block by NCCL all-gather, or by the QKV projection's own stores into "
                          "the peers' symmetric buffers (one per peer, or one multimem store through NVSwitch)")
     ap.add_argument("--only", default=None, help="--workload kernels: time this one kernel (e.g. layer_norm_affine)")
