@@ -59,12 +59,17 @@ __global__ void __launch_bounds__(kLnRowsPerBlock * 32)
   const int lane = threadIdx.x & 31;
   // The fp32 affine parameters are the same for every row: staged once per block in
   // shared memory ([weight | bias], NCH * 256 each, zero past C), so the per-row
-  // reads are short shared-memory loads instead of L1/L2 round trips.
+  // reads are short shared-memory loads instead of L1/L2 round trips.  Layout: the
+  // channels c*256 + 8 l + 4 h + k (lane l, half h, k < 4) of chunk c sit at float4
+  // (2c + h) * 32 + l, so each 16-byte load of a warp reads 512 contiguous bytes (4
+  // shared-memory wavefronts instead of 8 for the natural order's 32-byte lane stride).
   extern __shared__ float ln_wb[];
   if constexpr (AFFINE) {
     for (int i = threadIdx.x; i < NCH * 256; i += blockDim.x) {
-      ln_wb[i] = i < C ? weight[i] : 0.f;
-      ln_wb[NCH * 256 + i] = i < C ? bias[i] : 0.f;
+      const int c = i >> 8, l = (i >> 3) & 31, h = (i >> 2) & 1, k = i & 3;
+      const int pos = (((c * 2 + h) * 32 + l) << 2) + k;
+      ln_wb[pos] = i < C ? weight[i] : 0.f;
+      ln_wb[NCH * 256 + pos] = i < C ? bias[i] : 0.f;
     }
     __syncthreads();
   }
@@ -129,10 +134,9 @@ __global__ void __launch_bounds__(kLnRowsPerBlock * 32)
       }
       uint64_t wv[4], bv[4];
       if (AFFINE) {
-        const float4 w0 = *reinterpret_cast<const float4*>(ln_wb + base);
-        const float4 w1 = *reinterpret_cast<const float4*>(ln_wb + base + 4);
-        const float4 b0 = *reinterpret_cast<const float4*>(ln_wb + NCH * 256 + base);
-        const float4 b1 = *reinterpret_cast<const float4*>(ln_wb + NCH * 256 + base + 4);
+        const float4* w4 = reinterpret_cast<const float4*>(ln_wb) + c * 64 + lane;
+        const float4* b4 = reinterpret_cast<const float4*>(ln_wb + NCH * 256) + c * 64 + lane;
+        const float4 w0 = w4[0], w1 = w4[32], b0 = b4[0], b1 = b4[32];
         wv[0] = f2_pack(w0.x, w0.y), wv[1] = f2_pack(w0.z, w0.w), wv[2] = f2_pack(w1.x, w1.y),
         wv[3] = f2_pack(w1.z, w1.w);
         bv[0] = f2_pack(b0.x, b0.y), bv[1] = f2_pack(b0.z, b0.w), bv[2] = f2_pack(b1.x, b1.y),
