@@ -201,9 +201,11 @@ def stack_config(workload: str, nblocks: int, world: int, transport: str = "nccl
         name = (f"cfg1: {nblocks}-block sparse-DiT stack fwd, T={T_TOKENS} shell tokens in {GRID}^3, C={CHANNELS}, "
                 f"{HEADS}x{CHANNELS // HEADS} heads, {COND} cond tokens, fp16")
     if transport == "auto":
+        import torch
+
         from hi3d_b200.dist import auto_transport
 
-        transport = auto_transport(world)
+        transport = auto_transport(world, torch.device("cuda", 0) if torch.cuda.is_available() else None)
     kv = {"nccl": "NCCL all-gather", "peer": "QKV epilogue stores into peers' symmetric buffers",
           "multicast": "QKV epilogue multimem stores into every GPU's symmetric buffer"}[transport]
     return {"workload": name, "blocks": nblocks, "tokens": T_TOKENS,
@@ -675,8 +677,10 @@ def sharded_parity(weights, inputs_local, inputs_full, world: int, rank: int, de
     x_l, mod_d, cos_l, sin_l, cond_d = inputs_local
     two = weights[:2]
     kvs = [transformer.context_kv(w, cond_d, HEADS) for w in two]
-    y_local = hdist.ShardedBlockStack(two, HEADS, transport=transport)(x_l, mod_d, cos_l, sin_l, kvs)
+    stack = hdist.ShardedBlockStack(two, HEADS, transport=transport)
+    y_local = stack(x_l, mod_d, cos_l, sin_l, kvs)
     y_all = hdist.gather_rows(y_local)
+    stack.close()  # collective: no rank releases its buffers while another still stores into them
     if rank != 0:
         return None
     x_f, cos_f, sin_f = inputs_full
@@ -796,7 +800,8 @@ def run_ours(args) -> None:
         "metric": "block_tokens_per_s", "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-        "config": stack_config(args.workload, nblocks, world, args.kv_transport),
+        "config": stack_config(args.workload, nblocks, world,
+                               stack.transport if world > 1 else args.kv_transport),
         "roofline": roofline,
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": x_host.numel() * 2,
                 "d2h_bytes_per_step": out_host.numel() * 2},
@@ -855,6 +860,9 @@ def run_ours(args) -> None:
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
+        # every rank drops its symmetric K/V buffers (and their multicast binding) at the same
+        # point, with no kernel in flight, before the process group goes away
+        stack.close()  # collective: every rank drops its symmetric buffers at the same point
         dist.barrier()
         dist.destroy_process_group()
 

@@ -213,12 +213,22 @@ def block_forward_sharded(w: dict, x: torch.Tensor, mod: torch.Tensor, cos: torc
     return x
 
 
-def auto_transport(world: int) -> str:
-    """The K/V transport measured fastest for the cfg1 stack at this rank count: the peer stores
-    at 2 ranks (88.6 ms per step against 90.7 for NCCL), the NCCL all-gather above (at 8 ranks
-    the peer stores' seven remote stores per row cost more than the gather: 31.8 against
-    30.6 ms)."""
-    return "peer" if world == 2 else "nccl"
+def auto_transport(world: int, device=None) -> str:
+    """The K/V transport measured fastest for the cfg1 stack at this rank count (ms per step):
+    the peer stores at 2 ranks (88.6; NCCL 90.7), the multicast stores at 4 and 8 ranks (50.5
+    and 29.8; NCCL 51.3 and 30.6, the peer stores 31.8 at 8), or the NCCL all-gather there when
+    the GPUs offer no NVLink multicast (``device``: the CUDA device to ask; assumed to offer it
+    when None)."""
+    if world <= 2:
+        return "peer"
+    if device is not None:
+        import torch.distributed._symmetric_memory as symm
+
+        dev = torch.device(device)
+        if dev.type != "cuda" or not symm._SymmetricMemory.has_multicast_support(
+                torch._C._autograd.DeviceType.CUDA, dev.index if dev.index is not None else 0):
+            return "nccl"
+    return "multicast"
 
 
 class ShardedBlockStack:
@@ -229,9 +239,7 @@ class ShardedBlockStack:
     ``"multicast"`` (the same with one multimem store per row through NVSwitch)."""
 
     def __init__(self, weights: list[dict], heads: int, group=None, transport: str = "auto"):
-        if transport == "auto":
-            transport = auto_transport(dist.get_world_size(group))
-        if transport not in ("nccl", "peer", "multicast"):
+        if transport not in ("auto", "nccl", "peer", "multicast"):
             raise ValueError(f"unknown K/V transport {transport!r}")
         self.weights = weights
         self.heads = heads
@@ -241,6 +249,13 @@ class ShardedBlockStack:
         self._kv_key = None
         self._mod_w = None  # [blocks, 6C] stacked modulation parameters (built on first use)
 
+    def close(self) -> None:
+        """Release the K/V buffers; collective with the peer transports (:meth:`PeerKV.close`):
+        every rank calls it at the same point before the buffers go away."""
+        if isinstance(self._kv, PeerKV):
+            self._kv.close()
+        self._kv, self._kv_key = None, None
+
     def __call__(self, x_local: torch.Tensor, mod: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
                  kvs: list[tuple[torch.Tensor, torch.Tensor]], timer: PhaseTimer | None = None) -> torch.Tensor:
         x = x_local.clone()
@@ -248,7 +263,10 @@ class ShardedBlockStack:
         world = dist.get_world_size(self.group)
         key = (t_local, c, x.dtype, x.device)
         if self._kv is None or self._kv_key != key:  # (re)built on every rank alike: PeerKV is collective
+            self.close()
             d = c // self.heads
+            if self.transport == "auto":
+                self.transport = auto_transport(world, x.device)
             if self.transport in ("peer", "multicast") and world > 1:
                 self._kv = PeerKV(t_local, self.heads, d, x.dtype, x.device, self.group,
                                   multicast=self.transport == "multicast")

@@ -43,6 +43,7 @@ class PeerKV:
         import torch.distributed._symmetric_memory as symm
 
         pg = group if group is not None else dist.group.WORLD
+        self.group = group
         self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
         if not 1 < self.world <= 8:
             raise ValueError(f"peer stores need 2 to 8 ranks of one node, not {self.world}")
@@ -88,6 +89,21 @@ class PeerKV:
         buf, _, store = self._sets[self._next % 2]
         self._next += 1
         return buf[0], buf[1], store
+
+    def close(self) -> None:
+        """Drop the buffers on every rank at the same point (collective): each rank first waits
+        for its own kernels, then all ranks meet, so no GPU still stores into a buffer (or its
+        multicast mapping) while a peer releases it; all ranks meet again afterwards."""
+        import gc
+
+        if not self._sets:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        self._sets, self._flags, self._flag_ptrs = [], None, None
+        gc.collect()
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
 
     def barrier(self, like: torch.Tensor) -> None:
         """The cross-rank barrier on the current stream of ``like``'s device."""

@@ -60,6 +60,7 @@ def _worker(rank, world, port, result_path, transport="nccl"):
     from hi3d_b200 import _lib
 
     assert _lib.device_status()["code"] == 0
+    stack.close()
     if rank == 0:
         ref = transformer.BlockStack(ws, heads)(tt(x)[None], tt(mod), tt(cos), tt(sin), kvs)[0]
         yf, rf = y.float(), ref.float()
