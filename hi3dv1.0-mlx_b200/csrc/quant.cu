@@ -349,6 +349,164 @@ static void launch_w(int ipw, const void* x, const float* sign, int8_t* q, float
   }
 }
 
+// ---------------------------------------------------------------------------
+// The rotating quantiser with one thread per 64-element block.
+//
+// A tile is R whole rows, viewed as R * K/64 blocks of 128 bytes (at most 256: one
+// per thread).  One TMA load brings the tile into shared memory with the 128-byte
+// swizzle (16-byte chunk j of block b lands at chunk j ^ (b % 8)), so thread b
+// reads its own block with eight conflict-free 16-byte loads; two tile buffers
+// alternate, the next-but-one tile loading while the current one is computed.
+// The thread then runs the whole signed H64 in registers: the multiply, the six
+// butterfly stages in index-bit order 0..5 (stage 0 on scalars, stages 1-5 on
+// f32x2 pairs), the final * 0.125 - the same IEEE operations on the same values
+// as the warp-shuffle kernel above, so the codes are identical - with no
+// cross-lane traffic.  Row maxima meet in shared memory (atomicMax on the
+// non-negative floats' bits, NaN excluded as fmaxf excludes it), three slots
+// rotating over the tiles so that one block barrier per tile suffices.
+// The multipliers sit in shared memory transposed ([K/256][K/64] float4), so a
+// warp's threads, which hold consecutive blocks of a row, read consecutive float4.
+// ---------------------------------------------------------------------------
+constexpr int kQtThreads = 256;
+constexpr int kQtMaxRows = 256;  // rows per tile (a tile of 64-wide rows)
+constexpr int kSiteQuantTile = 960;
+
+template <typename T>
+__global__ void __launch_bounds__(kQtThreads, 2)
+    quant_h64_tile_kernel(const __grid_constant__ CUtensorMap tm, const float* __restrict__ mult,
+                          int8_t* __restrict__ q, float* __restrict__ scale, int64_t rows, int K, int R,
+                          int64_t ntiles) {
+  extern __shared__ uint8_t qt_smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(qt_smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* stage0 = smem;  // two tiles of 256 x 128 bytes
+  float* ms = reinterpret_cast<float*>(smem + 2 * kQtThreads * 128);
+  __shared__ __align__(8) uint64_t full[2];
+  __shared__ uint32_t rmax[3][kQtMaxRows];
+  __shared__ int abort_flag;
+  const int t = threadIdx.x;
+  const int bpr = K >> 6, tb = R * bpr;
+  const int bc = t % bpr, rl = t / bpr;  // this thread's block column and row within the tile
+  if (t == 0) {
+    mbar_init(&full[0], 1);
+    mbar_init(&full[1], 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  for (int i = t; i < K; i += kQtThreads) {
+    const int e = i & 63;
+    ms[(((e >> 2) * bpr + (i >> 6)) << 2) + (e & 3)] = mult[i];
+  }
+  for (int i = t; i < 3 * kQtMaxRows; i += kQtThreads) (&rmax[0][0])[i] = 0u;
+  __syncthreads();
+  const int64_t step = gridDim.x;
+  const uint32_t tile_bytes = (uint32_t)tb * 128u;
+  if (t == 0) {
+    tma_prefetch_desc(&tm);
+    for (int s = 0; s < 2; ++s) {
+      const int64_t tile = blockIdx.x + s * step;
+      if (tile < ntiles) {
+        mbar_arrive_expect_tx(&full[s], tile_bytes);
+        tma_load_2d(stage0 + s * kQtThreads * 128, &tm, &full[s], 0, (int)(tile * tb));
+      }
+    }
+  }
+  const float4* ms4 = reinterpret_cast<const float4*>(ms);
+  int it = 0;
+  for (int64_t tile = blockIdx.x; tile < ntiles; tile += step, ++it) {
+    const int s = it & 1;
+    const bool ok = mbar_wait(&full[s], (it >> 1) & 1, &abort_flag, kSiteQuantTile);
+    if (__syncthreads_or(!ok)) break;  // every thread leaves together on a time-out
+    const int64_t row = tile * R + rl;
+    const bool active = t < tb && row < rows;
+    uint64_t P[32];  // (y[2k], y[2k+1])
+    const uint8_t* src = stage0 + s * kQtThreads * 128 + t * 128;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(src + ((j ^ (t & 7)) << 4));
+      P[4 * j] = Cvt<T>::to_f2(raw.x);
+      P[4 * j + 1] = Cvt<T>::to_f2(raw.y);
+      P[4 * j + 2] = Cvt<T>::to_f2(raw.z);
+      P[4 * j + 3] = Cvt<T>::to_f2(raw.w);
+    }
+    // y = x * multiplier
+#pragma unroll
+    for (int e4 = 0; e4 < 16; ++e4) {
+      const float4 m = ms4[e4 * bpr + bc];
+      P[2 * e4] = f2_mul(P[2 * e4], f2_pack(m.x, m.y));
+      P[2 * e4 + 1] = f2_mul(P[2 * e4 + 1], f2_pack(m.z, m.w));
+    }
+    // stage 0 (index bit 0): the two halves of each pair
+#pragma unroll
+    for (int k = 0; k < 32; ++k) {
+      float a, b;
+      f2_unpack(P[k], a, b);
+      P[k] = f2_pack(__fadd_rn(a, b), __fsub_rn(a, b));
+    }
+    // stages 1..5 (index bits 1..5): pairs k and k + 2^(bit-1)
+#pragma unroll
+    for (int h = 1; h < 32; h <<= 1) {
+#pragma unroll
+      for (int k = 0; k < 32; ++k) {
+        if (k & h) continue;
+        const uint64_t u = P[k], v = P[k + h];
+        P[k] = f2_add(u, v);
+        P[k + h] = f2_sub(u, v);
+      }
+    }
+    float y[64];
+    float amax = 0.f;
+#pragma unroll
+    for (int k = 0; k < 32; ++k) {
+      f2_unpack(f2_mul(P[k], f2_splat(0.125f)), y[2 * k], y[2 * k + 1]);
+      amax = fmaxf(amax, fmaxf(fabsf(y[2 * k]), fabsf(y[2 * k + 1])));
+    }
+    if (active) atomicMax(&rmax[it % 3][rl], __float_as_uint(amax));
+    if (t < R) rmax[(it + 1) % 3][t] = 0u;  // the next tile's slot (its readers finished two tiles ago)
+    __syncthreads();  // the tile buffer is read and the row maxima are complete
+    if (t == 0 && tile + 2 * step < ntiles) {
+      // generic-proxy reads of the buffer above, then the TMA (async proxy) refills it
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      mbar_arrive_expect_tx(&full[s], tile_bytes);
+      tma_load_2d(stage0 + s * kQtThreads * 128, &tm, &full[s], 0, (int)((tile + 2 * step) * tb));
+    }
+    if (active) {
+      const float sc = __fdiv_rn(fmaxf(__uint_as_float(rmax[it % 3][rl]), 1e-8f), 127.0f);
+      const float inv = __frcp_rn(sc);
+      if (bc == 0) scale[row] = sc;
+      uint4* dst = reinterpret_cast<uint4*>(q + (tile * tb + t) * 64);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float(&lo)[8] = *reinterpret_cast<const float(*)[8]>(&y[16 * j]);
+        const float(&hi)[8] = *reinterpret_cast<const float(*)[8]>(&y[16 * j + 8]);
+        const uint2 a = quant_pack8(lo, sc, inv), b = quant_pack8(hi, sc, inv);
+        dst[j] = make_uint4(a.x, a.y, b.x, b.y);
+      }
+    }
+  }
+}
+
+template <typename T>
+static int launch_quant_tiles(const void* x, const float* sign, int8_t* q, float* scale, int64_t rows, int K,
+                              cudaStream_t st) {
+  const int bpr = K / 64, R = kQtThreads / bpr;
+  const int64_t nblocks = rows * bpr, ntiles = (rows + R - 1) / R;
+  CUtensorMap tm;
+  const uint64_t dims[2] = {64, (uint64_t)nblocks}, strides[1] = {128};
+  const uint32_t box[2] = {64, (uint32_t)(R * bpr)};
+  int rc = encode_tmap(&tm, std::is_same<T, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                           : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                       2, x, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  const size_t smem = 1024 + 2 * kQtThreads * 128 + (size_t)K * sizeof(float);
+  auto kern = quant_h64_tile_kernel<T>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return set_error(HI3D_ERR_CUDA, "quantize_act_i8: smem attribute: %s", cudaGetErrorString(e));
+  const int64_t cap = 2 * (int64_t)sm_count();  // two resident CTAs per SM
+  const int grid = (int)(ntiles < cap ? ntiles : cap);
+  kern<<<grid, kQtThreads, smem, st>>>(tm, sign, q, scale, rows, K, R, ntiles);
+  return check_launch("quantize_act_i8");
+}
+
 template <typename T, bool ROTATE>
 static int launch_quant(const void* x, const float* sign, int8_t* q, float* scale, int64_t rows, int K,
                         cudaStream_t st) {
@@ -381,12 +539,16 @@ extern "C" int hi3d_quantize_act_i8(const void* x, const float* multiplier, int8
   if (rows == 0) return HI3D_OK;
   cudaStream_t st = as_stream(stream);
   const int K = (int)k;
+  // the block-per-thread kernel for rotated rows of up to 16384 (256 blocks of 64)
+  const bool tiles = rotate && K <= 64 * kQtThreads && rows * (K / 64) < (int64_t)1 << 31;
   if (dtype == HI3D_F16)
-    return rotate ? launch_quant<__half, true>(x, multiplier, q, scale, rows, K, st)
-                  : launch_quant<__half, false>(x, multiplier, q, scale, rows, K, st);
+    return tiles ? launch_quant_tiles<__half>(x, multiplier, q, scale, rows, K, st)
+           : rotate ? launch_quant<__half, true>(x, multiplier, q, scale, rows, K, st)
+                    : launch_quant<__half, false>(x, multiplier, q, scale, rows, K, st);
   if (dtype == HI3D_BF16)
-    return rotate ? launch_quant<__nv_bfloat16, true>(x, multiplier, q, scale, rows, K, st)
-                  : launch_quant<__nv_bfloat16, false>(x, multiplier, q, scale, rows, K, st);
+    return tiles ? launch_quant_tiles<__nv_bfloat16>(x, multiplier, q, scale, rows, K, st)
+           : rotate ? launch_quant<__nv_bfloat16, true>(x, multiplier, q, scale, rows, K, st)
+                    : launch_quant<__nv_bfloat16, false>(x, multiplier, q, scale, rows, K, st);
   return set_error(HI3D_ERR_INVALID_ARGUMENT, "quantize_act_i8: dtype must be f16 or bf16");
 }
 

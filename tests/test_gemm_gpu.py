@@ -65,6 +65,18 @@ def test_linear_gelu_and_residual_epilogues():
     assert np.array_equal(res.cpu().numpy(), ops.gate_residual(res0, y.reshape(2, m // 2, n), None))
 
 
+@pytest.mark.parametrize("rows,k", [(20003, 1024), (8195, 4096), (3001, 2112)])
+def test_quantizer_bit_exact_many_tiles(rows, k):
+    """Enough rows that every CTA of the tiled quantiser runs several tiles (both tile buffers
+    refilled, the three row-maximum slots rotating) and the last tile is partial."""
+    rng = np.random.default_rng(rows)
+    x = (rng.standard_normal((rows, k)) * rng.uniform(0.1, 10, (rows, 1))).astype(np.float16)
+    q, s = w8a8.quantize_activation(_t(x))
+    q_ref, s_ref = ops.quantize_activation(x)
+    assert np.array_equal(s.cpu().numpy(), s_ref)
+    assert np.array_equal(q.cpu().numpy(), q_ref)
+
+
 @pytest.mark.parametrize("k", [64, 1024, 2112, 4096, 8448])
 def test_quantizer_bit_exact(k):
     rng = np.random.default_rng(k)
