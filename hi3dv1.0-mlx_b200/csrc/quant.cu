@@ -367,6 +367,39 @@ static void launch_w(int ipw, const void* x, const float* sign, int8_t* q, float
 // The multipliers sit in shared memory transposed ([K/256][K/64] float4), so a
 // warp's threads, which hold consecutive blocks of a row, read consecutive float4.
 // ---------------------------------------------------------------------------
+// Codes of 8 values (4 f32x2 pairs) for the tiled kernel: the quotient z = y * inv is rounded
+// with the 1.5 * 2^23 shift, (z + 2^23 * 1.5) - 2^23 * 1.5, which is round-half-even to an
+// integer for |z| < 2^22 (here |z| <= 127 * (1 + 3 * 2^-24)), on the FMA pipe and in pairs; the
+// two's-complement low byte of the shifted value's bits is then the code.  As in quant_pack8,
+// a quotient within 3e-5 of a rounding tie (or not finite) falls back to the exact division;
+// any such value sends all 8 through quant_pack8, so the codes are those of quant_pack8.
+__device__ __forceinline__ uint2 quant_pack8_pairs(const uint64_t (&Y)[4], float s, float inv) {
+  const uint64_t INV = f2_splat(inv), SHIFT = f2_splat(12582912.0f), UNSHIFT = f2_splat(-12582912.0f);
+  uint32_t tb[8];
+  bool near_tie = false;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint64_t z = f2_mul(Y[i], INV);
+    const uint64_t t = f2_add(z, SHIFT);
+    const uint64_t d = f2_sub(z, f2_add(t, UNSHIFT));
+    float d0, d1, t0, t1;
+    f2_unpack(d, d0, d1);
+    f2_unpack(t, t0, t1);
+    near_tie |= !(fabsf(d0) < 0.5f - 3e-5f) || !(fabsf(d1) < 0.5f - 3e-5f);
+    tb[2 * i] = __float_as_uint(t0);
+    tb[2 * i + 1] = __float_as_uint(t1);
+  }
+  if (near_tie) {
+    float y[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) f2_unpack(Y[i], y[2 * i], y[2 * i + 1]);
+    return quant_pack8(y, s, inv);
+  }
+  const uint32_t w0 = __byte_perm(__byte_perm(tb[0], tb[1], 0x0040), __byte_perm(tb[2], tb[3], 0x0040), 0x5410);
+  const uint32_t w1 = __byte_perm(__byte_perm(tb[4], tb[5], 0x0040), __byte_perm(tb[6], tb[7], 0x0040), 0x5410);
+  return make_uint2(w0, w1);
+}
+
 constexpr int kQtThreads = 256;
 constexpr int kQtMaxRows = 256;  // rows per tile (a tile of 64-wide rows)
 constexpr int kSiteQuantTile = 960;
@@ -453,12 +486,13 @@ __global__ void __launch_bounds__(kQtThreads, 2)
         P[k + h] = f2_sub(u, v);
       }
     }
-    float y[64];
     float amax = 0.f;
 #pragma unroll
     for (int k = 0; k < 32; ++k) {
-      f2_unpack(f2_mul(P[k], f2_splat(0.125f)), y[2 * k], y[2 * k + 1]);
-      amax = fmaxf(amax, fmaxf(fabsf(y[2 * k]), fabsf(y[2 * k + 1])));
+      P[k] = f2_mul(P[k], f2_splat(0.125f));
+      float lo, hi;
+      f2_unpack(P[k], lo, hi);
+      amax = fmaxf(amax, fmaxf(fabsf(lo), fabsf(hi)));
     }
     if (active) atomicMax(&rmax[it % 3][rl], __float_as_uint(amax));
     if (t < R) rmax[(it + 1) % 3][t] = 0u;  // the next tile's slot (its readers finished two tiles ago)
@@ -476,9 +510,9 @@ __global__ void __launch_bounds__(kQtThreads, 2)
       uint4* dst = reinterpret_cast<uint4*>(q + (tile * tb + t) * 64);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const float(&lo)[8] = *reinterpret_cast<const float(*)[8]>(&y[16 * j]);
-        const float(&hi)[8] = *reinterpret_cast<const float(*)[8]>(&y[16 * j + 8]);
-        const uint2 a = quant_pack8(lo, sc, inv), b = quant_pack8(hi, sc, inv);
+        const uint64_t(&lo)[4] = *reinterpret_cast<const uint64_t(*)[4]>(&P[8 * j]);
+        const uint64_t(&hi)[4] = *reinterpret_cast<const uint64_t(*)[4]>(&P[8 * j + 4]);
+        const uint2 a = quant_pack8_pairs(lo, sc, inv), b = quant_pack8_pairs(hi, sc, inv);
         dst[j] = make_uint4(a.x, a.y, b.x, b.y);
       }
     }
