@@ -96,6 +96,39 @@ __device__ __forceinline__ uint2 quant_pack8(const float (&y)[8], float s, float
   return make_uint2(w0, w1);
 }
 
+// Codes of 8 values (4 f32x2 pairs), for the tiled and the LayerNorm-fused kernels: the quotient z = y * inv is rounded
+// with the 1.5 * 2^23 shift, (z + 2^23 * 1.5) - 2^23 * 1.5, which is round-half-even to an
+// integer for |z| < 2^22 (here |z| <= 127 * (1 + 3 * 2^-24)), on the FMA pipe and in pairs; the
+// two's-complement low byte of the shifted value's bits is then the code.  As in quant_pack8,
+// a quotient within 3e-5 of a rounding tie (or not finite) falls back to the exact division;
+// any such value sends all 8 through quant_pack8, so the codes are those of quant_pack8.
+__device__ __forceinline__ uint2 quant_pack8_pairs(const uint64_t (&Y)[4], float s, float inv) {
+  const uint64_t INV = f2_splat(inv), SHIFT = f2_splat(12582912.0f), UNSHIFT = f2_splat(-12582912.0f);
+  uint32_t tb[8];
+  bool near_tie = false;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint64_t z = f2_mul(Y[i], INV);
+    const uint64_t t = f2_add(z, SHIFT);
+    const uint64_t d = f2_sub(z, f2_add(t, UNSHIFT));
+    float d0, d1, t0, t1;
+    f2_unpack(d, d0, d1);
+    f2_unpack(t, t0, t1);
+    near_tie |= !(fabsf(d0) < 0.5f - 3e-5f) || !(fabsf(d1) < 0.5f - 3e-5f);
+    tb[2 * i] = __float_as_uint(t0);
+    tb[2 * i + 1] = __float_as_uint(t1);
+  }
+  if (near_tie) {
+    float y[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) f2_unpack(Y[i], y[2 * i], y[2 * i + 1]);
+    return quant_pack8(y, s, inv);
+  }
+  const uint32_t w0 = __byte_perm(__byte_perm(tb[0], tb[1], 0x0040), __byte_perm(tb[2], tb[3], 0x0040), 0x5410);
+  const uint32_t w1 = __byte_perm(__byte_perm(tb[4], tb[5], 0x0040), __byte_perm(tb[6], tb[7], 0x0040), 0x5410);
+  return make_uint2(w0, w1);
+}
+
 // One row per WPR warps of a 256-thread block; warp `part` of a row handles the
 // 256-element chunks part, part + WPR, ... (IPW of them).
 template <typename T, int IPW, int WPR, bool ROTATE>
@@ -268,7 +301,9 @@ __global__ void __launch_bounds__(kLnqRowsPerBlock * 32)
     for (int c = 0; c < NCH; ++c) {
       const int base = c * 256 + lane * 8;
       if (base >= C) continue;
-      *reinterpret_cast<uint2*>(qr + base) = quant_pack8(y[c], sc, inv);
+      const uint64_t yp[4] = {f2_pack(y[c][0], y[c][1]), f2_pack(y[c][2], y[c][3]), f2_pack(y[c][4], y[c][5]),
+                              f2_pack(y[c][6], y[c][7])};
+      *reinterpret_cast<uint2*>(qr + base) = quant_pack8_pairs(yp, sc, inv);
     }
   }
 }
@@ -367,39 +402,6 @@ static void launch_w(int ipw, const void* x, const float* sign, int8_t* q, float
 // The multipliers sit in shared memory transposed ([K/256][K/64] float4), so a
 // warp's threads, which hold consecutive blocks of a row, read consecutive float4.
 // ---------------------------------------------------------------------------
-// Codes of 8 values (4 f32x2 pairs) for the tiled kernel: the quotient z = y * inv is rounded
-// with the 1.5 * 2^23 shift, (z + 2^23 * 1.5) - 2^23 * 1.5, which is round-half-even to an
-// integer for |z| < 2^22 (here |z| <= 127 * (1 + 3 * 2^-24)), on the FMA pipe and in pairs; the
-// two's-complement low byte of the shifted value's bits is then the code.  As in quant_pack8,
-// a quotient within 3e-5 of a rounding tie (or not finite) falls back to the exact division;
-// any such value sends all 8 through quant_pack8, so the codes are those of quant_pack8.
-__device__ __forceinline__ uint2 quant_pack8_pairs(const uint64_t (&Y)[4], float s, float inv) {
-  const uint64_t INV = f2_splat(inv), SHIFT = f2_splat(12582912.0f), UNSHIFT = f2_splat(-12582912.0f);
-  uint32_t tb[8];
-  bool near_tie = false;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const uint64_t z = f2_mul(Y[i], INV);
-    const uint64_t t = f2_add(z, SHIFT);
-    const uint64_t d = f2_sub(z, f2_add(t, UNSHIFT));
-    float d0, d1, t0, t1;
-    f2_unpack(d, d0, d1);
-    f2_unpack(t, t0, t1);
-    near_tie |= !(fabsf(d0) < 0.5f - 3e-5f) || !(fabsf(d1) < 0.5f - 3e-5f);
-    tb[2 * i] = __float_as_uint(t0);
-    tb[2 * i + 1] = __float_as_uint(t1);
-  }
-  if (near_tie) {
-    float y[8];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) f2_unpack(Y[i], y[2 * i], y[2 * i + 1]);
-    return quant_pack8(y, s, inv);
-  }
-  const uint32_t w0 = __byte_perm(__byte_perm(tb[0], tb[1], 0x0040), __byte_perm(tb[2], tb[3], 0x0040), 0x5410);
-  const uint32_t w1 = __byte_perm(__byte_perm(tb[4], tb[5], 0x0040), __byte_perm(tb[6], tb[7], 0x0040), 0x5410);
-  return make_uint2(w0, w1);
-}
-
 constexpr int kQtThreads = 256;
 constexpr int kQtMaxRows = 256;  // rows per tile (a tile of 64-wide rows)
 constexpr int kSiteQuantTile = 960;
