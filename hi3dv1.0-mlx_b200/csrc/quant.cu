@@ -206,6 +206,19 @@ __global__ void __launch_bounds__(kLnqRowsPerBlock * 32)
                     int8_t* __restrict__ q, float* __restrict__ qscale) {
   const int lane = threadIdx.x & 31;
   const int g = lane & 7;
+  // fp32 affine parameters staged once per block in shared memory, in the lane order of
+  // ln_mod_kernel (channel c*256 + 8 l + 4 h + k at float4 (2c + h) * 32 + l): each warp's
+  // 16-byte loads read 512 contiguous bytes
+  extern __shared__ float lnq_wb[];
+  if constexpr (AFFINE) {
+    for (int i = threadIdx.x; i < NCH * 256; i += blockDim.x) {
+      const int c = i >> 8, l = (i >> 3) & 31, h = (i >> 2) & 1, k = i & 3;
+      const int pos = (((c * 2 + h) * 32 + l) << 2) + k;
+      lnq_wb[pos] = i < C ? weight[i] : 0.f;
+      lnq_wb[NCH * 256 + pos] = i < C ? bias[i] : 0.f;
+    }
+    __syncthreads();
+  }
   for (int64_t row = (int64_t)blockIdx.x * kLnqRowsPerBlock + (threadIdx.x >> 5); row < rows;
        row += (int64_t)gridDim.x * kLnqRowsPerBlock) {
     const T* xr = x + row * C;
@@ -269,14 +282,20 @@ __global__ void __launch_bounds__(kLnqRowsPerBlock * 32)
         }
         const uint32_t* scw = reinterpret_cast<const uint32_t*>(&sc);
         const uint32_t* shw = reinterpret_cast<const uint32_t*>(&sh);
+        uint64_t wv[4], bv[4];
+        if (AFFINE) {
+          const float4* w4 = reinterpret_cast<const float4*>(lnq_wb) + c * 64 + lane;
+          const float4* b4 = reinterpret_cast<const float4*>(lnq_wb + NCH * 256) + c * 64 + lane;
+          const float4 w0 = w4[0], w1 = w4[32], b0 = b4[0], b1 = b4[32];
+          wv[0] = f2_pack(w0.x, w0.y), wv[1] = f2_pack(w0.z, w0.w), wv[2] = f2_pack(w1.x, w1.y),
+          wv[3] = f2_pack(w1.z, w1.w);
+          bv[0] = f2_pack(b0.x, b0.y), bv[1] = f2_pack(b0.z, b0.w), bv[2] = f2_pack(b1.x, b1.y),
+          bv[3] = f2_pack(b1.z, b1.w);
+        }
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           uint64_t yy = f2_mul(d[c][i], inv2);
-          if (AFFINE) {
-            const uint64_t w2 = f2_pack(weight[base + 2 * i], weight[base + 2 * i + 1]);
-            const uint64_t b2 = f2_pack(bias[base + 2 * i], bias[base + 2 * i + 1]);
-            yy = f2_add(f2_mul(yy, w2), b2);
-          }
+          if (AFFINE) yy = f2_add(f2_mul(yy, wv[i]), bv[i]);
           uint32_t h = Cvt<T>::from_f2(yy);
           if (MODULATE) h = Cvt<T>::add2(Cvt<T>::mul2(h, scw[i]), shw[i]);
           const T* hp = reinterpret_cast<const T*>(&h);
@@ -318,12 +337,13 @@ static void launch_lnq(const void* x, int64_t rows, int C, float eps, const floa
   const T* xt = (const T*)x;
   const T* s = (const T*)sc;
   const T* t = (const T*)sh;
+  const size_t wb = (size_t)2 * NCH * 256 * sizeof(float);  // affine parameters in shared memory
   if (w && sc)
-    ln_quant_kernel<T, NCH, true, true><<<grid, kLnqRowsPerBlock * 32, 0, st>>>(xt, rows, C, eps, w, b, s, t, rpb, ms,
-                                                                               sign, q, qs);
-  else if (w)
-    ln_quant_kernel<T, NCH, true, false><<<grid, kLnqRowsPerBlock * 32, 0, st>>>(xt, rows, C, eps, w, b, s, t, rpb,
+    ln_quant_kernel<T, NCH, true, true><<<grid, kLnqRowsPerBlock * 32, wb, st>>>(xt, rows, C, eps, w, b, s, t, rpb,
                                                                                 ms, sign, q, qs);
+  else if (w)
+    ln_quant_kernel<T, NCH, true, false><<<grid, kLnqRowsPerBlock * 32, wb, st>>>(xt, rows, C, eps, w, b, s, t, rpb,
+                                                                                 ms, sign, q, qs);
   else if (sc)
     ln_quant_kernel<T, NCH, false, true><<<grid, kLnqRowsPerBlock * 32, 0, st>>>(xt, rows, C, eps, w, b, s, t, rpb,
                                                                                 ms, sign, q, qs);
