@@ -2,10 +2,11 @@
 //
 // Each rank holds a contiguous slice of S rows of one sequence: its queries, keys
 // and values ([S, H, D], token-major).  The K/V slices of all ranks are
-// all-gathered over NCCL on a side stream while the caller's stream attends the
-// rank's own keys; the caller's stream then waits for the gather, attends the
-// keys before and after its own slice, and merges the partial results by their
-// log2-sum-exp weights (hi3d_flash_attn_fwd_partial / hi3d_flash_attn_merge).
+// all-gathered over NCCL on a high-priority side stream; the caller's stream waits
+// for the gather and attends all keys in one launch (key-split by the cost model
+// below when the grid is short of waves).  Attending the own keys while the gather
+// runs and merging partials was measured slower: the partial kernel and the merge
+// cost more than the exposed gather.
 //
 // NCCL is loaded at run time (dlopen of libnccl.so.2), so the library has no link
 // dependency on it; inside a process that already loaded NCCL (e.g. through

@@ -184,8 +184,9 @@ def auto_key_splits(q_rows: int, k_rows: int, heads: int, head_dim: int, batch: 
 class AttentionParts:
     """Attention of one set of queries over several disjoint key sets, combined exactly by their
     log-sum-exp weights: :meth:`add` one key set at a time (``hi3d_flash_attn_fwd_partial``), then
-    :meth:`merge` (``hi3d_flash_attn_merge``).  The sharded block attends its own key shard while
-    the other ranks' keys are still being gathered.  Queries and keys as in
+    :meth:`merge` (``hi3d_flash_attn_merge``), or finish with :meth:`add_final`, which merges in
+    the last launch's epilogue.  For key sets that arrive at different times; the sharded block
+    gathers all keys first and attends them in one pass, which measured faster.  Queries and keys as in
     :func:`flash_attention`; ``slots`` bounds the total key splits of all ``add`` calls."""
 
     def __init__(self, q: torch.Tensor, scale: float, slots: int, q_layout: str = "bhnd"):

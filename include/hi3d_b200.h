@@ -155,8 +155,8 @@ HI3D_API int hi3d_flash_attn_split_workspace_size(const hi3d_attn_args* args, in
 HI3D_API int hi3d_flash_attn_fwd_split(const hi3d_attn_args* args, int k_splits, void* workspace,
                                        int64_t workspace_bytes, void* stream);
 
-/* Partial results for combining attention over disjoint key sets of the same queries (a query
- * shard against its own keys first, other ranks' keys once gathered): k_splits key ranges of
+/* Partial results for combining attention over disjoint key sets of the same queries (key sets
+ * that become available at different times): k_splits key ranges of
  * args' keys, written as O / l (fp32) to part_o[slot0 + s][row][head][head_dim] and the
  * log2-sum-exp to part_lse[slot0 + s][row][head], row = query row (dense: b * nq + row;
  * varlen: packed row) with part_rows the number of query rows.  args->out is not touched.
