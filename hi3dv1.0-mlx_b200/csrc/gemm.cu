@@ -423,9 +423,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         // of the 32-row strip belongs to one batch element (else per row group below):
         // gated residual projection 93 -> 88 us at T = 32768.
         uint4 gate_pre[4];
-        const bool gate_hoist = EPI == EPI_RESIDUAL && p.gate && p.vec && (p.rows_per_batch % 32) == 0;
+        // rows_per_batch is at most M (the host clamps it), so the batch index takes a 32-bit division
+        const int rpb = (int)p.rows_per_batch;
+        const bool gated = EPI == EPI_RESIDUAL && p.gate != nullptr;
+        const bool gate_hoist = gated && p.vec && (rpb % 32) == 0;
         if (EPI == EPI_RESIDUAL && gate_hoist) {
-          const OutT* g0 = reinterpret_cast<const OutT*>(p.gate) + (int64_t)(m0 / p.rows_per_batch) * p.gate_stride;
+          const OutT* g0 = reinterpret_cast<const OutT*>(p.gate) + (int64_t)(m0 / rpb) * p.gate_stride;
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
             const int n = nh + c * 32 + (lane & 3) * 8;
@@ -492,9 +495,10 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (m >= p.M || n >= p.N) continue;
               OutT* orow = reinterpret_cast<OutT*>(p.out) + (int64_t)m * p.ldo;
               const OutT* ya = reinterpret_cast<const OutT*>(&yv);
-              const OutT* grow = nullptr;
-              if (EPI == EPI_RESIDUAL && p.gate)
-                grow = reinterpret_cast<const OutT*>(p.gate) + (m / p.rows_per_batch) * p.gate_stride;
+              // this row's gate vector (per batch element), unless hoisted for the whole strip
+              const OutT* grow = gated && !gate_hoist
+                                     ? reinterpret_cast<const OutT*>(p.gate) + (int64_t)(m / rpb) * p.gate_stride
+                                     : nullptr;
               if (p.vec && n + 8 <= p.N) {
                 if constexpr (EPI == EPI_RESIDUAL) {
                   // x + round(y * gate), rounded, on 16-bit pairs: the product of two 16-bit values
@@ -505,7 +509,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                    : grow ? __ldg(reinterpret_cast<const uint4*>(grow + n)) : make_uint4(0, 0, 0, 0);
                   const uint4 xv = res[c][i];
                   uint4 w;
-                  if (grow) {
+                  if (gated) {
                     w.x = Cvt<OutT>::add2(xv.x, Cvt<OutT>::mul2(yv.x, gv.x));
                     w.y = Cvt<OutT>::add2(xv.y, Cvt<OutT>::mul2(yv.y, gv.y));
                     w.z = Cvt<OutT>::add2(xv.z, Cvt<OutT>::mul2(yv.z, gv.z));
@@ -521,10 +525,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                   *reinterpret_cast<uint4*>(orow + n) = yv;
                 }
               } else {
+                const OutT* gr =
+                    gated ? reinterpret_cast<const OutT*>(p.gate) + (int64_t)(m / rpb) * p.gate_stride : nullptr;
                 for (int qq = 0; qq < 8 && n + qq < p.N; ++qq) {
                   if (EPI == EPI_RESIDUAL) {
                     float g = Cvt<OutT>::to_f(ya[qq]);
-                    if (grow) g = Cvt<OutT>::to_f(Cvt<OutT>::from_f(__fmul_rn(g, Cvt<OutT>::to_f(grow[n + qq]))));
+                    if (gr) g = Cvt<OutT>::to_f(Cvt<OutT>::from_f(__fmul_rn(g, Cvt<OutT>::to_f(gr[n + qq]))));
                     orow[n + qq] = Cvt<OutT>::from_f(__fadd_rn(Cvt<OutT>::to_f(orow[n + qq]), g));
                   } else {
                     orow[n + qq] = ya[qq];
@@ -710,7 +716,7 @@ extern "C" int hi3d_gemm_w8a8(const int8_t* a, const int8_t* w, const float* sa,
   p.sa = sa;
   p.sw = sw;
   p.gate = gate;
-  p.rows_per_batch = rows_per_batch > 0 ? rows_per_batch : m;
+  p.rows_per_batch = rows_per_batch > 0 && rows_per_batch < m ? rows_per_batch : m;  // <= m: fits 32 bits
   p.gate_stride = gate_stride;
   cudaStream_t st = as_stream(stream);
   if (out_dtype == HI3D_F16)
@@ -738,7 +744,7 @@ extern "C" int hi3d_gemm(const void* a, const void* w, const void* bias, void* o
   p.ldo = ldo;
   p.bias = bias;
   p.gate = gate;
-  p.rows_per_batch = rows_per_batch > 0 ? rows_per_batch : m;
+  p.rows_per_batch = rows_per_batch > 0 && rows_per_batch < m ? rows_per_batch : m;  // <= m: fits 32 bits
   p.gate_stride = gate_stride;
   cudaStream_t st = as_stream(stream);
   if (dtype == HI3D_F16) return dispatch_epi<gemm::KIND_F16, __half>(epilogue, a, w, (int)m, (int)n, (int)k, p, st);
