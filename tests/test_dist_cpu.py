@@ -126,6 +126,19 @@ def test_shard_slice():
         shard_slice(10, 0, 3)
 
 
+def test_auto_transport_follows_the_measurements():
+    """Peer stores at 2 ranks, multicast stores above when the device offers NVLink multicast,
+    the NCCL all-gather otherwise (a CPU device has none); unknown transports are refused."""
+    sys.path.insert(0, os.path.join(REPO, "hi3dv1.0-mlx_b200"))
+    from hi3d_b200.dist import ShardedBlockStack, auto_transport
+
+    assert auto_transport(2) == "peer"
+    assert auto_transport(4) == "multicast" and auto_transport(8) == "multicast"
+    assert auto_transport(8, "cpu") == "nccl"
+    with pytest.raises(ValueError):
+        ShardedBlockStack([], 4, transport="ring")
+
+
 def test_dead_rank_fails_collective_in_bounded_time():
     import time
 
