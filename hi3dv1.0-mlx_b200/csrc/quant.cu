@@ -196,6 +196,92 @@ __global__ void __launch_bounds__(256) quant_h64_kernel(const T* __restrict__ x,
 // codes.  The 16-bit h is never written: bit-identical to quantize(layer_norm_modulate(x)).
 // Lane l of the warp holds channels c * 256 + 8 l .. + 7 of chunk c (channels % 64 == 0).
 // ---------------------------------------------------------------------------
+// The LayerNorm32 (+ affine) (+ modulation) of one row by one warp, as ln_mod_kernel computes
+// it (rowwise.cu; kernels.py:162-201): lane l gets the rounded 16-bit h of channels
+// c * 256 + 8 l .. + 7 as four packed words per chunk c (zero past C).  `wb`: the fp32 affine
+// parameters in shared memory in lane order (float4 (2c + h) * 32 + l), when AFFINE.
+template <typename T, int NCH, bool AFFINE, bool MODULATE>
+__device__ __forceinline__ void ln_row_words(const T* __restrict__ xr, int64_t row, int C, float eps,
+                                             const float* wb, const T* __restrict__ scale,
+                                             const T* __restrict__ shift, int64_t rows_per_batch,
+                                             int64_t mod_stride, int lane, uint4 (&hw)[NCH]) {
+  uint4 raw[NCH];
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    raw[c] = make_uint4(0, 0, 0, 0);
+    if (c * 256 + lane * 8 < C) raw[c] = *reinterpret_cast<const uint4*>(xr + c * 256 + lane * 8);
+  }
+  uint64_t d[NCH][4];
+  uint64_t s2 = 0;
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    const uint32_t* rw = reinterpret_cast<const uint32_t*>(&raw[c]);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      d[c][i] = Cvt<T>::to_f2(rw[i]);
+      s2 = f2_add(s2, d[c][i]);
+    }
+  }
+  float slo, shi;
+  f2_unpack(s2, slo, shi);
+  float sum = slo + shi;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  const float mean = __fdiv_rn(sum, (float)C);
+  const uint64_t neg_mean = f2_splat(-mean);
+  uint64_t q2 = 0;
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    if (c * 256 + lane * 8 < C) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        d[c][i] = f2_add(d[c][i], neg_mean);
+        q2 = f2_fma(d[c][i], d[c][i], q2);
+      }
+    }
+  }
+  float qlo, qhi;
+  f2_unpack(q2, qlo, qhi);
+  float sq = qlo + qhi;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+  const uint64_t inv2 = f2_splat(__fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sq, (float)C), eps))));
+  const int64_t mb = MODULATE ? (row / rows_per_batch) * mod_stride : 0;
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    const int base = c * 256 + lane * 8;
+    hw[c] = make_uint4(0, 0, 0, 0);
+    if (base >= C) continue;
+    uint4 sc = make_uint4(0, 0, 0, 0), sh = make_uint4(0, 0, 0, 0);
+    if (MODULATE) {
+      sc = *reinterpret_cast<const uint4*>(scale + mb + base);
+      sh = *reinterpret_cast<const uint4*>(shift + mb + base);
+    }
+    const uint32_t* scw = reinterpret_cast<const uint32_t*>(&sc);
+    const uint32_t* shw = reinterpret_cast<const uint32_t*>(&sh);
+    uint64_t wv[4], bv[4];
+    if (AFFINE) {
+      const float4* w4 = reinterpret_cast<const float4*>(wb) + c * 64 + lane;
+      const float4* b4 = reinterpret_cast<const float4*>(wb + NCH * 256) + c * 64 + lane;
+      const float4 w0 = w4[0], w1 = w4[32], b0 = b4[0], b1 = b4[32];
+      wv[0] = f2_pack(w0.x, w0.y), wv[1] = f2_pack(w0.z, w0.w), wv[2] = f2_pack(w1.x, w1.y),
+      wv[3] = f2_pack(w1.z, w1.w);
+      bv[0] = f2_pack(b0.x, b0.y), bv[1] = f2_pack(b0.z, b0.w), bv[2] = f2_pack(b1.x, b1.y),
+      bv[3] = f2_pack(b1.z, b1.w);
+    }
+    uint32_t hv[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      uint64_t yy = f2_mul(d[c][i], inv2);
+      if (AFFINE) yy = f2_add(f2_mul(yy, wv[i]), bv[i]);
+      uint32_t h = Cvt<T>::from_f2(yy);
+      if (MODULATE) h = Cvt<T>::add2(Cvt<T>::mul2(h, scw[i]), shw[i]);
+      hv[i] = h;
+    }
+    hw[c] = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+  }
+}
+
 constexpr int kLnqRowsPerBlock = 4;
 
 template <typename T, int NCH, bool AFFINE, bool MODULATE>
@@ -221,52 +307,10 @@ __global__ void __launch_bounds__(kLnqRowsPerBlock * 32)
   }
   for (int64_t row = (int64_t)blockIdx.x * kLnqRowsPerBlock + (threadIdx.x >> 5); row < rows;
        row += (int64_t)gridDim.x * kLnqRowsPerBlock) {
-    const T* xr = x + row * C;
-    // ---- LayerNorm statistics (as ln_mod_kernel)
-    uint4 raw[NCH];
-#pragma unroll
-    for (int c = 0; c < NCH; ++c) {
-      raw[c] = make_uint4(0, 0, 0, 0);
-      if (c * 256 + lane * 8 < C) raw[c] = *reinterpret_cast<const uint4*>(xr + c * 256 + lane * 8);
-    }
-    uint64_t d[NCH][4];
-    uint64_t s2 = 0;
-#pragma unroll
-    for (int c = 0; c < NCH; ++c) {
-      const uint32_t* rw = reinterpret_cast<const uint32_t*>(&raw[c]);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        d[c][i] = Cvt<T>::to_f2(rw[i]);
-        s2 = f2_add(s2, d[c][i]);
-      }
-    }
-    float slo, shi;
-    f2_unpack(s2, slo, shi);
-    float sum = slo + shi;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-    const float mean = __fdiv_rn(sum, (float)C);
-    const uint64_t neg_mean = f2_splat(-mean);
-    uint64_t q2 = 0;
-#pragma unroll
-    for (int c = 0; c < NCH; ++c) {
-      if (c * 256 + lane * 8 < C) {
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          d[c][i] = f2_add(d[c][i], neg_mean);
-          q2 = f2_fma(d[c][i], d[c][i], q2);
-        }
-      }
-    }
-    float qlo, qhi;
-    f2_unpack(q2, qlo, qhi);
-    float sq = qlo + qhi;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
-    const uint64_t inv2 = f2_splat(__fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sq, (float)C), eps))));
-    const int64_t mb = MODULATE ? (row / rows_per_batch) * mod_stride : 0;
-
-    // ---- h (rounded as the separate kernel rounds it), then the rotation per 64-block
+    uint4 hw[NCH];
+    ln_row_words<T, NCH, AFFINE, MODULATE>(x + row * C, row, C, eps, lnq_wb, scale, shift, rows_per_batch,
+                                           mod_stride, lane, hw);
+    // ---- the rotation per 64-block of h
     float y[NCH][8];
     float amax = 0.f;
 #pragma unroll
@@ -275,30 +319,10 @@ __global__ void __launch_bounds__(kLnqRowsPerBlock * 32)
       const bool active = base < C;
       float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
       if (active) {
-        uint4 sc = make_uint4(0, 0, 0, 0), sh = make_uint4(0, 0, 0, 0);
-        if (MODULATE) {
-          sc = *reinterpret_cast<const uint4*>(scale + mb + base);
-          sh = *reinterpret_cast<const uint4*>(shift + mb + base);
-        }
-        const uint32_t* scw = reinterpret_cast<const uint32_t*>(&sc);
-        const uint32_t* shw = reinterpret_cast<const uint32_t*>(&sh);
-        uint64_t wv[4], bv[4];
-        if (AFFINE) {
-          const float4* w4 = reinterpret_cast<const float4*>(lnq_wb) + c * 64 + lane;
-          const float4* b4 = reinterpret_cast<const float4*>(lnq_wb + NCH * 256) + c * 64 + lane;
-          const float4 w0 = w4[0], w1 = w4[32], b0 = b4[0], b1 = b4[32];
-          wv[0] = f2_pack(w0.x, w0.y), wv[1] = f2_pack(w0.z, w0.w), wv[2] = f2_pack(w1.x, w1.y),
-          wv[3] = f2_pack(w1.z, w1.w);
-          bv[0] = f2_pack(b0.x, b0.y), bv[1] = f2_pack(b0.z, b0.w), bv[2] = f2_pack(b1.x, b1.y),
-          bv[3] = f2_pack(b1.z, b1.w);
-        }
+        const uint32_t* hv = reinterpret_cast<const uint32_t*>(&hw[c]);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          uint64_t yy = f2_mul(d[c][i], inv2);
-          if (AFFINE) yy = f2_add(f2_mul(yy, wv[i]), bv[i]);
-          uint32_t h = Cvt<T>::from_f2(yy);
-          if (MODULATE) h = Cvt<T>::add2(Cvt<T>::mul2(h, scw[i]), shw[i]);
-          const T* hp = reinterpret_cast<const T*>(&h);
+          const T* hp = reinterpret_cast<const T*>(&hv[i]);
           v[2 * i] = Cvt<T>::to_f(hp[0]);
           v[2 * i + 1] = Cvt<T>::to_f(hp[1]);
         }
@@ -422,6 +446,71 @@ static void launch_w(int ipw, const void* x, const float* sign, int8_t* q, float
 // The multipliers sit in shared memory transposed ([K/256][K/64] float4), so a
 // warp's threads, which hold consecutive blocks of a row, read consecutive float4.
 // ---------------------------------------------------------------------------
+// The signed H64 of one 64-element block held by one thread: block `b` of a swizzled shared
+// tile (16-byte chunk j of block b at chunk j ^ (b % 8) of its 128-byte row), times the
+// multipliers (`m4[e4 * stride]`, e4 = element / 4), the six butterfly stages in index-bit
+// order 0..5 (stage 0 on scalars, stages 1-5 on f32x2 pairs), * 0.125: the IEEE operations
+// of h64_rotate on the same values.  Leaves (y[2k], y[2k+1]) in P[k]; returns max |y|.
+template <typename T>
+__device__ __forceinline__ float h64_block(const uint8_t* tile, int b, const float4* m4, int stride,
+                                           uint64_t (&P)[32]) {
+  const uint8_t* src = tile + b * 128;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const uint4 raw = *reinterpret_cast<const uint4*>(src + ((j ^ (b & 7)) << 4));
+    P[4 * j] = Cvt<T>::to_f2(raw.x);
+    P[4 * j + 1] = Cvt<T>::to_f2(raw.y);
+    P[4 * j + 2] = Cvt<T>::to_f2(raw.z);
+    P[4 * j + 3] = Cvt<T>::to_f2(raw.w);
+  }
+  // y = x * multiplier
+#pragma unroll
+  for (int e4 = 0; e4 < 16; ++e4) {
+    const float4 m = m4[e4 * stride];
+    P[2 * e4] = f2_mul(P[2 * e4], f2_pack(m.x, m.y));
+    P[2 * e4 + 1] = f2_mul(P[2 * e4 + 1], f2_pack(m.z, m.w));
+  }
+  // stage 0 (index bit 0): the two halves of each pair
+#pragma unroll
+  for (int k = 0; k < 32; ++k) {
+    float a, c;
+    f2_unpack(P[k], a, c);
+    P[k] = f2_pack(__fadd_rn(a, c), __fsub_rn(a, c));
+  }
+  // stages 1..5 (index bits 1..5): pairs k and k + 2^(bit-1)
+#pragma unroll
+  for (int h = 1; h < 32; h <<= 1) {
+#pragma unroll
+    for (int k = 0; k < 32; ++k) {
+      if (k & h) continue;
+      const uint64_t u = P[k], v = P[k + h];
+      P[k] = f2_add(u, v);
+      P[k + h] = f2_sub(u, v);
+    }
+  }
+  float amax = 0.f;
+#pragma unroll
+  for (int k = 0; k < 32; ++k) {
+    P[k] = f2_mul(P[k], f2_splat(0.125f));
+    float lo, hi;
+    f2_unpack(P[k], lo, hi);
+    amax = fmaxf(amax, fmaxf(fabsf(lo), fabsf(hi)));
+  }
+  return amax;
+}
+
+// Codes of one block (P from h64_block) into 64 bytes at dst (16-byte aligned).
+__device__ __forceinline__ void store_block_codes(const uint64_t (&P)[32], float sc, float inv, int8_t* dst) {
+  uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint64_t(&lo)[4] = *reinterpret_cast<const uint64_t(*)[4]>(&P[8 * j]);
+    const uint64_t(&hi)[4] = *reinterpret_cast<const uint64_t(*)[4]>(&P[8 * j + 4]);
+    const uint2 a = quant_pack8_pairs(lo, sc, inv), b = quant_pack8_pairs(hi, sc, inv);
+    d4[j] = make_uint4(a.x, a.y, b.x, b.y);
+  }
+}
+
 constexpr int kQtThreads = 256;
 constexpr int kQtMaxRows = 256;  // rows per tile (a tile of 64-wide rows)
 constexpr int kSiteQuantTile = 960;
@@ -474,48 +563,7 @@ __global__ void __launch_bounds__(kQtThreads, 2)
     const int64_t row = tile * R + rl;
     const bool active = t < tb && row < rows;
     uint64_t P[32];  // (y[2k], y[2k+1])
-    const uint8_t* src = stage0 + s * kQtThreads * 128 + t * 128;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const uint4 raw = *reinterpret_cast<const uint4*>(src + ((j ^ (t & 7)) << 4));
-      P[4 * j] = Cvt<T>::to_f2(raw.x);
-      P[4 * j + 1] = Cvt<T>::to_f2(raw.y);
-      P[4 * j + 2] = Cvt<T>::to_f2(raw.z);
-      P[4 * j + 3] = Cvt<T>::to_f2(raw.w);
-    }
-    // y = x * multiplier
-#pragma unroll
-    for (int e4 = 0; e4 < 16; ++e4) {
-      const float4 m = ms4[e4 * bpr + bc];
-      P[2 * e4] = f2_mul(P[2 * e4], f2_pack(m.x, m.y));
-      P[2 * e4 + 1] = f2_mul(P[2 * e4 + 1], f2_pack(m.z, m.w));
-    }
-    // stage 0 (index bit 0): the two halves of each pair
-#pragma unroll
-    for (int k = 0; k < 32; ++k) {
-      float a, b;
-      f2_unpack(P[k], a, b);
-      P[k] = f2_pack(__fadd_rn(a, b), __fsub_rn(a, b));
-    }
-    // stages 1..5 (index bits 1..5): pairs k and k + 2^(bit-1)
-#pragma unroll
-    for (int h = 1; h < 32; h <<= 1) {
-#pragma unroll
-      for (int k = 0; k < 32; ++k) {
-        if (k & h) continue;
-        const uint64_t u = P[k], v = P[k + h];
-        P[k] = f2_add(u, v);
-        P[k + h] = f2_sub(u, v);
-      }
-    }
-    float amax = 0.f;
-#pragma unroll
-    for (int k = 0; k < 32; ++k) {
-      P[k] = f2_mul(P[k], f2_splat(0.125f));
-      float lo, hi;
-      f2_unpack(P[k], lo, hi);
-      amax = fmaxf(amax, fmaxf(fabsf(lo), fabsf(hi)));
-    }
+    const float amax = h64_block<T>(stage0 + s * kQtThreads * 128, t, ms4 + bc, bpr, P);
     if (active) atomicMax(&rmax[it % 3][rl], __float_as_uint(amax));
     if (t < R) rmax[(it + 1) % 3][t] = 0u;  // the next tile's slot (its readers finished two tiles ago)
     __syncthreads();  // the tile buffer is read and the row maxima are complete
@@ -529,14 +577,7 @@ __global__ void __launch_bounds__(kQtThreads, 2)
       const float sc = __fdiv_rn(fmaxf(__uint_as_float(rmax[it % 3][rl]), 1e-8f), 127.0f);
       const float inv = __frcp_rn(sc);
       if (bc == 0) scale[row] = sc;
-      uint4* dst = reinterpret_cast<uint4*>(q + (tile * tb + t) * 64);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const uint64_t(&lo)[4] = *reinterpret_cast<const uint64_t(*)[4]>(&P[8 * j]);
-        const uint64_t(&hi)[4] = *reinterpret_cast<const uint64_t(*)[4]>(&P[8 * j + 4]);
-        const uint2 a = quant_pack8_pairs(lo, sc, inv), b = quant_pack8_pairs(hi, sc, inv);
-        dst[j] = make_uint4(a.x, a.y, b.x, b.y);
-      }
+      store_block_codes(P, sc, inv, q + (tile * tb + t) * 64);
     }
   }
 }
@@ -561,6 +602,101 @@ static int launch_quant_tiles(const void* x, const float* sign, int8_t* q, float
   const int grid = (int)(ntiles < cap ? ntiles : cap);
   kern<<<grid, kQtThreads, smem, st>>>(tm, sign, q, scale, rows, K, R, ntiles);
   return check_launch("quantize_act_i8");
+}
+
+// ---------------------------------------------------------------------------
+// LayerNorm(-modulate) + quantiser with the rotation of the tiled kernel, for rows of at most
+// 1024 channels.  A tile is R = 256 / (C / 64) whole rows.  Phase 1: each warp computes the
+// LayerNorm of its rows (ln_row_words: the rounded 16-bit h of ln_mod_kernel) and writes h
+// into a swizzled shared tile of 64-element blocks.  Phase 2: one thread per block runs the
+// signed H64 in registers (h64_block), row maxima meet in shared memory, codes and scales
+// follow.  Same h, same rotation arithmetic, same rounding as quantize(layer_norm(x)).
+// ---------------------------------------------------------------------------
+template <typename T, int NCH, bool AFFINE, bool MODULATE>
+__global__ void __launch_bounds__(kQtThreads, 2)
+    ln_quant_tile_kernel(const T* __restrict__ x, int64_t rows, int C, float eps, const float* __restrict__ weight,
+                         const float* __restrict__ bias, const T* __restrict__ scale, const T* __restrict__ shift,
+                         int64_t rows_per_batch, int64_t mod_stride, const float* __restrict__ sign,
+                         int8_t* __restrict__ q, float* __restrict__ qscale, int R, int64_t ntiles) {
+  extern __shared__ __align__(16) uint8_t lqt_smem[];
+  uint8_t* hs = lqt_smem;                                             // [256 blocks][128 B], swizzled
+  float* ms = reinterpret_cast<float*>(lqt_smem + kQtThreads * 128);  // multipliers, transposed
+  float* wb = ms + NCH * 256;                                         // affine parameters, lane order
+  __shared__ uint32_t rmax[2][kQtMaxRows];
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const int bpr = C >> 6;
+  const int bc = t % bpr, rl = t / bpr;
+  for (int i = t; i < C; i += kQtThreads) {
+    const int e = i & 63;
+    ms[(((e >> 2) * bpr + (i >> 6)) << 2) + (e & 3)] = sign[i];
+  }
+  if constexpr (AFFINE) {
+    for (int i = t; i < NCH * 256; i += kQtThreads) {
+      const int c = i >> 8, l = (i >> 3) & 31, h = (i >> 2) & 1, k = i & 3;
+      const int pos = (((c * 2 + h) * 32 + l) << 2) + k;
+      wb[pos] = i < C ? weight[i] : 0.f;
+      wb[NCH * 256 + pos] = i < C ? bias[i] : 0.f;
+    }
+  }
+  __syncthreads();
+  const float4* ms4 = reinterpret_cast<const float4*>(ms);
+  int it = 0;
+  for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
+    // phase 1: LayerNorm rows -> swizzled h blocks; this tile's row-maximum slot cleared (its
+    // last readers, two tiles back, passed the previous tile's barriers)
+    if (t < R) rmax[it & 1][t] = 0u;
+    for (int r = warp; r < R; r += kQtThreads / 32) {
+      const int64_t row = tile * R + r;
+      if (row >= rows) break;
+      uint4 hw[NCH];
+      ln_row_words<T, NCH, AFFINE, MODULATE>(x + row * C, row, C, eps, wb, scale, shift, rows_per_batch,
+                                             mod_stride, lane, hw);
+#pragma unroll
+      for (int c = 0; c < NCH; ++c) {
+        const int base = c * 256 + lane * 8;
+        if (base >= C) continue;
+        const int b = r * bpr + (base >> 6), j = lane & 7;
+        *reinterpret_cast<uint4*>(hs + b * 128 + ((j ^ (b & 7)) << 4)) = hw[c];
+      }
+    }
+    __syncthreads();
+    // phase 2: one thread per 64-element block
+    const int64_t row = tile * R + rl;
+    const bool active = t < R * bpr && row < rows;
+    uint64_t P[32];
+    const float amax = h64_block<T>(hs, t, ms4 + bc, bpr, P);
+    if (active) atomicMax(&rmax[it & 1][rl], __float_as_uint(amax));
+    __syncthreads();  // row maxima complete; the h tile is read
+    if (active) {
+      const float sc = __fdiv_rn(fmaxf(__uint_as_float(rmax[it & 1][rl]), 1e-8f), 127.0f);
+      const float inv = __frcp_rn(sc);
+      if (bc == 0) qscale[row] = sc;
+      store_block_codes(P, sc, inv, q + row * C + bc * 64);
+    }
+  }
+}
+
+template <typename T, int NCH, bool AFFINE, bool MODULATE>
+static int launch_lnq_tiles_t(const void* x, int64_t rows, int C, float eps, const float* w, const float* b,
+                              const void* sc, const void* sh, int64_t rpb, int64_t ms, const float* sign, int8_t* q,
+                              float* qs, cudaStream_t st) {
+  const int bpr = C / 64, R = kQtThreads / bpr;
+  const int64_t ntiles = (rows + R - 1) / R, cap = 2 * (int64_t)sm_count();
+  const int grid = (int)(ntiles < cap ? ntiles : cap);
+  const size_t smem = kQtThreads * 128 + (size_t)NCH * 256 * sizeof(float) * (AFFINE ? 3 : 1);
+  ln_quant_tile_kernel<T, NCH, AFFINE, MODULATE><<<grid, kQtThreads, smem, st>>>(
+      (const T*)x, rows, C, eps, w, b, (const T*)sc, (const T*)sh, rpb, ms, sign, q, qs, R, ntiles);
+  return check_launch("layer_norm_quantize");
+}
+
+template <typename T, int NCH>
+static int launch_lnq_tiles(const void* x, int64_t rows, int C, float eps, const float* w, const float* b,
+                            const void* sc, const void* sh, int64_t rpb, int64_t ms, const float* sign, int8_t* q,
+                            float* qs, cudaStream_t st) {
+  if (w && sc) return launch_lnq_tiles_t<T, NCH, true, true>(x, rows, C, eps, w, b, sc, sh, rpb, ms, sign, q, qs, st);
+  if (w) return launch_lnq_tiles_t<T, NCH, true, false>(x, rows, C, eps, w, b, sc, sh, rpb, ms, sign, q, qs, st);
+  if (sc) return launch_lnq_tiles_t<T, NCH, false, true>(x, rows, C, eps, w, b, sc, sh, rpb, ms, sign, q, qs, st);
+  return launch_lnq_tiles_t<T, NCH, false, false>(x, rows, C, eps, w, b, sc, sh, rpb, ms, sign, q, qs, st);
 }
 
 template <typename T, bool ROTATE>
@@ -628,6 +764,19 @@ extern "C" int hi3d_layer_norm_quantize(const void* x, int8_t* q, float* qscale,
   if (rows_per_batch <= 0) rows_per_batch = rows;
   cudaStream_t st = as_stream(stream);
   const int C = (int)channels;
+  if (C <= 1024 && aligned16(q)) {  // the tiled rotation (codes stored 16 bytes at a time)
+    const int nch = (C + 255) / 256;
+#define HI3D_LNQT(TT, n) \
+  if (nch == n) return launch_lnq_tiles<TT, n>(x, rows, C, eps, weight, bias, scale, shift, rows_per_batch, \
+                                               mod_stride, sign, q, qscale, st);
+    if (dtype == HI3D_F16) {
+      HI3D_LNQT(__half, 1) HI3D_LNQT(__half, 2) HI3D_LNQT(__half, 3) HI3D_LNQT(__half, 4)
+    } else if (dtype == HI3D_BF16) {
+      HI3D_LNQT(__nv_bfloat16, 1) HI3D_LNQT(__nv_bfloat16, 2) HI3D_LNQT(__nv_bfloat16, 3)
+      HI3D_LNQT(__nv_bfloat16, 4)
+    }
+#undef HI3D_LNQT
+  }
   if (dtype == HI3D_F16)
     return dispatch_lnq<__half>(x, rows, C, eps, weight, bias, scale, shift, rows_per_batch, mod_stride, sign, q,
                                 qscale, st);
